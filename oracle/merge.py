@@ -1,0 +1,528 @@
+"""numpy restatement of the reference LoRA-merge kernels (TEST INFRASTRUCTURE ONLY).
+
+Arrays in, arrays out. Factors ``b`` (M x r) and ``a`` (r x N) are fp32 numpy
+arrays holding the exact compute-dtype values (bf16 / fp16 values upcast).
+``compute`` is the LoRA factor dtype: ``"bf16"``, ``"f16"`` or ``"f32"``.
+``seed`` is ``None`` for round-to-nearest, else the uint64 rounding seed.
+
+Every function cites the reference lines whose arithmetic it restates.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .numerics import (
+    bf16_round,
+    bits_f32,
+    clamp,
+    decode_e2m1,
+    decode_e8m0,
+    e2m1_value,
+    encode_e2m1,
+    fdiv,
+    fma_f32,
+    fp8_codec,
+    from_bits_f32,
+    maxnum,
+    minnum,
+    rint_half_even,
+    round_to_compute,
+)
+from .philox import philox_uniform
+
+EPS_2_23 = np.float32(1.1920928955078125e-07)
+FLT_MIN = np.float32(1.1754943508222875e-38)
+
+
+# ---------------------------------------------------------------------------
+# The rank-r update.
+# ---------------------------------------------------------------------------
+
+
+def lora_delta(b: np.ndarray, a: np.ndarray) -> np.ndarray:
+    """fp32 ``B @ A``; correctly rounded (tie class: GPU summation order)."""
+    return (np.asarray(b, np.float64) @ np.asarray(a, np.float64)).astype(np.float32)
+
+
+def merged_values(base: np.ndarray, acc: np.ndarray, strength: float, compute: str) -> np.ndarray:
+    """``(base.to(f32) + acc * strength).to(compute)``; Triton contracts it to an FMA."""
+    return round_to_compute(fma_f32(acc, np.float32(strength), base), compute)
+
+
+def nanmax_reduce(x: np.ndarray, axis: int) -> np.ndarray:
+    """``tl.max`` reduction: maxNum combine, NaN only if every element is NaN."""
+    return np.fmax.reduce(np.asarray(x, np.float32), axis=axis)
+
+
+def nanmin_reduce(x: np.ndarray, axis: int) -> np.ndarray:
+    return np.fmin.reduce(np.asarray(x, np.float32), axis=axis)
+
+
+# ---------------------------------------------------------------------------
+# Stochastic rounding helpers: _triton_stochastic_quantization.py:24-175.
+# ---------------------------------------------------------------------------
+
+
+def sr_round_to_int(values, deterministic, seed, offsets, qmin, qmax):
+    """``_stochastic_round_to_int`` (``_triton_stochastic_quantization.py:24-39``)."""
+    values = np.asarray(values, np.float32)
+    interior = (values > qmin) & (values < qmax)
+    safe = np.where(interior, values, np.float32(0.0)).astype(np.float32)
+    lower = np.floor(safe).astype(np.float32)
+    prob = (safe - lower).astype(np.float32)
+    u = philox_uniform(seed, offsets)
+    rounded = lower + (u < prob).astype(np.float32)
+    return np.where(interior & (prob > 0), rounded, np.asarray(deterministic, np.float32)).astype(np.float32)
+
+
+def sr_float8(values, seed, offsets, e4m3: bool, limit: float) -> np.ndarray:
+    """``_stochastic_float8`` (``_triton_stochastic_quantization.py:132-175``); returns codes."""
+    encode, decode, _ = fp8_codec(e4m3)
+    v = np.asarray(values, np.float32)
+    mag = np.abs(v)
+    det_bits = encode(mag).astype(np.int64)
+    det_val = decode(det_bits)
+    rounded_down = det_val > mag
+    lower_bits = np.where(rounded_down, det_bits - 1, det_bits) & 0xFF
+    upper_bits = np.where(rounded_down, det_bits, det_bits + 1) & 0xFF
+    lower = decode(lower_bits)
+    upper = decode(upper_bits)
+    with np.errstate(invalid="ignore"):
+        ok = upper > lower
+    prob = np.where(ok, fdiv(mag - lower, upper - lower), np.float32(0.0))
+    u = philox_uniform(seed, offsets)
+    mag_bits = np.where(u < prob, upper_bits, lower_bits)
+    sign = (bits_f32(v) >> 24).astype(np.int64) & 0x80
+    chosen = mag_bits | sign
+    det_signed = det_bits | sign
+    interior = (mag < limit) & (prob > 0)
+    return np.where(interior, chosen, det_signed).astype(np.uint8)
+
+
+def sr_e2m1(values, deterministic, seed, offsets) -> np.ndarray:
+    """``_stochastic_e2m1_code`` (``_triton_stochastic_quantization.py:109-129``)."""
+    v = np.asarray(values, np.float32)
+    mag = np.abs(v)
+    det = np.asarray(deterministic, np.int64)
+    nearest_code = det & 7
+    nearest = e2m1_value(nearest_code)
+    rounded_down = nearest > mag
+    lower_code = np.where(rounded_down, nearest_code - 1, nearest_code)
+    upper_code = np.where(rounded_down, nearest_code, nearest_code + 1)
+    lower = e2m1_value(lower_code)
+    upper = e2m1_value(upper_code)
+    prob = np.where(upper > lower, fdiv(mag - lower, upper - lower), np.float32(0.0))
+    u = philox_uniform(seed, offsets)
+    mag_code = np.where(u < prob, upper_code, lower_code)
+    sign = (bits_f32(v) >> 28).astype(np.int64) & 8
+    chosen = mag_code | sign
+    interior = (mag > 0) & (mag < 6.0) & (prob > 0)
+    return np.where(interior, chosen, det).astype(np.int64)
+
+
+def logical_offsets(rows: int, cols: int, base: int = 0) -> np.ndarray:
+    r = np.arange(rows, dtype=np.uint64)[:, None]
+    c = np.arange(cols, dtype=np.uint64)[None, :]
+    return (np.uint64(base) + r * np.uint64(cols) + c).astype(np.uint64)
+
+
+# ---------------------------------------------------------------------------
+# Swizzled (blocked 128x4) scale layout shared by MX and NVFP4:
+# _triton_mx_lora.py:97-112, _triton_nvfp4_lora.py:88-104.
+# ---------------------------------------------------------------------------
+
+
+def scale_index(rows: int, scale_cols: int, swizzled: bool) -> np.ndarray:
+    r = np.arange(rows, dtype=np.int64)[:, None]
+    c = np.arange(scale_cols, dtype=np.int64)[None, :]
+    if not swizzled:
+        return r * scale_cols + c
+    col_blocks = (scale_cols + 3) // 4
+    tile = ((r // 128) * col_blocks + c // 4) * 512
+    rin = r % 128
+    return tile + (rin % 32) * 16 + (rin // 32) * 4 + (c % 4)
+
+
+def unpack_fp4(packed: np.ndarray) -> np.ndarray:
+    """Byte j holds element 2j in its low nibble and 2j+1 in its high nibble."""
+    p = np.asarray(packed, np.uint8)
+    out = np.empty(p.shape[:-1] + (p.shape[-1] * 2,), dtype=np.int64)
+    out[..., 0::2] = p & 0xF
+    out[..., 1::2] = p >> 4
+    return out
+
+
+def pack_fp4(codes: np.ndarray) -> np.ndarray:
+    c = np.asarray(codes, np.int64) & 0xF
+    return (c[..., 0::2] | (c[..., 1::2] << 4)).astype(np.uint8)
+
+
+# ---------------------------------------------------------------------------
+# MX: _triton_mx_lora.py:115-295.
+# ---------------------------------------------------------------------------
+
+MX_FORMATS = {
+    # elem: (target_max_pow2, max_pos, mbits)  -- _triton_mx_lora.py:298-308
+    "e4m3": (8, 448.0, 3),
+    "e5m2": (15, 57344.0, 2),
+    "e2m1": (2, 6.0, 1),
+}
+MX_SCALE_MODES = {"floor": 0, "rceil": 1, "ceil": 2, "even": 3}
+
+
+def exact_ceil_log2(x: np.ndarray) -> np.ndarray:
+    """``ceil(log2(x))`` for positive finite fp32 x, computed exactly."""
+    x = np.asarray(x, np.float32)
+    mant, exp = np.frexp(x.astype(np.float64))  # x = mant * 2**exp, mant in [0.5, 1)
+    return np.where(mant == 0.5, exp - 1, exp).astype(np.float64)
+
+
+def mx_calculate_scale(max_abs, target_pow2, max_pos, mbits, mode):
+    """``_calculate_scale`` (``_triton_mx_lora.py:115-159``) -> (E8M0 code, inverse scale)."""
+    max_abs = np.asarray(max_abs, np.float32)
+    if mode == 1:  # RCEIL
+        descale = fdiv(max_abs, np.float32(max_pos))
+        with np.errstate(divide="ignore", invalid="ignore"):
+            pos = np.isfinite(descale) & (descale > 0)
+            lg = np.where(pos, exact_ceil_log2(np.where(pos, descale, 1.0)),
+                          np.where(descale == 0, -np.inf, np.where(np.isnan(descale), np.nan, np.inf)))
+        unbiased = np.fmin(np.fmax(lg, -127.0), 127.0)
+        encoded = (unbiased + 127.0).astype(np.int64)
+        encoded = np.where(np.isnan(descale), 255, encoded)
+        inv = np.where(encoded == 0, np.float32(1.0), np.exp2(-unbiased).astype(np.float32))
+        return encoded.astype(np.uint8), inv.astype(np.float32)
+    bits = bits_f32(max_abs).astype(np.int64)
+    if mode == 3:  # EVEN
+        bias = {3: 524288, 2: 1048576}.get(mbits, 2097152)
+        bits = ((bits + bias) & 0xFFFFFFFF) & (-8388608 & 0xFFFFFFFF)
+    extracted = ((bits >> 23) & 255) - 127
+    if mode == 2:  # CEIL
+        extracted = extracted + ((bits & 8388607) > 0).astype(np.int64)
+    unbiased = np.clip(extracted - target_pow2, -127, 128)
+    encoded = (unbiased + 127).astype(np.int64) & 0xFF
+    encoded = np.where(np.isnan(max_abs), 255, encoded)
+    scale = from_bits_f32((encoded.astype(np.uint32) << 23).astype(np.uint32))
+    scale = maxnum(scale, FLT_MIN)
+    return encoded.astype(np.uint8), fdiv(np.float32(1.0), scale)
+
+
+def merge_mx(qdata, scale, elem, b, a, strength, *, scaling_mode=0, swizzled=False, seed=None,
+             compute="bf16", offset_base=0):
+    """In-place MX merge (``_merge_mx_kernel``, ``_triton_mx_lora.py:162-295``).
+
+    ``qdata``: uint8 codes (M x N for e4m3/e5m2, M x N/2 packed for e2m1).
+    ``scale``: uint8 E8M0 codes in plain (M x N/32) or swizzled layout.
+    Returns new ``(qdata, scale)`` arrays.
+    """
+    target, max_pos, mbits = MX_FORMATS[elem]
+    M = b.shape[0]
+    N = a.shape[1]
+    nb = N // 32
+    acc = lora_delta(b, a)
+    if elem == "e2m1":
+        codes = unpack_fp4(qdata)
+        base_lp = decode_e2m1(codes)
+    else:
+        _, decode, _ = fp8_codec(elem == "e4m3")
+        base_lp = decode(qdata)
+    sidx = scale_index(M, nb, swizzled)
+    flat_scale = np.asarray(scale, np.uint8).reshape(-1).copy()
+    enc_in = flat_scale[sidx]
+    bscale = np.repeat(decode_e8m0(enc_in), 32, axis=1)
+    if compute == "bf16":
+        base = bf16_round(bf16_round(base_lp) * bf16_round(bscale))
+    else:
+        base = (base_lp * bscale).astype(np.float32)
+    merged = merged_values(base, acc, strength, compute)
+    max_abs = nanmax_reduce(np.abs(merged).reshape(M, nb, 32), axis=2)
+    enc_out, inv = mx_calculate_scale(max_abs, target, max_pos, mbits, scaling_mode)
+    normalized = (merged * np.repeat(inv, 32, axis=1)).astype(np.float32)
+    normalized = clamp(normalized, -max_pos, max_pos)
+    flat_scale[sidx] = enc_out
+    offs = logical_offsets(M, N, offset_base)
+    if elem == "e2m1":
+        out = encode_e2m1(normalized)
+        if seed is not None:
+            out = sr_e2m1(normalized, out, seed, offs)
+        new_q = pack_fp4(out)
+    else:
+        encode, _, _ = fp8_codec(elem == "e4m3")
+        if seed is not None:
+            new_q = sr_float8(normalized, seed, offs, elem == "e4m3", max_pos)
+        else:
+            new_q = encode(normalized)
+    return new_q.astype(np.uint8), flat_scale.reshape(np.shape(scale))
+
+
+# ---------------------------------------------------------------------------
+# NVFP4: _triton_nvfp4_lora.py:107-367 and the global-scale pass 190-266.
+# ---------------------------------------------------------------------------
+
+
+def _nvfp4_merged(qdata, scale, global_scale, swizzled, b, a, strength, compute):
+    """``_merged_tile`` over the whole tensor (``_triton_nvfp4_lora.py:107-187``)."""
+    from .numerics import decode_e4m3
+
+    M = b.shape[0]
+    N = a.shape[1]
+    sc = N // 16
+    codes = unpack_fp4(qdata)
+    base = decode_e2m1(codes)
+    sidx = scale_index(M, sc, swizzled)
+    flat_scale = np.asarray(scale, np.uint8).reshape(-1)
+    bs = decode_e4m3(flat_scale[sidx])
+    if compute == "bf16":
+        bs = bf16_round(bs)
+    if global_scale is not None:
+        bs = (bs * np.float32(global_scale)).astype(np.float32)
+        if compute == "bf16":
+            bs = bf16_round(bs)
+    base = (base * np.repeat(bs, 16, axis=1)).astype(np.float32)
+    if compute == "bf16":
+        base = bf16_round(base)
+    acc = lora_delta(b, a)
+    update = (acc * np.float32(strength)).astype(np.float32)
+    summed = fma_f32(acc, np.float32(strength), base)
+    merged = np.where(update == 0.0, base, summed).astype(np.float32)
+    if compute == "bf16":
+        merged = bf16_round(merged)
+    return merged, sidx
+
+
+def merge_nvfp4(qdata, scale, per_tensor_scale, b, a, strength, *, swizzled=False, seed=None,
+                compute="bf16", offset_base=0):
+    """NVFP4 merge (``merge_nvfp4_lora``, ``_triton_nvfp4_lora.py:515-595``).
+
+    ``qdata`` uint8 (M x N/2), ``scale`` uint8 E4M3 codes (plain or swizzled),
+    ``per_tensor_scale`` fp32 scalar or None. Returns ``(qdata, scale, global)``;
+    the returned scale has zeros in swizzle padding like the reference's
+    ``torch.zeros_like`` output buffer.
+    """
+    from .numerics import encode_e4m3, decode_e4m3
+
+    M = b.shape[0]
+    N = a.shape[1]
+    sc = N // 16
+    g_in = None if per_tensor_scale is None else np.float32(per_tensor_scale)
+    merged, sidx = _nvfp4_merged(qdata, scale, g_in, swizzled, b, a, strength, compute)
+    g_out = None
+    if g_in is not None:
+        amax = nanmax_reduce(np.abs(merged).reshape(-1), axis=0)
+        g_out = maxnum(fdiv(amax, np.float32(2688.0)), EPS_2_23)
+    blocks = merged.reshape(M, sc, 16)
+    max_abs = nanmax_reduce(np.abs(blocks), axis=2)
+    block_scale = fdiv(max_abs, np.float32(6.0))
+    fp8_scale = fdiv(block_scale, g_out) if g_out is not None else block_scale
+    fp8_scale = clamp(fp8_scale, 0.015625, 448.0)
+    fp8_codes = encode_e4m3(fp8_scale)
+    fp8_scale = decode_e4m3(fp8_codes)
+    new_scale = np.zeros(np.asarray(scale).size, dtype=np.uint8)
+    new_scale[sidx] = fp8_codes
+    if g_out is not None:
+        recip = fdiv(fdiv(np.float32(1.0), g_out), fp8_scale)
+        normalized = (merged * np.repeat(recip, 16, axis=1)).astype(np.float32)
+    else:
+        normalized = fdiv(merged, np.repeat(fp8_scale, 16, axis=1))
+    normalized = clamp(normalized, -6.0, 6.0)
+    codes = encode_e2m1(normalized)
+    if seed is not None:
+        codes = sr_e2m1(normalized, codes, seed, logical_offsets(M, N, offset_base))
+    new_q = pack_fp4(codes)
+    return new_q, new_scale.reshape(np.shape(scale)), g_out
+
+
+# ---------------------------------------------------------------------------
+# Scaled FP8: _triton_float8_lora.py:26-308.
+# ---------------------------------------------------------------------------
+
+
+def merge_float8(qdata, scale, block_size, b, a, strength, *, e4m3=True, seed=None, compute="bf16",
+                 offset_base=0):
+    """Scaled-FP8 merge (``merge_float8_lora``, ``_triton_float8_lora.py:486-588``).
+
+    ``qdata`` uint8 codes (M x N); ``scale`` fp32 of shape (M,1) per-row,
+    (1,1)/() per-tensor or (M, N/g) per-group. Returns ``(qdata, scale)``.
+    """
+    encode, decode, limit = fp8_codec(e4m3)
+    M = b.shape[0]
+    N = a.shape[1]
+    acc = lora_delta(b, a)
+    scale = np.asarray(scale, np.float32)
+    per_row = tuple(block_size) == (1, N)
+    per_tensor = tuple(block_size) == (M, N)
+    lp = decode(qdata)
+    if per_row:
+        s_in = scale.reshape(M, 1)
+    elif per_tensor:
+        s_in = scale.reshape(1, 1)
+    else:
+        g = block_size[1]
+        s_in = np.repeat(scale.reshape(M, N // g), g, axis=1)
+    base = round_to_compute((lp * s_in).astype(np.float32), compute)
+    merged = merged_values(base, acc, strength, compute)
+    absv = np.abs(merged)
+    if per_row or per_tensor:
+        amax = nanmax_reduce(absv, axis=1) if per_row else nanmax_reduce(absv.reshape(-1), axis=0)
+        new_scale = round_to_compute(fdiv(amax, np.float32(limit)), compute)
+        new_scale = np.where(new_scale == 0.0, EPS_2_23, new_scale).astype(np.float32)
+        s_out = new_scale.reshape(M, 1) if per_row else new_scale.reshape(1, 1)
+    else:
+        g = block_size[1]
+        amax = nanmax_reduce(absv.reshape(M, N // g, g), axis=2)
+        new_scale = round_to_compute(fdiv(amax, np.float32(limit)), compute)
+        new_scale = np.where(new_scale == 0.0, EPS_2_23, new_scale).astype(np.float32)
+        s_out = np.repeat(new_scale, g, axis=1)
+    scaled = clamp(fdiv(merged, s_out), -limit, limit)
+    if seed is not None:
+        new_q = sr_float8(scaled, seed, logical_offsets(M, N, offset_base), e4m3, limit)
+    else:
+        new_q = encode(scaled)
+    return new_q, new_scale.reshape(scale.shape).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# Affine INT8: _triton_int8_lora.py:24-236.
+# ---------------------------------------------------------------------------
+
+
+def merge_int8(qdata, scale, zero_point, block_size, b, a, strength, *, asymmetric=False,
+               reduce_range=False, seed=None, compute="bf16", qparam="bf16", offset_base=0):
+    """Affine-INT8 merge (``merge_int8_lora``, ``_triton_int8_lora.py:267-407``).
+
+    ``qdata`` int8 (M x N); ``scale`` float values (already in ``qparam``
+    precision) with one entry per quantization block; ``zero_point`` int8 or
+    None. Returns ``(qdata, scale, zero_point)`` (scale rounded to ``qparam``).
+    """
+    qmin, qmax = (-64, 63) if reduce_range else (-128, 127)
+    M = b.shape[0]
+    N = a.shape[1]
+    if tuple(block_size) == (M, N):
+        block_numel = M * N
+    else:
+        block_numel = block_size[1]
+    nq = (M * N) // block_numel
+    flat_q = np.asarray(qdata, np.int8).reshape(-1).astype(np.float32)
+    s_flat = np.asarray(scale, np.float32).reshape(-1)
+    zp_flat = (np.zeros(nq, np.int64) if zero_point is None
+               else np.asarray(zero_point, np.int8).reshape(-1).astype(np.int64))
+    qidx = np.arange(M * N, dtype=np.int64) // block_numel
+    base = round_to_compute(flat_q - zp_flat[qidx].astype(np.float32), compute)
+    base = round_to_compute((base * s_flat[qidx]).astype(np.float32), compute)
+    acc = lora_delta(b, a).reshape(-1)
+    dense = merged_values(base, acc, strength, compute)
+    blocks = dense.reshape(nq, block_numel)
+    min_v = nanmin_reduce(minnum(blocks, np.float32(0.0)), axis=1)
+    max_v = nanmax_reduce(maxnum(blocks, np.float32(0.0)), axis=1)
+    min_v = round_to_compute(min_v, compute)
+    max_v = round_to_compute(max_v, compute)
+    if asymmetric:
+        rng = round_to_compute((max_v - min_v).astype(np.float32), compute)
+        s = fdiv(rng, np.float32(qmax - qmin))
+    else:
+        s = fdiv(maxnum(-min_v, max_v), np.float32((qmax - qmin) / 2.0))
+    s = round_to_compute(s, compute)
+    s = maxnum(s, EPS_2_23)
+    s = round_to_compute(s, compute)
+    if asymmetric:
+        ratio = round_to_compute(fdiv(min_v, s), compute)
+        zp = np.clip(qmin - rint_half_even(ratio), qmin, qmax)
+    else:
+        zp = np.zeros(nq, np.int64)
+    # The output scale buffer has the scale tensor's dtype.
+    s_store = round_to_compute(s, qparam)
+    values = dense
+    sv = s_store[qidx]
+    stochastic_scaled = fdiv(values, sv)
+    inv = round_to_compute(fdiv(np.float32(1.0), sv), qparam)
+    scaled = round_to_compute((values * inv).astype(np.float32), qparam)
+    quant = rint_half_even(scaled) + zp[qidx]
+    quant = quant.astype(np.float32)
+    if seed is not None:
+        offs = (np.uint64(offset_base) + np.arange(M * N, dtype=np.uint64)).astype(np.uint64)
+        quant = sr_round_to_int((stochastic_scaled + zp[qidx].astype(np.float32)).astype(np.float32),
+                                quant, seed, offs, qmin, qmax)
+    quant = np.clip(quant, qmin, qmax).astype(np.int8).reshape(M, N)
+    return quant, s_store.reshape(np.shape(scale)), zp.astype(np.int8).reshape(np.shape(scale))
+
+
+# ---------------------------------------------------------------------------
+# GGUF Q8_0 / Q4_0. Decoding follows gguf_dequant.py:57-61 and :107-115 (the
+# reference's bf16 dequantization on H2D). The reference has no GGUF merge;
+# re-encoding follows the gguf package (0.19.0) quantizers
+# gguf/quants.py Q8_0.quantize_blocks and Q4_0.quantize_blocks.
+# ---------------------------------------------------------------------------
+
+Q8_0 = 8
+Q4_0 = 2
+GGUF_BLOCK = {Q8_0: (32, 34), Q4_0: (32, 18)}
+
+
+def gguf_dequant(raw: np.ndarray, quant_type: int, rows: int, cols: int, compute="bf16") -> np.ndarray:
+    """``gguf_dequant.dequantize(data, qtype, dtype=bf16)`` for Q8_0/Q4_0 as fp32 values."""
+    bs, ts = GGUF_BLOCK[quant_type]
+    blocks = np.asarray(raw, np.uint8).reshape(-1, ts)
+    d = blocks[:, :2].copy().view(np.float16).astype(np.float32)
+    d = round_to_compute(d, compute)
+    if quant_type == Q8_0:
+        q = blocks[:, 2:].view(np.int8).astype(np.float32)
+    else:
+        qs = blocks[:, 2:]
+        q = np.concatenate([qs & 0xF, qs >> 4], axis=1).astype(np.int64) - 8
+        q = q.astype(np.float32)
+    out = round_to_compute((d * q).astype(np.float32), compute)
+    return out.reshape(rows, cols)
+
+
+def roundf_away(x: np.ndarray) -> np.ndarray:
+    """``gguf.quants.np_roundf``: round half away from zero."""
+    a = np.abs(x)
+    fl = np.floor(a)
+    return (np.sign(x) * (fl + np.floor(2 * (a - fl)))).astype(np.float32)
+
+
+def gguf_quantize(values: np.ndarray, quant_type: int, seed=None, offset_base=0) -> np.ndarray:
+    """Re-encode fp32 values (M x N) into raw GGUF blocks.
+
+    RTN reproduces ``gguf.quants.Q8_0/Q4_0.quantize_blocks`` bit for bit.
+    SR (no reference stream exists) draws ``_random`` by logical element
+    offset and rounds the pre-rounding quotient to an adjacent integer code,
+    the same rule as ``_stochastic_round_to_int``.
+    """
+    M, N = values.shape
+    v = np.asarray(values, np.float32).reshape(-1, 32)
+    nblk = v.shape[0]
+    offs = (np.uint64(offset_base) + np.arange(M * N, dtype=np.uint64)).reshape(-1, 32)
+    if quant_type == Q8_0:
+        d = (np.max(np.abs(v), axis=1, keepdims=True) / np.float32(127)).astype(np.float32)
+        with np.errstate(divide="ignore"):
+            inv = np.where(d == 0, np.float32(0), (np.float32(1) / d)).astype(np.float32)
+        x = (v * inv).astype(np.float32)
+        q = roundf_away(x)
+        if seed is not None:
+            q = sr_round_to_int(x, q, seed, offs, -127, 127)
+        q = np.clip(q, -128, 127).astype(np.int8).view(np.uint8)
+        dh = d.astype(np.float16).view(np.uint8).reshape(nblk, 2)
+        return np.concatenate([dh, q], axis=1).reshape(M, N // 32 * 34)
+    imax = np.abs(v).argmax(axis=1)[:, None]
+    mx = np.take_along_axis(v, imax, axis=1)
+    d = (mx / np.float32(-8)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d == 0, np.float32(0), (np.float32(1) / d)).astype(np.float32)
+    x = (v * inv).astype(np.float32)
+    q = np.trunc((x + np.float32(8.5)).astype(np.float32))
+    if seed is not None:
+        q = sr_round_to_int((x + np.float32(8.0)).astype(np.float32), q, seed, offs, 0, 15)
+    q = np.clip(q, 0, 15).astype(np.uint8)
+    packed = (q[:, :16] | (q[:, 16:] << 4)).astype(np.uint8)
+    dh = d.astype(np.float16).view(np.uint8).reshape(nblk, 2)
+    return np.concatenate([dh, packed], axis=1).reshape(M, N // 32 * 18)
+
+
+def merge_gguf(raw, quant_type, b, a, strength, *, seed=None, compute="bf16", offset_base=0):
+    """GGUF merge: dequant (bf16) + fp32 FMA update rounded to bf16 + gguf re-encode."""
+    M = b.shape[0]
+    N = a.shape[1]
+    base = gguf_dequant(raw, quant_type, M, N, compute)
+    merged = merged_values(base, lora_delta(b, a), strength, compute)
+    return gguf_quantize(merged, quant_type, seed=seed, offset_base=offset_base)

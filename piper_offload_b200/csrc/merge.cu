@@ -1,0 +1,1623 @@
+// merge.cu - fused quantized LoRA merge for B200 (sm_100a).
+//
+// One CTA (128 threads) owns a 128-row strip of one weight and a range of its
+// columns, walked in tiles of BN columns. Per tile:
+//   1. codes (and GGUF inline scales) stream global -> shared with 1-D bulk
+//      (TMA-engine) copies, one per row, double-buffered and prefetched one
+//      tile ahead; rows are padded by 16 bytes so the thread-per-row epilogue
+//      reads shared memory without bank conflicts;
+//   2. the rank-r update D = B[rows, :] @ A[:, cols] runs on the 5th-gen tensor
+//      core: B (128 x r, K-major) stays resident in shared memory for the
+//      whole strip, the A tile (r x BN, MN-major) is staged per tile, one
+//      thread issues r/16 tcgen05.mma (M=128, N=BN, K=16) into a BN-column fp32
+//      accumulator in tensor memory and commits to an mbarrier;
+//   3. the epilogue: thread t owns row t (tensor-memory lane t), pulls 32
+//      accumulator columns at a time with tcgen05.ld, decodes codes+scales,
+//      adds the update with the reference's rounding points, computes block /
+//      group amax in registers, encodes scales and codes (round-to-nearest or
+//      Philox stochastic rounding by logical element offset) and writes the
+//      codes back in place through the same shared-memory row with a bulk store.
+// Formats whose scale spans more than one tile (per-row / per-tensor FP8 and
+// INT8, NVFP4 two-level global scale) run a REDUCE launch (amax / min into a
+// workspace with atomics) and then an ENCODE launch; the host planner groups
+// row ranges so that the ENCODE pass re-reads codes from L2.
+//
+// Reference kernels restated here (Piper Offload 0.2.5):
+//   src/piper_offload/_triton_mx_lora.py:162-295      (MX, in place)
+//   src/piper_offload/_triton_nvfp4_lora.py:107-367   (NVFP4)
+//   src/piper_offload/_triton_float8_lora.py:26-308   (scaled FP8)
+//   src/piper_offload/_triton_int8_lora.py:24-236     (affine INT8)
+//   src/piper_offload/_triton_stochastic_quantization.py (SR helpers)
+//   src/piper_offload/gguf_dequant.py:57-115 + gguf quants (GGUF Q8_0 / Q4_0)
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/piper_merge.h"
+#include "numerics.cuh"
+#include "ptx.cuh"
+
+namespace pm {
+
+constexpr int kThreads = 128;
+constexpr int kMaxWeights = 24;
+constexpr int kMaxRank = 256;
+
+enum Pass : int { kLocal = 0, kReduce = 1, kEncode = 2 };
+
+// Device-side descriptor of one weight (or a row range of one weight).
+struct DevWeight {
+  uint8_t* q;
+  void* scale;
+  int8_t* zp;
+  float* gscale;
+  const uint16_t* b;
+  const uint16_t* a;
+  uint32_t* qmax;      // workspace: per-qparam max(|x|) or max(x, 0) as float bits
+  uint32_t* qmin;      // workspace: per-qparam -min(x, 0) as float bits (INT8)
+  float* old_scale;    // workspace: per-qparam input scale (two-pass)
+  int32_t* old_zp;     // workspace: per-qparam input zero point (two-pass)
+  int64_t row_bytes;   // code bytes per row
+  uint64_t offset_base;
+  uint32_t k0, k1;     // Philox key (seed lo / hi)
+  float strength;
+  uint32_t flags;
+  int M, N, r, KP;
+  int row_begin;       // first row of this launch's range (multiple of 128)
+  int row_blocks;      // 128-row strips in the range
+  int col_items;       // work items per strip
+  int item_cols;       // columns per work item (multiple of the tile width)
+  int item_begin;      // first blockIdx of this weight
+  int group;           // FP8/INT8 quantization block width in columns
+  int nq_row;          // FP8/INT8 quantization blocks per row (0 = per tensor)
+  int scale_cols;      // MX: N/32, NVFP4: N/16
+  int scale_mode;      // MX E8M0 rounding
+  int scale_dt;        // INT8 scale dtype
+};
+
+struct LaunchParams {
+  DevWeight w[kMaxWeights];
+  int n_weights;
+};
+
+__host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+// Code bytes for `cols` columns of one row.
+template <int FMT>
+__host__ __device__ constexpr int code_bytes(int cols) {
+  if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) return cols / 2;
+  else if constexpr (FMT == PIPER_FMT_GGUF_Q8_0) return cols / 32 * 34;
+  else if constexpr (FMT == PIPER_FMT_GGUF_Q4_0) return cols / 32 * 18;
+  else return cols;
+}
+
+// Shared-memory row stride of a code tile: 16-byte multiple plus 16 bytes of
+// padding, so 8 consecutive rows start in 8 different 16-byte bank groups.
+template <int FMT, int BN>
+__host__ __device__ constexpr int row_stride() {
+  return align_up(code_bytes<FMT>(BN), 16) + 16;
+}
+
+template <int FMT, int BN>
+__host__ __device__ constexpr int smem_bytes(int kp) {
+  return 128 * kp * 2 + kp * BN * 2 + 2 * 128 * row_stride<FMT, BN>() + 64;
+}
+
+// Blocked 128x4 scale layout (_triton_mx_lora.py:97-112, _triton_nvfp4_lora.py:88-104).
+__device__ __forceinline__ int64_t swizzled_index(int row, int col, int scale_cols) {
+  const int col_blocks = (scale_cols + 3) / 4;
+  const int rin = row & 127;
+  return (static_cast<int64_t>(row >> 7) * col_blocks + (col >> 2)) * 512 + (rin & 31) * 16 +
+         (rin >> 5) * 4 + (col & 3);
+}
+
+__device__ __forceinline__ int64_t scale_index(const DevWeight& W, int row, int col) {
+  if (W.flags & PIPER_FLAG_SWIZZLED) return swizzled_index(row, col, W.scale_cols);
+  return static_cast<int64_t>(row) * W.scale_cols + col;
+}
+
+__device__ __forceinline__ float load_scale_dt(const void* p, int64_t i, int dt) {
+  if (dt == kBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dt == kF16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_scale_dt(void* p, int64_t i, int dt, float v) {
+  if (dt == kBF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else if (dt == kF16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+__device__ __forceinline__ void atomic_max_nonneg(uint32_t* p, float v) {
+  // fmaxf-based accumulation never carries NaN; non-negative floats order like their bits.
+  if (v > 0.0f) atomicMax(p, __float_as_uint(v));
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// ------------------------------------------------------------ MX scales
+struct MxScale {
+  uint32_t code;
+  float inv;
+};
+
+// Exact ceil(log2(d)) for d > 0 (finite or +inf).
+__device__ __forceinline__ float ceil_log2_exact(float d) {
+  const uint32_t bits = __float_as_uint(d);
+  const int ex = static_cast<int>((bits >> 23) & 0xFFu);
+  const uint32_t man = bits & 0x7FFFFFu;
+  if (ex == 0xFF) return __int_as_float(0x7F800000);
+  if (ex == 0) {  // subnormal: d = man * 2^-149
+    const int fl = 31 - __clz(man);
+    return static_cast<float>(fl + ((man & (man - 1u)) ? 1 : 0) - 149);
+  }
+  return static_cast<float>(ex - 127 + (man ? 1 : 0));
+}
+
+__device__ __forceinline__ float exp2_int(float u) {  // 2^u for integral u in [-127, 127]
+  const int e = static_cast<int>(u);
+  if (e >= -126) return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+  return __uint_as_float(1u << (22 + (e + 127)));
+}
+
+// _calculate_scale (_triton_mx_lora.py:115-159).
+__device__ __forceinline__ MxScale mx_scale(float amax, int mode, int target, float maxpos,
+                                            int mbits) {
+  MxScale s;
+  if (mode == PIPER_MX_RCEIL) {
+    const float d = div_full(amax, maxpos);
+    float u;
+    if (d != d) u = __int_as_float(0x7FC00000);
+    else if (d == 0.0f) u = __int_as_float(0xFF800000);
+    else u = ceil_log2_exact(d);
+    u = fminf(fmaxf(u, -127.0f), 127.0f);
+    uint32_t code = static_cast<uint32_t>(__float2int_rz(u + 127.0f)) & 0xFFu;
+    if (d != d) code = 255u;
+    s.code = code;
+    s.inv = code == 0u ? 1.0f : exp2_int(-u);
+    return s;
+  }
+  uint32_t bits = __float_as_uint(amax);
+  if (mode == PIPER_MX_EVEN) {
+    const uint32_t bias = mbits == 3 ? 524288u : (mbits == 2 ? 1048576u : 2097152u);
+    bits = (bits + bias) & 0xFF800000u;
+  }
+  int ex = static_cast<int>((bits >> 23) & 255u) - 127;
+  if (mode == PIPER_MX_CEIL) ex += (bits & 0x7FFFFFu) != 0u ? 1 : 0;
+  int ub = ex - target;
+  ub = ub < -127 ? -127 : (ub > 128 ? 128 : ub);
+  uint32_t code = static_cast<uint32_t>(ub + 127) & 0xFFu;
+  if (amax != amax) code = 255u;
+  float sc = __uint_as_float(code << 23);
+  sc = fmaxf(sc, 1.1754943508222875e-38f);
+  s.code = code;
+  s.inv = div_full(1.0f, sc);
+  return s;
+}
+
+template <int FMT>
+struct MxParams;
+template <>
+struct MxParams<PIPER_FMT_MXFP8_E4M3> {
+  static constexpr int kTarget = 8, kMbits = 3;
+  static constexpr float kMax = 448.0f;
+};
+template <>
+struct MxParams<PIPER_FMT_MXFP8_E5M2> {
+  static constexpr int kTarget = 15, kMbits = 2;
+  static constexpr float kMax = 57344.0f;
+};
+template <>
+struct MxParams<PIPER_FMT_MXFP4> {
+  static constexpr int kTarget = 2, kMbits = 1;
+  static constexpr float kMax = 6.0f;
+};
+
+// ------------------------------------------------------- per-thread context
+struct RowCtx {
+  int row;          // global row
+  bool valid;       // row < M
+  uint8_t* srow;    // this row's code segment in shared memory
+  int tile_col0;    // first column of the tile
+  int tile_cols;    // valid columns in the tile
+};
+
+__device__ __forceinline__ void load_bytes32(const uint8_t* s, uint32_t (&w)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(s);
+  const uint4 b = *reinterpret_cast<const uint4*>(s + 16);
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+__device__ __forceinline__ void store_bytes32(uint8_t* s, const uint32_t (&w)[8]) {
+  *reinterpret_cast<uint4*>(s) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(s + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+}
+__device__ __forceinline__ uint32_t byte_of(const uint32_t (&w)[8], int i) {
+  return (w[i >> 2] >> ((i & 3) * 8)) & 0xFFu;
+}
+
+// ================================================================ MX epilogue
+template <int FMT, int CDT>
+__device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, int k,
+                                         const float (&acc)[32]) {
+  using P = MxParams<FMT>;
+  const int col = c.tile_col0 + 32 * k;
+  const int blk = col >> 5;
+  uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
+  const int64_t sidx = scale_index(W, c.row, blk);
+  const float bscale = dec_e8m0(c.valid ? scale8[sidx] : 127u);
+  float merged[32];
+  if constexpr (FMT == PIPER_FMT_MXFP4) {
+    const uint4 pk = *reinterpret_cast<const uint4*>(c.srow + 16 * k);
+    const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
+    const float bs = CDT == kBF16 ? bf16r(bscale) : bscale;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const uint32_t code = (wv[i >> 3] >> ((i & 7) * 4)) & 0xFu;
+      const float lp = dec_e2m1(code);
+      const float base = CDT == kBF16 ? bf16r(__fmul_rn(bf16r(lp), bs)) : __fmul_rn(lp, bs);
+      merged[i] = round_dt<CDT>(fmaf(acc[i], W.strength, base));
+    }
+  } else {
+    uint32_t wv[8];
+    load_bytes32(c.srow + 32 * k, wv);
+    const float bs = CDT == kBF16 ? bf16r(bscale) : bscale;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float lp = dec_fp8<FMT == PIPER_FMT_MXFP8_E4M3>(byte_of(wv, i));
+      const float base = CDT == kBF16 ? bf16r(__fmul_rn(bf16r(lp), bs)) : __fmul_rn(lp, bs);
+      merged[i] = round_dt<CDT>(fmaf(acc[i], W.strength, base));
+    }
+  }
+  float amax = fabsf(merged[0]);
+#pragma unroll
+  for (int i = 1; i < 32; ++i) amax = fmaxf(amax, fabsf(merged[i]));
+  const MxScale s = mx_scale(amax, W.scale_mode, P::kTarget, P::kMax, P::kMbits);
+  const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+  const PhiloxKey key{W.k0, W.k1};
+  const uint64_t off0 =
+      W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
+  if constexpr (FMT == PIPER_FMT_MXFP4) {
+    uint32_t out[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
+      uint32_t code = enc_e2m1(n);
+      if (sr) code = sr_e2m1(n, code, key, off0 + i);
+      out[i >> 3] |= (code & 0xFu) << ((i & 7) * 4);
+    }
+    *reinterpret_cast<uint4*>(c.srow + 16 * k) = make_uint4(out[0], out[1], out[2], out[3]);
+  } else {
+    constexpr bool kE4 = FMT == PIPER_FMT_MXFP8_E4M3;
+    uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
+      const uint32_t code = sr ? sr_fp8<kE4>(n, P::kMax, key, off0 + i) : enc_fp8<kE4>(n);
+      out[i >> 2] |= code << ((i & 3) * 8);
+    }
+    store_bytes32(c.srow + 32 * k, out);
+  }
+  if (c.valid) scale8[sidx] = static_cast<uint8_t>(s.code);
+}
+
+// ============================================================= NVFP4 epilogue
+// PASS kReduce: accumulate |merged| into `amax_acc`; kLocal: encode.
+template <int PASS, int CDT>
+__device__ __forceinline__ void nvfp4_chunk(const DevWeight& W, const RowCtx& c, int k,
+                                            const float (&acc)[32], float g_in, float g_out,
+                                            bool two_level, float& amax_acc) {
+  const int col = c.tile_col0 + 32 * k;
+  uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
+  const uint4 pk = *reinterpret_cast<const uint4*>(c.srow + 16 * k);
+  const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
+  const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+  const PhiloxKey key{W.k0, W.k1};
+  uint32_t out[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int blk = (col >> 4) + h;
+    const int64_t sidx = scale_index(W, c.row, blk);
+    float bsc = dec_e4m3(c.valid ? scale8[sidx] : 0u);
+    if (CDT == kBF16) bsc = bf16r(bsc);
+    if (two_level) {
+      bsc = __fmul_rn(bsc, g_in);
+      if (CDT == kBF16) bsc = bf16r(bsc);
+    }
+    float merged[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int e = 16 * h + i;
+      const uint32_t code = (wv[e >> 3] >> ((e & 7) * 4)) & 0xFu;
+      float base = __fmul_rn(dec_e2m1(code), bsc);
+      if (CDT == kBF16) base = bf16r(base);
+      const float upd = __fmul_rn(acc[e], W.strength);
+      float m = upd == 0.0f ? base : fmaf(acc[e], W.strength, base);
+      merged[i] = round_dt<CDT>(m);
+    }
+    float amax = fabsf(merged[0]);
+#pragma unroll
+    for (int i = 1; i < 16; ++i) amax = fmaxf(amax, fabsf(merged[i]));
+    if constexpr (PASS == kReduce) {
+      if (c.valid) amax_acc = fmaxf(amax_acc, amax);
+    } else {
+      float fs = div_full(amax, 6.0f);
+      if (two_level) fs = div_full(fs, g_out);
+      fs = fminf(fmaxf(fs, 0.015625f), 448.0f);
+      const uint32_t fcode = enc_e4m3(fs);
+      fs = dec_e4m3(fcode);
+      if (c.valid) scale8[sidx] = static_cast<uint8_t>(fcode);
+      else if (W.flags & PIPER_FLAG_SWIZZLED) scale8[sidx] = 0u;  // padding rows
+      const float recip = two_level ? div_full(div_full(1.0f, g_out), fs) : 0.0f;
+      const uint64_t off0 = W.offset_base +
+                            static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col +
+                            16 * h;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float n = two_level ? __fmul_rn(merged[i], recip) : div_full(merged[i], fs);
+        n = fminf(fmaxf(n, -6.0f), 6.0f);
+        uint32_t code = enc_e2m1(n);
+        if (sr) code = sr_e2m1(n, code, key, off0 + i);
+        const int e = 16 * h + i;
+        out[e >> 3] |= (code & 0xFu) << ((e & 7) * 4);
+      }
+    }
+  }
+  if constexpr (PASS != kReduce)
+    *reinterpret_cast<uint4*>(c.srow + 16 * k) = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// ========================================================= FP8 / INT8 helpers
+template <int FMT>
+struct Int8Range {
+  int qmin, qmax;
+};
+
+__device__ __forceinline__ int qparam_index(const DevWeight& W, int row, int col) {
+  return W.nq_row == 0 ? 0 : row * W.nq_row + col / W.group;
+}
+
+// New FP8 scale from the block amax (_reduce_row_scale_kernel, _triton_float8_lora.py:249-271).
+template <int CDT>
+__device__ __forceinline__ float fp8_new_scale(float amax, float limit) {
+  float s = round_dt<CDT>(div_full(amax, limit));
+  return s == 0.0f ? 1.1920928955078125e-07f : s;
+}
+
+// INT8 qparams (_choose_qparams_kernel, _triton_int8_lora.py:122-186).
+struct Int8Q {
+  float scale;   // value of the stored scale (scale dtype)
+  int zp;
+};
+template <int CDT>
+__device__ __forceinline__ Int8Q int8_qparams(float min_v, float max_v, bool asym, int qmin,
+                                              int qmax, int scale_dt) {
+  min_v = round_dt<CDT>(min_v);
+  max_v = round_dt<CDT>(max_v);
+  float s;
+  if (asym) {
+    const float rng = round_dt<CDT>(__fsub_rn(max_v, min_v));
+    s = div_full(rng, static_cast<float>(qmax - qmin));
+  } else {
+    s = div_full(fmaxf(-min_v, max_v), static_cast<float>(qmax - qmin) / 2.0f);
+  }
+  s = round_dt<CDT>(s);
+  s = fmaxf(s, 1.1920928955078125e-07f);
+  s = round_dt<CDT>(s);
+  int zp = 0;
+  if (asym) {
+    const float ratio = round_dt<CDT>(div_full(min_v, s));
+    long long z = static_cast<long long>(qmin) - __float2ll_rn(ratio);
+    z = z < qmin ? qmin : (z > qmax ? qmax : z);
+    zp = static_cast<int>(z);
+  }
+  Int8Q q;
+  q.scale = round_dt_rt(s, scale_dt);
+  q.zp = zp;
+  return q;
+}
+
+// _quantize_kernel (_triton_int8_lora.py:189-236) for one value.
+__device__ __forceinline__ uint32_t int8_encode(float v, const Int8Q& q, int qmin, int qmax,
+                                                int scale_dt, bool sr, PhiloxKey key,
+                                                uint64_t off) {
+  const float inv = round_dt_rt(div_full(1.0f, q.scale), scale_dt);
+  const float scaled = round_dt_rt(__fmul_rn(v, inv), scale_dt);
+  long long qi = __float2ll_rn(scaled) + q.zp;
+  float qf = static_cast<float>(qi);
+  if (sr) {
+    const float ss = __fadd_rn(div_full(v, q.scale), static_cast<float>(q.zp));
+    qf = sr_int(ss, qf, static_cast<float>(qmin), static_cast<float>(qmax), key, off);
+  }
+  qf = fminf(fmaxf(qf, static_cast<float>(qmin)), static_cast<float>(qmax));
+  return static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu;
+}
+
+// Decode + merge 32 columns of an FP8/INT8 row chunk. Columns >= N are masked
+// (their merged value is 0 and they are excluded by `nvalid`).
+template <int FMT, int CDT>
+__device__ __forceinline__ void affine_merged(const DevWeight& W, const RowCtx& c, int k,
+                                              const float (&acc)[32], const float* scale_in,
+                                              const int* zp_in, float (&merged)[32]) {
+  uint32_t wv[8];
+  load_bytes32(c.srow + 32 * k, wv);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint32_t byte = byte_of(wv, i);
+    float base;
+    if constexpr (FMT == PIPER_FMT_INT8) {
+      const float qv = static_cast<float>(static_cast<int8_t>(byte));
+      base = round_dt<CDT>(__fsub_rn(qv, static_cast<float>(zp_in[i])));
+      base = round_dt<CDT>(__fmul_rn(base, scale_in[i]));
+    } else {
+      base = round_dt<CDT>(__fmul_rn(dec_fp8<FMT == PIPER_FMT_FP8_E4M3>(byte), scale_in[i]));
+    }
+    merged[i] = round_dt<CDT>(fmaf(acc[i], W.strength, base));
+  }
+}
+
+// Input scale / zero point of each column of a chunk.
+template <int FMT, int PASS>
+__device__ __forceinline__ void affine_inputs(const DevWeight& W, const RowCtx& c, int col,
+                                              float (&scale_in)[32], int (&zp_in)[32]) {
+  if (!c.valid) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      scale_in[i] = 1.0f;
+      zp_in[i] = 0;
+    }
+    return;
+  }
+  const bool uniform = W.nq_row == 0 || W.group >= 32;
+  if (uniform && (W.nq_row == 0 || (col % W.group) + 32 <= W.group)) {
+    const int qp = qparam_index(W, c.row, col);
+    float s;
+    int z = 0;
+    if (PASS == kEncode) {
+      s = W.old_scale[qp];
+      z = W.old_zp[qp];
+    } else if (FMT == PIPER_FMT_INT8) {
+      s = c.valid ? load_scale_dt(W.scale, qp, W.scale_dt) : 1.0f;
+      z = (W.zp != nullptr && c.valid) ? static_cast<int>(W.zp[qp]) : 0;
+    } else {
+      s = c.valid ? reinterpret_cast<const float*>(W.scale)[qp] : 1.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      scale_in[i] = s;
+      zp_in[i] = z;
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int cc = min(col + i, W.N - 1);
+    const int qp = qparam_index(W, c.row, cc);
+    if (PASS == kEncode) {
+      scale_in[i] = W.old_scale[qp];
+      zp_in[i] = W.old_zp[qp];
+    } else if (FMT == PIPER_FMT_INT8) {
+      scale_in[i] = c.valid ? load_scale_dt(W.scale, qp, W.scale_dt) : 1.0f;
+      zp_in[i] = (W.zp != nullptr && c.valid) ? static_cast<int>(W.zp[qp]) : 0;
+    } else {
+      scale_in[i] = c.valid ? reinterpret_cast<const float*>(W.scale)[qp] : 1.0f;
+      zp_in[i] = 0;
+    }
+  }
+}
+
+// ============================================================ GGUF epilogue
+__device__ __forceinline__ float roundf_away(float x) {  // gguf.quants.np_roundf
+  const float a = fabsf(x);
+  const float fl = floorf(a);
+  const float b = __fadd_rn(fl, floorf(__fmul_rn(2.0f, __fsub_rn(a, fl))));
+  return x > 0.0f ? b : (x < 0.0f ? -b : 0.0f * x);
+}
+
+template <int FMT, int CDT>
+__device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, int k,
+                                           const float (&acc)[32]) {
+  constexpr bool kQ8 = FMT == PIPER_FMT_GGUF_Q8_0;
+  constexpr int kTS = kQ8 ? 34 : 18;
+  uint8_t* blk = c.srow + kTS * k;
+  const unsigned short dbits = static_cast<unsigned short>(blk[0] | (blk[1] << 8));
+  const float d_in = round_dt<CDT>(__half2float(__ushort_as_half(dbits)));
+  float merged[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float qv;
+    if constexpr (kQ8) {
+      qv = static_cast<float>(static_cast<int8_t>(blk[2 + i]));
+    } else {
+      const uint32_t byte = blk[2 + (i & 15)];
+      qv = static_cast<float>(static_cast<int>(i < 16 ? (byte & 0xFu) : (byte >> 4)) - 8);
+    }
+    const float base = round_dt<CDT>(__fmul_rn(d_in, qv));
+    merged[i] = round_dt<CDT>(fmaf(acc[i], W.strength, base));
+  }
+  const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+  const PhiloxKey key{W.k0, W.k1};
+  const int col = c.tile_col0 + 32 * k;
+  const uint64_t off0 =
+      W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
+  if constexpr (kQ8) {
+    float amax = fabsf(merged[0]);
+#pragma unroll
+    for (int i = 1; i < 32; ++i) amax = fmaxf(amax, fabsf(merged[i]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+    const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+    blk[0] = static_cast<uint8_t>(dh & 0xFFu);
+    blk[1] = static_cast<uint8_t>(dh >> 8);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float x = __fmul_rn(merged[i], id);
+      float q = roundf_away(x);
+      if (sr) q = sr_int(x, q, -127.0f, 127.0f, key, off0 + i);
+      q = fminf(fmaxf(q, -128.0f), 127.0f);
+      blk[2 + i] = static_cast<uint8_t>(static_cast<int8_t>(static_cast<int>(q)));
+    }
+  } else {
+    int imax = 0;
+    float best = fabsf(merged[0]);
+#pragma unroll
+    for (int i = 1; i < 32; ++i) {
+      const float a = fabsf(merged[i]);
+      if (a > best) {
+        best = a;
+        imax = i;
+      }
+    }
+    float mx = merged[0];
+#pragma unroll
+    for (int i = 1; i < 32; ++i) mx = (i == imax) ? merged[i] : mx;
+    const float d = __fdiv_rn(mx, -8.0f);
+    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+    const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+    uint32_t q[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float x = __fmul_rn(merged[i], id);
+      float qf = truncf(__fadd_rn(x, 8.5f));
+      if (sr) qf = sr_int(__fadd_rn(x, 8.0f), qf, 0.0f, 15.0f, key, off0 + i);
+      qf = fminf(fmaxf(qf, 0.0f), 15.0f);
+      q[i] = static_cast<uint32_t>(qf);
+    }
+    blk[0] = static_cast<uint8_t>(dh & 0xFFu);
+    blk[1] = static_cast<uint8_t>(dh >> 8);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) blk[2 + j] = static_cast<uint8_t>(q[j] | (q[j + 16] << 4));
+  }
+}
+
+// ============================================================== the kernel
+template <int FMT, int PASS, int BN, int CDT>
+__global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__ LaunchParams P) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+
+  // Locate this CTA's weight and work item.
+  int wi = 0;
+  while (wi + 1 < P.n_weights && P.w[wi + 1].item_begin <= static_cast<int>(blockIdx.x)) ++wi;
+  const DevWeight& W = P.w[wi];
+  const int local = static_cast<int>(blockIdx.x) - W.item_begin;
+  const int strip = local / W.col_items;
+  const int ci = local - strip * W.col_items;
+  const int row0 = W.row_begin + strip * 128;
+  const int col_begin = ci * W.item_cols;
+  const int col_end = min(W.N, col_begin + W.item_cols);
+  const int n_tiles = (col_end - col_begin + BN - 1) / BN;
+
+  constexpr int RS = row_stride<FMT, BN>();
+  const int KP = W.KP;
+  uint8_t* sB = smem;
+  uint8_t* sA = smem + 128 * KP * 2;
+  uint8_t* sC = sA + KP * BN * 2;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sC + 2 * 128 * RS);
+  uint64_t* bar_load = bars;      // [2]
+  uint64_t* bar_mma = bars + 2;   // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+
+  const int row = row0 + tid;
+  const bool valid = row < W.M;
+
+  if (tid == 0) {
+    mbar_init(&bar_load[0], kThreads);
+    mbar_init(&bar_load[1], kThreads);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+  }
+
+  // ---- resident B strip (K-major canonical): chunk kc of row t at kc*2048 + (t/8)*128 + (t%8)*16.
+  {
+    const uint16_t* brow = W.b + static_cast<int64_t>(row) * W.r;
+    const bool vec = ((reinterpret_cast<uintptr_t>(W.b) | (W.r * 2)) & 15) == 0;
+    for (int kc = 0; kc < KP / 8; ++kc) {
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (valid) {
+        if (vec && kc * 8 + 8 <= W.r) {
+          v = __ldg(reinterpret_cast<const uint4*>(brow + kc * 8));
+        } else {
+          uint16_t e[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) e[j] = (kc * 8 + j < W.r) ? brow[kc * 8 + j] : 0;
+          v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16),
+                         e[6] | (e[7] << 16));
+        }
+      }
+      *reinterpret_cast<uint4*>(sB + kc * 2048 + (tid >> 3) * 128 + (tid & 7) * 16) = v;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // ---- code-tile loader: thread t moves its own row segment.
+  auto issue_load = [&](int tile, int stage) {
+    uint8_t* dst = sC + stage * 128 * RS + tid * RS;
+    const int c0 = col_begin + tile * BN;
+    const int ncols = min(BN, col_end - c0);
+    int off, nbytes;
+    if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
+      off = code_bytes<FMT>(c0);
+      nbytes = code_bytes<FMT>(ncols);
+    } else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) {
+      off = c0 / 2;
+      nbytes = ncols / 2;
+    } else {
+      off = c0;
+      nbytes = ncols;
+    }
+    if (!valid || nbytes <= 0) {
+      mbar_arrive(&bar_load[stage]);
+      return;
+    }
+    const uint8_t* src = W.q + static_cast<int64_t>(row) * W.row_bytes + off;
+    if (((reinterpret_cast<uintptr_t>(src) | nbytes) & 15) == 0) {
+      bulk_wait_read_all();  // a previous bulk store may still read this row
+      mbar_arrive_expect_tx(&bar_load[stage], static_cast<uint32_t>(nbytes));
+      bulk_g2s(dst, src, static_cast<uint32_t>(nbytes), &bar_load[stage]);
+    } else {
+      bulk_wait_read_all();
+      for (int i = 0; i < nbytes; ++i) dst[i] = src[i];
+      mbar_arrive(&bar_load[stage]);
+    }
+  };
+
+  const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+  (void)sr;
+  // Per-thread running reductions for REDUCE passes.
+  float red_max = 0.0f, red_nmin = 0.0f;
+  int red_qp = -1;
+  auto flush_reduce = [&]() {
+    if (red_qp >= 0) {
+      atomic_max_nonneg(&W.qmax[red_qp], red_max);
+      if (FMT == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[red_qp], red_nmin);
+    }
+    red_max = 0.0f;
+    red_nmin = 0.0f;
+  };
+  // NVFP4 global scales (two-level).
+  const bool two_level = (FMT == PIPER_FMT_NVFP4) && W.gscale != nullptr;
+  float g_in = 1.0f, g_out = 1.0f;
+  if constexpr (FMT == PIPER_FMT_NVFP4) {
+    if (two_level) {
+      if (PASS == kReduce) {
+        g_in = *W.gscale;
+        if (blockIdx.x == static_cast<unsigned>(W.item_begin) && tid == 0) W.old_scale[0] = g_in;
+      } else {
+        g_in = W.old_scale[0];
+        const float amax = __uint_as_float(*W.qmax);
+        g_out = fmaxf(div_full(amax, 2688.0f), 1.1920928955078125e-07f);
+      }
+    }
+  }
+
+  bool ok = true;
+  if (n_tiles > 0) issue_load(0, 0);
+  for (int tile = 0; tile < n_tiles && ok; ++tile) {
+    const int stage = tile & 1;
+    const int c0 = col_begin + tile * BN;
+    const int tcols = min(BN, col_end - c0);
+
+    // ---- stage the A tile (MN-major canonical): element (k, n) at
+    //      (k/8)*(BN*16) + (n/8)*128 + (k%8)*16 + (n%8)*2.
+    {
+      const bool vec = (((reinterpret_cast<uintptr_t>(W.a)) | (W.N * 2)) & 15) == 0;
+      const int chunks = KP * BN / 8;
+      for (int idx = tid; idx < chunks; idx += kThreads) {
+        const int kk = idx & 7;
+        const int ng = (idx >> 3) % (BN / 8);
+        const int kg = idx / BN;
+        const int kr = kg * 8 + kk;
+        const int n = c0 + ng * 8;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (kr < W.r) {
+          const uint16_t* ap = W.a + static_cast<int64_t>(kr) * W.N + n;
+          if (vec && n + 8 <= col_end) {
+            v = __ldg(reinterpret_cast<const uint4*>(ap));
+          } else {
+            uint16_t e[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) e[j] = (n + j < col_end) ? ap[j] : 0;
+            v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16),
+                           e[6] | (e[7] << 16));
+          }
+        }
+        *reinterpret_cast<uint4*>(sA + kg * (BN * 16) + ng * 128 + kk * 16) = v;
+      }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    // ---- issue the update on the tensor core.
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t a_base = smem_u32(sB);
+      const uint32_t b_base = smem_u32(sA);
+      constexpr uint32_t idesc = idesc_f16(BN, CDT == kBF16 ? 1u : 0u);
+      for (int ks = 0; ks < KP / 16; ++ks) {
+        const uint64_t adesc = smem_desc(a_base + ks * 2 * 2048, 2048, 128);
+        const uint64_t bdesc = smem_desc(b_base + ks * 2 * (BN * 16), BN * 16, 128);
+        umma_f16(tmem, adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
+      }
+      umma_commit(bar_mma);
+    }
+
+    // ---- prefetch the next code tile into the other stage.
+    if (tile + 1 < n_tiles) issue_load(tile + 1, stage ^ 1);
+
+    ok = mbar_wait(&bar_load[stage], (tile >> 1) & 1, kStatusTimeoutLoad);
+    ok = mbar_wait(bar_mma, tile & 1, kStatusTimeoutMma) && ok;
+    // Keep the CTA uniform: tcgen05.ld below is warp-collective.
+    ok = __syncthreads_and(ok) != 0;
+    tc_fence_after();
+    if (!ok) {
+      // Give copies and MMAs in flight a bounded chance to land before exit.
+      if (tile + 1 < n_tiles) mbar_wait(&bar_load[stage ^ 1], ((tile + 1) >> 1) & 1, kStatusTimeoutLoad);
+      break;
+    }
+
+    RowCtx c;
+    c.row = row;
+    c.valid = valid;
+    c.srow = sC + stage * 128 * RS + tid * RS;
+    c.tile_col0 = c0;
+    c.tile_cols = tcols;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+
+    if (ok) {
+      if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 ||
+                    FMT == PIPER_FMT_MXFP4) {
+        for (int k = 0; k < tcols / 32; ++k) {
+          float acc[32];
+          tmem_ld32(taddr + 32 * k, acc);
+          mx_chunk<FMT, CDT>(W, c, k, acc);
+        }
+      } else if constexpr (FMT == PIPER_FMT_NVFP4) {
+        for (int k = 0; k < tcols / 32; ++k) {
+          float acc[32];
+          tmem_ld32(taddr + 32 * k, acc);
+          nvfp4_chunk<PASS, CDT>(W, c, k, acc, g_in, g_out, two_level, red_max);
+        }
+        if (tcols & 31) {  // trailing 16-column block
+          float acc[32];
+          const int k = tcols / 32;
+          tmem_ld32(taddr + 32 * k, acc);
+          // Process as a chunk whose second half is ignored: reuse the 32-wide
+          // routine on a copy with the second block neutralised.
+          // (N % 16 == 0 is validated on the host.)
+          const int col = c0 + 32 * k;
+          uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
+          const int blk = col >> 4;
+          const int64_t sidx = scale_index(W, row, blk);
+          float bsc = dec_e4m3(valid ? scale8[sidx] : 0u);
+          if (CDT == kBF16) bsc = bf16r(bsc);
+          if (two_level) {
+            bsc = __fmul_rn(bsc, g_in);
+            if (CDT == kBF16) bsc = bf16r(bsc);
+          }
+          const uint2 pk = *reinterpret_cast<const uint2*>(c.srow + 16 * k);
+          const uint32_t wv[2] = {pk.x, pk.y};
+          float merged[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint32_t code = (wv[i >> 3] >> ((i & 7) * 4)) & 0xFu;
+            float base = __fmul_rn(dec_e2m1(code), bsc);
+            if (CDT == kBF16) base = bf16r(base);
+            const float upd = __fmul_rn(acc[i], W.strength);
+            merged[i] = round_dt<CDT>(upd == 0.0f ? base : fmaf(acc[i], W.strength, base));
+          }
+          float amax = fabsf(merged[0]);
+#pragma unroll
+          for (int i = 1; i < 16; ++i) amax = fmaxf(amax, fabsf(merged[i]));
+          if (PASS == kReduce) {
+            if (valid) red_max = fmaxf(red_max, amax);
+          } else {
+            float fs = div_full(amax, 6.0f);
+            if (two_level) fs = div_full(fs, g_out);
+            fs = fminf(fmaxf(fs, 0.015625f), 448.0f);
+            const uint32_t fcode = enc_e4m3(fs);
+            fs = dec_e4m3(fcode);
+            if (valid) scale8[sidx] = static_cast<uint8_t>(fcode);
+            else if (W.flags & PIPER_FLAG_SWIZZLED) scale8[sidx] = 0u;
+            const float recip = two_level ? div_full(div_full(1.0f, g_out), fs) : 0.0f;
+            const uint64_t off0 =
+                W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + col;
+            const PhiloxKey key{W.k0, W.k1};
+            uint32_t out[2] = {0u, 0u};
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float n = two_level ? __fmul_rn(merged[i], recip) : div_full(merged[i], fs);
+              n = fminf(fmaxf(n, -6.0f), 6.0f);
+              uint32_t code = enc_e2m1(n);
+              if (W.flags & PIPER_FLAG_STOCHASTIC) code = sr_e2m1(n, code, key, off0 + i);
+              out[i >> 3] |= (code & 0xFu) << ((i & 7) * 4);
+            }
+            *reinterpret_cast<uint2*>(c.srow + 16 * k) = make_uint2(out[0], out[1]);
+          }
+        }
+      } else if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
+        for (int k = 0; k < tcols / 32; ++k) {
+          float acc[32];
+          tmem_ld32(taddr + 32 * k, acc);
+          gguf_chunk<FMT, CDT>(W, c, k, acc);
+        }
+      } else {
+        // ------------------------------------------- FP8 / INT8 (affine) paths
+        constexpr bool kInt8 = FMT == PIPER_FMT_INT8;
+        constexpr bool kE4 = FMT == PIPER_FMT_FP8_E4M3;
+        constexpr float kLimit = kE4 ? 448.0f : 57344.0f;
+        const bool asym = (W.flags & PIPER_FLAG_ASYMMETRIC) != 0u;
+        const int qmin = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? -64 : -128;
+        const int qmax = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? 63 : 127;
+        const PhiloxKey key{W.k0, W.k1};
+        const int nchunks = (tcols + 31) / 32;
+        if constexpr (PASS == kLocal) {
+          // Groups of W.group (multiple of 32, dividing the tile width) are local.
+          const int gch = W.group / 32;
+          for (int g0 = 0; g0 < nchunks; g0 += gch) {
+            float gmax = 0.0f, gmin = 0.0f, gabs = 0.0f;
+            float scale_in[32];
+            int zp_in[32];
+            for (int k = g0; k < g0 + gch; ++k) {
+              float acc[32], merged[32];
+              tmem_ld32(taddr + 32 * k, acc);
+              affine_inputs<FMT, PASS>(W, c, c0 + 32 * k, scale_in, zp_in);
+              affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                gabs = fmaxf(gabs, fabsf(merged[i]));
+                gmax = fmaxf(gmax, merged[i]);
+                gmin = fminf(gmin, merged[i]);
+              }
+            }
+            const int qp = qparam_index(W, row, c0 + 32 * g0);
+            if constexpr (kInt8) {
+              const Int8Q q = int8_qparams<CDT>(gmin, gmax, asym, qmin, qmax, W.scale_dt);
+              if (valid) {
+                store_scale_dt(W.scale, qp, W.scale_dt, q.scale);
+                if (W.zp != nullptr) W.zp[qp] = static_cast<int8_t>(q.zp);
+              }
+              for (int k = g0; k < g0 + gch; ++k) {
+                float acc[32], merged[32];
+                tmem_ld32(taddr + 32 * k, acc);
+                affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
+                uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+                const uint64_t off0 = W.offset_base +
+                                      static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) +
+                                      c0 + 32 * k;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  out[i >> 2] |= int8_encode(merged[i], q, qmin, qmax, W.scale_dt,
+                                             (W.flags & PIPER_FLAG_STOCHASTIC) != 0u, key,
+                                             off0 + i)
+                                 << ((i & 3) * 8);
+                store_bytes32(c.srow + 32 * k, out);
+              }
+            } else {
+              const float s = fp8_new_scale<CDT>(gabs, kLimit);
+              if (valid) reinterpret_cast<float*>(W.scale)[qp] = s;
+              for (int k = g0; k < g0 + gch; ++k) {
+                float acc[32], merged[32];
+                tmem_ld32(taddr + 32 * k, acc);
+                affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
+                uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+                const uint64_t off0 = W.offset_base +
+                                      static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) +
+                                      c0 + 32 * k;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
+                  const uint32_t code = (W.flags & PIPER_FLAG_STOCHASTIC)
+                                            ? sr_fp8<kE4>(x, kLimit, key, off0 + i)
+                                            : enc_fp8<kE4>(x);
+                  out[i >> 2] |= code << ((i & 3) * 8);
+                }
+                store_bytes32(c.srow + 32 * k, out);
+              }
+            }
+          }
+        } else {
+          for (int k = 0; k < nchunks; ++k) {
+            float acc[32], merged[32], scale_in[32];
+            int zp_in[32];
+            tmem_ld32(taddr + 32 * k, acc);
+            const int col = c0 + 32 * k;
+            affine_inputs<FMT, PASS>(W, c, col, scale_in, zp_in);
+            affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
+            const int nvalid = min(32, tcols - 32 * k);
+            if constexpr (PASS == kReduce) {
+              if (valid) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  if (i < nvalid) {
+                    const int qp = qparam_index(W, row, col + i);
+                    if (qp != red_qp) {
+                      flush_reduce();
+                      red_qp = qp;
+                      // First touch of a quantization block saves its input qparams.
+                      if (W.nq_row == 0 ? (row == 0 && col + i == 0) : ((col + i) % W.group == 0)) {
+                        if (kInt8) {
+                          W.old_scale[qp] = load_scale_dt(W.scale, qp, W.scale_dt);
+                          W.old_zp[qp] = W.zp != nullptr ? static_cast<int>(W.zp[qp]) : 0;
+                        } else {
+                          W.old_scale[qp] = reinterpret_cast<const float*>(W.scale)[qp];
+                        }
+                      }
+                    }
+                    if (kInt8) {
+                      red_max = fmaxf(red_max, merged[i]);
+                      red_nmin = fmaxf(red_nmin, -merged[i]);
+                    } else {
+                      red_max = fmaxf(red_max, fabsf(merged[i]));
+                    }
+                  }
+                }
+              }
+            } else {  // kEncode
+              uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+              const uint64_t off0 =
+                  W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + col;
+              int cur_qp = -1;
+              Int8Q q;
+              q.scale = 1.0f;
+              q.zp = 0;
+              float s = 1.0f;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                if (i < nvalid && valid) {
+                  const int qp = qparam_index(W, row, col + i);
+                  if (qp != cur_qp) {
+                    cur_qp = qp;
+                    const float qmx = __uint_as_float(W.qmax[qp]);
+                    if (kInt8) {
+                      const float qmn = -__uint_as_float(W.qmin[qp]);
+                      q = int8_qparams<CDT>(qmn, qmx, asym, qmin, qmax, W.scale_dt);
+                    } else {
+                      s = fp8_new_scale<CDT>(qmx, kLimit);
+                    }
+                    const bool owner =
+                        W.nq_row == 0 ? (row == 0 && col + i == 0) : ((col + i) % W.group == 0);
+                    if (owner) {
+                      if (kInt8) {
+                        store_scale_dt(W.scale, qp, W.scale_dt, q.scale);
+                        if (W.zp != nullptr) W.zp[qp] = static_cast<int8_t>(q.zp);
+                      } else {
+                        reinterpret_cast<float*>(W.scale)[qp] = s;
+                      }
+                    }
+                  }
+                  uint32_t code;
+                  if (kInt8) {
+                    code = int8_encode(merged[i], q, qmin, qmax, W.scale_dt,
+                                       (W.flags & PIPER_FLAG_STOCHASTIC) != 0u, key, off0 + i);
+                  } else {
+                    const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
+                    code = (W.flags & PIPER_FLAG_STOCHASTIC) ? sr_fp8<kE4>(x, kLimit, key, off0 + i)
+                                                             : enc_fp8<kE4>(x);
+                  }
+                  out[i >> 2] |= code << ((i & 3) * 8);
+                }
+              }
+              store_bytes32(c.srow + 32 * k, out);
+            }
+          }
+        }
+      }
+    }
+
+    // ---- write the tile back (in place).
+    if (PASS != kReduce && ok && valid) {
+      int off, nbytes;
+      if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
+        off = code_bytes<FMT>(c0);
+        nbytes = code_bytes<FMT>(tcols);
+      } else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) {
+        off = c0 / 2;
+        nbytes = tcols / 2;
+      } else {
+        off = c0;
+        nbytes = tcols;
+      }
+      uint8_t* dst = W.q + static_cast<int64_t>(row) * W.row_bytes + off;
+      if (((reinterpret_cast<uintptr_t>(dst) | nbytes) & 15) == 0) {
+        fence_proxy_async_smem();
+        bulk_s2g(dst, c.srow, static_cast<uint32_t>(nbytes));
+        bulk_commit();
+      } else {
+        for (int i = 0; i < nbytes; ++i) dst[i] = c.srow[i];
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+
+  // ---- REDUCE epilogue: publish running maxima.
+  if constexpr (PASS == kReduce) {
+    if constexpr (FMT == PIPER_FMT_NVFP4) {
+      const float m = warp_max(red_max);
+      if ((tid & 31) == 0) atomic_max_nonneg(W.qmax, m);
+    } else {
+      if (W.nq_row == 0) {
+        const float m = warp_max(red_max);
+        const float n = warp_max(red_nmin);
+        if ((tid & 31) == 0) {
+          atomic_max_nonneg(&W.qmax[0], m);
+          if (FMT == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[0], n);
+        }
+      } else {
+        flush_reduce();
+      }
+    }
+  }
+
+  // ---- NVFP4: zero swizzle padding columns and publish the new global scale.
+  if constexpr (FMT == PIPER_FMT_NVFP4 && PASS == kLocal) {
+    if ((W.flags & PIPER_FLAG_SWIZZLED) && col_end == W.N) {
+      const int padded = align_up(W.scale_cols, 4);
+      uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
+      for (int pc = W.scale_cols; pc < padded; ++pc) scale8[swizzled_index(row, pc, W.scale_cols)] = 0u;
+    }
+    if (two_level && blockIdx.x == static_cast<unsigned>(W.item_begin) && tid == 0) *W.gscale = g_out;
+  }
+
+  bulk_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+}  // namespace pm
+
+
+// =================================================================== host side
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+using pm::DevWeight;
+using pm::LaunchParams;
+
+// Bytes of codes a two-pass launch group covers, so that its ENCODE launch
+// re-reads them from L2 (126 MB on B200).
+constexpr int64_t kL2GroupBytes = 48ll << 20;
+
+struct Plan {
+  int bn = 128;
+  bool two_pass = false;
+  int nq = 0;          // quantization blocks held in the workspace
+  int nq_row = 0;      // blocks per row (0 = per tensor)
+  int group = 0;
+  size_t ws_off = 0;
+};
+
+bool is_fp_dt(int dt) { return dt == PIPER_DT_BF16 || dt == PIPER_DT_F16 || dt == PIPER_DT_F32; }
+
+int64_t row_bytes_of(const piper_merge_desc& d) {
+  switch (d.format) {
+    case PIPER_FMT_MXFP4:
+    case PIPER_FMT_NVFP4: return d.cols / 2;
+    case PIPER_FMT_GGUF_Q8_0: return d.cols / 32 * 34;
+    case PIPER_FMT_GGUF_Q4_0: return d.cols / 32 * 18;
+    default: return d.cols;
+  }
+}
+
+// Argument checks mirror the reference launchers (e.g. _triton_mx_lora.py:348-393).
+int validate(const piper_merge_desc& d, Plan& p) {
+  if (d.rows <= 0 || d.cols <= 0 || d.rank <= 0)
+    return fail(PIPER_MERGE_EINVAL, "merge requires non-empty weight and factors.");
+  if (d.rows > (1 << 30) || d.cols > (1 << 30) || d.rows * d.cols > (int64_t(1) << 40))
+    return fail(PIPER_MERGE_EINVAL, "weight dimensions are too large.");
+  if (d.rank > pm::kMaxRank)
+    return fail(PIPER_MERGE_EINVAL, "LoRA rank above 256 is not supported by the sm_100a merge (rank " +
+                                        std::to_string(d.rank) + ").");
+  if (d.qdata == nullptr || d.b == nullptr || d.a == nullptr)
+    return fail(PIPER_MERGE_EINVAL, "null qdata or factor pointer.");
+  if (d.compute_dtype != PIPER_DT_BF16 && d.compute_dtype != PIPER_DT_F16)
+    return fail(PIPER_MERGE_EINVAL, "the sm_100a merge supports bfloat16 and float16 LoRA factors.");
+  p = Plan();
+  switch (d.format) {
+    case PIPER_FMT_MXFP8_E4M3:
+    case PIPER_FMT_MXFP8_E5M2:
+    case PIPER_FMT_MXFP4:
+      if (d.cols % 32 != 0) return fail(PIPER_MERGE_EINVAL, "MX merge requires columns divisible by 32.");
+      if (d.compute_dtype != PIPER_DT_BF16)
+        return fail(PIPER_MERGE_EINVAL, "MX merge supports bfloat16 weights and factors.");
+      if (d.scale_mode < 0 || d.scale_mode > 3)
+        return fail(PIPER_MERGE_EINVAL, "Unsupported MX scaling mode id " + std::to_string(d.scale_mode) + ".");
+      if (d.scale == nullptr) return fail(PIPER_MERGE_EINVAL, "MX merge requires E8M0 scales.");
+      break;
+    case PIPER_FMT_NVFP4:
+      if (d.cols % 16 != 0) return fail(PIPER_MERGE_EINVAL, "NVFP4 merge requires columns divisible by 16.");
+      if (d.compute_dtype != PIPER_DT_BF16)
+        return fail(PIPER_MERGE_EINVAL, "NVFP4 merge supports bfloat16 factors.");
+      if (d.scale == nullptr) return fail(PIPER_MERGE_EINVAL, "NVFP4 merge requires E4M3 block scales.");
+      if (d.global_scale != nullptr) {
+        p.two_pass = true;
+        p.nq = 1;
+      }
+      break;
+    case PIPER_FMT_FP8_E4M3:
+    case PIPER_FMT_FP8_E5M2:
+    case PIPER_FMT_INT8: {
+      if (d.scale == nullptr) return fail(PIPER_MERGE_EINVAL, "scaled merge requires scales.");
+      if (d.format == PIPER_FMT_INT8 && !is_fp_dt(d.scale_dtype))
+        return fail(PIPER_MERGE_EINVAL, "INT8 merge supports float16, bfloat16 and float32 scales.");
+      const bool per_tensor = d.block_rows == d.rows && d.block_cols == d.cols;
+      const bool per_block = d.block_rows == 1 && d.block_cols > 0 && d.block_cols <= d.cols &&
+                             d.cols % d.block_cols == 0;
+      if (!per_tensor && !per_block)
+        return fail(PIPER_MERGE_EINVAL,
+                    "supports two-dimensional per-tensor, per-row and per-group layouts, got block size (" +
+                        std::to_string(d.block_rows) + ", " + std::to_string(d.block_cols) + ").");
+      if (per_tensor) {
+        p.two_pass = true;
+        p.nq = 1;
+        p.nq_row = 0;
+        p.group = static_cast<int>(d.cols);
+      } else {
+        const int g = static_cast<int>(d.block_cols);
+        p.group = g;
+        p.nq_row = static_cast<int>(d.cols / g);
+        if (g < d.cols && (g == 32 || g == 64 || g == 128 || g == 256)) {
+          p.bn = g <= 128 ? 128 : 256;
+        } else {
+          p.two_pass = true;
+          p.nq = static_cast<int>(d.rows * p.nq_row);
+        }
+      }
+      break;
+    }
+    case PIPER_FMT_GGUF_Q8_0:
+    case PIPER_FMT_GGUF_Q4_0:
+      if (d.cols % 32 != 0) return fail(PIPER_MERGE_EINVAL, "GGUF merge requires columns divisible by 32.");
+      p.bn = 256;
+      break;
+    default:
+      return fail(PIPER_MERGE_EINVAL, "unknown format id " + std::to_string(d.format) + ".");
+  }
+  return PIPER_MERGE_OK;
+}
+
+size_t scratch_bytes(int nq) {
+  // qmax, qmin, old_scale, old_zp: four words per quantization block, 256-byte aligned.
+  return nq == 0 ? 0 : (static_cast<size_t>(nq) * 16 + 255) / 256 * 256;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// ------------------------------------------------------------- dispatch
+// Each CTA allocates BN tensor-memory columns of the SM's 512. Request enough
+// shared memory that at most 512 / BN CTAs can be resident on one SM, so a
+// tcgen05.alloc never has to wait for another CTA to release its columns.
+constexpr int kSmemPerSm = 233472;      // 228 KB
+constexpr int kSmemReservedPerCta = 1024;
+constexpr int min_smem_for_tmem(int bn) {
+  return kSmemPerSm / (512 / bn + 1) - kSmemReservedPerCta + 16;
+}
+
+template <int FMT, int PASS, int BN, int CDT>
+int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
+  auto kern = pm::merge_kernel<FMT, PASS, BN, CDT>;
+  const int smem = std::max(pm::smem_bytes<FMT, BN>(kp_max), min_smem_for_tmem(BN));
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess)
+    return fail(PIPER_MERGE_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  kern<<<items, pm::kThreads, smem, stream>>>(lp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  return PIPER_MERGE_OK;
+}
+
+template <int FMT, int PASS, int CDT>
+int launch_bn(int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
+  if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
+    return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
+  } else if constexpr (FMT == PIPER_FMT_FP8_E4M3 || FMT == PIPER_FMT_FP8_E5M2 || FMT == PIPER_FMT_INT8) {
+    if (PASS == pm::kLocal && bn == 256) return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
+    return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
+  } else {
+    (void)bn;
+    return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
+  }
+}
+
+template <int PASS, int CDT>
+int launch_fmt(int fmt, int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
+  switch (fmt) {
+    case PIPER_FMT_MXFP8_E4M3:
+      if constexpr (PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_MXFP8_E5M2:
+      if constexpr (PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_MXFP4:
+      if constexpr (PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP4, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_NVFP4:
+      if constexpr (PASS != pm::kEncode && CDT == pm::kBF16) return launch_bn<PIPER_FMT_NVFP4, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_FP8_E4M3: return launch_bn<PIPER_FMT_FP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
+    case PIPER_FMT_FP8_E5M2: return launch_bn<PIPER_FMT_FP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
+    case PIPER_FMT_INT8: return launch_bn<PIPER_FMT_INT8, PASS, CDT>(bn, lp, items, kp, s);
+    case PIPER_FMT_GGUF_Q8_0:
+      if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_GGUF_Q8_0, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_GGUF_Q4_0:
+      if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_GGUF_Q4_0, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    default: break;
+  }
+  return fail(PIPER_MERGE_EINVAL, "no kernel for this format / pass / dtype combination.");
+}
+
+int launch(int pass, int cdt, int fmt, int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
+  if (items <= 0) return PIPER_MERGE_OK;
+  if (cdt == PIPER_DT_BF16) {
+    if (pass == pm::kLocal) return launch_fmt<pm::kLocal, pm::kBF16>(fmt, bn, lp, items, kp, s);
+    if (pass == pm::kReduce) return launch_fmt<pm::kReduce, pm::kBF16>(fmt, bn, lp, items, kp, s);
+    return launch_fmt<pm::kEncode, pm::kBF16>(fmt, bn, lp, items, kp, s);
+  }
+  if (pass == pm::kLocal) return launch_fmt<pm::kLocal, pm::kF16>(fmt, bn, lp, items, kp, s);
+  if (pass == pm::kReduce) return launch_fmt<pm::kReduce, pm::kF16>(fmt, bn, lp, items, kp, s);
+  return launch_fmt<pm::kEncode, pm::kF16>(fmt, bn, lp, items, kp, s);
+}
+
+// A row range of one weight scheduled in one launch.
+struct Segment {
+  int desc;
+  int row_begin, rows;
+};
+
+DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws, const Segment& seg) {
+  DevWeight w;
+  std::memset(&w, 0, sizeof(w));
+  w.q = static_cast<uint8_t*>(d.qdata);
+  w.scale = d.scale;
+  w.zp = static_cast<int8_t*>(d.zero_point);
+  w.gscale = static_cast<float*>(d.global_scale);
+  w.b = static_cast<const uint16_t*>(d.b);
+  w.a = static_cast<const uint16_t*>(d.a);
+  if (p.nq > 0) {
+    uint8_t* base = ws + p.ws_off;
+    w.qmax = reinterpret_cast<uint32_t*>(base);
+    w.qmin = reinterpret_cast<uint32_t*>(base + 4 * static_cast<size_t>(p.nq));
+    w.old_scale = reinterpret_cast<float*>(base + 8 * static_cast<size_t>(p.nq));
+    w.old_zp = reinterpret_cast<int32_t*>(base + 12 * static_cast<size_t>(p.nq));
+  }
+  w.row_bytes = row_bytes_of(d);
+  w.offset_base = d.offset_base;
+  w.k0 = static_cast<uint32_t>(d.seed & 0xFFFFFFFFull);
+  w.k1 = static_cast<uint32_t>(d.seed >> 32);
+  w.strength = d.strength;
+  w.flags = d.flags;
+  w.M = static_cast<int>(d.rows);
+  w.N = static_cast<int>(d.cols);
+  w.r = static_cast<int>(d.rank);
+  w.KP = pm::align_up(static_cast<int>(d.rank), 16);
+  w.row_begin = seg.row_begin;
+  w.row_blocks = (seg.rows + 127) / 128;
+  w.group = p.group;
+  w.nq_row = p.nq_row;
+  w.scale_cols = d.format == PIPER_FMT_NVFP4 ? static_cast<int>(d.cols / 16) : static_cast<int>(d.cols / 32);
+  w.scale_mode = d.scale_mode;
+  w.scale_dt = d.scale_dtype;
+  return w;
+}
+
+// Launch one group of segments that share a kernel instantiation.
+int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uint8_t* ws,
+              const std::vector<Segment>& segs, cudaStream_t stream) {
+  if (segs.empty()) return PIPER_MERGE_OK;
+  const piper_merge_desc& d0 = descs[segs[0].desc];
+  const Plan& p0 = plans[segs[0].desc];
+  LaunchParams lp;
+  std::memset(&lp, 0, sizeof(lp));
+  lp.n_weights = static_cast<int>(segs.size());
+  int strips = 0, kp_max = 16;
+  for (const Segment& s : segs) strips += (s.rows + 127) / 128;
+  const int target = 4 * sm_count();
+  int items = 0;
+  for (size_t i = 0; i < segs.size(); ++i) {
+    const piper_merge_desc& d = descs[segs[i].desc];
+    const Plan& p = plans[segs[i].desc];
+    DevWeight w = make_dev_weight(d, p, ws, segs[i]);
+    const int max_items = static_cast<int>((d.cols + p.bn - 1) / p.bn);
+    int ci = (target + strips - 1) / strips;
+    ci = std::max(1, std::min(ci, max_items));
+    int item_cols = static_cast<int>((d.cols + ci - 1) / ci);
+    item_cols = (item_cols + p.bn - 1) / p.bn * p.bn;
+    w.item_cols = item_cols;
+    w.col_items = static_cast<int>((d.cols + item_cols - 1) / item_cols);
+    w.item_begin = items;
+    items += w.row_blocks * w.col_items;
+    kp_max = std::max(kp_max, w.KP);
+    lp.w[i] = w;
+  }
+  int rc;
+  if (p0.two_pass) {
+    rc = launch(pm::kReduce, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
+    if (rc) return rc;
+    const int second = d0.format == PIPER_FMT_NVFP4 ? pm::kLocal : pm::kEncode;
+    rc = launch(second, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
+  } else {
+    rc = launch(pm::kLocal, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
+  }
+  return rc;
+}
+
+bool same_kernel(const piper_merge_desc& a, const Plan& pa, const piper_merge_desc& b, const Plan& pb) {
+  return a.format == b.format && a.compute_dtype == b.compute_dtype && pa.bn == pb.bn &&
+         pa.two_pass == pb.two_pass;
+}
+
+int plan_all(const piper_merge_desc* descs, int count, std::vector<Plan>& plans, size_t& ws_total) {
+  if (count < 0) return fail(PIPER_MERGE_EINVAL, "negative descriptor count.");
+  if (count > 0 && descs == nullptr) return fail(PIPER_MERGE_EINVAL, "null descriptor array.");
+  plans.assign(count, Plan());
+  ws_total = 0;
+  for (int i = 0; i < count; ++i) {
+    int rc = validate(descs[i], plans[i]);
+    if (rc) return rc;
+    plans[i].ws_off = ws_total;
+    ws_total += scratch_bytes(plans[i].nq);
+  }
+  return PIPER_MERGE_OK;
+}
+
+}  // namespace
+
+// ================================================================= C ABI
+extern "C" {
+
+int piper_merge_workspace_size(const piper_merge_desc* descs, int32_t count, size_t* bytes) {
+  std::vector<Plan> plans;
+  size_t total = 0;
+  int rc = plan_all(descs, count, plans, total);
+  if (rc) return rc;
+  if (bytes) *bytes = total;
+  return PIPER_MERGE_OK;
+}
+
+int piper_merge_batch(const piper_merge_desc* descs, int32_t count, void* workspace,
+                      size_t workspace_bytes, void* stream_ptr) {
+  std::vector<Plan> plans;
+  size_t total = 0;
+  int rc = plan_all(descs, count, plans, total);
+  if (rc) return rc;
+  if (total > 0 && (workspace == nullptr || workspace_bytes < total))
+    return fail(PIPER_MERGE_EWORKSPACE, "workspace of " + std::to_string(workspace_bytes) +
+                                             " bytes is smaller than the required " +
+                                             std::to_string(total) + ".");
+  if (total > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(PIPER_MERGE_EINVAL, "workspace must be 256-byte aligned.");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (total > 0) {
+    cudaError_t e = cudaMemsetAsync(ws, 0, total, stream);
+    if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  }
+  // Cut weights into segments: two-pass per-row/per-block weights by row
+  // ranges of about kL2GroupBytes, everything else whole.
+  std::vector<Segment> segs;
+  for (int i = 0; i < count; ++i) {
+    const piper_merge_desc& d = descs[i];
+    const Plan& p = plans[i];
+    const int rows = static_cast<int>(d.rows);
+    if (p.two_pass && p.nq_row > 0) {
+      const int64_t rb = row_bytes_of(d);
+      int step = static_cast<int>(std::max<int64_t>(128, kL2GroupBytes / std::max<int64_t>(rb, 1) / 128 * 128));
+      for (int r0 = 0; r0 < rows; r0 += step) segs.push_back({i, r0, std::min(step, rows - r0)});
+    } else {
+      segs.push_back({i, 0, rows});
+    }
+  }
+  std::vector<Segment> group;
+  int64_t group_bytes = 0;
+  for (const Segment& s : segs) {
+    const piper_merge_desc& d = descs[s.desc];
+    const Plan& p = plans[s.desc];
+    const int64_t bytes = row_bytes_of(d) * s.rows;
+    bool flush = !group.empty() &&
+                 (!same_kernel(descs[group[0].desc], plans[group[0].desc], d, p) ||
+                  static_cast<int>(group.size()) >= pm::kMaxWeights ||
+                  (p.two_pass && group_bytes + bytes > kL2GroupBytes));
+    if (flush) {
+      rc = run_group(descs, plans, ws, group, stream);
+      if (rc) return rc;
+      group.clear();
+      group_bytes = 0;
+    }
+    group.push_back(s);
+    group_bytes += bytes;
+  }
+  return run_group(descs, plans, ws, group, stream);
+}
+
+int piper_merge_mx(void* qdata, void* scale, const void* b, const void* a, int64_t rows, int64_t cols,
+                   int64_t rank, int32_t elem_format, int32_t compute_dtype, int32_t scaling_mode,
+                   int32_t swizzled, float strength, int32_t has_seed, uint64_t seed, uint64_t offset_base,
+                   void* stream) {
+  piper_merge_desc d;
+  std::memset(&d, 0, sizeof(d));
+  if (elem_format < 0 || elem_format > 2) return fail(PIPER_MERGE_EINVAL, "MX element format must be 0 (e4m3), 1 (e5m2) or 2 (e2m1).");
+  d.format = elem_format == 0 ? PIPER_FMT_MXFP8_E4M3 : (elem_format == 1 ? PIPER_FMT_MXFP8_E5M2 : PIPER_FMT_MXFP4);
+  d.qdata = qdata;
+  d.scale = scale;
+  d.b = b;
+  d.a = a;
+  d.rows = rows;
+  d.cols = cols;
+  d.rank = rank;
+  d.compute_dtype = compute_dtype;
+  d.scale_mode = scaling_mode;
+  d.flags = (swizzled ? PIPER_FLAG_SWIZZLED : 0u) | (has_seed ? PIPER_FLAG_STOCHASTIC : 0u);
+  d.strength = strength;
+  d.seed = seed;
+  d.offset_base = offset_base;
+  return piper_merge_batch(&d, 1, nullptr, 0, stream);
+}
+
+int piper_merge_nvfp4(void* qdata, void* scale, void* global_scale, const void* b, const void* a,
+                      int64_t rows, int64_t cols, int64_t rank, int32_t compute_dtype, int32_t swizzled,
+                      float strength, int32_t has_seed, uint64_t seed, uint64_t offset_base,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  piper_merge_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.format = PIPER_FMT_NVFP4;
+  d.qdata = qdata;
+  d.scale = scale;
+  d.global_scale = global_scale;
+  d.b = b;
+  d.a = a;
+  d.rows = rows;
+  d.cols = cols;
+  d.rank = rank;
+  d.compute_dtype = compute_dtype;
+  d.flags = (swizzled ? PIPER_FLAG_SWIZZLED : 0u) | (has_seed ? PIPER_FLAG_STOCHASTIC : 0u);
+  d.strength = strength;
+  d.seed = seed;
+  d.offset_base = offset_base;
+  return piper_merge_batch(&d, 1, workspace, workspace_bytes, stream);
+}
+
+int piper_merge_float8(void* qdata, void* scale, const void* b, const void* a, int64_t rows, int64_t cols,
+                       int64_t rank, int64_t block_rows, int64_t block_cols, int32_t e5m2,
+                       int32_t compute_dtype, float strength, int32_t has_seed, uint64_t seed,
+                       uint64_t offset_base, void* workspace, size_t workspace_bytes, void* stream) {
+  piper_merge_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.format = e5m2 ? PIPER_FMT_FP8_E5M2 : PIPER_FMT_FP8_E4M3;
+  d.qdata = qdata;
+  d.scale = scale;
+  d.b = b;
+  d.a = a;
+  d.rows = rows;
+  d.cols = cols;
+  d.rank = rank;
+  d.block_rows = block_rows;
+  d.block_cols = block_cols;
+  d.compute_dtype = compute_dtype;
+  d.flags = has_seed ? PIPER_FLAG_STOCHASTIC : 0u;
+  d.strength = strength;
+  d.seed = seed;
+  d.offset_base = offset_base;
+  return piper_merge_batch(&d, 1, workspace, workspace_bytes, stream);
+}
+
+int piper_merge_int8(void* qdata, void* scale, void* zero_point, const void* b, const void* a, int64_t rows,
+                     int64_t cols, int64_t rank, int64_t block_rows, int64_t block_cols, int32_t compute_dtype,
+                     int32_t scale_dtype, int32_t asymmetric, int32_t reduce_range, float strength,
+                     int32_t has_seed, uint64_t seed, uint64_t offset_base, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  piper_merge_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.format = PIPER_FMT_INT8;
+  d.qdata = qdata;
+  d.scale = scale;
+  d.zero_point = zero_point;
+  d.b = b;
+  d.a = a;
+  d.rows = rows;
+  d.cols = cols;
+  d.rank = rank;
+  d.block_rows = block_rows;
+  d.block_cols = block_cols;
+  d.compute_dtype = compute_dtype;
+  d.scale_dtype = scale_dtype;
+  d.flags = (asymmetric ? PIPER_FLAG_ASYMMETRIC : 0u) | (reduce_range ? PIPER_FLAG_REDUCE_RANGE : 0u) |
+            (has_seed ? PIPER_FLAG_STOCHASTIC : 0u);
+  d.strength = strength;
+  d.seed = seed;
+  d.offset_base = offset_base;
+  return piper_merge_batch(&d, 1, workspace, workspace_bytes, stream);
+}
+
+int piper_merge_gguf(void* raw, const void* b, const void* a, int64_t rows, int64_t cols, int64_t rank,
+                     int32_t quant_type, int32_t compute_dtype, float strength, int32_t has_seed,
+                     uint64_t seed, uint64_t offset_base, void* stream) {
+  piper_merge_desc d;
+  std::memset(&d, 0, sizeof(d));
+  if (quant_type == 8) d.format = PIPER_FMT_GGUF_Q8_0;
+  else if (quant_type == 2) d.format = PIPER_FMT_GGUF_Q4_0;
+  else return fail(PIPER_MERGE_EINVAL, "GGUF merge supports Q8_0 (8) and Q4_0 (2), got " + std::to_string(quant_type) + ".");
+  d.qdata = raw;
+  d.b = b;
+  d.a = a;
+  d.rows = rows;
+  d.cols = cols;
+  d.rank = rank;
+  d.compute_dtype = compute_dtype;
+  d.flags = has_seed ? PIPER_FLAG_STOCHASTIC : 0u;
+  d.strength = strength;
+  d.seed = seed;
+  d.offset_base = offset_base;
+  return piper_merge_batch(&d, 1, nullptr, 0, stream);
+}
+
+const char* piper_merge_last_error(void) { return g_last_error.c_str(); }
+
+int piper_merge_device_status(void* stream, uint32_t* status) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("cudaStreamSynchronize: ") + cudaGetErrorString(e));
+  unsigned int v = 0, zero = 0;
+  e = cudaMemcpyFromSymbol(&v, pm::g_status, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(pm::g_status, &zero, sizeof(zero));
+  if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("status word: ") + cudaGetErrorString(e));
+  if (status) *status = v;
+  return v == 0 ? PIPER_MERGE_OK : fail(PIPER_MERGE_ETIMEOUT, "a bounded device-side wait timed out.");
+}
+
+const char* piper_merge_version(void) { return "piper-merge 0.1 sm_100a"; }
+
+}  // extern "C"

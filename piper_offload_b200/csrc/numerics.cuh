@@ -1,0 +1,195 @@
+// numerics.cuh - element-level arithmetic of the merge, kept bit-compatible with
+// the reference kernels (src/piper_offload/_triton_*_lora.py):
+//   * casts to bf16 / fp16 / e4m3 / e5m2 round to nearest even;
+//   * fp32 quotients that the reference writes with `/` use the same
+//     `div.full.f32` instruction Triton emits for fp32 division;
+//   * `tl.minimum` / `tl.maximum` are IEEE minNum/maxNum (fminf/fmaxf);
+//   * `base + acc * strength` is one fused multiply-add, as Triton contracts it.
+// The file is compiled with --fmad=false so no other mul+add pair is fused.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+namespace pm {
+
+enum : int { kBF16 = 0, kF16 = 1, kF32 = 2 };
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ float f16r(float x) { return __half2float(__float2half_rn(x)); }
+
+template <int DT>
+__device__ __forceinline__ float round_dt(float x) {
+  if constexpr (DT == kBF16) return bf16r(x);
+  else if constexpr (DT == kF16) return f16r(x);
+  else return x;
+}
+
+__device__ __forceinline__ float round_dt_rt(float x, int dt) {
+  return dt == kBF16 ? bf16r(x) : (dt == kF16 ? f16r(x) : x);
+}
+
+// fp32 division as emitted by Triton for `a / b` on fp32 tensors.
+__device__ __forceinline__ float div_full(float a, float b) {
+  float r;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// ------------------------------------------------------------------ FP8
+__device__ __forceinline__ uint32_t enc_e4m3(float x) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x));
+  return r & 0xFFu;
+}
+__device__ __forceinline__ uint32_t enc_e5m2(float x) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x));
+  return r & 0xFFu;
+}
+__device__ __forceinline__ float dec_e4m3(uint32_t code) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(code & 0xFFu)));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
+}
+__device__ __forceinline__ float dec_e5m2(uint32_t code) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(code & 0xFFu)));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
+}
+template <bool E4M3>
+__device__ __forceinline__ uint32_t enc_fp8(float x) {
+  if constexpr (E4M3) return enc_e4m3(x);
+  else return enc_e5m2(x);
+}
+template <bool E4M3>
+__device__ __forceinline__ float dec_fp8(uint32_t c) {
+  if constexpr (E4M3) return dec_e4m3(c);
+  else return dec_e5m2(c);
+}
+
+// ------------------------------------------------------------------ E2M1
+// Magnitudes of the low three code bits (_e2m1_value /
+// _triton_stochastic_quantization.py:82-106).
+__device__ __forceinline__ float e2m1_mag(uint32_t code) {
+  const uint32_t c = code & 7u;
+  // 0, .5, 1, 1.5, 2, 3, 4, 6
+  return c < 4u ? 0.5f * static_cast<float>(c) : (c == 7u ? 6.0f : static_cast<float>(c - 2u));
+}
+__device__ __forceinline__ float dec_e2m1(uint32_t code) {
+  const float m = e2m1_mag(code);
+  return (code & 8u) ? -m : m;
+}
+// Threshold ladder of _encode_fp4 (_triton_mx_lora.py:67-94); sign from the fp32 sign bit.
+__device__ __forceinline__ uint32_t enc_e2m1(float v) {
+  const float m = fabsf(v);
+  uint32_t c = m <= 0.25f ? 0u
+             : m < 0.75f  ? 1u
+             : m <= 1.25f ? 2u
+             : m < 1.75f  ? 3u
+             : m <= 2.5f  ? 4u
+             : m < 3.5f   ? 5u
+             : m <= 5.0f  ? 6u
+                          : 7u;
+  return c | ((__float_as_uint(v) >> 28) & 8u);
+}
+
+// E8M0 code -> fp32 (_e8m0_to_fp32, _triton_mx_lora.py:30-37).
+__device__ __forceinline__ float dec_e8m0(uint32_t code) {
+  code &= 0xFFu;
+  if (code == 255u) return __uint_as_float(0x7FC00000u);
+  return __uint_as_float(code == 0u ? (1u << 22) : (code << 23));
+}
+
+// ---------------------------------------------------------------- Philox
+// Counter-based uniform of the reference's `_random(seed, offset)` =
+// Triton `tl.rand`: Philox4x32 with 10 rounds, key = (seed lo, seed hi),
+// counter = (offset lo, offset hi, 0, 0); output word 0 folded to a
+// non-negative int32 and scaled by the fp32 constant 0x2FFFFFFF.
+struct PhiloxKey {
+  uint32_t k0, k1;
+};
+
+__device__ __forceinline__ uint32_t philox_word0(PhiloxKey key, uint64_t offset) {
+  uint32_t c0 = static_cast<uint32_t>(offset);
+  uint32_t c1 = static_cast<uint32_t>(offset >> 32);
+  uint32_t c2 = 0u, c3 = 0u;
+  uint32_t k0 = key.k0, k1 = key.k1;
+#pragma unroll
+  for (int round = 0; round < 10; ++round) {
+    const uint32_t hb = __umulhi(0xCD9E8D57u, c2);
+    const uint32_t lb = 0xCD9E8D57u * c2;
+    const uint32_t ha = __umulhi(0xD2511F53u, c0);
+    const uint32_t la = 0xD2511F53u * c0;
+    c0 = hb ^ c1 ^ k0;
+    c2 = ha ^ c3 ^ k1;
+    c1 = lb;
+    c3 = la;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c0;
+}
+
+__device__ __forceinline__ float philox_uniform(PhiloxKey key, uint64_t offset) {
+  int32_t x = static_cast<int32_t>(philox_word0(key, offset));
+  x = x < 0 ? -x - 1 : x;
+  return __fmul_rn(__int2float_rn(x), __uint_as_float(0x2FFFFFFFu));
+}
+
+// ------------------------------------------------- stochastic terminal codes
+// _stochastic_float8 (_triton_stochastic_quantization.py:132-175): `v` is the
+// clamped, normalized value; returns the E4M3/E5M2 code.
+template <bool E4M3>
+__device__ __forceinline__ uint32_t sr_fp8(float v, float limit, PhiloxKey key, uint64_t off) {
+  const float mag = fabsf(v);
+  const uint32_t det = enc_fp8<E4M3>(mag);
+  const float det_v = dec_fp8<E4M3>(det);
+  const bool down = det_v > mag;
+  const uint32_t lo = (down ? det - 1u : det) & 0xFFu;
+  const uint32_t hi = (down ? det : det + 1u) & 0xFFu;
+  const float lov = dec_fp8<E4M3>(lo);
+  const float hiv = dec_fp8<E4M3>(hi);
+  const float p = hiv > lov ? div_full(mag - lov, hiv - lov) : 0.0f;
+  const uint32_t sign = (__float_as_uint(v) >> 24) & 0x80u;
+  if (mag < limit && p > 0.0f) {
+    const float u = philox_uniform(key, off);
+    return (u < p ? hi : lo) | sign;
+  }
+  return det | sign;
+}
+
+// _stochastic_e2m1_code (_triton_stochastic_quantization.py:109-129).
+__device__ __forceinline__ uint32_t sr_e2m1(float v, uint32_t det, PhiloxKey key, uint64_t off) {
+  const float mag = fabsf(v);
+  const uint32_t nc = det & 7u;
+  const bool down = e2m1_mag(nc) > mag;
+  const uint32_t lc = down ? nc - 1u : nc;
+  const uint32_t uc = down ? nc : nc + 1u;
+  const float lv = e2m1_mag(lc);
+  const float uv = e2m1_mag(uc);
+  const float p = uv > lv ? div_full(mag - lv, uv - lv) : 0.0f;
+  if (mag > 0.0f && mag < 6.0f && p > 0.0f) {
+    const float u = philox_uniform(key, off);
+    return (u < p ? uc : lc) | ((__float_as_uint(v) >> 28) & 8u);
+  }
+  return det;
+}
+
+// _stochastic_round_to_int (_triton_stochastic_quantization.py:24-39);
+// returns the (possibly) re-rounded value as a float.
+__device__ __forceinline__ float sr_int(float v, float det, float qmin, float qmax, PhiloxKey key,
+                                        uint64_t off) {
+  if (v > qmin && v < qmax) {
+    const float lower = floorf(v);
+    const float p = __fsub_rn(v, lower);
+    if (p > 0.0f) {
+      const float u = philox_uniform(key, off);
+      return __fadd_rn(lower, u < p ? 1.0f : 0.0f);
+    }
+  }
+  return det;
+}
+
+}  // namespace pm
