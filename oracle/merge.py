@@ -21,6 +21,7 @@ from .numerics import (
     e2m1_value,
     encode_e2m1,
     fdiv,
+    fdiv_t,
     fma_f32,
     fp8_codec,
     from_bits_f32,
@@ -90,7 +91,7 @@ def sr_float8(values, seed, offsets, e4m3: bool, limit: float) -> np.ndarray:
     upper = decode(upper_bits)
     with np.errstate(invalid="ignore"):
         ok = upper > lower
-    prob = np.where(ok, fdiv(mag - lower, upper - lower), np.float32(0.0))
+    prob = np.where(ok, fdiv_t(mag - lower, upper - lower), np.float32(0.0))
     u = philox_uniform(seed, offsets)
     mag_bits = np.where(u < prob, upper_bits, lower_bits)
     sign = (bits_f32(v) >> 24).astype(np.int64) & 0x80
@@ -112,7 +113,7 @@ def sr_e2m1(values, deterministic, seed, offsets) -> np.ndarray:
     upper_code = np.where(rounded_down, nearest_code, nearest_code + 1)
     lower = e2m1_value(lower_code)
     upper = e2m1_value(upper_code)
-    prob = np.where(upper > lower, fdiv(mag - lower, upper - lower), np.float32(0.0))
+    prob = np.where(upper > lower, fdiv_t(mag - lower, upper - lower), np.float32(0.0))
     u = philox_uniform(seed, offsets)
     mag_code = np.where(u < prob, upper_code, lower_code)
     sign = (bits_f32(v) >> 28).astype(np.int64) & 8
@@ -204,7 +205,7 @@ def mx_calculate_scale(max_abs, target_pow2, max_pos, mbits, mode):
     encoded = np.where(np.isnan(max_abs), 255, encoded)
     scale = from_bits_f32((encoded.astype(np.uint32) << 23).astype(np.uint32))
     scale = maxnum(scale, FLT_MIN)
-    return encoded.astype(np.uint8), fdiv(np.float32(1.0), scale)
+    return encoded.astype(np.uint8), fdiv_t(np.float32(1.0), scale)
 
 
 def merge_mx(qdata, scale, elem, b, a, strength, *, scaling_mode=0, swizzled=False, seed=None,
@@ -313,17 +314,17 @@ def merge_nvfp4(qdata, scale, per_tensor_scale, b, a, strength, *, swizzled=Fals
     blocks = merged.reshape(M, sc, 16)
     max_abs = nanmax_reduce(np.abs(blocks), axis=2)
     block_scale = fdiv(max_abs, np.float32(6.0))
-    fp8_scale = fdiv(block_scale, g_out) if g_out is not None else block_scale
+    fp8_scale = fdiv_t(block_scale, g_out) if g_out is not None else block_scale
     fp8_scale = clamp(fp8_scale, 0.015625, 448.0)
     fp8_codes = encode_e4m3(fp8_scale)
     fp8_scale = decode_e4m3(fp8_codes)
     new_scale = np.zeros(np.asarray(scale).size, dtype=np.uint8)
     new_scale[sidx] = fp8_codes
     if g_out is not None:
-        recip = fdiv(fdiv(np.float32(1.0), g_out), fp8_scale)
+        recip = fdiv_t(fdiv_t(np.float32(1.0), g_out), fp8_scale)
         normalized = (merged * np.repeat(recip, 16, axis=1)).astype(np.float32)
     else:
-        normalized = fdiv(merged, np.repeat(fp8_scale, 16, axis=1))
+        normalized = fdiv_t(merged, np.repeat(fp8_scale, 16, axis=1))
     normalized = clamp(normalized, -6.0, 6.0)
     codes = encode_e2m1(normalized)
     if seed is not None:
@@ -373,7 +374,7 @@ def merge_float8(qdata, scale, block_size, b, a, strength, *, e4m3=True, seed=No
         new_scale = round_to_compute(fdiv(amax, np.float32(limit)), compute)
         new_scale = np.where(new_scale == 0.0, EPS_2_23, new_scale).astype(np.float32)
         s_out = np.repeat(new_scale, g, axis=1)
-    scaled = clamp(fdiv(merged, s_out), -limit, limit)
+    scaled = clamp(fdiv_t(merged, s_out), -limit, limit)
     if seed is not None:
         new_q = sr_float8(scaled, seed, logical_offsets(M, N, offset_base), e4m3, limit)
     else:
@@ -425,7 +426,7 @@ def merge_int8(qdata, scale, zero_point, block_size, b, a, strength, *, asymmetr
     s = maxnum(s, EPS_2_23)
     s = round_to_compute(s, compute)
     if asymmetric:
-        ratio = round_to_compute(fdiv(min_v, s), compute)
+        ratio = round_to_compute(fdiv_t(min_v, s), compute)
         zp = np.clip(qmin - rint_half_even(ratio), qmin, qmax)
     else:
         zp = np.zeros(nq, np.int64)
@@ -433,8 +434,8 @@ def merge_int8(qdata, scale, zero_point, block_size, b, a, strength, *, asymmetr
     s_store = round_to_compute(s, qparam)
     values = dense
     sv = s_store[qidx]
-    stochastic_scaled = fdiv(values, sv)
-    inv = round_to_compute(fdiv(np.float32(1.0), sv), qparam)
+    stochastic_scaled = fdiv_t(values, sv)
+    inv = round_to_compute(fdiv_t(np.float32(1.0), sv), qparam)
     scaled = round_to_compute((values * inv).astype(np.float32), qparam)
     quant = rint_half_even(scaled) + zp[qidx]
     quant = quant.astype(np.float32)

@@ -173,7 +173,7 @@ __device__ __forceinline__ MxScale mx_scale(float amax, int mode, int target, fl
                                             int mbits) {
   MxScale s;
   if (mode == PIPER_MX_RCEIL) {
-    const float d = div_full(amax, maxpos);
+    const float d = __fdiv_rn(amax, maxpos);  // `/ MAX_POS` (constexpr): IEEE
     float u;
     if (d != d) u = __int_as_float(0x7FC00000);
     else if (d == 0.0f) u = __int_as_float(0xFF800000);
@@ -349,7 +349,7 @@ __device__ __forceinline__ void nvfp4_chunk(const DevWeight& W, const RowCtx& c,
     if constexpr (PASS == kReduce) {
       if (c.valid) amax_acc = fmaxf(amax_acc, amax);
     } else {
-      float fs = div_full(amax, 6.0f);
+      float fs = __fdiv_rn(amax, 6.0f);  // `/ 6.0` (literal): IEEE
       if (two_level) fs = div_full(fs, g_out);
       fs = fminf(fmaxf(fs, 0.015625f), 448.0f);
       const uint32_t fcode = enc_e4m3(fs);
@@ -388,7 +388,7 @@ __device__ __forceinline__ int qparam_index(const DevWeight& W, int row, int col
 // New FP8 scale from the block amax (_reduce_row_scale_kernel, _triton_float8_lora.py:249-271).
 template <int CDT>
 __device__ __forceinline__ float fp8_new_scale(float amax, float limit) {
-  float s = round_dt<CDT>(div_full(amax, limit));
+  float s = round_dt<CDT>(__fdiv_rn(amax, limit));  // `/ FP8_LIMIT` (constexpr): IEEE
   return s == 0.0f ? 1.1920928955078125e-07f : s;
 }
 
@@ -405,9 +405,9 @@ __device__ __forceinline__ Int8Q int8_qparams(float min_v, float max_v, bool asy
   float s;
   if (asym) {
     const float rng = round_dt<CDT>(__fsub_rn(max_v, min_v));
-    s = div_full(rng, static_cast<float>(qmax - qmin));
+    s = __fdiv_rn(rng, static_cast<float>(qmax - qmin));  // constexpr divisor: IEEE
   } else {
-    s = div_full(fmaxf(-min_v, max_v), static_cast<float>(qmax - qmin) / 2.0f);
+    s = __fdiv_rn(fmaxf(-min_v, max_v), static_cast<float>(qmax - qmin) / 2.0f);
   }
   s = round_dt<CDT>(s);
   s = fmaxf(s, 1.1920928955078125e-07f);
@@ -723,7 +723,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
       } else {
         g_in = W.old_scale[0];
         const float amax = __uint_as_float(*W.qmax);
-        g_out = fmaxf(div_full(amax, 2688.0f), 1.1920928955078125e-07f);
+        g_out = fmaxf(__fdiv_rn(amax, 2688.0f), 1.1920928955078125e-07f);  // `/ 2688.0`: IEEE
       }
     }
   }
@@ -849,7 +849,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
           if (PASS == kReduce) {
             if (valid) red_max = fmaxf(red_max, amax);
           } else {
-            float fs = div_full(amax, 6.0f);
+            float fs = __fdiv_rn(amax, 6.0f);
             if (two_level) fs = div_full(fs, g_out);
             fs = fminf(fmaxf(fs, 0.015625f), 448.0f);
             const uint32_t fcode = enc_e4m3(fs);
@@ -1221,6 +1221,15 @@ int validate(const piper_merge_desc& d, Plan& p) {
     default:
       return fail(PIPER_MERGE_EINVAL, "unknown format id " + std::to_string(d.format) + ".");
   }
+  // 256-column tiles need 768 * KP bytes of operand staging; above rank 192
+  // they would not fit in 227 KB of shared memory, so use 128-column tiles.
+  if (p.bn == 256 && pm::align_up(static_cast<int>(d.rank), 16) > 192) {
+    p.bn = 128;
+    if (d.format == PIPER_FMT_FP8_E4M3 || d.format == PIPER_FMT_FP8_E5M2 || d.format == PIPER_FMT_INT8) {
+      p.two_pass = true;  // a 256-wide group no longer fits one tile
+      p.nq = static_cast<int>(d.rows * p.nq_row);
+    }
+  }
   return PIPER_MERGE_OK;
 }
 
@@ -1262,6 +1271,7 @@ int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
 template <int FMT, int PASS, int CDT>
 int launch_bn(int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
   if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
+    if (bn == 128) return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
     return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
   } else if constexpr (FMT == PIPER_FMT_FP8_E4M3 || FMT == PIPER_FMT_FP8_E5M2 || FMT == PIPER_FMT_INT8) {
     if (PASS == pm::kLocal && bn == 256) return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);

@@ -1,0 +1,99 @@
+"""CPU: the C-ABI library loads, exports every declared symbol, and rejects bad
+arguments before touching the device."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from piper_offload_b200 import _native as nat
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "piper_merge.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(piper_merge_\w+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_all_declared_symbols():
+    lib = nat.load()
+    names = declared_functions()
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(nat.EXPORTED_SYMBOLS) == set(names)
+
+
+def test_version_string():
+    assert "sm_100a" in nat.version()
+
+
+def _desc(**kw) -> nat.MergeDesc:
+    d = nat.MergeDesc()
+    d.qdata = 0x1000
+    d.b = 0x2000
+    d.a = 0x3000
+    d.scale = 0x4000
+    d.rows, d.cols, d.rank = 64, 256, 16
+    d.compute_dtype = nat.DT_BF16
+    d.format = nat.FMT_FP8_E4M3
+    d.block_rows, d.block_cols = 1, 256
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize(
+    "kw,match",
+    [
+        ({"rows": 0}, "non-empty"),
+        ({"rank": 300}, "rank above 256"),
+        ({"format": 99}, "unknown format"),
+        ({"compute_dtype": nat.DT_F32}, "bfloat16 and float16"),
+        ({"block_rows": 3, "block_cols": 7}, "per-group"),
+        ({"format": nat.FMT_MXFP8_E4M3, "cols": 100}, "divisible by 32"),
+        ({"format": nat.FMT_MXFP8_E4M3, "scale_mode": 9}, "scaling mode"),
+        ({"format": nat.FMT_NVFP4, "cols": 40}, "divisible by 16"),
+        ({"format": nat.FMT_GGUF_Q8_0, "cols": 48}, "divisible by 32"),
+        ({"format": nat.FMT_INT8, "scale_dtype": 7}, "scales"),
+        ({"qdata": None}, "null"),
+    ],
+)
+def test_invalid_descriptors_are_rejected_on_host(kw, match):
+    d = _desc(**kw)
+    with pytest.raises(ValueError, match=match):
+        nat.workspace_bytes([d])
+    arr = (nat.MergeDesc * 1)(d)
+    rc = nat.load().piper_merge_batch(arr, 1, None, 0, None)
+    assert rc == nat.EINVAL
+
+
+def test_workspace_sizes():
+    assert nat.workspace_bytes([_desc(format=nat.FMT_MXFP8_E4M3)]) == 0
+    per_row = nat.workspace_bytes([_desc()])  # 64 row blocks x 16 bytes
+    assert per_row == 1024
+    per_tensor = nat.workspace_bytes([_desc(block_rows=64, block_cols=256)])
+    assert per_tensor == 256
+    grouped_local = nat.workspace_bytes([_desc(block_cols=64)])
+    assert grouped_local == 0
+    two = nat.workspace_bytes([_desc(), _desc(block_rows=64, block_cols=256)])
+    assert two == 1024 + 256
+
+
+def test_workspace_too_small_is_reported():
+    d = _desc()
+    arr = (nat.MergeDesc * 1)(d)
+    rc = nat.load().piper_merge_batch(arr, 1, ctypes.c_void_p(0x100000), 16, None)
+    assert rc == nat.EWORKSPACE
+    assert b"workspace" in nat.load().piper_merge_last_error()
+
+
+def test_convenience_entry_points_validate():
+    lib = nat.load()
+    assert lib.piper_merge_mx(1, 1, 1, 1, 32, 64, 16, 5, 0, 0, 0, 1.0, 0, 0, 0, None) == nat.EINVAL
+    assert lib.piper_merge_gguf(1, 1, 1, 32, 64, 16, 3, 0, 1.0, 0, 0, 0, None) == nat.EINVAL
+    assert lib.piper_merge_float8(1, 1, 1, 1, 0, 64, 16, 1, 64, 0, 0, 1.0, 0, 0, 0, None, 0, None) == nat.EINVAL
