@@ -1,0 +1,447 @@
+"""Benchmark of the fused quantized LoRA merge on B200.
+
+Default workload: scaled-FP8 e4m3 per-row weights of a
+Llama-3-8B-shaped stack (32 layers x {q,o 4096x4096; k,v 1024x4096; gate,up
+14336x4096; down 4096x14336}), base N(0, 0.02) quantized per row, rank-32
+bf16 LoRA N(0, 0.01), strength 1.0, stochastic rounding seeded per weight with
+``derive_seed(f"model.layers.{i}.{proj}.weight", merge_index)``. One step
+merges every weight once (in place). Inputs total ~7 GB of codes, far larger
+than the 126 MB L2, so no flush is needed between steps.
+
+Metric: weight GB/s = (codes + scales read + codes + scales written) / time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+                    [--config fp8|int8|nvfp4|mxfp8|mxfp4|q8_0|q4_0] [--rtn]
+
+Under ``torch.distributed.run`` each rank merges its own copy of the model
+(weak scaling, no data-path collective); the step time is the max over ranks.
+``--impl reference`` times the reference algorithm's CPU restatement
+(``oracle``) on the host cores on a bounded sample (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+LLAMA3_8B = [("q_proj", 4096, 4096), ("k_proj", 1024, 4096), ("v_proj", 1024, 4096),
+             ("o_proj", 4096, 4096), ("gate_proj", 14336, 4096), ("up_proj", 14336, 4096),
+             ("down_proj", 4096, 14336)]
+DIT_12B = [("attn_q", 3072, 3072), ("attn_k", 3072, 3072), ("attn_v", 3072, 3072), ("attn_o", 3072, 3072),
+           ("mlp_up", 12288, 3072), ("mlp_down", 3072, 12288)]
+LLAMA_70B = [("attn_qo", 8192, 8192), ("attn_kv", 1024, 8192), ("mlp_gate", 28672, 8192),
+             ("mlp_down", 8192, 28672)]
+
+CONFIGS = {
+    # name: (layer list, layers, rank, lora std, base std, stochastic, description)
+    "fp8": (LLAMA3_8B, 32, 32, 0.01, 0.02, True, "scaled-FP8 e4m3 per-row, Llama-3-8B x32, r32, SR"),
+    "int8": (LLAMA3_8B, 32, 16, 0.01, 0.02, False, "INT8 per-row symmetric, Llama-3-8B x32, r16, RTN"),
+    "nvfp4": ([("up", 14336, 4096), ("down", 4096, 14336)], 32, 64, 0.005, 0.02, False,
+              "NVFP4 two-level, 14336x4096 + 4096x14336 x32, r64, RTN"),
+    "mxfp8": (DIT_12B, 57, 128, 0.005, 0.02, False, "MXFP8 e4m3 FLOOR, DiT-12B 57 blocks, r128, RTN"),
+    "mxfp4": (DIT_12B, 57, 128, 0.005, 0.02, False, "MXFP4 FLOOR, DiT-12B 57 blocks, r128, RTN"),
+    "q8_0": (LLAMA_70B, 80, 16, 0.01, 0.015, False, "GGUF Q8_0, 70B-shaped x80, r16, RTN"),
+    "q4_0": (LLAMA_70B, 80, 16, 0.01, 0.015, False, "GGUF Q4_0, 70B-shaped x80, r16, RTN"),
+}
+# Algorithmic bytes per element (read + write) and per-row scale bytes.
+BYTES_PER_ELEM = {"fp8": 2.0, "int8": 2.0, "nvfp4": 1.125, "mxfp8": 2.0625, "mxfp4": 1.0625,
+                  "q8_0": 2.125, "q4_0": 1.125}
+ROW_SCALE_BYTES = {"fp8": 8, "int8": 4}  # fp32 / bf16 row scale read + written
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def weight_list(cfg: str, model_copies: int = 1):
+    layers, n_layers, *_ = CONFIGS[cfg]
+    out = []
+    for copy in range(model_copies):
+        for i in range(n_layers):
+            for name, rows, cols in layers:
+                prefix = f"model{copy}." if copy else ""
+                out.append((f"{prefix}model.layers.{i}.{name}.weight", rows, cols))
+    return out
+
+
+def algorithmic_bytes(cfg: str, rows: int, cols: int) -> int:
+    return int(rows * cols * BYTES_PER_ELEM[cfg]) + rows * ROW_SCALE_BYTES.get(cfg, 0)
+
+
+def measured_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi during the timed region (recipe's clocks line)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for _, _, parts in rows:
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# --------------------------------------------------------------- workload
+def build_weights(cfg: str, device, seed_base: int):
+    """Quantized weights + factors on `device` (torch ops, seeded per weight)."""
+    import torch
+
+    from piper_offload_b200 import synthetic as S
+    from piper_offload_b200 import weights as WT
+
+    layers, n_layers, rank, lora_std, base_std, _, _ = CONFIGS[cfg]
+    items = []
+    for k, (key, rows, cols) in enumerate(weight_list(cfg)):
+        s = seed_base + 7919 * k
+        w = S.normal((rows, cols), base_std, seed=s, device=device,
+                     outlier_frac=0.001 if cfg.startswith("mx") else 0.0)
+        if cfg == "fp8":
+            q = S.quantize_fp8(w)
+            t = WT.Float8Weight(q.qdata, q.scale, (1, cols))
+        elif cfg == "int8":
+            q = S.quantize_int8_per_row(w)
+            t = WT.Int8Weight(q.qdata, q.scale, (1, cols))
+        elif cfg == "nvfp4":
+            q = S.quantize_nvfp4(w, two_level=True)
+            t = WT.NVFP4Weight(q.qdata, q.scale, q.per_tensor_scale)
+        elif cfg in ("mxfp8", "mxfp4"):
+            elem = "e4m3" if cfg == "mxfp8" else "e2m1"
+            q = S.quantize_mx(w, elem)
+            edt = torch.float8_e4m3fn if cfg == "mxfp8" else torch.float4_e2m1fn_x2
+            t = WT.MXWeight(q.qdata, q.scale.view(torch.float8_e8m0fnu), edt)
+        else:
+            q = S.quantize_gguf(w, 8 if cfg == "q8_0" else 2)
+            t = WT.GGUFWeight(q.qdata, 8 if cfg == "q8_0" else 2)
+        del w
+        b, a = S.lora_factors(rows, cols, rank, lora_std, seed=s + 1, device=device)
+        items.append((key, rows, cols, t, b, a))
+    torch.cuda.synchronize(device)
+    return items
+
+
+def storage_tensors(t):
+    out = []
+    for name in ("qdata", "scale", "zero_point", "per_tensor_scale", "raw"):
+        v = getattr(t, name, None)
+        if v is not None:
+            out.append(v)
+    return out
+
+
+# ------------------------------------------------------------ CPU baseline
+def _oracle_chunk(args):
+    """Oracle merge of one row chunk (runs in a spawned worker)."""
+    import numpy as np
+
+    from oracle import merge as om
+
+    cfg, q, scale, b, a, seed, offset_base = args
+    t0 = time.perf_counter()
+    if cfg == "fp8":
+        om.merge_float8(q, scale, (1, a.shape[1]), b, a, 1.0, seed=seed, offset_base=offset_base)
+    elif cfg == "int8":
+        om.merge_int8(q, scale, None, (1, a.shape[1]), b, a, 1.0, seed=seed, offset_base=offset_base)
+    else:
+        raise ValueError(cfg)
+    return time.perf_counter() - t0, int(np.asarray(q).size)
+
+
+def cpu_baseline(cfg: str, steps: int, warmup: int, rows_per_step: int = 1024, cols: int = 4096):
+    """Time the oracle (port of the reference algorithm) on the host cores."""
+    import multiprocessing as mp
+
+    import numpy as np
+    import torch
+
+    from piper_offload_b200 import synthetic as S
+
+    if cfg not in ("fp8", "int8"):
+        cfg_eff = "fp8"
+    else:
+        cfg_eff = cfg
+    _, _, rank, lora_std, base_std, stochastic, _ = CONFIGS[cfg]
+    cores = max(1, min(os.cpu_count() or 1, 32))
+    chunk = max(16, rows_per_step // cores)
+    w = S.normal((rows_per_step, cols), base_std, seed=11, device="cpu")
+    q = S.quantize_fp8(w) if cfg_eff == "fp8" else S.quantize_int8_per_row(w)
+    b, a = S.lora_factors(rows_per_step, cols, rank, lora_std, seed=12, device="cpu")
+    qn = q.qdata.view(torch.uint8).numpy() if cfg_eff == "fp8" else q.qdata.numpy()
+    sn = q.scale.float().numpy()
+    bn, an = b.float().numpy(), a.float().numpy()
+    seed = 0x9C3EA68DBAC91AAD if stochastic else None
+    tasks = [(cfg_eff, qn[r:r + chunk], sn[r:r + chunk], bn[r:r + chunk], an, seed, r * cols)
+             for r in range(0, rows_per_step, chunk)]
+    ctx = mp.get_context("spawn")
+    times = []
+    with ctx.Pool(cores) as pool:
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            pool.map(_oracle_chunk, tasks)
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                times.append(dt)
+    nbytes = algorithmic_bytes(cfg_eff, rows_per_step, cols)
+    t = statistics.median(times)
+    return {"value": nbytes / t / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{rows_per_step}x{cols} {cfg_eff} per-row{' SR' if stochastic else ' RTN'} rows of one weight, "
+                      f"{len(tasks)} row chunks over {cores} spawned processes (numpy restatement, not reference code)",
+            "ms_per_sample": t * 1e3}
+
+
+# ------------------------------------------------------------------ main
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--config", default="fp8", choices=sorted(CONFIGS))
+    ap.add_argument("--rtn", action="store_true", help="round-to-nearest instead of the config's rounding")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    args = ap.parse_args()
+    warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = args.config
+    _, _, lrank, _, _, cfg_sr, desc = CONFIGS[cfg]
+    stochastic = cfg_sr and not args.rtn
+    metric = "LoRA-merge weight GB/s (read+write)"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        res = cpu_baseline(cfg, args.steps, warmup)
+        line = {"metric": metric, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": warmup, "ms_per_step": res["ms_per_sample"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "impl": "reference",
+                "config": {"workload": desc, "rank": lrank, "stochastic": stochastic},
+                "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    from piper_offload_b200 import _native
+    from piper_offload_b200 import adapters as AD
+    from piper_offload_b200.seeding import derive_seed
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # CPU baseline first (spawned pool, before heavy GPU allocations), rank 0 only.
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(cfg, steps=1, warmup=1)
+
+    items = build_weights(cfg, device, seed_base=1000 * rank)
+    total_bytes = sum(algorithmic_bytes(cfg, r, c) for _, r, c, *_ in items)
+
+    # Device-resident path: descriptors built once through the adapters, then
+    # one piper_merge_batch call per step with that step's seeds.
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    keep: list = []
+    descs = [AD.select_adapter(t).merge_desc(t, b, a, 1.0, rounding_seed=0 if stochastic else None, keep=keep)
+             for key, rows, cols, t, b, a in items]
+    arr = (_native.MergeDesc * len(descs))(*descs)
+    need = _native.workspace_bytes(descs)
+    assert need <= ws.numel(), need
+    ws_ptr, ws_len = ws.data_ptr(), ws.numel()
+    lib = _native.load()
+    total_steps = warmup + args.steps
+    seeds = [[derive_seed(key, s) for key, *_ in items] for s in range(total_steps + args.e2e_steps + 2)] \
+        if stochastic else None
+
+    def run_step(s: int) -> None:
+        if seeds is not None:
+            for i, sd in enumerate(seeds[s]):
+                arr[i].seed = sd
+        _native.check(lib.piper_merge_batch(arr, len(descs), ws_ptr, ws_len, stream.cuda_stream))
+
+    step = 0
+    for _ in range(warmup):
+        run_step(step)
+        step += 1
+    torch.cuda.synchronize(device)
+    assert _native.device_status(device) == 0
+
+    launches0 = _native.launches()
+    barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local_rank) as clk:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            run_step(step)
+            step += 1
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier()
+    launches = _native.launches() - launches0
+    ms = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms)
+    value = total_bytes * world / (ms / 1e3) / 1e9
+    clocks = clk.summary()
+    status = _native.device_status(device)
+
+    peak, peak_kind = measured_peak()
+    per_gpu = value / world
+    roofline = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(per_gpu / peak, 4), "peak_source": peak_kind,
+                "kernel": "merge_kernel (all launches of one step)", "traffic": None}
+    tfile = ROOT / "profiles" / f"traffic_{cfg}.json"
+    if tfile.exists():
+        try:
+            tj = json.loads(tfile.read_text())
+            roofline["traffic"] = tj.get("dram_bytes_per_algorithmic_byte")
+            roofline["traffic_note"] = tj.get("note")
+        except Exception:  # noqa: BLE001
+            pass
+
+    # End to end: pinned host codes -> device -> merge -> host, through the public API.
+    e2e = None
+    if not args.no_e2e:
+        host = []
+        h2d = d2h = 0
+        for key, rows, cols, t, b, a in items:
+            hs = [s.detach().cpu().pin_memory() for s in storage_tensors(t)]
+            hf = [b.cpu().pin_memory(), a.cpu().pin_memory()]
+            host.append((hs, hf))
+            h2d += sum(x.numel() * x.element_size() for x in hs + hf)
+            d2h += sum(x.numel() * x.element_size() for x in hs)
+        torch.cuda.synchronize(device)
+
+        def e2e_step(stp: int):
+            ops = []
+            for (key, rows, cols, t, b, a), (hs, hf) in zip(items, host):
+                for dst, src in zip(storage_tensors(t), hs):
+                    dst.copy_(src, non_blocking=True)
+                b.copy_(hf[0], non_blocking=True)
+                a.copy_(hf[1], non_blocking=True)
+                ops.append((t, b, a, 1.0, derive_seed(key, stp) if stochastic else None))
+            AD.merge_lora_batch(ops, workspace=ws)
+            for (key, rows, cols, t, b, a), (hs, hf) in zip(items, host):
+                for dst, src in zip(hs, storage_tensors(t)):
+                    dst.copy_(src, non_blocking=True)
+
+        e2e_step(step)
+        torch.cuda.synchronize(device)
+        barrier()
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_end = torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for i in range(args.e2e_steps):
+            e2e_step(step + 1 + i)
+        e_end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        e_ms = max_over_ranks(e_start.elapsed_time(e_end) / args.e2e_steps)
+        e2e = {"value": total_bytes * world / (e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": args.e2e_steps,
+               "path": "pinned host -> H2D -> adapters.merge_lora_batch (C ABI) -> D2H, one stream"}
+
+    if rank == 0:
+        line = {
+            "metric": metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": desc, "weights_per_gpu": len(items), "rank": lrank, "stochastic": stochastic,
+                       "weight_bytes_per_gpu": total_bytes, "l2": "inputs (~GBs) exceed the 126 MB L2; no flush",
+                       "parallelism": f"weak x{world}: one model per GPU, no collective"},
+            "roofline": roofline,
+            "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": e2e, "gpu_launches": launches, "clocks": clocks, "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

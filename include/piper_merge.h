@@ -173,6 +173,10 @@ int piper_merge_device_status(void* stream, uint32_t* status);
 /* Library version string, e.g. "piper-merge 0.1 sm_100a". */
 const char* piper_merge_version(void);
 
+/* Number of merge kernels this process has launched so far (all devices).
+ * No counterpart in the reference: a measurement aid for benchmarks. */
+uint64_t piper_merge_launches(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,7 @@ EXPORTED_SYMBOLS = (
     "piper_merge_last_error",
     "piper_merge_device_status",
     "piper_merge_version",
+    "piper_merge_launches",
 )
 
 
@@ -126,6 +127,8 @@ def load() -> ctypes.CDLL:
         lib.piper_merge_last_error.argtypes = []
         lib.piper_merge_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32)]
         lib.piper_merge_version.restype = ctypes.c_char_p
+        lib.piper_merge_launches.restype = ctypes.c_uint64
+        lib.piper_merge_launches.argtypes = []
         for name in (
             "piper_merge_workspace_size",
             "piper_merge_batch",
@@ -201,3 +204,8 @@ def device_status(device: torch.device) -> int:
 
 def version() -> str:
     return load().piper_merge_version().decode()
+
+
+def launches() -> int:
+    """Merge kernels launched by this process so far."""
+    return int(load().piper_merge_launches())

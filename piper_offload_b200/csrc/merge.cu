@@ -32,6 +32,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -102,9 +103,14 @@ __host__ __device__ constexpr int row_stride() {
   return align_up(code_bytes<FMT>(BN), 16) + 16;
 }
 
+// Shared memory: resident B strip (128 x KP bf16), one A tile (KP x BN bf16),
+// two code-tile stages (128 rows x RS bytes) and two per-row scale stages
+// (16 bytes per row), then the mbarrier and the tensor-memory address slot.
+constexpr int kScaleSlot = 16;
+
 template <int FMT, int BN>
 __host__ __device__ constexpr int smem_bytes(int kp) {
-  return 128 * kp * 2 + kp * BN * 2 + 2 * 128 * row_stride<FMT, BN>() + 64;
+  return 128 * kp * 2 + kp * BN * 2 + 2 * 128 * row_stride<FMT, BN>() + 2 * 128 * kScaleSlot + 64;
 }
 
 // Blocked 128x4 scale layout (_triton_mx_lora.py:97-112, _triton_nvfp4_lora.py:88-104).
@@ -223,11 +229,13 @@ struct MxParams<PIPER_FMT_MXFP4> {
 
 // ------------------------------------------------------- per-thread context
 struct RowCtx {
-  int row;          // global row
-  bool valid;       // row < M
-  uint8_t* srow;    // this row's code segment in shared memory
-  int tile_col0;    // first column of the tile
-  int tile_cols;    // valid columns in the tile
+  int row;               // global row
+  bool valid;            // row < M
+  uint8_t* srow;         // this row's code segment in shared memory
+  const uint8_t* sscale; // this row's prefetched scale bytes for the tile (MX / NVFP4)
+  int blk0;              // scale block index of sscale[0]
+  int tile_col0;         // first column of the tile
+  int tile_cols;         // valid columns in the tile
 };
 
 __device__ __forceinline__ void load_bytes32(const uint8_t* s, uint32_t (&w)[8]) {
@@ -253,7 +261,7 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
   const int blk = col >> 5;
   uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
   const int64_t sidx = scale_index(W, c.row, blk);
-  const float bscale = dec_e8m0(c.valid ? scale8[sidx] : 127u);
+  const float bscale = dec_e8m0(c.valid ? c.sscale[blk - c.blk0] : 127u);
   float merged[32];
   if constexpr (FMT == PIPER_FMT_MXFP4) {
     const uint4 pk = *reinterpret_cast<const uint4*>(c.srow + 16 * k);
@@ -287,22 +295,35 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
       W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
   if constexpr (FMT == PIPER_FMT_MXFP4) {
     uint32_t out[4] = {0u, 0u, 0u, 0u};
+    if (sr) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
-      uint32_t code = enc_e2m1(n);
-      if (sr) code = sr_e2m1(n, code, key, off0 + i);
-      out[i >> 3] |= (code & 0xFu) << ((i & 7) * 4);
+      for (int i = 0; i < 32; ++i) {
+        const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
+        out[i >> 3] |= (sr_e2m1(n, enc_e2m1(n), key, off0 + i) & 0xFu) << ((i & 7) * 4);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
+        out[i >> 3] |= (enc_e2m1(n) & 0xFu) << ((i & 7) * 4);
+      }
     }
     *reinterpret_cast<uint4*>(c.srow + 16 * k) = make_uint4(out[0], out[1], out[2], out[3]);
   } else {
     constexpr bool kE4 = FMT == PIPER_FMT_MXFP8_E4M3;
     uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    if (sr) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
-      const uint32_t code = sr ? sr_fp8<kE4>(n, P::kMax, key, off0 + i) : enc_fp8<kE4>(n);
-      out[i >> 2] |= code << ((i & 3) * 8);
+      for (int i = 0; i < 32; ++i) {
+        const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
+        out[i >> 2] |= sr_fp8<kE4>(n, P::kMax, key, off0 + i) << ((i & 3) * 8);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
+        out[i >> 2] |= enc_fp8<kE4>(n) << ((i & 3) * 8);
+      }
     }
     store_bytes32(c.srow + 32 * k, out);
   }
@@ -326,7 +347,7 @@ __device__ __forceinline__ void nvfp4_chunk(const DevWeight& W, const RowCtx& c,
   for (int h = 0; h < 2; ++h) {
     const int blk = (col >> 4) + h;
     const int64_t sidx = scale_index(W, c.row, blk);
-    float bsc = dec_e4m3(c.valid ? scale8[sidx] : 0u);
+    float bsc = dec_e4m3(c.valid ? c.sscale[blk - c.blk0] : 0u);
     if (CDT == kBF16) bsc = bf16r(bsc);
     if (two_level) {
       bsc = __fmul_rn(bsc, g_in);
@@ -360,14 +381,24 @@ __device__ __forceinline__ void nvfp4_chunk(const DevWeight& W, const RowCtx& c,
       const uint64_t off0 = W.offset_base +
                             static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col +
                             16 * h;
+      float nv[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        float n = two_level ? __fmul_rn(merged[i], recip) : div_full(merged[i], fs);
-        n = fminf(fmaxf(n, -6.0f), 6.0f);
-        uint32_t code = enc_e2m1(n);
-        if (sr) code = sr_e2m1(n, code, key, off0 + i);
-        const int e = 16 * h + i;
-        out[e >> 3] |= (code & 0xFu) << ((e & 7) * 4);
+        const float n = two_level ? __fmul_rn(merged[i], recip) : div_full(merged[i], fs);
+        nv[i] = fminf(fmaxf(n, -6.0f), 6.0f);
+      }
+      if (sr) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e = 16 * h + i;
+          out[e >> 3] |= (sr_e2m1(nv[i], enc_e2m1(nv[i]), key, off0 + i) & 0xFu) << ((e & 7) * 4);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e = 16 * h + i;
+          out[e >> 3] |= (enc_e2m1(nv[i]) & 0xFu) << ((e & 7) * 4);
+        }
       }
     }
   }
@@ -622,17 +653,15 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   uint8_t* sB = smem;
   uint8_t* sA = smem + 128 * KP * 2;
   uint8_t* sC = sA + KP * BN * 2;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sC + 2 * 128 * RS);
-  uint64_t* bar_load = bars;      // [2]
-  uint64_t* bar_mma = bars + 2;   // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  uint8_t* sS = sC + 2 * 128 * RS;
+  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sS + 2 * 128 * kScaleSlot);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
 
   const int row = row0 + tid;
   const bool valid = row < W.M;
+  const int rows_here = min(128, W.M - row0);
 
   if (tid == 0) {
-    mbar_init(&bar_load[0], kThreads);
-    mbar_init(&bar_load[1], kThreads);
     mbar_init(bar_mma, 1);
     fence_mbar_init();
   }
@@ -646,58 +675,135 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     const uint16_t* brow = W.b + static_cast<int64_t>(row) * W.r;
     const bool vec = ((reinterpret_cast<uintptr_t>(W.b) | (W.r * 2)) & 15) == 0;
     for (int kc = 0; kc < KP / 8; ++kc) {
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (valid) {
-        if (vec && kc * 8 + 8 <= W.r) {
-          v = __ldg(reinterpret_cast<const uint4*>(brow + kc * 8));
-        } else {
+      uint8_t* dst = sB + kc * 2048 + (tid >> 3) * 128 + (tid & 7) * 16;
+      if (valid && vec && kc * 8 + 8 <= W.r) {
+        cp_async16(dst, brow + kc * 8);
+      } else {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (valid) {
           uint16_t e[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) e[j] = (kc * 8 + j < W.r) ? brow[kc * 8 + j] : 0;
           v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16),
                          e[6] | (e[7] << 16));
         }
+        *reinterpret_cast<uint4*>(dst) = v;
       }
-      *reinterpret_cast<uint4*>(sB + kc * 2048 + (tid >> 3) * 128 + (tid & 7) * 16) = v;
     }
   }
+
+  // ---- tile byte ranges and copy granularity (16 B when everything is aligned).
+  auto tile_off = [&](int c0) -> int64_t {
+    if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) return code_bytes<FMT>(c0);
+    else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) return c0 / 2;
+    else return c0;
+  };
+  auto tile_nbytes = [&](int ncols) -> int {
+    if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) return code_bytes<FMT>(ncols);
+    else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) return ncols / 2;
+    else return ncols;
+  };
+  auto granularity = [&](int64_t off, int nbytes) -> int {
+    const int64_t m = W.row_bytes | off | nbytes | static_cast<int64_t>(reinterpret_cast<uintptr_t>(W.q));
+    return (m & 15) == 0 ? 16 : ((m & 3) == 0 ? 4 : 1);
+  };
+
+  // Coalesced async copy of one code tile (rows row0.., bytes [off, off+nbytes)) into a stage.
+  auto issue_codes = [&](int tile, int stage) {
+    const int c0 = col_begin + tile * BN;
+    const int ncols = min(BN, col_end - c0);
+    const int64_t off = tile_off(c0);
+    const int nbytes = tile_nbytes(ncols);
+    const int g = granularity(off, nbytes);
+    const int per = nbytes / g;
+    const int total = rows_here * per;
+    uint8_t* base = sC + stage * 128 * RS;
+    const uint8_t* src0 = W.q + static_cast<int64_t>(row0) * W.row_bytes + off;
+    for (int k = tid; k < total; k += kThreads) {
+      const int r = k / per;
+      const int i = k - r * per;
+      uint8_t* dst = base + r * RS + i * g;
+      const uint8_t* src = src0 + static_cast<int64_t>(r) * W.row_bytes + i * g;
+      if (g == 16) cp_async16(dst, src);
+      else if (g == 4) cp_async4(dst, src);
+      else *dst = *src;
+    }
+    // Per-row scale bytes of MX / NVFP4 tiles.
+    if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 || FMT == PIPER_FMT_MXFP4 ||
+                  FMT == PIPER_FMT_NVFP4) {
+      constexpr int kBlk = FMT == PIPER_FMT_NVFP4 ? 16 : 32;
+      const int b0 = c0 / kBlk;
+      const int nb = (ncols + kBlk - 1) / kBlk;
+      uint8_t* dst = sS + stage * 128 * kScaleSlot + tid * kScaleSlot;
+      if (valid) {
+        const uint8_t* scale8 = reinterpret_cast<const uint8_t*>(W.scale);
+        const bool sw = (W.flags & PIPER_FLAG_SWIZZLED) != 0u;
+        const bool vec4 = ((b0 | nb) & 3) == 0 && (sw || (W.scale_cols & 3) == 0) &&
+                          (reinterpret_cast<uintptr_t>(W.scale) & 3) == 0;
+        if (vec4) {
+          for (int j = 0; j < nb; j += 4) cp_async4(dst + j, scale8 + scale_index(W, row, b0 + j));
+        } else {
+          for (int j = 0; j < nb; ++j) dst[j] = scale8[scale_index(W, row, b0 + j)];
+        }
+      }
+    }
+  };
+
+  // A tile (MN-major canonical): element (k, n) at (k/8)*(BN*16) + (n/8)*128 + (k%8)*16 + (n%8)*2.
+  auto issue_a = [&](int tile) {
+    const int c0 = col_begin + tile * BN;
+    const bool vec = (((reinterpret_cast<uintptr_t>(W.a)) | (W.N * 2)) & 15) == 0;
+    const int chunks = KP * BN / 8;
+    for (int idx = tid; idx < chunks; idx += kThreads) {
+      const int kk = idx & 7;
+      const int ng = (idx >> 3) % (BN / 8);
+      const int kg = idx / BN;
+      const int kr = kg * 8 + kk;
+      const int n = c0 + ng * 8;
+      uint8_t* dst = sA + kg * (BN * 16) + ng * 128 + kk * 16;
+      const uint16_t* ap = W.a + static_cast<int64_t>(kr) * W.N + n;
+      if (kr < W.r && vec && n + 8 <= col_end) {
+        cp_async16(dst, ap);
+      } else {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (kr < W.r) {
+          uint16_t e[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) e[j] = (n + j < col_end) ? ap[j] : 0;
+          v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16),
+                         e[6] | (e[7] << 16));
+        }
+        *reinterpret_cast<uint4*>(dst) = v;
+      }
+    }
+  };
+
+  // Coalesced write-back of a stage to global memory (in place).
+  auto store_codes = [&](int tile, int stage) {
+    const int c0 = col_begin + tile * BN;
+    const int ncols = min(BN, col_end - c0);
+    const int64_t off = tile_off(c0);
+    const int nbytes = tile_nbytes(ncols);
+    const int g = granularity(off, nbytes);
+    const int per = nbytes / g;
+    const int total = rows_here * per;
+    const uint8_t* base = sC + stage * 128 * RS;
+    uint8_t* dst0 = W.q + static_cast<int64_t>(row0) * W.row_bytes + off;
+    for (int k = tid; k < total; k += kThreads) {
+      const int r = k / per;
+      const int i = k - r * per;
+      const uint8_t* src = base + r * RS + i * g;
+      uint8_t* dst = dst0 + static_cast<int64_t>(r) * W.row_bytes + i * g;
+      if (g == 16) *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+      else if (g == 4) *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(src);
+      else *dst = *src;
+    }
+  };
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  // ---- code-tile loader: thread t moves its own row segment.
-  auto issue_load = [&](int tile, int stage) {
-    uint8_t* dst = sC + stage * 128 * RS + tid * RS;
-    const int c0 = col_begin + tile * BN;
-    const int ncols = min(BN, col_end - c0);
-    int off, nbytes;
-    if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
-      off = code_bytes<FMT>(c0);
-      nbytes = code_bytes<FMT>(ncols);
-    } else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) {
-      off = c0 / 2;
-      nbytes = ncols / 2;
-    } else {
-      off = c0;
-      nbytes = ncols;
-    }
-    if (!valid || nbytes <= 0) {
-      mbar_arrive(&bar_load[stage]);
-      return;
-    }
-    const uint8_t* src = W.q + static_cast<int64_t>(row) * W.row_bytes + off;
-    if (((reinterpret_cast<uintptr_t>(src) | nbytes) & 15) == 0) {
-      bulk_wait_read_all();  // a previous bulk store may still read this row
-      mbar_arrive_expect_tx(&bar_load[stage], static_cast<uint32_t>(nbytes));
-      bulk_g2s(dst, src, static_cast<uint32_t>(nbytes), &bar_load[stage]);
-    } else {
-      bulk_wait_read_all();
-      for (int i = 0; i < nbytes; ++i) dst[i] = src[i];
-      mbar_arrive(&bar_load[stage]);
-    }
-  };
 
   const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
   (void)sr;
@@ -729,39 +835,18 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   }
 
   bool ok = true;
-  if (n_tiles > 0) issue_load(0, 0);
-  for (int tile = 0; tile < n_tiles && ok; ++tile) {
+  if (n_tiles > 0) {
+    issue_codes(0, 0);
+    issue_a(0);
+    cp_async_commit();
+  }
+  for (int tile = 0; tile < n_tiles; ++tile) {
     const int stage = tile & 1;
     const int c0 = col_begin + tile * BN;
     const int tcols = min(BN, col_end - c0);
 
-    // ---- stage the A tile (MN-major canonical): element (k, n) at
-    //      (k/8)*(BN*16) + (n/8)*128 + (k%8)*16 + (n%8)*2.
-    {
-      const bool vec = (((reinterpret_cast<uintptr_t>(W.a)) | (W.N * 2)) & 15) == 0;
-      const int chunks = KP * BN / 8;
-      for (int idx = tid; idx < chunks; idx += kThreads) {
-        const int kk = idx & 7;
-        const int ng = (idx >> 3) % (BN / 8);
-        const int kg = idx / BN;
-        const int kr = kg * 8 + kk;
-        const int n = c0 + ng * 8;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (kr < W.r) {
-          const uint16_t* ap = W.a + static_cast<int64_t>(kr) * W.N + n;
-          if (vec && n + 8 <= col_end) {
-            v = __ldg(reinterpret_cast<const uint4*>(ap));
-          } else {
-            uint16_t e[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) e[j] = (n + j < col_end) ? ap[j] : 0;
-            v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16),
-                           e[6] | (e[7] << 16));
-          }
-        }
-        *reinterpret_cast<uint4*>(sA + kg * (BN * 16) + ng * 128 + kk * 16) = v;
-      }
-    }
+    // ---- tile `tile` (codes, scales, A) has landed in shared memory.
+    cp_async_wait_all();
     fence_proxy_async_smem();
     __syncthreads();
 
@@ -779,24 +864,25 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
       umma_commit(bar_mma);
     }
 
-    // ---- prefetch the next code tile into the other stage.
-    if (tile + 1 < n_tiles) issue_load(tile + 1, stage ^ 1);
+    // ---- prefetch the next tile's codes and scales into the other stage.
+    if (tile + 1 < n_tiles) issue_codes(tile + 1, stage ^ 1);
 
-    ok = mbar_wait(&bar_load[stage], (tile >> 1) & 1, kStatusTimeoutLoad);
-    ok = mbar_wait(bar_mma, tile & 1, kStatusTimeoutMma) && ok;
+    ok = mbar_wait(bar_mma, tile & 1, kStatusTimeoutMma);
     // Keep the CTA uniform: tcgen05.ld below is warp-collective.
     ok = __syncthreads_and(ok) != 0;
     tc_fence_after();
-    if (!ok) {
-      // Give copies and MMAs in flight a bounded chance to land before exit.
-      if (tile + 1 < n_tiles) mbar_wait(&bar_load[stage ^ 1], ((tile + 1) >> 1) & 1, kStatusTimeoutLoad);
-      break;
-    }
+    if (!ok) break;
+
+    // The MMA has consumed the A tile: fetch the next one behind the epilogue.
+    if (tile + 1 < n_tiles) issue_a(tile + 1);
+    cp_async_commit();
 
     RowCtx c;
     c.row = row;
     c.valid = valid;
     c.srow = sC + stage * 128 * RS + tid * RS;
+    c.sscale = sS + stage * 128 * kScaleSlot + tid * kScaleSlot;
+    c.blk0 = (FMT == PIPER_FMT_NVFP4) ? c0 / 16 : c0 / 32;
     c.tile_col0 = c0;
     c.tile_cols = tcols;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
@@ -826,7 +912,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
           uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
           const int blk = col >> 4;
           const int64_t sidx = scale_index(W, row, blk);
-          float bsc = dec_e4m3(valid ? scale8[sidx] : 0u);
+          float bsc = dec_e4m3(valid ? c.sscale[blk - c.blk0] : 0u);
           if (CDT == kBF16) bsc = bf16r(bsc);
           if (two_level) {
             bsc = __fmul_rn(bsc, g_in);
@@ -963,7 +1049,34 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
             affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
             const int nvalid = min(32, tcols - 32 * k);
             if constexpr (PASS == kReduce) {
-              if (valid) {
+              const bool uniform_chunk =
+                  W.nq_row == 0 || (W.group >= 32 && (col % W.group) + 32 <= W.group);
+              if (valid && uniform_chunk && nvalid == 32) {
+                const int qp = qparam_index(W, row, col);
+                if (qp != red_qp) {
+                  flush_reduce();
+                  red_qp = qp;
+                }
+                // First touch of a quantization block saves its input qparams.
+                if (W.nq_row == 0 ? (row == 0 && col == 0) : (col % W.group == 0)) {
+                  if (kInt8) {
+                    W.old_scale[qp] = load_scale_dt(W.scale, qp, W.scale_dt);
+                    W.old_zp[qp] = W.zp != nullptr ? static_cast<int>(W.zp[qp]) : 0;
+                  } else {
+                    W.old_scale[qp] = reinterpret_cast<const float*>(W.scale)[qp];
+                  }
+                }
+                if (kInt8) {
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) {
+                    red_max = fmaxf(red_max, merged[i]);
+                    red_nmin = fmaxf(red_nmin, -merged[i]);
+                  }
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) red_max = fmaxf(red_max, fabsf(merged[i]));
+                }
+              } else if (valid) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                   if (i < nvalid) {
@@ -971,7 +1084,6 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
                     if (qp != red_qp) {
                       flush_reduce();
                       red_qp = qp;
-                      // First touch of a quantization block saves its input qparams.
                       if (W.nq_row == 0 ? (row == 0 && col + i == 0) : ((col + i) % W.group == 0)) {
                         if (kInt8) {
                           W.old_scale[qp] = load_scale_dt(W.scale, qp, W.scale_dt);
@@ -994,14 +1106,56 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
               uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
               const uint64_t off0 =
                   W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + col;
-              int cur_qp = -1;
-              Int8Q q;
-              q.scale = 1.0f;
-              q.zp = 0;
-              float s = 1.0f;
+              const bool sr_on = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+              const bool uniform_chunk =
+                  W.nq_row == 0 || (W.group >= 32 && (col % W.group) + 32 <= W.group);
+              if (valid && uniform_chunk) {
+                // One quantization block covers the whole chunk (per-row / per-tensor).
+                const int qp = qparam_index(W, row, col);
+                const float qmx = __uint_as_float(W.qmax[qp]);
+                const bool owner = W.nq_row == 0 ? (row == 0 && col == 0) : (col % W.group == 0);
+                if constexpr (kInt8) {
+                  const Int8Q q = int8_qparams<CDT>(-__uint_as_float(W.qmin[qp]), qmx, asym, qmin, qmax,
+                                                    W.scale_dt);
+                  if (owner) {
+                    store_scale_dt(W.scale, qp, W.scale_dt, q.scale);
+                    if (W.zp != nullptr) W.zp[qp] = static_cast<int8_t>(q.zp);
+                  }
+                  if (sr_on) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                if (i < nvalid && valid) {
+                    for (int i = 0; i < 32; ++i)
+                      out[i >> 2] |= int8_encode(merged[i], q, qmin, qmax, W.scale_dt, true, key, off0 + i)
+                                     << ((i & 3) * 8);
+                  } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                      out[i >> 2] |= int8_encode(merged[i], q, qmin, qmax, W.scale_dt, false, key, off0 + i)
+                                     << ((i & 3) * 8);
+                  }
+                } else {
+                  const float s = fp8_new_scale<CDT>(qmx, kLimit);
+                  if (owner) reinterpret_cast<float*>(W.scale)[qp] = s;
+                  if (sr_on) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                      const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
+                      out[i >> 2] |= sr_fp8<kE4>(x, kLimit, key, off0 + i) << ((i & 3) * 8);
+                    }
+                  } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                      const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
+                      out[i >> 2] |= enc_fp8<kE4>(x) << ((i & 3) * 8);
+                    }
+                  }
+                }
+              } else if (valid) {
+                int cur_qp = -1;
+                Int8Q q;
+                q.scale = 1.0f;
+                q.zp = 0;
+                float s = 1.0f;
+                for (int i = 0; i < nvalid; ++i) {
                   const int qp = qparam_index(W, row, col + i);
                   if (qp != cur_qp) {
                     cur_qp = qp;
@@ -1023,14 +1177,15 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
                       }
                     }
                   }
+                  float mi = merged[0];
+#pragma unroll
+                  for (int j = 1; j < 32; ++j) mi = (j == i) ? merged[j] : mi;
                   uint32_t code;
                   if (kInt8) {
-                    code = int8_encode(merged[i], q, qmin, qmax, W.scale_dt,
-                                       (W.flags & PIPER_FLAG_STOCHASTIC) != 0u, key, off0 + i);
+                    code = int8_encode(mi, q, qmin, qmax, W.scale_dt, sr_on, key, off0 + i);
                   } else {
-                    const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
-                    code = (W.flags & PIPER_FLAG_STOCHASTIC) ? sr_fp8<kE4>(x, kLimit, key, off0 + i)
-                                                             : enc_fp8<kE4>(x);
+                    const float x = fminf(fmaxf(div_full(mi, s), -kLimit), kLimit);
+                    code = sr_on ? sr_fp8<kE4>(x, kLimit, key, off0 + i) : enc_fp8<kE4>(x);
                   }
                   out[i >> 2] |= code << ((i & 3) * 8);
                 }
@@ -1042,31 +1197,15 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
       }
     }
 
-    // ---- write the tile back (in place).
-    if (PASS != kReduce && ok && valid) {
-      int off, nbytes;
-      if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
-        off = code_bytes<FMT>(c0);
-        nbytes = code_bytes<FMT>(tcols);
-      } else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) {
-        off = c0 / 2;
-        nbytes = tcols / 2;
-      } else {
-        off = c0;
-        nbytes = tcols;
-      }
-      uint8_t* dst = W.q + static_cast<int64_t>(row) * W.row_bytes + off;
-      if (((reinterpret_cast<uintptr_t>(dst) | nbytes) & 15) == 0) {
-        fence_proxy_async_smem();
-        bulk_s2g(dst, c.srow, static_cast<uint32_t>(nbytes));
-        bulk_commit();
-      } else {
-        for (int i = 0; i < nbytes; ++i) dst[i] = c.srow[i];
-      }
+    // ---- write the tile back (in place), coalesced.
+    if (PASS != kReduce) {
+      __syncthreads();
+      store_codes(tile, stage);
     }
     tc_fence_before();
     __syncthreads();
   }
+  cp_async_wait_all();
 
   // ---- REDUCE epilogue: publish running maxima.
   if constexpr (PASS == kReduce) {
@@ -1097,7 +1236,6 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     if (two_level && blockIdx.x == static_cast<unsigned>(W.item_begin) && tid == 0) *W.gscale = g_out;
   }
 
-  bulk_wait_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -1113,6 +1251,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
 namespace {
 
 thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
 
 int fail(int code, const std::string& msg) {
   g_last_error = msg;
@@ -1263,6 +1402,7 @@ int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
   if (e != cudaSuccess)
     return fail(PIPER_MERGE_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   kern<<<items, pm::kThreads, smem, stream>>>(lp);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
   return PIPER_MERGE_OK;
@@ -1629,5 +1769,7 @@ int piper_merge_device_status(void* stream, uint32_t* status) {
 }
 
 const char* piper_merge_version(void) { return "piper-merge 0.1 sm_100a"; }
+
+uint64_t piper_merge_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"

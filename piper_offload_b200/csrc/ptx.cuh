@@ -192,3 +192,24 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t n, uint32_t ab_bf16) {
 }
 
 }  // namespace pm
+
+namespace pm {
+// ------------------------------------------------ cp.async (LDGSTS) copies
+// Asynchronous global -> shared copies of 16 / 8 / 4 bytes, completed with
+// cp.async.wait_group by the issuing thread. Addresses must be aligned to the
+// copy size.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+}  // namespace pm

@@ -1,0 +1,96 @@
+"""Light stand-ins for the quantized weight wrappers the adapters merge into.
+
+They carry TorchAO's attribute names (``Int8Tensor``, ``Float8Tensor``,
+``NVFP4Tensor``, ``MXTensor``) and the reference's ``GGUFWeight``
+(``gguf_adapter.py:61-105``) so that the adapters can be used and tested
+without TorchAO, which is absent from this image. A real TorchAO tensor with
+the same attributes dispatches to the same adapter.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+
+
+@dataclass
+class Int8Weight:
+    qdata: torch.Tensor
+    scale: torch.Tensor
+    block_size: tuple[int, int]
+    dtype: torch.dtype = torch.bfloat16
+    zero_point: torch.Tensor | None = None
+    act_pre_scale: torch.Tensor | None = None
+    reduce_range: bool = False
+
+    @property
+    def shape(self) -> torch.Size:
+        return self.qdata.shape
+
+
+@dataclass
+class Float8Weight:
+    qdata: torch.Tensor
+    scale: torch.Tensor
+    block_size: tuple[int, int]
+    dtype: torch.dtype = torch.bfloat16
+
+    @property
+    def shape(self) -> torch.Size:
+        return self.qdata.shape
+
+
+@dataclass
+class NVFP4Weight:
+    qdata: torch.Tensor
+    scale: torch.Tensor
+    per_tensor_scale: torch.Tensor | None = None
+    block_size: int = 16
+    orig_dtype: torch.dtype = torch.bfloat16
+    is_swizzled_scales: bool = False
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return self.qdata.shape[0], self.qdata.shape[1] * 2
+
+
+@dataclass
+class MXScalingMode:
+    value: str = "floor"
+
+
+@dataclass
+class MXActQuantKwargs:
+    scaling_mode: Any = None
+
+
+@dataclass
+class MXWeight:
+    qdata: torch.Tensor
+    scale: torch.Tensor
+    elem_dtype: Any
+    block_size: int = 32
+    orig_dtype: torch.dtype = torch.bfloat16
+    is_swizzled_scales: bool = False
+    act_quant_kwargs: Any = field(default_factory=MXActQuantKwargs)
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        fp4 = getattr(torch, "float4_e2m1fn_x2", None)
+        rows, cols = self.qdata.shape
+        return (rows, cols * 2) if fp4 is not None and self.elem_dtype is fp4 else (rows, cols)
+
+
+@dataclass
+class GGUFWeight:
+    raw: torch.Tensor
+    quant_type: int
+    compute_dtype: torch.dtype = torch.bfloat16
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        from .kernels import gguf_logical_cols
+
+        return self.raw.shape[0], gguf_logical_cols(self.raw.shape[1], self.quant_type)
