@@ -34,6 +34,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -44,7 +45,7 @@
 
 namespace pm {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;  // two warpgroups; thread t owns tile row (t & 127)
 constexpr int kMaxWeights = 24;
 constexpr int kMaxRank = 256;
 
@@ -83,6 +84,8 @@ struct DevWeight {
 struct LaunchParams {
   DevWeight w[kMaxWeights];
   int n_weights;
+  int n_items;  // work items over all weights; CTAs stride over them
+  int kp_max;   // shared-memory layout is sized for the largest padded rank
 };
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -260,31 +263,41 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
   const int col = c.tile_col0 + 32 * k;
   const int blk = col >> 5;
   uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
-  const int64_t sidx = scale_index(W, c.row, blk);
-  const float bscale = dec_e8m0(c.valid ? c.sscale[blk - c.blk0] : 127u);
+  const uint32_t sc = c.valid ? c.sscale[blk - c.blk0] : 127u;
+  const float bscale = dec_e8m0(sc);
+  // Decode: FP8 / FP4 values are exactly representable in bf16, so the
+  // reference's bf16 cast of the element is the identity.
   float merged[32];
   if constexpr (FMT == PIPER_FMT_MXFP4) {
     const uint4 pk = *reinterpret_cast<const uint4*>(c.srow + 16 * k);
     const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
-    const float bs = CDT == kBF16 ? bf16r(bscale) : bscale;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const uint32_t code = (wv[i >> 3] >> ((i & 7) * 4)) & 0xFu;
-      const float lp = dec_e2m1(code);
-      const float base = CDT == kBF16 ? bf16r(__fmul_rn(bf16r(lp), bs)) : __fmul_rn(lp, bs);
-      merged[i] = round_dt<CDT>(fmaf(acc[i], W.strength, base));
-    }
+    for (int j = 0; j < 16; ++j) dec_e2m1x2(wv[j >> 2] >> ((j & 3) * 8), merged[2 * j], merged[2 * j + 1]);
   } else {
     uint32_t wv[8];
     load_bytes32(c.srow + 32 * k, wv);
-    const float bs = CDT == kBF16 ? bf16r(bscale) : bscale;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float lp = dec_fp8<FMT == PIPER_FMT_MXFP8_E4M3>(byte_of(wv, i));
-      const float base = CDT == kBF16 ? bf16r(__fmul_rn(bf16r(lp), bs)) : __fmul_rn(lp, bs);
-      merged[i] = round_dt<CDT>(fmaf(acc[i], W.strength, base));
+    for (int w = 0; w < 8; ++w) {
+      float f[4];
+      dec_fp8x4<FMT == PIPER_FMT_MXFP8_E4M3>(wv[w], f);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) merged[4 * w + j] = f[j];
     }
   }
+  // base = bf16(elem * bf16(scale)): for scale codes 20..230 every product is
+  // an exact bf16 normal, so the rounding is the identity.
+  if (sc >= 20u && sc <= 230u) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) merged[i] = __fmul_rn(merged[i], bscale);
+  } else {
+    const float bs = bf16r(bscale);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) merged[i] = bf16r(__fmul_rn(merged[i], bs));
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], W.strength, merged[i]);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) bf16r2(merged[i], merged[i + 1]);
   float amax = fabsf(merged[0]);
 #pragma unroll
   for (int i = 1; i < 32; ++i) amax = fmaxf(amax, fabsf(merged[i]));
@@ -293,117 +306,138 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
   const PhiloxKey key{W.k0, W.k1};
   const uint64_t off0 =
       W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) merged[i] = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
   if constexpr (FMT == PIPER_FMT_MXFP4) {
     uint32_t out[4] = {0u, 0u, 0u, 0u};
     if (sr) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
-        out[i >> 3] |= (sr_e2m1(n, enc_e2m1(n), key, off0 + i) & 0xFu) << ((i & 7) * 4);
-      }
+      for (int i = 0; i < 32; ++i)
+        out[i >> 3] |= (sr_e2m1(merged[i], enc_e2m1(merged[i]), key, off0 + i) & 0xFu) << ((i & 7) * 4);
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
-        out[i >> 3] |= (enc_e2m1(n) & 0xFu) << ((i & 7) * 4);
-      }
+      for (int j = 0; j < 16; ++j) out[j >> 2] |= enc_e2m1x2(merged[2 * j], merged[2 * j + 1]) << ((j & 3) * 8);
     }
     *reinterpret_cast<uint4*>(c.srow + 16 * k) = make_uint4(out[0], out[1], out[2], out[3]);
   } else {
     constexpr bool kE4 = FMT == PIPER_FMT_MXFP8_E4M3;
-    uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    uint32_t out[8];
     if (sr) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
-        out[i >> 2] |= sr_fp8<kE4>(n, P::kMax, key, off0 + i) << ((i & 3) * 8);
-      }
+      for (int w = 0; w < 8; ++w) out[w] = 0u;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) out[i >> 2] |= sr_fp8<kE4>(merged[i], P::kMax, key, off0 + i) << ((i & 3) * 8);
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float n = fminf(fmaxf(__fmul_rn(merged[i], s.inv), -P::kMax), P::kMax);
-        out[i >> 2] |= enc_fp8<kE4>(n) << ((i & 3) * 8);
-      }
+      for (int w = 0; w < 8; ++w)
+        out[w] = enc_fp8x4<kE4>(merged[4 * w], merged[4 * w + 1], merged[4 * w + 2], merged[4 * w + 3]);
     }
     store_bytes32(c.srow + 32 * k, out);
   }
-  if (c.valid) scale8[sidx] = static_cast<uint8_t>(s.code);
+  if (c.valid) scale8[scale_index(W, c.row, blk)] = static_cast<uint8_t>(s.code);
 }
 
 // ============================================================= NVFP4 epilogue
-// PASS kReduce: accumulate |merged| into `amax_acc`; kLocal: encode.
+// One 16-element block. `codes` holds its 8 packed bytes (in: input codes,
+// out: merged codes). PASS kReduce accumulates |merged| into `amax_acc`.
+template <int PASS, int CDT>
+__device__ __forceinline__ void nvfp4_block(const DevWeight& W, const RowCtx& c, int col,
+                                            const float* acc, float g_in, float g_out,
+                                            bool two_level, float& amax_acc, uint2& codes) {
+  uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
+  const int blk = col >> 4;
+  float bsc = dec_e4m3(c.valid ? c.sscale[blk - c.blk0] : 0u);  // E4M3 values are exact in bf16
+  if (two_level) {
+    bsc = __fmul_rn(bsc, g_in);
+    if (CDT == kBF16) bsc = bf16r(bsc);
+  }
+  float m[16];
+  const uint32_t wv[2] = {codes.x, codes.y};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) dec_e2m1x2(wv[j >> 2] >> ((j & 3) * 8), m[2 * j], m[2 * j + 1]);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m[i] = __fmul_rn(m[i], bsc);
+  // Single-level: e2m1 (<= 2 significant bits) x e4m3 (<= 4) is an exact bf16
+  // normal, so only the two-level product needs rounding.
+  if (CDT == kBF16 && two_level) {
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) bf16r2(m[i], m[i + 1]);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float upd = __fmul_rn(acc[i], W.strength);
+    m[i] = upd == 0.0f ? m[i] : fmaf(acc[i], W.strength, m[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+  float amax = fabsf(m[0]);
+#pragma unroll
+  for (int i = 1; i < 16; ++i) amax = fmaxf(amax, fabsf(m[i]));
+  if constexpr (PASS == kReduce) {
+    if (c.valid) amax_acc = fmaxf(amax_acc, amax);
+  } else {
+    float fs = __fdiv_rn(amax, 6.0f);  // `/ 6.0` (literal): IEEE
+    if (two_level) fs = div_full(fs, g_out);
+    fs = fminf(fmaxf(fs, 0.015625f), 448.0f);
+    const uint32_t fcode = enc_e4m3(fs);
+    fs = dec_e4m3(fcode);
+    const int64_t sidx = scale_index(W, c.row, blk);
+    if (c.valid) scale8[sidx] = static_cast<uint8_t>(fcode);
+    else if (W.flags & PIPER_FLAG_SWIZZLED) scale8[sidx] = 0u;  // swizzle padding rows
+    const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+    if (two_level) {
+      const float recip = div_full(div_full(1.0f, g_out), fs);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m[i] = __fmul_rn(m[i], recip);
+    } else if (sr) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m[i] = div_full(m[i], fs);
+    } else {
+      // x * RN(1/fs), re-checked with div.full near an E2M1 rounding boundary.
+      const float inv = __frcp_rn(fs);
+      float q[16];
+      bool near = false;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        q[i] = __fmul_rn(m[i], inv);
+        near |= near_e2m1_edge(q[i]);
+      }
+      if (near) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) q[i] = div_full(m[i], fs);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m[i] = q[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m[i] = fminf(fmaxf(m[i], -6.0f), 6.0f);
+    uint32_t out[2] = {0u, 0u};
+    if (sr) {
+      const PhiloxKey key{W.k0, W.k1};
+      const uint64_t off0 =
+          W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        out[i >> 3] |= (sr_e2m1(m[i], enc_e2m1(m[i]), key, off0 + i) & 0xFu) << ((i & 7) * 4);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j >> 2] |= enc_e2m1x2(m[2 * j], m[2 * j + 1]) << ((j & 3) * 8);
+    }
+    codes = make_uint2(out[0], out[1]);
+  }
+}
+
 template <int PASS, int CDT>
 __device__ __forceinline__ void nvfp4_chunk(const DevWeight& W, const RowCtx& c, int k,
                                             const float (&acc)[32], float g_in, float g_out,
                                             bool two_level, float& amax_acc) {
   const int col = c.tile_col0 + 32 * k;
-  uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
-  const uint4 pk = *reinterpret_cast<const uint4*>(c.srow + 16 * k);
-  const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
-  const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
-  const PhiloxKey key{W.k0, W.k1};
-  uint32_t out[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int blk = (col >> 4) + h;
-    const int64_t sidx = scale_index(W, c.row, blk);
-    float bsc = dec_e4m3(c.valid ? c.sscale[blk - c.blk0] : 0u);
-    if (CDT == kBF16) bsc = bf16r(bsc);
-    if (two_level) {
-      bsc = __fmul_rn(bsc, g_in);
-      if (CDT == kBF16) bsc = bf16r(bsc);
-    }
-    float merged[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int e = 16 * h + i;
-      const uint32_t code = (wv[e >> 3] >> ((e & 7) * 4)) & 0xFu;
-      float base = __fmul_rn(dec_e2m1(code), bsc);
-      if (CDT == kBF16) base = bf16r(base);
-      const float upd = __fmul_rn(acc[e], W.strength);
-      float m = upd == 0.0f ? base : fmaf(acc[e], W.strength, base);
-      merged[i] = round_dt<CDT>(m);
-    }
-    float amax = fabsf(merged[0]);
-#pragma unroll
-    for (int i = 1; i < 16; ++i) amax = fmaxf(amax, fabsf(merged[i]));
-    if constexpr (PASS == kReduce) {
-      if (c.valid) amax_acc = fmaxf(amax_acc, amax);
-    } else {
-      float fs = __fdiv_rn(amax, 6.0f);  // `/ 6.0` (literal): IEEE
-      if (two_level) fs = div_full(fs, g_out);
-      fs = fminf(fmaxf(fs, 0.015625f), 448.0f);
-      const uint32_t fcode = enc_e4m3(fs);
-      fs = dec_e4m3(fcode);
-      if (c.valid) scale8[sidx] = static_cast<uint8_t>(fcode);
-      else if (W.flags & PIPER_FLAG_SWIZZLED) scale8[sidx] = 0u;  // padding rows
-      const float recip = two_level ? div_full(div_full(1.0f, g_out), fs) : 0.0f;
-      const uint64_t off0 = W.offset_base +
-                            static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col +
-                            16 * h;
-      float nv[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float n = two_level ? __fmul_rn(merged[i], recip) : div_full(merged[i], fs);
-        nv[i] = fminf(fmaxf(n, -6.0f), 6.0f);
-      }
-      if (sr) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int e = 16 * h + i;
-          out[e >> 3] |= (sr_e2m1(nv[i], enc_e2m1(nv[i]), key, off0 + i) & 0xFu) << ((e & 7) * 4);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int e = 16 * h + i;
-          out[e >> 3] |= (enc_e2m1(nv[i]) & 0xFu) << ((e & 7) * 4);
-        }
-      }
-    }
-  }
+  uint4 pk = *reinterpret_cast<const uint4*>(c.srow + 16 * k);
+  uint2 lo = make_uint2(pk.x, pk.y), hi = make_uint2(pk.z, pk.w);
+  nvfp4_block<PASS, CDT>(W, c, col, acc, g_in, g_out, two_level, amax_acc, lo);
+  nvfp4_block<PASS, CDT>(W, c, col + 16, acc + 16, g_in, g_out, two_level, amax_acc, hi);
   if constexpr (PASS != kReduce)
-    *reinterpret_cast<uint4*>(c.srow + 16 * k) = make_uint4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<uint4*>(c.srow + 16 * k) = make_uint4(lo.x, lo.y, hi.x, hi.y);
 }
 
 // ========================================================= FP8 / INT8 helpers
@@ -456,7 +490,47 @@ __device__ __forceinline__ Int8Q int8_qparams(float min_v, float max_v, bool asy
   return q;
 }
 
-// _quantize_kernel (_triton_int8_lora.py:189-236) for one value.
+// _quantize_kernel (_triton_int8_lora.py:189-236) for 32 values sharing one
+// quantization block: inverse_scale = scale_dtype(1 / scale) (div.full),
+// scaled = scale_dtype(x * inverse_scale), q = rint(scaled) + zp, optional
+// stochastic rounding of x / scale + zp, clamp.
+__device__ __forceinline__ void round_rt2(float& a, float& b, int dt) {
+  if (dt == kBF16) bf16r2(a, b);
+  else if (dt == kF16) f16r2(a, b);
+}
+
+__device__ __forceinline__ void int8_encode32(const float (&m)[32], const Int8Q& q, int qmin, int qmax,
+                                              int scale_dt, bool sr, PhiloxKey key, uint64_t off0,
+                                              uint32_t (&out)[8]) {
+  float inv = div_full(1.0f, q.scale);
+  inv = round_dt_rt(inv, scale_dt);
+  float x[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] = __fmul_rn(m[i], inv);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_rt2(x[i], x[i + 1], scale_dt);
+  const float zpf = static_cast<float>(q.zp);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) out[w] = 0u;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    // rint (half to even) of |x| < 2^22 via the 1.5 * 2^23 magic addend.
+    float qf;
+    if (fabsf(x[i]) < 4194304.0f) {
+      const float y = __fadd_rn(x[i], 12582912.0f);
+      qf = static_cast<float>(static_cast<int>(__float_as_uint(y) - 0x4B400000u) + q.zp);
+    } else {
+      qf = static_cast<float>(__float2ll_rn(x[i]) + q.zp);
+    }
+    if (sr) {
+      const float ss = __fadd_rn(div_full(m[i], q.scale), zpf);
+      qf = sr_int(ss, qf, static_cast<float>(qmin), static_cast<float>(qmax), key, off0 + i);
+    }
+    qf = fminf(fmaxf(qf, static_cast<float>(qmin)), static_cast<float>(qmax));
+    out[i >> 2] |= (static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu) << ((i & 3) * 8);
+  }
+}
+
 __device__ __forceinline__ uint32_t int8_encode(float v, const Int8Q& q, int qmin, int qmax,
                                                 int scale_dt, bool sr, PhiloxKey key,
                                                 uint64_t off) {
@@ -472,27 +546,59 @@ __device__ __forceinline__ uint32_t int8_encode(float v, const Int8Q& q, int qmi
   return static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu;
 }
 
-// Decode + merge 32 columns of an FP8/INT8 row chunk. Columns >= N are masked
-// (their merged value is 0 and they are excluded by `nvalid`).
+// Decode + merge 32 columns of an FP8/INT8 row chunk. Columns >= N are
+// garbage and excluded by the callers.
 template <int FMT, int CDT>
 __device__ __forceinline__ void affine_merged(const DevWeight& W, const RowCtx& c, int k,
                                               const float (&acc)[32], const float* scale_in,
                                               const int* zp_in, float (&merged)[32]) {
   uint32_t wv[8];
   load_bytes32(c.srow + 32 * k, wv);
+  if constexpr (FMT == PIPER_FMT_INT8) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
+      // q - zp is an integer in [-255, 255]: exact in bf16 / fp16.
+      merged[i] = __fmul_rn(__fsub_rn(qv, static_cast<float>(zp_in[i])), scale_in[i]);
+    }
+  } else {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      float f[4];
+      dec_fp8x4<FMT == PIPER_FMT_FP8_E4M3>(wv[w], f);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) merged[4 * w + j] = __fmul_rn(f[j], scale_in[4 * w + j]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], W.strength, merged[i]);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+}
+
+// FP8 codes of 32 merged values for one scale `s` (round to nearest).
+// The reference quotient is div.full(x, s); x * RN(1/s) is used unless some
+// element lands within 4 ulp of an FP8 rounding boundary.
+template <bool E4M3>
+__device__ __forceinline__ void fp8_encode_rtn(const float (&m)[32], float s, float limit, uint32_t (&out)[8]) {
+  const float inv = __frcp_rn(s);
+  float q[32];
+  bool near = false;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    const uint32_t byte = byte_of(wv, i);
-    float base;
-    if constexpr (FMT == PIPER_FMT_INT8) {
-      const float qv = static_cast<float>(static_cast<int8_t>(byte));
-      base = round_dt<CDT>(__fsub_rn(qv, static_cast<float>(zp_in[i])));
-      base = round_dt<CDT>(__fmul_rn(base, scale_in[i]));
-    } else {
-      base = round_dt<CDT>(__fmul_rn(dec_fp8<FMT == PIPER_FMT_FP8_E4M3>(byte), scale_in[i]));
-    }
-    merged[i] = round_dt<CDT>(fmaf(acc[i], W.strength, base));
+    q[i] = __fmul_rn(m[i], inv);
+    near |= near_fp8_edge<E4M3>(q[i]);
   }
+  if (near) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) q[i] = div_full(m[i], s);
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) q[i] = fminf(fmaxf(q[i], -limit), limit);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) out[w] = enc_fp8x4<E4M3>(q[4 * w], q[4 * w + 1], q[4 * w + 2], q[4 * w + 3]);
 }
 
 // Input scale / zero point of each column of a chunk.
@@ -571,9 +677,14 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
       const uint32_t byte = blk[2 + (i & 15)];
       qv = static_cast<float>(static_cast<int>(i < 16 ? (byte & 0xFu) : (byte >> 4)) - 8);
     }
-    const float base = round_dt<CDT>(__fmul_rn(d_in, qv));
-    merged[i] = round_dt<CDT>(fmaf(acc[i], W.strength, base));
+    merged[i] = __fmul_rn(d_in, qv);
   }
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], W.strength, merged[i]);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
   const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
   const PhiloxKey key{W.k0, W.k1};
   const int col = c.tile_col0 + 32 * k;
@@ -631,51 +742,62 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
 
 // ============================================================== the kernel
 template <int FMT, int PASS, int BN, int CDT>
-__global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__ LaunchParams P) {
+__global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constant__ LaunchParams P) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
-  const int warp = tid >> 5;
+  const int rt = tid & 127;        // tile row / tensor-memory lane of this thread
+  const int wg = tid >> 7;         // warpgroup: takes every other accumulator chunk
+  const int lane_warp = (tid >> 5) & 3;
 
-  // Locate this CTA's weight and work item.
+  constexpr int RS = row_stride<FMT, BN>();
+  const int KPL = P.kp_max;  // layout rank (all items of this launch share it)
+  uint8_t* sB = smem;
+  uint8_t* sA = smem + 128 * KPL * 2;
+  uint8_t* sC = sA + KPL * BN * 2;
+  uint8_t* sS = sC + 2 * 128 * RS;
+  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sS + 2 * 128 * kScaleSlot);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+
+  if (tid == 0) {
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (tid < 32) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t taddr = tmem + (static_cast<uint32_t>(lane_warp * 32) << 16);
+
+  uint32_t gt = 0;  // tiles processed by this CTA (mbarrier phase)
+  bool ok = true;
+  for (int item = static_cast<int>(blockIdx.x); item < P.n_items && ok; item += static_cast<int>(gridDim.x)) {
+  // Locate this item's weight, 128-row strip and column range.
   int wi = 0;
-  while (wi + 1 < P.n_weights && P.w[wi + 1].item_begin <= static_cast<int>(blockIdx.x)) ++wi;
+  while (wi + 1 < P.n_weights && P.w[wi + 1].item_begin <= item) ++wi;
   const DevWeight& W = P.w[wi];
-  const int local = static_cast<int>(blockIdx.x) - W.item_begin;
+  const int local = item - W.item_begin;
   const int strip = local / W.col_items;
   const int ci = local - strip * W.col_items;
   const int row0 = W.row_begin + strip * 128;
   const int col_begin = ci * W.item_cols;
   const int col_end = min(W.N, col_begin + W.item_cols);
   const int n_tiles = (col_end - col_begin + BN - 1) / BN;
-
-  constexpr int RS = row_stride<FMT, BN>();
   const int KP = W.KP;
-  uint8_t* sB = smem;
-  uint8_t* sA = smem + 128 * KP * 2;
-  uint8_t* sC = sA + KP * BN * 2;
-  uint8_t* sS = sC + 2 * 128 * RS;
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sS + 2 * 128 * kScaleSlot);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
 
-  const int row = row0 + tid;
+  const int row = row0 + rt;
   const bool valid = row < W.M;
   const int rows_here = min(128, W.M - row0);
-
-  if (tid == 0) {
-    mbar_init(bar_mma, 1);
-    fence_mbar_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, BN);
-    tmem_relinquish();
-  }
 
   // ---- resident B strip (K-major canonical): chunk kc of row t at kc*2048 + (t/8)*128 + (t%8)*16.
   {
     const uint16_t* brow = W.b + static_cast<int64_t>(row) * W.r;
     const bool vec = ((reinterpret_cast<uintptr_t>(W.b) | (W.r * 2)) & 15) == 0;
-    for (int kc = 0; kc < KP / 8; ++kc) {
-      uint8_t* dst = sB + kc * 2048 + (tid >> 3) * 128 + (tid & 7) * 16;
+    for (int kc = wg; kc < KP / 8; kc += 2) {
+      uint8_t* dst = sB + kc * 2048 + (rt >> 3) * 128 + (rt & 7) * 16;
       if (valid && vec && kc * 8 + 8 <= W.r) {
         cp_async16(dst, brow + kc * 8);
       } else {
@@ -728,14 +850,14 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
       else if (g == 4) cp_async4(dst, src);
       else *dst = *src;
     }
-    // Per-row scale bytes of MX / NVFP4 tiles.
+    // Per-row scale bytes of MX / NVFP4 tiles (one warpgroup).
     if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 || FMT == PIPER_FMT_MXFP4 ||
                   FMT == PIPER_FMT_NVFP4) {
       constexpr int kBlk = FMT == PIPER_FMT_NVFP4 ? 16 : 32;
       const int b0 = c0 / kBlk;
       const int nb = (ncols + kBlk - 1) / kBlk;
-      uint8_t* dst = sS + stage * 128 * kScaleSlot + tid * kScaleSlot;
-      if (valid) {
+      uint8_t* dst = sS + stage * 128 * kScaleSlot + rt * kScaleSlot;
+      if (valid && wg == 0) {
         const uint8_t* scale8 = reinterpret_cast<const uint8_t*>(W.scale);
         const bool sw = (W.flags & PIPER_FLAG_SWIZZLED) != 0u;
         const bool vec4 = ((b0 | nb) & 3) == 0 && (sw || (W.scale_cols & 3) == 0) &&
@@ -800,13 +922,6 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     }
   };
 
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
-  (void)sr;
   // Per-thread running reductions for REDUCE passes.
   float red_max = 0.0f, red_nmin = 0.0f;
   int red_qp = -1;
@@ -825,7 +940,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     if (two_level) {
       if (PASS == kReduce) {
         g_in = *W.gscale;
-        if (blockIdx.x == static_cast<unsigned>(W.item_begin) && tid == 0) W.old_scale[0] = g_in;
+        if (local == 0 && tid == 0) W.old_scale[0] = g_in;
       } else {
         g_in = W.old_scale[0];
         const float amax = __uint_as_float(*W.qmax);
@@ -834,18 +949,17 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     }
   }
 
-  bool ok = true;
   if (n_tiles > 0) {
-    issue_codes(0, 0);
+    issue_codes(0, gt & 1);
     issue_a(0);
-    cp_async_commit();
   }
-  for (int tile = 0; tile < n_tiles; ++tile) {
-    const int stage = tile & 1;
+  cp_async_commit();
+  for (int tile = 0; tile < n_tiles; ++tile, ++gt) {
+    const int stage = gt & 1;
     const int c0 = col_begin + tile * BN;
     const int tcols = min(BN, col_end - c0);
 
-    // ---- tile `tile` (codes, scales, A) has landed in shared memory.
+    // ---- tile `tile` (codes, scales, A; B for the first tile) is in shared memory.
     cp_async_wait_all();
     fence_proxy_async_smem();
     __syncthreads();
@@ -867,7 +981,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     // ---- prefetch the next tile's codes and scales into the other stage.
     if (tile + 1 < n_tiles) issue_codes(tile + 1, stage ^ 1);
 
-    ok = mbar_wait(bar_mma, tile & 1, kStatusTimeoutMma);
+    ok = mbar_wait(bar_mma, gt & 1, kStatusTimeoutMma);
     // Keep the CTA uniform: tcgen05.ld below is warp-collective.
     ok = __syncthreads_and(ok) != 0;
     tc_fence_after();
@@ -880,86 +994,37 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     RowCtx c;
     c.row = row;
     c.valid = valid;
-    c.srow = sC + stage * 128 * RS + tid * RS;
-    c.sscale = sS + stage * 128 * kScaleSlot + tid * kScaleSlot;
+    c.srow = sC + stage * 128 * RS + rt * RS;
+    c.sscale = sS + stage * 128 * kScaleSlot + rt * kScaleSlot;
     c.blk0 = (FMT == PIPER_FMT_NVFP4) ? c0 / 16 : c0 / 32;
     c.tile_col0 = c0;
     c.tile_cols = tcols;
-    const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-
+    const int tid = rt;  // the epilogue below addresses rows by tile row
+    (void)tid;
     if (ok) {
       if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 ||
                     FMT == PIPER_FMT_MXFP4) {
-        for (int k = 0; k < tcols / 32; ++k) {
+        for (int k = wg; k < tcols / 32; k += 2) {
           float acc[32];
           tmem_ld32(taddr + 32 * k, acc);
           mx_chunk<FMT, CDT>(W, c, k, acc);
         }
       } else if constexpr (FMT == PIPER_FMT_NVFP4) {
-        for (int k = 0; k < tcols / 32; ++k) {
+        for (int k = wg; k < tcols / 32; k += 2) {
           float acc[32];
           tmem_ld32(taddr + 32 * k, acc);
           nvfp4_chunk<PASS, CDT>(W, c, k, acc, g_in, g_out, two_level, red_max);
         }
-        if (tcols & 31) {  // trailing 16-column block
+        if ((tcols & 31) && ((tcols / 32) & 1) == wg) {  // trailing 16-column block
           float acc[32];
           const int k = tcols / 32;
           tmem_ld32(taddr + 32 * k, acc);
-          // Process as a chunk whose second half is ignored: reuse the 32-wide
-          // routine on a copy with the second block neutralised.
-          // (N % 16 == 0 is validated on the host.)
-          const int col = c0 + 32 * k;
-          uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
-          const int blk = col >> 4;
-          const int64_t sidx = scale_index(W, row, blk);
-          float bsc = dec_e4m3(valid ? c.sscale[blk - c.blk0] : 0u);
-          if (CDT == kBF16) bsc = bf16r(bsc);
-          if (two_level) {
-            bsc = __fmul_rn(bsc, g_in);
-            if (CDT == kBF16) bsc = bf16r(bsc);
-          }
-          const uint2 pk = *reinterpret_cast<const uint2*>(c.srow + 16 * k);
-          const uint32_t wv[2] = {pk.x, pk.y};
-          float merged[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint32_t code = (wv[i >> 3] >> ((i & 7) * 4)) & 0xFu;
-            float base = __fmul_rn(dec_e2m1(code), bsc);
-            if (CDT == kBF16) base = bf16r(base);
-            const float upd = __fmul_rn(acc[i], W.strength);
-            merged[i] = round_dt<CDT>(upd == 0.0f ? base : fmaf(acc[i], W.strength, base));
-          }
-          float amax = fabsf(merged[0]);
-#pragma unroll
-          for (int i = 1; i < 16; ++i) amax = fmaxf(amax, fabsf(merged[i]));
-          if (PASS == kReduce) {
-            if (valid) red_max = fmaxf(red_max, amax);
-          } else {
-            float fs = __fdiv_rn(amax, 6.0f);
-            if (two_level) fs = div_full(fs, g_out);
-            fs = fminf(fmaxf(fs, 0.015625f), 448.0f);
-            const uint32_t fcode = enc_e4m3(fs);
-            fs = dec_e4m3(fcode);
-            if (valid) scale8[sidx] = static_cast<uint8_t>(fcode);
-            else if (W.flags & PIPER_FLAG_SWIZZLED) scale8[sidx] = 0u;
-            const float recip = two_level ? div_full(div_full(1.0f, g_out), fs) : 0.0f;
-            const uint64_t off0 =
-                W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + col;
-            const PhiloxKey key{W.k0, W.k1};
-            uint32_t out[2] = {0u, 0u};
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float n = two_level ? __fmul_rn(merged[i], recip) : div_full(merged[i], fs);
-              n = fminf(fmaxf(n, -6.0f), 6.0f);
-              uint32_t code = enc_e2m1(n);
-              if (W.flags & PIPER_FLAG_STOCHASTIC) code = sr_e2m1(n, code, key, off0 + i);
-              out[i >> 3] |= (code & 0xFu) << ((i & 7) * 4);
-            }
-            *reinterpret_cast<uint2*>(c.srow + 16 * k) = make_uint2(out[0], out[1]);
-          }
+          uint2 codes = *reinterpret_cast<const uint2*>(c.srow + 16 * k);
+          nvfp4_block<PASS, CDT>(W, c, c0 + 32 * k, acc, g_in, g_out, two_level, red_max, codes);
+          if (PASS != kReduce) *reinterpret_cast<uint2*>(c.srow + 16 * k) = codes;
         }
       } else if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
-        for (int k = 0; k < tcols / 32; ++k) {
+        for (int k = wg; k < tcols / 32; k += 2) {
           float acc[32];
           tmem_ld32(taddr + 32 * k, acc);
           gguf_chunk<FMT, CDT>(W, c, k, acc);
@@ -977,7 +1042,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
         if constexpr (PASS == kLocal) {
           // Groups of W.group (multiple of 32, dividing the tile width) are local.
           const int gch = W.group / 32;
-          for (int g0 = 0; g0 < nchunks; g0 += gch) {
+          for (int g0 = wg * gch; g0 < nchunks; g0 += 2 * gch) {
             float gmax = 0.0f, gmin = 0.0f, gabs = 0.0f;
             float scale_in[32];
             int zp_in[32];
@@ -1004,16 +1069,12 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
                 float acc[32], merged[32];
                 tmem_ld32(taddr + 32 * k, acc);
                 affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
-                uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+                uint32_t out[8];
                 const uint64_t off0 = W.offset_base +
                                       static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) +
                                       c0 + 32 * k;
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  out[i >> 2] |= int8_encode(merged[i], q, qmin, qmax, W.scale_dt,
-                                             (W.flags & PIPER_FLAG_STOCHASTIC) != 0u, key,
-                                             off0 + i)
-                                 << ((i & 3) * 8);
+                int8_encode32(merged, q, qmin, qmax, W.scale_dt, (W.flags & PIPER_FLAG_STOCHASTIC) != 0u,
+                              key, off0, out);
                 store_bytes32(c.srow + 32 * k, out);
               }
             } else {
@@ -1027,20 +1088,21 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
                 const uint64_t off0 = W.offset_base +
                                       static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) +
                                       c0 + 32 * k;
+                if (W.flags & PIPER_FLAG_STOCHASTIC) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                  const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
-                  const uint32_t code = (W.flags & PIPER_FLAG_STOCHASTIC)
-                                            ? sr_fp8<kE4>(x, kLimit, key, off0 + i)
-                                            : enc_fp8<kE4>(x);
-                  out[i >> 2] |= code << ((i & 3) * 8);
+                  for (int i = 0; i < 32; ++i) {
+                    const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
+                    out[i >> 2] |= sr_fp8<kE4>(x, kLimit, key, off0 + i) << ((i & 3) * 8);
+                  }
+                } else {
+                  fp8_encode_rtn<kE4>(merged, s, kLimit, out);
                 }
                 store_bytes32(c.srow + 32 * k, out);
               }
             }
           }
         } else {
-          for (int k = 0; k < nchunks; ++k) {
+          for (int k = wg; k < nchunks; k += 2) {
             float acc[32], merged[32], scale_in[32];
             int zp_in[32];
             tmem_ld32(taddr + 32 * k, acc);
@@ -1121,17 +1183,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
                     store_scale_dt(W.scale, qp, W.scale_dt, q.scale);
                     if (W.zp != nullptr) W.zp[qp] = static_cast<int8_t>(q.zp);
                   }
-                  if (sr_on) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                      out[i >> 2] |= int8_encode(merged[i], q, qmin, qmax, W.scale_dt, true, key, off0 + i)
-                                     << ((i & 3) * 8);
-                  } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                      out[i >> 2] |= int8_encode(merged[i], q, qmin, qmax, W.scale_dt, false, key, off0 + i)
-                                     << ((i & 3) * 8);
-                  }
+                  int8_encode32(merged, q, qmin, qmax, W.scale_dt, sr_on, key, off0, out);
                 } else {
                   const float s = fp8_new_scale<CDT>(qmx, kLimit);
                   if (owner) reinterpret_cast<float*>(W.scale)[qp] = s;
@@ -1142,11 +1194,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
                       out[i >> 2] |= sr_fp8<kE4>(x, kLimit, key, off0 + i) << ((i & 3) * 8);
                     }
                   } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                      const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
-                      out[i >> 2] |= enc_fp8<kE4>(x) << ((i & 3) * 8);
-                    }
+                    fp8_encode_rtn<kE4>(merged, s, kLimit, out);
                   }
                 }
               } else if (valid) {
@@ -1205,18 +1253,17 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     tc_fence_before();
     __syncthreads();
   }
-  cp_async_wait_all();
 
-  // ---- REDUCE epilogue: publish running maxima.
+  // ---- REDUCE: publish this item's running maxima.
   if constexpr (PASS == kReduce) {
     if constexpr (FMT == PIPER_FMT_NVFP4) {
       const float m = warp_max(red_max);
-      if ((tid & 31) == 0) atomic_max_nonneg(W.qmax, m);
+      if ((threadIdx.x & 31) == 0) atomic_max_nonneg(W.qmax, m);
     } else {
       if (W.nq_row == 0) {
         const float m = warp_max(red_max);
         const float n = warp_max(red_nmin);
-        if ((tid & 31) == 0) {
+        if ((threadIdx.x & 31) == 0) {
           atomic_max_nonneg(&W.qmax[0], m);
           if (FMT == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[0], n);
         }
@@ -1228,17 +1275,19 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
 
   // ---- NVFP4: zero swizzle padding columns and publish the new global scale.
   if constexpr (FMT == PIPER_FMT_NVFP4 && PASS == kLocal) {
-    if ((W.flags & PIPER_FLAG_SWIZZLED) && col_end == W.N) {
+    if ((W.flags & PIPER_FLAG_SWIZZLED) && col_end == W.N && wg == 0) {
       const int padded = align_up(W.scale_cols, 4);
       uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
       for (int pc = W.scale_cols; pc < padded; ++pc) scale8[swizzled_index(row, pc, W.scale_cols)] = 0u;
     }
-    if (two_level && blockIdx.x == static_cast<unsigned>(W.item_begin) && tid == 0) *W.gscale = g_out;
+    if (two_level && local == 0 && threadIdx.x == 0) *W.gscale = g_out;
   }
+  }  // item loop
+  cp_async_wait_all();
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (threadIdx.x < 32) {
     tc_fence_after();
     tmem_dealloc(tmem, BN);
   }
@@ -1401,7 +1450,28 @@ int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess)
     return fail(PIPER_MERGE_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-  kern<<<items, pm::kThreads, smem, stream>>>(lp);
+  lp.n_items = items;
+  lp.kp_max = kp_max;
+  // Resident CTAs per SM from registers and shared memory (tensor-memory
+  // columns are bounded by the shared-memory request above). The carveout is
+  // set to maximum shared memory so that several CTAs fit per SM.
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  int occ = 1;
+  {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess && fa.numRegs > 0) {
+      const int regs_per_warp = ((fa.numRegs * 32 + 255) / 256) * 256;
+      const int by_regs = 65536 / (regs_per_warp * (pm::kThreads / 32));
+      const int by_smem = kSmemPerSm / (smem + kSmemReservedPerCta);
+      occ = std::max(1, std::min(by_regs, by_smem));
+    }
+    cudaGetLastError();
+  }
+  const int grid = std::min(items, occ * sm_count());
+  if (std::getenv("PIPER_MERGE_DEBUG") != nullptr)
+    std::fprintf(stderr, "[piper-merge] fmt=%d pass=%d bn=%d smem=%d occ=%d items=%d grid=%d\n", FMT, PASS, BN,
+                 smem, occ, items, grid);
+  kern<<<grid, pm::kThreads, smem, stream>>>(lp);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
@@ -1514,21 +1584,26 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
   LaunchParams lp;
   std::memset(&lp, 0, sizeof(lp));
   lp.n_weights = static_cast<int>(segs.size());
-  int strips = 0, kp_max = 16;
-  for (const Segment& s : segs) strips += (s.rows + 127) / 128;
-  const int target = 4 * sm_count();
+  // Work items: (128-row strip, column range) pairs. Persistent CTAs stride
+  // over them; aim for ~12 items per SM so the last wave is short.
+  int kp_max = 16;
+  int64_t total_tiles = 0;
+  for (const Segment& sg : segs) {
+    const Plan& p = plans[sg.desc];
+    total_tiles += static_cast<int64_t>((sg.rows + 127) / 128) * ((descs[sg.desc].cols + p.bn - 1) / p.bn);
+  }
+  const int64_t target_items = 12ll * sm_count();
+  const int tiles_per_item = static_cast<int>(std::max<int64_t>(1, total_tiles / target_items));
   int items = 0;
   for (size_t i = 0; i < segs.size(); ++i) {
     const piper_merge_desc& d = descs[segs[i].desc];
     const Plan& p = plans[segs[i].desc];
     DevWeight w = make_dev_weight(d, p, ws, segs[i]);
-    const int max_items = static_cast<int>((d.cols + p.bn - 1) / p.bn);
-    int ci = (target + strips - 1) / strips;
-    ci = std::max(1, std::min(ci, max_items));
-    int item_cols = static_cast<int>((d.cols + ci - 1) / ci);
-    item_cols = (item_cols + p.bn - 1) / p.bn * p.bn;
-    w.item_cols = item_cols;
-    w.col_items = static_cast<int>((d.cols + item_cols - 1) / item_cols);
+    const int col_tiles = static_cast<int>((d.cols + p.bn - 1) / p.bn);
+    const int ci = std::max(1, (col_tiles + tiles_per_item - 1) / tiles_per_item);
+    const int tiles_each = (col_tiles + ci - 1) / ci;
+    w.item_cols = tiles_each * p.bn;
+    w.col_items = (col_tiles + tiles_each - 1) / tiles_each;
     w.item_begin = items;
     items += w.row_blocks * w.col_items;
     kp_max = std::max(kp_max, w.KP);

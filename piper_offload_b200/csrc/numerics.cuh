@@ -193,3 +193,108 @@ __device__ __forceinline__ float sr_int(float v, float det, float qmin, float qm
 }
 
 }  // namespace pm
+
+namespace pm {
+// ------------------------------------------------------ packed conversions
+// Two fp32 values rounded to bf16 (RTNE) and widened back; one packed cvt.
+__device__ __forceinline__ void bf16r2(float& a, float& b) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
+  a = __uint_as_float(d << 16);
+  b = __uint_as_float(d & 0xFFFF0000u);
+}
+__device__ __forceinline__ void f16r2(float& a, float& b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 f = __half22float2(h);
+  a = f.x;
+  b = f.y;
+}
+template <int DT>
+__device__ __forceinline__ void round_dt2(float& a, float& b) {
+  if constexpr (DT == kBF16) bf16r2(a, b);
+  else if constexpr (DT == kF16) f16r2(a, b);
+}
+
+// Four FP8 codes (little-endian bytes of w) to fp32, two per cvt.
+template <bool E4M3>
+__device__ __forceinline__ void dec_fp8x4(uint32_t w, float (&f)[4]) {
+  uint32_t lo, hi;
+  if constexpr (E4M3) {
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(lo) : "h"(static_cast<uint16_t>(w & 0xFFFFu)));
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(hi) : "h"(static_cast<uint16_t>(w >> 16)));
+  } else {
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(lo) : "h"(static_cast<uint16_t>(w & 0xFFFFu)));
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(hi) : "h"(static_cast<uint16_t>(w >> 16)));
+  }
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+  f[0] = a.x;
+  f[1] = a.y;
+  f[2] = b.x;
+  f[3] = b.y;
+}
+
+// Four fp32 values to FP8 codes (RTNE, satfinite), packed little-endian.
+template <bool E4M3>
+__device__ __forceinline__ uint32_t enc_fp8x4(float a, float b, float c, float d) {
+  uint16_t lo, hi;
+  if constexpr (E4M3) {
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
+  } else {
+    asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
+    asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
+  }
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// Two E2M1 codes (low nibble first) of one byte to fp32.
+__device__ __forceinline__ void dec_e2m1x2(uint32_t byte, float& a, float& b) {
+  uint32_t h;
+  asm("{\n\t.reg .b8 t0, t1;\n\tmov.b16 {t0, t1}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t0;\n\t}"
+      : "=r"(h)
+      : "h"(static_cast<uint16_t>(byte & 0xFFu)));
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+  a = f.x;
+  b = f.y;
+}
+
+// Two fp32 values to one byte of E2M1 codes (RTNE, satfinite; first value in the low nibble).
+__device__ __forceinline__ uint32_t enc_e2m1x2(float lo, float hi) {
+  uint16_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tmov.b16 %0, {t, 0};\n\t}"
+      : "=h"(r)
+      : "f"(hi), "f"(lo));
+  return r & 0xFFu;
+}
+
+// ------------------------------------------- quotients near rounding edges
+// The reference divides with `div.full.f32`, whose result is within 2 ulp of
+// the exact quotient. A quotient computed as x * RN(1/s) is within 1.5 ulp.
+// When that approximation is farther than 4 ulp from every rounding boundary
+// of the target format, both quotients round to the same code; otherwise the
+// caller recomputes with div.full.f32 itself.
+
+// FP8 boundary test: midpoints have the bits below the kept mantissa equal to
+// exactly half; values in the subnormal range are always re-checked.
+template <bool E4M3>
+__device__ __forceinline__ bool near_fp8_edge(float q) {
+  const uint32_t a = __float_as_uint(q) & 0x7FFFFFFFu;
+  constexpr uint32_t kMinNormal = E4M3 ? 0x3C800000u : 0x38800000u;  // 2^-6 / 2^-14
+  constexpr int kDrop = E4M3 ? 20 : 21;
+  constexpr uint32_t kMask = (1u << kDrop) - 1u;
+  constexpr uint32_t kHalf = 1u << (kDrop - 1);
+  const uint32_t low = a & kMask;
+  const uint32_t dist = low > kHalf ? low - kHalf : kHalf - low;
+  return a < kMinNormal || dist <= 4u;
+}
+
+// E2M1 boundary test (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5): within 4 ulp of a
+// value whose mantissa is a multiple of 2^21 in binades 2^-3 .. 2^2.
+__device__ __forceinline__ bool near_e2m1_edge(float q) {
+  const uint32_t a = __float_as_uint(q) & 0x7FFFFFFFu;
+  const int e = static_cast<int>(a >> 23) - 127;
+  const uint32_t low = a & 0x1FFFFFu;
+  return e >= -3 && e <= 2 && (low <= 4u || low >= 0x200000u - 4u);
+}
+}  // namespace pm
