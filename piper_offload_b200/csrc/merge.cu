@@ -29,7 +29,9 @@
 //   src/piper_offload/_triton_int8_lora.py:24-236     (affine INT8)
 //   src/piper_offload/_triton_stochastic_quantization.py (SR helpers)
 //   src/piper_offload/gguf_dequant.py:57-115 + gguf quants (GGUF Q8_0 / Q4_0)
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <atomic>
@@ -52,7 +54,8 @@ constexpr int kMaxRank = 256;
 enum Pass : int { kLocal = 0, kReduce = 1, kEncode = 2 };
 
 // Device-side descriptor of one weight (or a row range of one weight).
-struct DevWeight {
+struct alignas(64) DevWeight {
+  CUtensorMap tmap;    // 2-D map of the code bytes (rows x row_bytes), valid when use_tma
   uint8_t* q;
   void* scale;
   int8_t* zp;
@@ -79,6 +82,8 @@ struct DevWeight {
   int scale_cols;      // MX: N/32, NVFP4: N/16
   int scale_mode;      // MX E8M0 rounding
   int scale_dt;        // INT8 scale dtype
+  int use_tma;         // code tiles move by bulk tensor copies (swizzled rows)
+  int swz;             // smem row swizzle of TMA tiles: 2 = 128 B, 1 = 64 B
 };
 
 struct LaunchParams {
@@ -111,9 +116,19 @@ __host__ __device__ constexpr int row_stride() {
 // (16 bytes per row), then the mbarrier and the tensor-memory address slot.
 constexpr int kScaleSlot = 16;
 
+constexpr int kStages = 3;
+
+template <int FMT, int BN>
+__host__ __device__ constexpr int stage_bytes() {
+  return align_up(128 * row_stride<FMT, BN>(), 1024);
+}
+
+// Code stages first (1024-byte aligned for swizzled TMA tiles), then the B
+// strip, the A tile, per-row scale stages, barriers and the TMEM slot; plus
+// 1 KB of slack to align the dynamic shared-memory base.
 template <int FMT, int BN>
 __host__ __device__ constexpr int smem_bytes(int kp) {
-  return 128 * kp * 2 + kp * BN * 2 + 2 * 128 * row_stride<FMT, BN>() + 2 * 128 * kScaleSlot + 64;
+  return 1024 + kStages * stage_bytes<FMT, BN>() + 128 * kp * 2 + kp * BN * 2 + kStages * 128 * kScaleSlot + 64;
 }
 
 // Blocked 128x4 scale layout (_triton_mx_lora.py:97-112, _triton_nvfp4_lora.py:88-104).
@@ -235,12 +250,26 @@ struct RowCtx {
   int row;               // global row
   bool valid;            // row < M
   uint8_t* srow;         // this row's code segment in shared memory
+  uint32_t swz;          // XOR applied to 16-byte chunk indices (swizzled TMA rows)
   const uint8_t* sscale; // this row's prefetched scale bytes for the tile (MX / NVFP4)
   int blk0;              // scale block index of sscale[0]
   int tile_col0;         // first column of the tile
   int tile_cols;         // valid columns in the tile
 };
 
+__device__ __forceinline__ uint8_t* chunk_ptr(const RowCtx& c, int c16) {
+  return c.srow + ((static_cast<uint32_t>(c16) ^ c.swz) << 4);
+}
+__device__ __forceinline__ void load_chunks32(const RowCtx& c, int k, uint32_t (&w)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(chunk_ptr(c, 2 * k));
+  const uint4 b = *reinterpret_cast<const uint4*>(chunk_ptr(c, 2 * k + 1));
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+__device__ __forceinline__ void store_chunks32(const RowCtx& c, int k, const uint32_t (&w)[8]) {
+  *reinterpret_cast<uint4*>(chunk_ptr(c, 2 * k)) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(chunk_ptr(c, 2 * k + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+}
 __device__ __forceinline__ void load_bytes32(const uint8_t* s, uint32_t (&w)[8]) {
   const uint4 a = *reinterpret_cast<const uint4*>(s);
   const uint4 b = *reinterpret_cast<const uint4*>(s + 16);
@@ -269,13 +298,13 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
   // reference's bf16 cast of the element is the identity.
   float merged[32];
   if constexpr (FMT == PIPER_FMT_MXFP4) {
-    const uint4 pk = *reinterpret_cast<const uint4*>(c.srow + 16 * k);
+    const uint4 pk = *reinterpret_cast<const uint4*>(chunk_ptr(c, k));
     const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
 #pragma unroll
     for (int j = 0; j < 16; ++j) dec_e2m1x2(wv[j >> 2] >> ((j & 3) * 8), merged[2 * j], merged[2 * j + 1]);
   } else {
     uint32_t wv[8];
-    load_bytes32(c.srow + 32 * k, wv);
+    load_chunks32(c, k, wv);
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       float f[4];
@@ -318,7 +347,7 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
 #pragma unroll
       for (int j = 0; j < 16; ++j) out[j >> 2] |= enc_e2m1x2(merged[2 * j], merged[2 * j + 1]) << ((j & 3) * 8);
     }
-    *reinterpret_cast<uint4*>(c.srow + 16 * k) = make_uint4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<uint4*>(chunk_ptr(c, k)) = make_uint4(out[0], out[1], out[2], out[3]);
   } else {
     constexpr bool kE4 = FMT == PIPER_FMT_MXFP8_E4M3;
     uint32_t out[8];
@@ -332,7 +361,7 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
       for (int w = 0; w < 8; ++w)
         out[w] = enc_fp8x4<kE4>(merged[4 * w], merged[4 * w + 1], merged[4 * w + 2], merged[4 * w + 3]);
     }
-    store_bytes32(c.srow + 32 * k, out);
+    store_chunks32(c, k, out);
   }
   if (c.valid) scale8[scale_index(W, c.row, blk)] = static_cast<uint8_t>(s.code);
 }
@@ -432,12 +461,12 @@ __device__ __forceinline__ void nvfp4_chunk(const DevWeight& W, const RowCtx& c,
                                             const float (&acc)[32], float g_in, float g_out,
                                             bool two_level, float& amax_acc) {
   const int col = c.tile_col0 + 32 * k;
-  uint4 pk = *reinterpret_cast<const uint4*>(c.srow + 16 * k);
+  uint4 pk = *reinterpret_cast<const uint4*>(chunk_ptr(c, k));
   uint2 lo = make_uint2(pk.x, pk.y), hi = make_uint2(pk.z, pk.w);
   nvfp4_block<PASS, CDT>(W, c, col, acc, g_in, g_out, two_level, amax_acc, lo);
   nvfp4_block<PASS, CDT>(W, c, col + 16, acc + 16, g_in, g_out, two_level, amax_acc, hi);
   if constexpr (PASS != kReduce)
-    *reinterpret_cast<uint4*>(c.srow + 16 * k) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+    *reinterpret_cast<uint4*>(chunk_ptr(c, k)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
 }
 
 // ========================================================= FP8 / INT8 helpers
@@ -553,7 +582,7 @@ __device__ __forceinline__ void affine_merged(const DevWeight& W, const RowCtx& 
                                               const float (&acc)[32], const float* scale_in,
                                               const int* zp_in, float (&merged)[32]) {
   uint32_t wv[8];
-  load_bytes32(c.srow + 32 * k, wv);
+  load_chunks32(c, k, wv);
   if constexpr (FMT == PIPER_FMT_INT8) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -750,18 +779,25 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
   const int lane_warp = (tid >> 5) & 3;
 
   constexpr int RS = row_stride<FMT, BN>();
+  constexpr int kStageB = stage_bytes<FMT, BN>();
+  constexpr int kTileRowBytes = code_bytes<FMT>(BN);  // dense (TMA) row of a tile
   const int KPL = P.kp_max;  // layout rank (all items of this launch share it)
-  uint8_t* sB = smem;
-  uint8_t* sA = smem + 128 * KPL * 2;
-  uint8_t* sC = sA + KPL * BN * 2;
-  uint8_t* sS = sC + 2 * 128 * RS;
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sS + 2 * 128 * kScaleSlot);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  uint8_t* base1k = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);
+  uint8_t* sC = base1k;  // kStages code stages
+  uint8_t* sB = sC + kStages * kStageB;
+  uint8_t* sA = sB + 128 * KPL * 2;
+  uint8_t* sS = sA + KPL * BN * 2;
+  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sS + kStages * 128 * kScaleSlot);
+  uint64_t* bar_full = bar_mma + 1;  // [kStages] TMA code tiles landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_full + kStages);
 
   if (tid == 0) {
     mbar_init(bar_mma, 1);
+    for (int i = 0; i < kStages; ++i) mbar_init(&bar_full[i], 1);
     fence_mbar_init();
   }
+  uint32_t full_uses[kStages] = {0u, 0u, 0u};    // consumed phases per stage (thread-uniform)
+  uint32_t full_issued[kStages] = {0u, 0u, 0u};  // loads issued per stage (thread 0)
   if (tid < 32) {
     tmem_alloc(tmem_slot, BN);
     tmem_relinquish();
@@ -839,7 +875,7 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
     const int g = granularity(off, nbytes);
     const int per = nbytes / g;
     const int total = rows_here * per;
-    uint8_t* base = sC + stage * 128 * RS;
+    uint8_t* base = sC + stage * kStageB;
     const uint8_t* src0 = W.q + static_cast<int64_t>(row0) * W.row_bytes + off;
     for (int k = tid; k < total; k += kThreads) {
       const int r = k / per;
@@ -850,13 +886,26 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
       else if (g == 4) cp_async4(dst, src);
       else *dst = *src;
     }
-    // Per-row scale bytes of MX / NVFP4 tiles (one warpgroup).
+  };
+
+  // TMA code tile: one thread, completion on bar_full[stage].
+  auto issue_codes_tma = [&](int tile, int stage) {
+    const int c0 = col_begin + tile * BN;
+    ++full_issued[stage];
+    mbar_arrive_expect_tx(&bar_full[stage], 128u * kTileRowBytes);
+    tma_load_2d(sC + stage * kStageB, &W.tmap, static_cast<int>(tile_off(c0)), row0, &bar_full[stage]);
+  };
+
+  // Per-row scale bytes of MX / NVFP4 tiles (one warpgroup, cp.async).
+  auto issue_scales = [&](int tile, int stage) {
+    const int c0 = col_begin + tile * BN;
+    const int ncols = min(BN, col_end - c0);
     if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 || FMT == PIPER_FMT_MXFP4 ||
                   FMT == PIPER_FMT_NVFP4) {
       constexpr int kBlk = FMT == PIPER_FMT_NVFP4 ? 16 : 32;
       const int b0 = c0 / kBlk;
       const int nb = (ncols + kBlk - 1) / kBlk;
-      uint8_t* dst = sS + stage * 128 * kScaleSlot + rt * kScaleSlot;
+      uint8_t* dst = sS + stage * 128 * kScaleSlot + rt * kScaleSlot;  // stage of the scale ring
       if (valid && wg == 0) {
         const uint8_t* scale8 = reinterpret_cast<const uint8_t*>(W.scale);
         const bool sw = (W.flags & PIPER_FLAG_SWIZZLED) != 0u;
@@ -909,7 +958,7 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
     const int g = granularity(off, nbytes);
     const int per = nbytes / g;
     const int total = rows_here * per;
-    const uint8_t* base = sC + stage * 128 * RS;
+    const uint8_t* base = sC + stage * kStageB;
     uint8_t* dst0 = W.q + static_cast<int64_t>(row0) * W.row_bytes + off;
     for (int k = tid; k < total; k += kThreads) {
       const int r = k / per;
@@ -949,20 +998,37 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
     }
   }
 
+  const bool tma = W.use_tma != 0;
+  // Prologue: codes of the first tiles (TMA keeps two in flight), scales and
+  // A of the first tile (cp.async, with the B strip above).
   if (n_tiles > 0) {
-    issue_codes(0, gt & 1);
+    if (tma) {
+      if (tid == 0) {
+        bulk_wait_read_all();  // earlier stores have finished reading their stages
+        issue_codes_tma(0, gt % kStages);
+        if (n_tiles > 1) issue_codes_tma(1, (gt + 1) % kStages);
+      }
+    } else {
+      issue_codes(0, gt % kStages);
+    }
+    issue_scales(0, gt % kStages);
     issue_a(0);
   }
   cp_async_commit();
   for (int tile = 0; tile < n_tiles; ++tile, ++gt) {
-    const int stage = gt & 1;
+    const int stage = gt % kStages;
     const int c0 = col_begin + tile * BN;
     const int tcols = min(BN, col_end - c0);
 
     // ---- tile `tile` (codes, scales, A; B for the first tile) is in shared memory.
     cp_async_wait_all();
+    if (tma) {
+      ok = mbar_wait(&bar_full[stage], full_uses[stage] & 1u, kStatusTimeoutLoad);
+      ++full_uses[stage];
+    }
     fence_proxy_async_smem();
-    __syncthreads();
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
 
     // ---- issue the update on the tensor core.
     if (tid == 0) {
@@ -978,8 +1044,16 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
       umma_commit(bar_mma);
     }
 
-    // ---- prefetch the next tile's codes and scales into the other stage.
-    if (tile + 1 < n_tiles) issue_codes(tile + 1, stage ^ 1);
+    // ---- prefetch code tiles: TMA two ahead (after the store that last used
+    //      that stage has read it), cp.async one ahead.
+    if (tma) {
+      if (tid == 0 && tile + 2 < n_tiles) {
+        bulk_wait_read_all();
+        issue_codes_tma(tile + 2, (gt + 2) % kStages);
+      }
+    } else if (tile + 1 < n_tiles) {
+      issue_codes(tile + 1, (gt + 1) % kStages);
+    }
 
     ok = mbar_wait(bar_mma, gt & 1, kStatusTimeoutMma);
     // Keep the CTA uniform: tcgen05.ld below is warp-collective.
@@ -987,14 +1061,23 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
     tc_fence_after();
     if (!ok) break;
 
-    // The MMA has consumed the A tile: fetch the next one behind the epilogue.
-    if (tile + 1 < n_tiles) issue_a(tile + 1);
+    // The MMA has consumed the A tile: fetch the next one (and its scales) behind the epilogue.
+    if (tile + 1 < n_tiles) {
+      issue_a(tile + 1);
+      issue_scales(tile + 1, (gt + 1) % kStages);
+    }
     cp_async_commit();
 
     RowCtx c;
     c.row = row;
     c.valid = valid;
-    c.srow = sC + stage * 128 * RS + rt * RS;
+    if (tma) {
+      c.srow = sC + stage * kStageB + rt * kTileRowBytes;
+      c.swz = W.swz == 2 ? static_cast<uint32_t>(rt & 7) : static_cast<uint32_t>((rt >> 1) & 3);
+    } else {
+      c.srow = sC + stage * kStageB + rt * RS;
+      c.swz = 0u;
+    }
     c.sscale = sS + stage * 128 * kScaleSlot + rt * kScaleSlot;
     c.blk0 = (FMT == PIPER_FMT_NVFP4) ? c0 / 16 : c0 / 32;
     c.tile_col0 = c0;
@@ -1019,9 +1102,9 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
           float acc[32];
           const int k = tcols / 32;
           tmem_ld32(taddr + 32 * k, acc);
-          uint2 codes = *reinterpret_cast<const uint2*>(c.srow + 16 * k);
+          uint2 codes = *reinterpret_cast<const uint2*>(chunk_ptr(c, k));
           nvfp4_block<PASS, CDT>(W, c, c0 + 32 * k, acc, g_in, g_out, two_level, red_max, codes);
-          if (PASS != kReduce) *reinterpret_cast<uint2*>(c.srow + 16 * k) = codes;
+          if (PASS != kReduce) *reinterpret_cast<uint2*>(chunk_ptr(c, k)) = codes;
         }
       } else if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
         for (int k = wg; k < tcols / 32; k += 2) {
@@ -1075,7 +1158,7 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
                                       c0 + 32 * k;
                 int8_encode32(merged, q, qmin, qmax, W.scale_dt, (W.flags & PIPER_FLAG_STOCHASTIC) != 0u,
                               key, off0, out);
-                store_bytes32(c.srow + 32 * k, out);
+                store_chunks32(c, k, out);
               }
             } else {
               const float s = fp8_new_scale<CDT>(gabs, kLimit);
@@ -1097,7 +1180,7 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
                 } else {
                   fp8_encode_rtn<kE4>(merged, s, kLimit, out);
                 }
-                store_bytes32(c.srow + 32 * k, out);
+                store_chunks32(c, k, out);
               }
             }
           }
@@ -1238,17 +1321,26 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
                   out[i >> 2] |= code << ((i & 3) * 8);
                 }
               }
-              store_bytes32(c.srow + 32 * k, out);
+              store_chunks32(c, k, out);
             }
           }
         }
       }
     }
 
-    // ---- write the tile back (in place), coalesced.
+    // ---- write the tile back (in place): one TMA store, or coalesced stores.
     if (PASS != kReduce) {
-      __syncthreads();
-      store_codes(tile, stage);
+      if (tma) {
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+          tma_store_2d(&W.tmap, static_cast<int>(tile_off(c0)), row0, sC + stage * kStageB);
+          bulk_commit();
+        }
+      } else {
+        __syncthreads();
+        store_codes(tile, stage);
+      }
     }
     tc_fence_before();
     __syncthreads();
@@ -1284,6 +1376,16 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
   }
   }  // item loop
   cp_async_wait_all();
+  if (tid == 0) {
+    // Loads issued but never consumed (only after a timed-out wait): give them
+    // a bounded chance to land before shared memory is released.
+    for (int st = 0; st < kStages; ++st)
+      while (full_issued[st] > full_uses[st]) {
+        mbar_wait(&bar_full[st], full_uses[st] & 1u, kStatusTimeoutLoad);
+        ++full_uses[st];
+      }
+    bulk_wait_all();  // TMA stores complete before the CTA exits
+  }
 
   tc_fence_before();
   __syncthreads();
@@ -1539,6 +1641,48 @@ struct Segment {
   int row_begin, rows;
 };
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    cudaGetLastError();
+  }
+  return fn;
+}
+
+int64_t row_bytes_of(const piper_merge_desc& d);
+
+// Code tiles of `bn` columns move by 2-D bulk tensor copies when a row of the
+// tile is 64 or 128 bytes (so the 64 B / 128 B swizzle spans it) and rows are
+// 16-byte aligned; otherwise by cp.async.
+void setup_tma(DevWeight& w, const piper_merge_desc& d, int bn) {
+  w.use_tma = 0;
+  if (d.format == PIPER_FMT_GGUF_Q8_0 || d.format == PIPER_FMT_GGUF_Q4_0) return;
+  const int tile_row = (d.format == PIPER_FMT_MXFP4 || d.format == PIPER_FMT_NVFP4) ? bn / 2 : bn;
+  if (tile_row != 64 && tile_row != 128) return;
+  const int64_t rb = row_bytes_of(d);
+  if ((rb & 15) != 0 || (reinterpret_cast<uintptr_t>(d.qdata) & 15) != 0) return;
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rb), static_cast<cuuint64_t>(d.rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(rb)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(tile_row), 128u};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUtensorMapSwizzle sw = tile_row == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = enc(&w.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, d.qdata, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return;
+  w.use_tma = 1;
+  w.swz = tile_row == 128 ? 2 : 1;
+}
+
 DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws, const Segment& seg) {
   DevWeight w;
   std::memset(&w, 0, sizeof(w));
@@ -1572,6 +1716,7 @@ DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws,
   w.scale_cols = d.format == PIPER_FMT_NVFP4 ? static_cast<int>(d.cols / 16) : static_cast<int>(d.cols / 32);
   w.scale_mode = d.scale_mode;
   w.scale_dt = d.scale_dtype;
+  if (std::getenv("PIPER_MERGE_NO_TMA") == nullptr) setup_tma(w, d, p.bn);
   return w;
 }
 
