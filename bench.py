@@ -61,8 +61,9 @@ ROW_SCALE_BYTES = {"fp8": 8, "int8": 4}  # fp32 / bf16 row scale read + written
 FALLBACK_HBM_GBS = 6650.0
 
 
-def weight_list(cfg: str, model_copies: int = 1):
-    layers, n_layers, *_ = CONFIGS[cfg]
+def weight_list(cfg: str, model_copies: int = 1, n_layers: int | None = None):
+    layers, cfg_layers, *_ = CONFIGS[cfg]
+    n_layers = cfg_layers if n_layers is None else n_layers
     out = []
     for copy in range(model_copies):
         for i in range(n_layers):
@@ -143,16 +144,16 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- workload
-def build_weights(cfg: str, device, seed_base: int):
+def build_weights(cfg: str, device, seed_base: int, n_layers: int | None = None):
     """Quantized weights + factors on `device` (torch ops, seeded per weight)."""
     import torch
 
     from piper_offload_b200 import synthetic as S
     from piper_offload_b200 import weights as WT
 
-    layers, n_layers, rank, lora_std, base_std, _, _ = CONFIGS[cfg]
+    _, _, rank, lora_std, base_std, _, _ = CONFIGS[cfg]
     items = []
-    for k, (key, rows, cols) in enumerate(weight_list(cfg)):
+    for k, (key, rows, cols) in enumerate(weight_list(cfg, n_layers=n_layers)):
         s = seed_base + 7919 * k
         w = S.normal((rows, cols), base_std, seed=s, device=device,
                      outlier_frac=0.001 if cfg.startswith("mx") else 0.0)
@@ -261,6 +262,10 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=None,
+                    help="override the layer count (small profiling case; the headline uses the config's)")
+    ap.add_argument("--kernel-reps", type=int, default=5,
+                    help="timed repetitions of the dominant-weight roofline leg")
     args = ap.parse_args()
     warmup = max(3, args.warmup)
 
@@ -316,7 +321,7 @@ def main() -> int:
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(cfg, steps=1, warmup=1)
 
-    items = build_weights(cfg, device, seed_base=1000 * rank)
+    items = build_weights(cfg, device, seed_base=1000 * rank, n_layers=args.layers)
     total_bytes = sum(algorithmic_bytes(cfg, r, c) for _, r, c, *_ in items)
 
     # Device-resident path: descriptors built once through the adapters, then
@@ -368,17 +373,49 @@ def main() -> int:
     clocks = clk.summary()
     status = _native.device_status(device)
 
+    # Roofline leg: the dominant weight shape (largest algorithmic bytes) merged
+    # on its own, CUDA events on the launching stream around `kernel_reps`
+    # calls; per launch = the call's bytes and time divided by its launches.
+    dom = max(range(len(items)), key=lambda i: algorithmic_bytes(cfg, items[i][1], items[i][2]))
+    dom_arr = (_native.MergeDesc * 1)(arr[dom])
+    dom_bytes = algorithmic_bytes(cfg, items[dom][1], items[dom][2])
+
+    def run_dom(s: int) -> None:
+        if seeds is not None:
+            dom_arr[0].seed = seeds[s][dom]
+        _native.check(lib.piper_merge_batch(dom_arr, 1, ws_ptr, ws_len, stream.cuda_stream))
+
+    for i in range(3):
+        run_dom(i)
+    torch.cuda.synchronize(device)
+    l0 = _native.launches()
+    k_start = torch.cuda.Event(enable_timing=True)
+    k_end = torch.cuda.Event(enable_timing=True)
+    k_start.record(stream)
+    for i in range(args.kernel_reps):
+        run_dom(3 + i)
+    k_end.record(stream)
+    torch.cuda.synchronize(device)
+    dom_launches = (_native.launches() - l0) / args.kernel_reps
+    dom_ms = k_start.elapsed_time(k_end) / args.kernel_reps
+    launch_ms = dom_ms / dom_launches
+    launch_bytes = dom_bytes / dom_launches
+
     peak, peak_kind = measured_peak()
-    per_gpu = value / world
-    roofline = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(per_gpu / peak, 4), "peak_source": peak_kind,
-                "kernel": "merge_kernel (all launches of one step)", "traffic": None}
+    achieved = launch_bytes / (launch_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (hbm_gbs copy)",
+                "kernel": f"merge_kernel over {items[dom][1]}x{items[dom][2]} ({items[dom][0].split('.')[-2]}), "
+                          f"{dom_launches:g} launches per merge",
+                "algorithmic_bytes_per_launch": int(launch_bytes), "launch_ms": round(launch_ms, 5),
+                "step_achieved": round(value / world, 1), "traffic": None}
     tfile = ROOT / "profiles" / f"traffic_{cfg}.json"
     if tfile.exists():
         try:
             tj = json.loads(tfile.read_text())
-            roofline["traffic"] = tj.get("dram_bytes_per_algorithmic_byte")
-            roofline["traffic_note"] = tj.get("note")
+            ratio = float(tj["dram_bytes_per_algorithmic_byte"])
+            roofline["traffic"] = int(ratio * launch_bytes)
+            roofline["traffic_source"] = tj.get("note")
         except Exception:  # noqa: BLE001
             pass
 
@@ -431,6 +468,7 @@ def main() -> int:
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": desc, "weights_per_gpu": len(items), "rank": lrank, "stochastic": stochastic,
                        "weight_bytes_per_gpu": total_bytes, "l2": "inputs (~GBs) exceed the 126 MB L2; no flush",
+                       "layers": args.layers or CONFIGS[cfg][1],
                        "parallelism": f"weak x{world}: one model per GPU, no collective"},
             "roofline": roofline,
             "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},

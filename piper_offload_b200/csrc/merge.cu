@@ -47,7 +47,6 @@
 
 namespace pm {
 
-constexpr int kThreads = 256;  // two warpgroups; thread t owns tile row (t & 127)
 constexpr int kMaxWeights = 24;
 constexpr int kMaxRank = 256;
 
@@ -83,7 +82,6 @@ struct alignas(64) DevWeight {
   int scale_mode;      // MX E8M0 rounding
   int scale_dt;        // INT8 scale dtype
   int use_tma;         // code tiles move by bulk tensor copies (swizzled rows)
-  int swz;             // smem row swizzle of TMA tiles: 2 = 128 B, 1 = 64 B
 };
 
 struct LaunchParams {
@@ -91,6 +89,7 @@ struct LaunchParams {
   int n_weights;
   int n_items;  // work items over all weights; CTAs stride over them
   int kp_max;   // shared-memory layout is sized for the largest padded rank
+  int stages;   // depth of the (codes, A tile, scales) ring
 };
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -111,25 +110,8 @@ __host__ __device__ constexpr int row_stride() {
   return align_up(code_bytes<FMT>(BN), 16) + 16;
 }
 
-// Shared memory: resident B strip (128 x KP bf16), one A tile (KP x BN bf16),
-// two code-tile stages (128 rows x RS bytes) and two per-row scale stages
-// (16 bytes per row), then the mbarrier and the tensor-memory address slot.
+// Per-row scale bytes of one tile in shared memory (MX: BN/32, NVFP4: BN/16).
 constexpr int kScaleSlot = 16;
-
-constexpr int kStages = 3;
-
-template <int FMT, int BN>
-__host__ __device__ constexpr int stage_bytes() {
-  return align_up(128 * row_stride<FMT, BN>(), 1024);
-}
-
-// Code stages first (1024-byte aligned for swizzled TMA tiles), then the B
-// strip, the A tile, per-row scale stages, barriers and the TMEM slot; plus
-// 1 KB of slack to align the dynamic shared-memory base.
-template <int FMT, int BN>
-__host__ __device__ constexpr int smem_bytes(int kp) {
-  return 1024 + kStages * stage_bytes<FMT, BN>() + 128 * kp * 2 + kp * BN * 2 + kStages * 128 * kScaleSlot + 64;
-}
 
 // Blocked 128x4 scale layout (_triton_mx_lora.py:97-112, _triton_nvfp4_lora.py:88-104).
 __device__ __forceinline__ int64_t swizzled_index(int row, int col, int scale_cols) {
@@ -251,14 +233,18 @@ struct RowCtx {
   bool valid;            // row < M
   uint8_t* srow;         // this row's code segment in shared memory
   uint32_t swz;          // XOR applied to 16-byte chunk indices (swizzled TMA rows)
+  int box_shift;         // log2(16-byte chunks per box row)
+  int box_stride;        // bytes between consecutive boxes of a tile
   const uint8_t* sscale; // this row's prefetched scale bytes for the tile (MX / NVFP4)
   int blk0;              // scale block index of sscale[0]
   int tile_col0;         // first column of the tile
   int tile_cols;         // valid columns in the tile
 };
 
+// 16-byte chunk `c16` of this row: box c16 >> box_shift, swizzled chunk within it.
 __device__ __forceinline__ uint8_t* chunk_ptr(const RowCtx& c, int c16) {
-  return c.srow + ((static_cast<uint32_t>(c16) ^ c.swz) << 4);
+  const uint32_t in_box = static_cast<uint32_t>(c16) & ((1u << c.box_shift) - 1u);
+  return c.srow + (c16 >> c.box_shift) * c.box_stride + ((in_box ^ c.swz) << 4);
 }
 __device__ __forceinline__ void load_chunks32(const RowCtx& c, int k, uint32_t (&w)[8]) {
   const uint4 a = *reinterpret_cast<const uint4*>(chunk_ptr(c, 2 * k));
@@ -726,8 +712,6 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
     const unsigned short dh = __half_as_ushort(__float2half_rn(d));
-    blk[0] = static_cast<uint8_t>(dh & 0xFFu);
-    blk[1] = static_cast<uint8_t>(dh >> 8);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const float x = __fmul_rn(merged[i], id);
@@ -736,6 +720,7 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
       q = fminf(fmaxf(q, -128.0f), 127.0f);
       blk[2 + i] = static_cast<uint8_t>(static_cast<int8_t>(static_cast<int>(q)));
     }
+    *reinterpret_cast<unsigned short*>(blk) = dh;  // blocks start at even offsets
   } else {
     int imax = 0;
     float best = fabsf(merged[0]);
@@ -762,329 +747,410 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
       qf = fminf(fmaxf(qf, 0.0f), 15.0f);
       q[i] = static_cast<uint32_t>(qf);
     }
-    blk[0] = static_cast<uint8_t>(dh & 0xFFu);
-    blk[1] = static_cast<uint8_t>(dh >> 8);
 #pragma unroll
     for (int j = 0; j < 16; ++j) blk[2 + j] = static_cast<uint8_t>(q[j] | (q[j + 16] << 4));
+    *reinterpret_cast<unsigned short*>(blk) = dh;
   }
 }
 
 // ============================================================== the kernel
+// ================================================================== kernel
+// Warp-specialised persistent kernel, one CTA per SM (384 threads):
+//   warp 0      code tiles by 2-D bulk tensor copies (one elected lane);
+//   warp 1      tcgen05.mma of the rank-r update into a double-buffered TMEM
+//               accumulator (one elected lane), plus TMEM allocation;
+//   warps 2-3   A tiles, per-tile scale bytes and the B strip by cp.async
+//               (and code tiles of weights whose rows cannot use the TMA);
+//   warps 4-11  epilogue: two warpgroups, thread e owns tile row (e & 127) and
+//               every other 32-column chunk; decode, merge, re-scale, encode
+//               in place in shared memory, then one bulk tensor store.
+// Stages of (codes, A tile, scales) circulate through full/empty mbarriers;
+// accumulators through afull/aempty; B strips through bfull/bempty. Every
+// wait is bounded (ptx.cuh); a role whose wait gives up stops issuing work and
+// the others then give up in turn, so the CTA always reaches its exit.
+constexpr int kWsThreads = 384;
+constexpr int kEpiThreads = 256;
+constexpr int kLoadThreads = 64;  // warps 2-3
+constexpr int kMaxStages = 6;
+constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
+
+template <int FMT>
+__host__ __device__ constexpr bool is_gguf() {
+  return FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0;
+}
+
+// Geometry of one code tile (128 rows x BN columns) in shared memory. TMA
+// tiles arrive as `kBoxes` boxes of 128 rows x kBoxRow bytes, swizzled in
+// 16-byte chunks (128 / 64 / 32-byte rows); GGUF boxes are dense rows.
+template <int FMT, int BN>
+struct TileGeom {
+  static constexpr int kRowBytes = code_bytes<FMT>(BN);
+  static constexpr int kBoxRow = is_gguf<FMT>() ? kRowBytes : (kRowBytes >= 128 ? 128 : kRowBytes);
+  static constexpr int kBoxes = kRowBytes / kBoxRow;
+  static constexpr int kBoxShift = kBoxRow == 128 ? 3 : (kBoxRow == 64 ? 2 : 1);
+  static constexpr int kPadRS = row_stride<FMT, BN>();
+  static constexpr int kCodeSlot = align_up(128 * (kPadRS > kRowBytes ? kPadRS : kRowBytes), 1024);
+};
+
+__host__ __device__ constexpr int ws_stage_bytes(int code_slot, int kp, int bn) {
+  return align_up(code_slot + kp * bn * 2 + 128 * kScaleSlot, 1024);
+}
+// Stages, then two B strips, then the barriers and the TMEM slot (+1 KB of
+// alignment slack for the dynamic shared-memory base).
+__host__ __device__ constexpr int ws_smem_bytes(int stage_bytes, int stages, int kp) {
+  return 1024 + stages * stage_bytes + 2 * 128 * kp * 2 + 256;
+}
+
+struct ItemGeom {
+  int wi, strip, row0, col_begin, col_end, n_tiles;
+};
+
+template <int BN>
+__device__ __forceinline__ ItemGeom item_geom(const LaunchParams& P, int item) {
+  ItemGeom g;
+  int wi = 0;
+  while (wi + 1 < P.n_weights && P.w[wi + 1].item_begin <= item) ++wi;
+  const DevWeight& W = P.w[wi];
+  const int local = item - W.item_begin;
+  g.wi = wi;
+  g.strip = local / W.col_items;
+  const int ci = local - g.strip * W.col_items;
+  g.row0 = W.row_begin + g.strip * 128;
+  g.col_begin = ci * W.item_cols;
+  g.col_end = min(W.N, g.col_begin + W.item_cols);
+  g.n_tiles = (g.col_end - g.col_begin + BN - 1) / BN;
+  return g;
+}
+
+// Byte offset of column c0 within a row of codes.
+template <int FMT>
+__device__ __forceinline__ int64_t code_off(int c0) {
+  if constexpr (is_gguf<FMT>()) return code_bytes<FMT>(c0);
+  else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) return c0 / 2;
+  else return c0;
+}
+
 template <int FMT, int PASS, int BN, int CDT>
-__global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constant__ LaunchParams P) {
+__global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_constant__ LaunchParams P) {
+  using G = TileGeom<FMT, BN>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
-  const int rt = tid & 127;        // tile row / tensor-memory lane of this thread
-  const int wg = tid >> 7;         // warpgroup: takes every other accumulator chunk
-  const int lane_warp = (tid >> 5) & 3;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int KPL = P.kp_max;
+  const int S = P.stages;
+  const int kStageB = ws_stage_bytes(G::kCodeSlot, KPL, BN);
 
-  constexpr int RS = row_stride<FMT, BN>();
-  constexpr int kStageB = stage_bytes<FMT, BN>();
-  constexpr int kTileRowBytes = code_bytes<FMT>(BN);  // dense (TMA) row of a tile
-  const int KPL = P.kp_max;  // layout rank (all items of this launch share it)
   uint8_t* base1k = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);
-  uint8_t* sC = base1k;  // kStages code stages
-  uint8_t* sB = sC + kStages * kStageB;
-  uint8_t* sA = sB + 128 * KPL * 2;
-  uint8_t* sS = sA + KPL * BN * 2;
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sS + kStages * 128 * kScaleSlot);
-  uint64_t* bar_full = bar_mma + 1;  // [kStages] TMA code tiles landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_full + kStages);
+  uint8_t* sStage = base1k;
+  uint8_t* sB = sStage + S * kStageB;  // two B strips
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + 2 * 128 * KPL * 2);
+  uint64_t* full = bars;                  // [kMaxStages]
+  uint64_t* empty = full + kMaxStages;    // [kMaxStages]
+  uint64_t* bfull = empty + kMaxStages;   // [2]
+  uint64_t* bempty = bfull + 2;           // [2]
+  uint64_t* afull = bempty + 2;           // [2]
+  uint64_t* aempty = afull + 2;           // [2]
+  uint64_t* mma_done = aempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  auto stage_codes = [&](int s) { return sStage + s * kStageB; };
+  auto stage_a = [&](int s) { return sStage + s * kStageB + G::kCodeSlot; };
+  auto stage_scales = [&](int s) { return sStage + s * kStageB + G::kCodeSlot + KPL * BN * 2; };
 
   if (tid == 0) {
-    mbar_init(bar_mma, 1);
-    for (int i = 0; i < kStages; ++i) mbar_init(&bar_full[i], 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1 + kLoadThreads);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bfull[i], kLoadThreads);
+      mbar_init(&bempty[i], 1);
+      mbar_init(&afull[i], 1);
+      mbar_init(&aempty[i], kEpiThreads / 32);
+    }
+    mbar_init(mma_done, 1);
     fence_mbar_init();
   }
-  uint32_t full_uses[kStages] = {0u, 0u, 0u};    // consumed phases per stage (thread-uniform)
-  uint32_t full_issued[kStages] = {0u, 0u, 0u};  // loads issued per stage (thread 0)
-  if (tid < 32) {
-    tmem_alloc(tmem_slot, BN);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t taddr = tmem + (static_cast<uint32_t>(lane_warp * 32) << 16);
 
-  uint32_t gt = 0;  // tiles processed by this CTA (mbarrier phase)
-  bool ok = true;
-  for (int item = static_cast<int>(blockIdx.x); item < P.n_items && ok; item += static_cast<int>(gridDim.x)) {
-  // Locate this item's weight, 128-row strip and column range.
-  int wi = 0;
-  while (wi + 1 < P.n_weights && P.w[wi + 1].item_begin <= item) ++wi;
-  const DevWeight& W = P.w[wi];
-  const int local = item - W.item_begin;
-  const int strip = local / W.col_items;
-  const int ci = local - strip * W.col_items;
-  const int row0 = W.row_begin + strip * 128;
-  const int col_begin = ci * W.item_cols;
-  const int col_end = min(W.N, col_begin + W.item_cols);
-  const int n_tiles = (col_end - col_begin + BN - 1) / BN;
-  const int KP = W.KP;
-
-  const int row = row0 + rt;
-  const bool valid = row < W.M;
-  const int rows_here = min(128, W.M - row0);
-
-  // ---- resident B strip (K-major canonical): chunk kc of row t at kc*2048 + (t/8)*128 + (t%8)*16.
-  {
-    const uint16_t* brow = W.b + static_cast<int64_t>(row) * W.r;
-    const bool vec = ((reinterpret_cast<uintptr_t>(W.b) | (W.r * 2)) & 15) == 0;
-    for (int kc = wg; kc < KP / 8; kc += 2) {
-      uint8_t* dst = sB + kc * 2048 + (rt >> 3) * 128 + (rt & 7) * 16;
-      if (valid && vec && kc * 8 + 8 <= W.r) {
-        cp_async16(dst, brow + kc * 8);
-      } else {
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (valid) {
-          uint16_t e[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) e[j] = (kc * 8 + j < W.r) ? brow[kc * 8 + j] : 0;
-          v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16),
-                         e[6] | (e[7] << 16));
-        }
-        *reinterpret_cast<uint4*>(dst) = v;
-      }
-    }
-  }
-
-  // ---- tile byte ranges and copy granularity (16 B when everything is aligned).
-  auto tile_off = [&](int c0) -> int64_t {
-    if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) return code_bytes<FMT>(c0);
-    else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) return c0 / 2;
-    else return c0;
-  };
-  auto tile_nbytes = [&](int ncols) -> int {
-    if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) return code_bytes<FMT>(ncols);
-    else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) return ncols / 2;
-    else return ncols;
-  };
-  auto granularity = [&](int64_t off, int nbytes) -> int {
-    const int64_t m = W.row_bytes | off | nbytes | static_cast<int64_t>(reinterpret_cast<uintptr_t>(W.q));
-    return (m & 15) == 0 ? 16 : ((m & 3) == 0 ? 4 : 1);
-  };
-
-  // Coalesced async copy of one code tile (rows row0.., bytes [off, off+nbytes)) into a stage.
-  auto issue_codes = [&](int tile, int stage) {
-    const int c0 = col_begin + tile * BN;
-    const int ncols = min(BN, col_end - c0);
-    const int64_t off = tile_off(c0);
-    const int nbytes = tile_nbytes(ncols);
-    const int g = granularity(off, nbytes);
-    const int per = nbytes / g;
-    const int total = rows_here * per;
-    uint8_t* base = sC + stage * kStageB;
-    const uint8_t* src0 = W.q + static_cast<int64_t>(row0) * W.row_bytes + off;
-    for (int k = tid; k < total; k += kThreads) {
-      const int r = k / per;
-      const int i = k - r * per;
-      uint8_t* dst = base + r * RS + i * g;
-      const uint8_t* src = src0 + static_cast<int64_t>(r) * W.row_bytes + i * g;
-      if (g == 16) cp_async16(dst, src);
-      else if (g == 4) cp_async4(dst, src);
-      else *dst = *src;
-    }
-  };
-
-  // TMA code tile: one thread, completion on bar_full[stage].
-  auto issue_codes_tma = [&](int tile, int stage) {
-    const int c0 = col_begin + tile * BN;
-    ++full_issued[stage];
-    mbar_arrive_expect_tx(&bar_full[stage], 128u * kTileRowBytes);
-    tma_load_2d(sC + stage * kStageB, &W.tmap, static_cast<int>(tile_off(c0)), row0, &bar_full[stage]);
-  };
-
-  // Per-row scale bytes of MX / NVFP4 tiles (one warpgroup, cp.async).
-  auto issue_scales = [&](int tile, int stage) {
-    const int c0 = col_begin + tile * BN;
-    const int ncols = min(BN, col_end - c0);
-    if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 || FMT == PIPER_FMT_MXFP4 ||
-                  FMT == PIPER_FMT_NVFP4) {
-      constexpr int kBlk = FMT == PIPER_FMT_NVFP4 ? 16 : 32;
-      const int b0 = c0 / kBlk;
-      const int nb = (ncols + kBlk - 1) / kBlk;
-      uint8_t* dst = sS + stage * 128 * kScaleSlot + rt * kScaleSlot;  // stage of the scale ring
-      if (valid && wg == 0) {
-        const uint8_t* scale8 = reinterpret_cast<const uint8_t*>(W.scale);
-        const bool sw = (W.flags & PIPER_FLAG_SWIZZLED) != 0u;
-        const bool vec4 = ((b0 | nb) & 3) == 0 && (sw || (W.scale_cols & 3) == 0) &&
-                          (reinterpret_cast<uintptr_t>(W.scale) & 3) == 0;
-        if (vec4) {
-          for (int j = 0; j < nb; j += 4) cp_async4(dst + j, scale8 + scale_index(W, row, b0 + j));
-        } else {
-          for (int j = 0; j < nb; ++j) dst[j] = scale8[scale_index(W, row, b0 + j)];
+  if (warp == 0) {
+    // ------------------------------------------------ code tiles (bulk tensor)
+    if (lane == 0) {
+      uint32_t t = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x) {
+        const ItemGeom g = item_geom<BN>(P, item);
+        const DevWeight& W = P.w[g.wi];
+        if (W.use_tma) prefetch_tmap(&W.tmap);
+        for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
+          const int s = t % S;
+          if (t >= static_cast<uint32_t>(S)) {
+            ok = mbar_wait(&empty[s], ((t / S) - 1) & 1u, kStatusTimeoutLoad);
+            if (!ok) break;
+          }
+          if (W.use_tma) {
+            const int c0 = g.col_begin + tile * BN;
+            const int64_t off = code_off<FMT>(c0);
+            int boxes = 0;
+            for (int j = 0; j < G::kBoxes; ++j) boxes += (off + j * G::kBoxRow < W.row_bytes) ? 1 : 0;
+            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(boxes * 128 * G::kBoxRow));
+            for (int j = 0; j < boxes; ++j) {
+              const int x = static_cast<int>(off + j * G::kBoxRow);
+              tma_load_2d(stage_codes(s) + j * 128 * G::kBoxRow, &W.tmap, is_gguf<FMT>() ? x / 8 : x, g.row0,
+                          &full[s]);
+            }
+          } else {
+            mbar_arrive(&full[s]);
+          }
         }
       }
+      // Loads still in flight after an early exit land before the CTA retires.
+      const uint32_t issued = t;
+      for (uint32_t u = issued > static_cast<uint32_t>(S) ? issued - S : 0u; u < issued; ++u)
+        mbar_wait(&full[u % S], (u / S) & 1u, kStatusTimeoutLoad);
     }
-  };
-
-  // A tile (MN-major canonical): element (k, n) at (k/8)*(BN*16) + (n/8)*128 + (k%8)*16 + (n%8)*2.
-  auto issue_a = [&](int tile) {
-    const int c0 = col_begin + tile * BN;
-    const bool vec = (((reinterpret_cast<uintptr_t>(W.a)) | (W.N * 2)) & 15) == 0;
-    const int chunks = KP * BN / 8;
-    for (int idx = tid; idx < chunks; idx += kThreads) {
-      const int kk = idx & 7;
-      const int ng = (idx >> 3) % (BN / 8);
-      const int kg = idx / BN;
-      const int kr = kg * 8 + kk;
-      const int n = c0 + ng * 8;
-      uint8_t* dst = sA + kg * (BN * 16) + ng * 128 + kk * 16;
-      const uint16_t* ap = W.a + static_cast<int64_t>(kr) * W.N + n;
-      if (kr < W.r && vec && n + 8 <= col_end) {
-        cp_async16(dst, ap);
-      } else {
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (kr < W.r) {
-          uint16_t e[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) e[j] = (n + j < col_end) ? ap[j] : 0;
-          v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16),
-                         e[6] | (e[7] << 16));
-        }
-        *reinterpret_cast<uint4*>(dst) = v;
-      }
-    }
-  };
-
-  // Coalesced write-back of a stage to global memory (in place).
-  auto store_codes = [&](int tile, int stage) {
-    const int c0 = col_begin + tile * BN;
-    const int ncols = min(BN, col_end - c0);
-    const int64_t off = tile_off(c0);
-    const int nbytes = tile_nbytes(ncols);
-    const int g = granularity(off, nbytes);
-    const int per = nbytes / g;
-    const int total = rows_here * per;
-    const uint8_t* base = sC + stage * kStageB;
-    uint8_t* dst0 = W.q + static_cast<int64_t>(row0) * W.row_bytes + off;
-    for (int k = tid; k < total; k += kThreads) {
-      const int r = k / per;
-      const int i = k - r * per;
-      const uint8_t* src = base + r * RS + i * g;
-      uint8_t* dst = dst0 + static_cast<int64_t>(r) * W.row_bytes + i * g;
-      if (g == 16) *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
-      else if (g == 4) *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(src);
-      else *dst = *src;
-    }
-  };
-
-  // Per-thread running reductions for REDUCE passes.
-  float red_max = 0.0f, red_nmin = 0.0f;
-  int red_qp = -1;
-  auto flush_reduce = [&]() {
-    if (red_qp >= 0) {
-      atomic_max_nonneg(&W.qmax[red_qp], red_max);
-      if (FMT == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[red_qp], red_nmin);
-    }
-    red_max = 0.0f;
-    red_nmin = 0.0f;
-  };
-  // NVFP4 global scales (two-level).
-  const bool two_level = (FMT == PIPER_FMT_NVFP4) && W.gscale != nullptr;
-  float g_in = 1.0f, g_out = 1.0f;
-  if constexpr (FMT == PIPER_FMT_NVFP4) {
-    if (two_level) {
-      if (PASS == kReduce) {
-        g_in = *W.gscale;
-        if (local == 0 && tid == 0) W.old_scale[0] = g_in;
-      } else {
-        g_in = W.old_scale[0];
-        const float amax = __uint_as_float(*W.qmax);
-        g_out = fmaxf(__fdiv_rn(amax, 2688.0f), 1.1920928955078125e-07f);  // `/ 2688.0`: IEEE
-      }
-    }
-  }
-
-  const bool tma = W.use_tma != 0;
-  // Prologue: codes of the first tiles (TMA keeps two in flight), scales and
-  // A of the first tile (cp.async, with the B strip above).
-  if (n_tiles > 0) {
-    if (tma) {
-      if (tid == 0) {
-        bulk_wait_read_all();  // earlier stores have finished reading their stages
-        issue_codes_tma(0, gt % kStages);
-        if (n_tiles > 1) issue_codes_tma(1, (gt + 1) % kStages);
-      }
-    } else {
-      issue_codes(0, gt % kStages);
-    }
-    issue_scales(0, gt % kStages);
-    issue_a(0);
-  }
-  cp_async_commit();
-  for (int tile = 0; tile < n_tiles; ++tile, ++gt) {
-    const int stage = gt % kStages;
-    const int c0 = col_begin + tile * BN;
-    const int tcols = min(BN, col_end - c0);
-
-    // ---- tile `tile` (codes, scales, A; B for the first tile) is in shared memory.
-    cp_async_wait_all();
-    if (tma) {
-      ok = mbar_wait(&bar_full[stage], full_uses[stage] & 1u, kStatusTimeoutLoad);
-      ++full_uses[stage];
-    }
-    fence_proxy_async_smem();
-    ok = __syncthreads_and(ok) != 0;
-    if (!ok) break;
-
-    // ---- issue the update on the tensor core.
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t a_base = smem_u32(sB);
-      const uint32_t b_base = smem_u32(sA);
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ tensor core
+    if (lane == 0) {
+      uint32_t t = 0, it = 0;
+      bool ok = true;
       constexpr uint32_t idesc = idesc_f16(BN, CDT == kBF16 ? 1u : 0u);
-      for (int ks = 0; ks < KP / 16; ++ks) {
-        const uint64_t adesc = smem_desc(a_base + ks * 2 * 2048, 2048, 128);
-        const uint64_t bdesc = smem_desc(b_base + ks * 2 * (BN * 16), BN * 16, 128);
-        umma_f16(tmem, adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
+      for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x, ++it) {
+        const ItemGeom g = item_geom<BN>(P, item);
+        const int KP = P.w[g.wi].KP;
+        const int jb = it & 1;
+        ok = mbar_wait(&bfull[jb], (it >> 1) & 1u, kStatusTimeoutLoad);
+        if (!ok) break;
+        const uint32_t a_base = smem_u32(sB + jb * 128 * KPL * 2);
+        for (int tile = 0; tile < g.n_tiles && ok; ++tile, ++t) {
+          const int s = t % S;
+          const int ab = t & 1;
+          ok = mbar_wait(&full[s], (t / S) & 1u, kStatusTimeoutLoad);
+          if (ok && t >= 2) ok = mbar_wait(&aempty[ab], ((t >> 1) - 1) & 1u, kStatusTimeoutMma);
+          if (!ok) break;
+          fence_proxy_async_smem();  // cp.async-written operands -> tensor core
+          tc_fence_after();
+          const uint32_t b_base = smem_u32(stage_a(s));
+          for (int ks = 0; ks < KP / 16; ++ks) {
+            const uint64_t adesc = smem_desc(a_base + ks * 2 * 2048, 2048, 128);
+            const uint64_t bdesc = smem_desc(b_base + ks * 2 * (BN * 16), BN * 16, 128);
+            umma_f16(tmem + ab * BN, adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
+          }
+          umma_commit(&afull[ab]);
+        }
+        umma_commit(&bempty[jb]);  // the strip is free once these MMAs complete
       }
-      umma_commit(bar_mma);
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0u, kStatusTimeoutMma);
     }
-
-    // ---- prefetch code tiles: TMA two ahead (after the store that last used
-    //      that stage has read it), cp.async one ahead.
-    if (tma) {
-      if (tid == 0 && tile + 2 < n_tiles) {
-        bulk_wait_read_all();
-        issue_codes_tma(tile + 2, (gt + 2) % kStages);
+    __syncwarp();
+  } else if (warp < 4) {
+    // ------------------------------------- A tiles, scales, B strips (cp.async)
+    const int lt = tid - 64;
+    uint32_t t = 0, it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x, ++it) {
+      const ItemGeom g = item_geom<BN>(P, item);
+      const DevWeight& W = P.w[g.wi];
+      const int KP = W.KP;
+      const int rows_here = min(128, W.M - g.row0);
+      // B strip (K-major canonical): chunk kc of row t at kc*2048 + (t/8)*128 + (t%8)*16.
+      const int jb = it & 1;
+      if (it >= 2) {
+        ok = mbar_wait(&bempty[jb], ((it >> 1) - 1) & 1u, kStatusTimeoutMma);
+        if (!ok) break;
       }
-    } else if (tile + 1 < n_tiles) {
-      issue_codes(tile + 1, (gt + 1) % kStages);
+      {
+        uint8_t* sBj = sB + jb * 128 * KPL * 2;
+        const bool vec = ((reinterpret_cast<uintptr_t>(W.b) | (W.r * 2)) & 15) == 0;
+        for (int idx = lt; idx < 128 * (KP / 8); idx += kLoadThreads) {
+          const int rt = idx & 127;
+          const int kc = idx >> 7;
+          const int row = g.row0 + rt;
+          uint8_t* dst = sBj + kc * 2048 + (rt >> 3) * 128 + (rt & 7) * 16;
+          const uint16_t* brow = W.b + static_cast<int64_t>(row) * W.r;
+          if (row < W.M && vec && kc * 8 + 8 <= W.r) {
+            cp_async16(dst, brow + kc * 8);
+          } else {
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (row < W.M) {
+              uint16_t e[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) e[j] = (kc * 8 + j < W.r) ? brow[kc * 8 + j] : 0;
+              v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16), e[6] | (e[7] << 16));
+            }
+            *reinterpret_cast<uint4*>(dst) = v;
+          }
+        }
+        __threadfence_block();  // plain smem stores of ragged rows precede the arrival
+        cp_async_mbar_arrive(&bfull[jb]);
+      }
+      const bool vec_a = ((reinterpret_cast<uintptr_t>(W.a) | (W.N * 2)) & 15) == 0;
+      for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
+        const int s = t % S;
+        if (t >= static_cast<uint32_t>(S)) {
+          ok = mbar_wait(&empty[s], ((t / S) - 1) & 1u, kStatusTimeoutLoad);
+          if (!ok) break;
+        }
+        const int c0 = g.col_begin + tile * BN;
+        const int ncols = min(BN, g.col_end - c0);
+        if (!W.use_tma) {
+          // Codes into the padded row layout (rows of kPadRS bytes).
+          const int64_t off = code_off<FMT>(c0);
+          const int nbytes = static_cast<int>(code_off<FMT>(c0 + ncols) - off);
+          const int64_t m = W.row_bytes | off | nbytes | static_cast<int64_t>(reinterpret_cast<uintptr_t>(W.q));
+          const int gran = (m & 15) == 0 ? 16 : ((m & 3) == 0 ? 4 : 1);
+          const int per = nbytes / gran;
+          const uint8_t* src0 = W.q + static_cast<int64_t>(g.row0) * W.row_bytes + off;
+          uint8_t* dst0 = stage_codes(s);
+          for (int k = lt; k < rows_here * per; k += kLoadThreads) {
+            const int r = k / per;
+            const int i = k - r * per;
+            uint8_t* dst = dst0 + r * G::kPadRS + i * gran;
+            const uint8_t* src = src0 + static_cast<int64_t>(r) * W.row_bytes + i * gran;
+            if (gran == 16) cp_async16(dst, src);
+            else if (gran == 4) cp_async4(dst, src);
+            else *dst = *src;
+          }
+        }
+        // Per-row scale bytes of MX / NVFP4 tiles.
+        if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 || FMT == PIPER_FMT_MXFP4 ||
+                      FMT == PIPER_FMT_NVFP4) {
+          constexpr int kBlk = FMT == PIPER_FMT_NVFP4 ? 16 : 32;
+          const int b0 = c0 / kBlk;
+          const int nb = (ncols + kBlk - 1) / kBlk;
+          const uint8_t* scale8 = reinterpret_cast<const uint8_t*>(W.scale);
+          const bool sw = (W.flags & PIPER_FLAG_SWIZZLED) != 0u;
+          const bool vec4 = ((b0 | nb) & 3) == 0 && (sw || (W.scale_cols & 3) == 0) &&
+                            (reinterpret_cast<uintptr_t>(W.scale) & 3) == 0;
+          for (int rt = lt; rt < rows_here; rt += kLoadThreads) {
+            const int row = g.row0 + rt;
+            uint8_t* dst = stage_scales(s) + rt * kScaleSlot;
+            if (vec4) {
+              for (int j = 0; j < nb; j += 4) cp_async4(dst + j, scale8 + scale_index(W, row, b0 + j));
+            } else {
+              for (int j = 0; j < nb; ++j) dst[j] = scale8[scale_index(W, row, b0 + j)];
+            }
+          }
+        }
+        // A tile (MN-major canonical): element (k, n) at (k/8)*(BN*16) + (n/8)*128 + (k%8)*16 + (n%8)*2.
+        {
+          uint8_t* sA = stage_a(s);
+          const int chunks = KP * BN / 8;
+          for (int idx = lt; idx < chunks; idx += kLoadThreads) {
+            const int kk = idx & 7;
+            const int ng = (idx >> 3) % (BN / 8);
+            const int kg = idx / BN;
+            const int kr = kg * 8 + kk;
+            const int n = c0 + ng * 8;
+            uint8_t* dst = sA + kg * (BN * 16) + ng * 128 + kk * 16;
+            const uint16_t* ap = W.a + static_cast<int64_t>(kr) * W.N + n;
+            if (kr < W.r && vec_a && n + 8 <= g.col_end) {
+              cp_async16(dst, ap);
+            } else {
+              uint4 v = make_uint4(0u, 0u, 0u, 0u);
+              if (kr < W.r) {
+                uint16_t e[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) e[j] = (n + j < g.col_end) ? ap[j] : 0;
+                v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16), e[6] | (e[7] << 16));
+              }
+              *reinterpret_cast<uint4*>(dst) = v;
+            }
+          }
+        }
+        __threadfence_block();
+        cp_async_mbar_arrive(&full[s]);
+      }
     }
+    cp_async_wait_all();
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int e = tid - 128;
+    const int rt = e & 127;         // tile row / tensor-memory lane of this thread
+    const int wg = e >> 7;          // takes every other accumulator chunk
+    const uint32_t lane_off = static_cast<uint32_t>((e >> 5) & 3) * 32u << 16;
+    uint32_t t = 0;
+    int pending = -1;  // stage whose bulk store may still be reading it
+    bool ok = true;
+    for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x) {
+      const ItemGeom g = item_geom<BN>(P, item);
+      const DevWeight& W = P.w[g.wi];
+      const int local = item - W.item_begin;
+      const int row = g.row0 + rt;
+      const bool valid = row < W.M;
+      const int rows_here = min(128, W.M - g.row0);
+      const bool tma = W.use_tma != 0;
 
-    ok = mbar_wait(bar_mma, gt & 1, kStatusTimeoutMma);
-    // Keep the CTA uniform: tcgen05.ld below is warp-collective.
-    ok = __syncthreads_and(ok) != 0;
-    tc_fence_after();
-    if (!ok) break;
+      // Per-thread running reductions for REDUCE passes.
+      float red_max = 0.0f, red_nmin = 0.0f;
+      int red_qp = -1;
+      auto flush_reduce = [&]() {
+        if (red_qp >= 0) {
+          atomic_max_nonneg(&W.qmax[red_qp], red_max);
+          if (FMT == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[red_qp], red_nmin);
+        }
+        red_max = 0.0f;
+        red_nmin = 0.0f;
+      };
+      // NVFP4 global scales (two-level).
+      const bool two_level = (FMT == PIPER_FMT_NVFP4) && W.gscale != nullptr;
+      float g_in = 1.0f, g_out = 1.0f;
+      if constexpr (FMT == PIPER_FMT_NVFP4) {
+        if (two_level) {
+          if (PASS == kReduce) {
+            g_in = *W.gscale;
+            if (local == 0 && e == 0) W.old_scale[0] = g_in;
+          } else {
+            g_in = W.old_scale[0];
+            const float amax = __uint_as_float(*W.qmax);
+            g_out = fmaxf(__fdiv_rn(amax, 2688.0f), 1.1920928955078125e-07f);  // `/ 2688.0`: IEEE
+          }
+        }
+      }
 
-    // The MMA has consumed the A tile: fetch the next one (and its scales) behind the epilogue.
-    if (tile + 1 < n_tiles) {
-      issue_a(tile + 1);
-      issue_scales(tile + 1, (gt + 1) % kStages);
-    }
-    cp_async_commit();
+      for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
+        const int s = t % S;
+        const int ab = t & 1;
+        const int c0 = g.col_begin + tile * BN;
+        const int tcols = min(BN, g.col_end - c0);
+        ok = mbar_wait(&full[s], (t / S) & 1u, kStatusTimeoutLoad);
+        if (ok) ok = mbar_wait(&afull[ab], (t >> 1) & 1u, kStatusTimeoutMma);
+        // One decision for all epilogue threads: the barriers below need them all.
+        ok = named_bar_and(1, kEpiThreads, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem + lane_off + ab * BN;
 
-    RowCtx c;
-    c.row = row;
-    c.valid = valid;
-    if (tma) {
-      c.srow = sC + stage * kStageB + rt * kTileRowBytes;
-      c.swz = W.swz == 2 ? static_cast<uint32_t>(rt & 7) : static_cast<uint32_t>((rt >> 1) & 3);
-    } else {
-      c.srow = sC + stage * kStageB + rt * RS;
-      c.swz = 0u;
-    }
-    c.sscale = sS + stage * 128 * kScaleSlot + rt * kScaleSlot;
-    c.blk0 = (FMT == PIPER_FMT_NVFP4) ? c0 / 16 : c0 / 32;
-    c.tile_col0 = c0;
-    c.tile_cols = tcols;
-    const int tid = rt;  // the epilogue below addresses rows by tile row
-    (void)tid;
-    if (ok) {
+        RowCtx c;
+        c.row = row;
+        c.valid = valid;
+        if (tma) {
+          c.srow = stage_codes(s) + rt * G::kBoxRow;
+          c.box_stride = 128 * G::kBoxRow;
+          c.box_shift = is_gguf<FMT>() ? 16 : G::kBoxShift;
+          c.swz = is_gguf<FMT>() ? 0u
+                  : (G::kBoxRow == 128 ? static_cast<uint32_t>(rt & 7)
+                     : (G::kBoxRow == 64 ? static_cast<uint32_t>((rt >> 1) & 3) : static_cast<uint32_t>((rt >> 2) & 1)));
+        } else {
+          c.srow = stage_codes(s) + rt * G::kPadRS;
+          c.box_stride = 0;
+          c.box_shift = 16;
+          c.swz = 0u;
+        }
+        c.sscale = stage_scales(s) + rt * kScaleSlot;
+        c.blk0 = (FMT == PIPER_FMT_NVFP4) ? c0 / 16 : c0 / 32;
+        c.tile_col0 = c0;
+        c.tile_cols = tcols;
+        {
       if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 ||
                     FMT == PIPER_FMT_MXFP4) {
         for (int k = wg; k < tcols / 32; k += 2) {
@@ -1326,74 +1392,102 @@ __global__ void __launch_bounds__(kThreads, 2) merge_kernel(const __grid_constan
           }
         }
       }
-    }
-
-    // ---- write the tile back (in place): one TMA store, or coalesced stores.
-    if (PASS != kReduce) {
-      if (tma) {
-        fence_proxy_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-          tma_store_2d(&W.tmap, static_cast<int>(tile_off(c0)), row0, sC + stage * kStageB);
-          bulk_commit();
         }
-      } else {
-        __syncthreads();
-        store_codes(tile, stage);
-      }
-    }
-    tc_fence_before();
-    __syncthreads();
-  }
+        // Accumulator drained: hand it back to the tensor core.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aempty[ab]);
 
-  // ---- REDUCE: publish this item's running maxima.
-  if constexpr (PASS == kReduce) {
-    if constexpr (FMT == PIPER_FMT_NVFP4) {
-      const float m = warp_max(red_max);
-      if ((threadIdx.x & 31) == 0) atomic_max_nonneg(W.qmax, m);
-    } else {
-      if (W.nq_row == 0) {
-        const float m = warp_max(red_max);
-        const float n = warp_max(red_nmin);
-        if ((threadIdx.x & 31) == 0) {
-          atomic_max_nonneg(&W.qmax[0], m);
-          if (FMT == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[0], n);
+        // ---- write the tile back (in place) and release the stage.
+        if (PASS != kReduce && tma) {
+          fence_proxy_async_smem();
+          named_bar_sync(1, kEpiThreads);
+          if (e == 0) {
+            const int64_t off = code_off<FMT>(c0);
+            for (int j = 0; j < G::kBoxes; ++j) {
+              if (off + j * G::kBoxRow >= W.row_bytes) break;
+              const int x = static_cast<int>(off + j * G::kBoxRow);
+              tma_store_2d(&W.tmap, is_gguf<FMT>() ? x / 8 : x, g.row0, stage_codes(s) + j * 128 * G::kBoxRow);
+            }
+            bulk_commit();
+            if (pending >= 0) {
+              bulk_wait_read_1();
+              mbar_arrive(&empty[pending]);
+            }
+            pending = s;
+          }
+        } else {
+          named_bar_sync(1, kEpiThreads);
+          if (PASS != kReduce) {
+            // Coalesced write-back of the padded layout.
+            const int64_t off = code_off<FMT>(c0);
+            const int nbytes = static_cast<int>(code_off<FMT>(c0 + tcols) - off);
+            const int64_t m = W.row_bytes | off | nbytes | static_cast<int64_t>(reinterpret_cast<uintptr_t>(W.q));
+            const int gran = (m & 15) == 0 ? 16 : ((m & 3) == 0 ? 4 : 1);
+            const int per = nbytes / gran;
+            uint8_t* dst0 = W.q + static_cast<int64_t>(g.row0) * W.row_bytes + off;
+            const uint8_t* base = stage_codes(s);
+            for (int k = e; k < rows_here * per; k += kEpiThreads) {
+              const int r = k / per;
+              const int i = k - r * per;
+              const uint8_t* src = base + r * G::kPadRS + i * gran;
+              uint8_t* dst = dst0 + static_cast<int64_t>(r) * W.row_bytes + i * gran;
+              if (gran == 16) *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+              else if (gran == 4) *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(src);
+              else *dst = *src;
+            }
+            named_bar_sync(1, kEpiThreads);
+          }
+          if (e == 0) {
+            if (pending >= 0) {
+              bulk_wait_read_all();
+              mbar_arrive(&empty[pending]);
+              pending = -1;
+            }
+            mbar_arrive(&empty[s]);
+          }
         }
-      } else {
-        flush_reduce();
       }
-    }
-  }
 
-  // ---- NVFP4: zero swizzle padding columns and publish the new global scale.
-  if constexpr (FMT == PIPER_FMT_NVFP4 && PASS == kLocal) {
-    if ((W.flags & PIPER_FLAG_SWIZZLED) && col_end == W.N && wg == 0) {
-      const int padded = align_up(W.scale_cols, 4);
-      uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
-      for (int pc = W.scale_cols; pc < padded; ++pc) scale8[swizzled_index(row, pc, W.scale_cols)] = 0u;
-    }
-    if (two_level && local == 0 && threadIdx.x == 0) *W.gscale = g_out;
-  }
-  }  // item loop
-  cp_async_wait_all();
-  if (tid == 0) {
-    // Loads issued but never consumed (only after a timed-out wait): give them
-    // a bounded chance to land before shared memory is released.
-    for (int st = 0; st < kStages; ++st)
-      while (full_issued[st] > full_uses[st]) {
-        mbar_wait(&bar_full[st], full_uses[st] & 1u, kStatusTimeoutLoad);
-        ++full_uses[st];
+      // ---- REDUCE: publish this item's running maxima.
+      if constexpr (PASS == kReduce) {
+        if constexpr (FMT == PIPER_FMT_NVFP4) {
+          const float m = warp_max(red_max);
+          if (lane == 0) atomic_max_nonneg(W.qmax, m);
+        } else {
+          if (W.nq_row == 0) {
+            const float m = warp_max(red_max);
+            const float n = warp_max(red_nmin);
+            if (lane == 0) {
+              atomic_max_nonneg(&W.qmax[0], m);
+              if (FMT == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[0], n);
+            }
+          } else {
+            flush_reduce();
+          }
+        }
       }
-    bulk_wait_all();  // TMA stores complete before the CTA exits
+      // ---- NVFP4: zero swizzle padding columns and publish the new global scale.
+      if constexpr (FMT == PIPER_FMT_NVFP4 && PASS == kLocal) {
+        if ((W.flags & PIPER_FLAG_SWIZZLED) && g.col_end == W.N && wg == 0) {
+          const int padded = align_up(W.scale_cols, 4);
+          uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
+          for (int pc = W.scale_cols; pc < padded; ++pc) scale8[swizzled_index(row, pc, W.scale_cols)] = 0u;
+        }
+        if (two_level && local == 0 && e == 0) *W.gscale = g_out;
+      }
+    }
+    if (e == 0) bulk_wait_all();  // bulk stores complete before the CTA exits
   }
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x < 32) {
+  if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
+
 
 }  // namespace pm
 
@@ -1415,6 +1509,31 @@ using pm::LaunchParams;
 // Bytes of codes a two-pass launch group covers, so that its ENCODE launch
 // re-reads them from L2 (126 MB on B200).
 constexpr int64_t kL2GroupBytes = 48ll << 20;
+
+// Code bytes of `cols` columns (host mirror of code_bytes<FMT>).
+int host_code_bytes(int fmt, int cols) {
+  switch (fmt) {
+    case PIPER_FMT_MXFP4:
+    case PIPER_FMT_NVFP4: return cols / 2;
+    case PIPER_FMT_GGUF_Q8_0: return cols / 32 * 34;
+    case PIPER_FMT_GGUF_Q4_0: return cols / 32 * 18;
+    default: return cols;
+  }
+}
+
+// Shared-memory bytes of one stage's code slot (host mirror of TileGeom::kCodeSlot).
+int ws_code_slot(int fmt, int bn) {
+  const int rb = host_code_bytes(fmt, bn);
+  const int rs = pm::align_up(rb, 16) + 16;
+  return pm::align_up(128 * std::max(rs, rb), 1024);
+}
+
+// Pipeline stages that fit in the per-CTA shared-memory limit.
+int ws_stages(int fmt, int bn, int kp) {
+  const int stage = pm::ws_stage_bytes(ws_code_slot(fmt, bn), kp, bn);
+  const int fixed = pm::ws_smem_bytes(0, 0, kp);
+  return std::min(pm::kMaxStages, (pm::kSmemLimit - fixed) / stage);
+}
 
 struct Plan {
   int bn = 128;
@@ -1495,7 +1614,7 @@ int validate(const piper_merge_desc& d, Plan& p) {
         p.group = g;
         p.nq_row = static_cast<int>(d.cols / g);
         if (g < d.cols && (g == 32 || g == 64 || g == 128 || g == 256)) {
-          p.bn = g <= 128 ? 128 : 256;
+          // groups are local to a tile: encoded in one pass
         } else {
           p.two_pass = true;
           p.nq = static_cast<int>(d.rows * p.nq_row);
@@ -1506,19 +1625,22 @@ int validate(const piper_merge_desc& d, Plan& p) {
     case PIPER_FMT_GGUF_Q8_0:
     case PIPER_FMT_GGUF_Q4_0:
       if (d.cols % 32 != 0) return fail(PIPER_MERGE_EINVAL, "GGUF merge requires columns divisible by 32.");
-      p.bn = 256;
       break;
     default:
       return fail(PIPER_MERGE_EINVAL, "unknown format id " + std::to_string(d.format) + ".");
   }
-  // 256-column tiles need 768 * KP bytes of operand staging; above rank 192
-  // they would not fit in 227 KB of shared memory, so use 128-column tiles.
-  if (p.bn == 256 && pm::align_up(static_cast<int>(d.rank), 16) > 192) {
-    p.bn = 128;
-    if (d.format == PIPER_FMT_FP8_E4M3 || d.format == PIPER_FMT_FP8_E5M2 || d.format == PIPER_FMT_INT8) {
-      p.two_pass = true;  // a 256-wide group no longer fits one tile
-      p.nq = static_cast<int>(d.rows * p.nq_row);
-    }
+  // The widest tile (256, 128 or 64 columns) whose pipeline keeps three
+  // stages of (codes, A tile, scales) next to two B strips; 64-column tiles
+  // (large ranks) may run with two.
+  const int kp = pm::align_up(static_cast<int>(d.rank), 16);
+  if (ws_stages(d.format, 256, kp) >= 3) p.bn = 256;
+  else if (ws_stages(d.format, 128, kp) >= 3) p.bn = 128;
+  else if (ws_stages(d.format, 64, kp) >= 2) p.bn = 64;
+  else return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(d.rank) + " is too large for the merge pipeline.");
+  if ((d.format == PIPER_FMT_FP8_E4M3 || d.format == PIPER_FMT_FP8_E5M2 || d.format == PIPER_FMT_INT8) &&
+      !p.two_pass && p.group > p.bn) {
+    p.two_pass = true;  // the group no longer fits one tile
+    p.nq = static_cast<int>(d.rows * p.nq_row);
   }
   return PIPER_MERGE_OK;
 }
@@ -1536,44 +1658,30 @@ int sm_count() {
 }
 
 // ------------------------------------------------------------- dispatch
-// Each CTA allocates BN tensor-memory columns of the SM's 512. Request enough
-// shared memory that at most 512 / BN CTAs can be resident on one SM, so a
-// tcgen05.alloc never has to wait for another CTA to release its columns.
-constexpr int kSmemPerSm = 233472;      // 228 KB
-constexpr int kSmemReservedPerCta = 1024;
-constexpr int min_smem_for_tmem(int bn) {
-  return kSmemPerSm / (512 / bn + 1) - kSmemReservedPerCta + 16;
-}
+// One CTA per SM: the kernel allocates 2 * BN of the SM's 512 tensor-memory
+// columns, and the shared-memory request (at least half the SM's) keeps a
+// second CTA off the SM so a tcgen05.alloc never waits on another CTA.
+constexpr int kMinSmem = 120 * 1024;
 
 template <int FMT, int PASS, int BN, int CDT>
 int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
   auto kern = pm::merge_kernel<FMT, PASS, BN, CDT>;
-  const int smem = std::max(pm::smem_bytes<FMT, BN>(kp_max), min_smem_for_tmem(BN));
+  const int stages = ws_stages(FMT, BN, kp_max);
+  if (stages < 2)
+    return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(kp_max) + " does not fit the shared-memory pipeline.");
+  const int stage_bytes = pm::ws_stage_bytes(pm::TileGeom<FMT, BN>::kCodeSlot, kp_max, BN);
+  const int smem = std::max(pm::ws_smem_bytes(stage_bytes, stages, kp_max), kMinSmem);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess)
     return fail(PIPER_MERGE_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   lp.n_items = items;
   lp.kp_max = kp_max;
-  // Resident CTAs per SM from registers and shared memory (tensor-memory
-  // columns are bounded by the shared-memory request above). The carveout is
-  // set to maximum shared memory so that several CTAs fit per SM.
-  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-  int occ = 1;
-  {
-    cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess && fa.numRegs > 0) {
-      const int regs_per_warp = ((fa.numRegs * 32 + 255) / 256) * 256;
-      const int by_regs = 65536 / (regs_per_warp * (pm::kThreads / 32));
-      const int by_smem = kSmemPerSm / (smem + kSmemReservedPerCta);
-      occ = std::max(1, std::min(by_regs, by_smem));
-    }
-    cudaGetLastError();
-  }
-  const int grid = std::min(items, occ * sm_count());
+  lp.stages = stages;
+  const int grid = std::min(items, sm_count());
   if (std::getenv("PIPER_MERGE_DEBUG") != nullptr)
-    std::fprintf(stderr, "[piper-merge] fmt=%d pass=%d bn=%d smem=%d occ=%d items=%d grid=%d\n", FMT, PASS, BN,
-                 smem, occ, items, grid);
-  kern<<<grid, pm::kThreads, smem, stream>>>(lp);
+    std::fprintf(stderr, "[piper-merge] fmt=%d pass=%d bn=%d kp=%d stages=%d smem=%d items=%d grid=%d\n", FMT, PASS,
+                 BN, kp_max, stages, smem, items, grid);
+  kern<<<grid, pm::kWsThreads, smem, stream>>>(lp);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
@@ -1582,16 +1690,9 @@ int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
 
 template <int FMT, int PASS, int CDT>
 int launch_bn(int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
-  if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
-    if (bn == 128) return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
-    return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
-  } else if constexpr (FMT == PIPER_FMT_FP8_E4M3 || FMT == PIPER_FMT_FP8_E5M2 || FMT == PIPER_FMT_INT8) {
-    if (PASS == pm::kLocal && bn == 256) return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
-    return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
-  } else {
-    (void)bn;
-    return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
-  }
+  if (bn == 256) return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
+  if (bn == 128) return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
+  return launch_t<FMT, PASS, 64, CDT>(lp, items, kp, s);
 }
 
 template <int PASS, int CDT>
@@ -1661,26 +1762,42 @@ int64_t row_bytes_of(const piper_merge_desc& d);
 // Code tiles of `bn` columns move by 2-D bulk tensor copies when a row of the
 // tile is 64 or 128 bytes (so the 64 B / 128 B swizzle spans it) and rows are
 // 16-byte aligned; otherwise by cp.async.
+// Tensor map of the code bytes for bulk tensor tiles of 128 rows x bn columns:
+// boxes of min(128, tile row) bytes with the matching smem swizzle (a 16-byte
+// chunk XOR of 128 / 64 / 32-byte rows), or for GGUF one dense box of the
+// whole tile row in 8-byte elements. Requires 16-byte aligned rows and base.
 void setup_tma(DevWeight& w, const piper_merge_desc& d, int bn) {
   w.use_tma = 0;
-  if (d.format == PIPER_FMT_GGUF_Q8_0 || d.format == PIPER_FMT_GGUF_Q4_0) return;
-  const int tile_row = (d.format == PIPER_FMT_MXFP4 || d.format == PIPER_FMT_NVFP4) ? bn / 2 : bn;
-  if (tile_row != 64 && tile_row != 128) return;
+  const bool gguf = d.format == PIPER_FMT_GGUF_Q8_0 || d.format == PIPER_FMT_GGUF_Q4_0;
+  const int tile_row = host_code_bytes(d.format, bn);
+  const int box_row = gguf ? tile_row : std::min(128, tile_row);
+  if (gguf ? (tile_row % 16 != 0 || tile_row / 8 > 256) : (box_row != 32 && box_row != 64 && box_row != 128))
+    return;
   const int64_t rb = row_bytes_of(d);
   if ((rb & 15) != 0 || (reinterpret_cast<uintptr_t>(d.qdata) & 15) != 0) return;
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rb), static_cast<cuuint64_t>(d.rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(rb)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(tile_row), 128u};
-  const cuuint32_t estr[2] = {1u, 1u};
-  const CUtensorMapSwizzle sw = tile_row == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  CUresult r = enc(&w.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, d.qdata, dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (gguf) {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rb / 8), static_cast<cuuint64_t>(d.rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(rb)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_row / 8), 128u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    r = enc(&w.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, d.qdata, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rb), static_cast<cuuint64_t>(d.rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(rb)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_row), 128u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    const CUtensorMapSwizzle sw = box_row == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : (box_row == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+    r = enc(&w.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, d.qdata, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) return;
   w.use_tma = 1;
-  w.swz = tile_row == 128 ? 2 : 1;
 }
 
 DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws, const Segment& seg) {
@@ -1730,14 +1847,14 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
   std::memset(&lp, 0, sizeof(lp));
   lp.n_weights = static_cast<int>(segs.size());
   // Work items: (128-row strip, column range) pairs. Persistent CTAs stride
-  // over them; aim for ~12 items per SM so the last wave is short.
+  // over them; aim for ~32 items per SM so the last wave is short.
   int kp_max = 16;
   int64_t total_tiles = 0;
   for (const Segment& sg : segs) {
     const Plan& p = plans[sg.desc];
     total_tiles += static_cast<int64_t>((sg.rows + 127) / 128) * ((descs[sg.desc].cols + p.bn - 1) / p.bn);
   }
-  const int64_t target_items = 12ll * sm_count();
+  const int64_t target_items = 32ll * sm_count();
   const int tiles_per_item = static_cast<int>(std::max<int64_t>(1, total_tiles / target_items));
   int items = 0;
   for (size_t i = 0; i < segs.size(); ++i) {

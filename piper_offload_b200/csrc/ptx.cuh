@@ -239,18 +239,35 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
 }  // namespace pm
 
 namespace pm {
-// 4-D tile load (used to land factor tiles directly in the UMMA canonical
-// core-matrix layout).
-__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, int c0, int c1, int c2, int c3,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
-      "%5}], [%6];" ::"r"(smem_u32(smem_dst)),
-      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
-      : "memory");
+// One arrival on `bar` once every cp.async this thread issued before has
+// landed; the arrival is one of the barrier's expected arrivals (.noinc).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// Commit this thread's prior tcgen05.mma to an mbarrier (one arrival).
-__device__ __forceinline__ void mbar_arrive_count(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+
+// Barrier among `count` threads (a multiple of 32) on hardware barrier `id`.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Barrier among `count` threads on hardware barrier `id` that also returns the
+// AND of every participant's `v` (the same value in all of them).
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t count, bool v) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(count)
+      : "memory");
+  return out != 0u;
+}
+
+// Wait until all but the newest committed bulk store of this thread have
+// finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 }  // namespace pm
