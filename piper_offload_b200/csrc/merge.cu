@@ -55,6 +55,8 @@ enum Pass : int { kLocal = 0, kReduce = 1, kEncode = 2 };
 // Device-side descriptor of one weight (or a row range of one weight).
 struct alignas(64) DevWeight {
   CUtensorMap tmap;    // 2-D map of the code bytes (rows x row_bytes), valid when use_tma
+  CUtensorMap tmap_a;  // A factor (r x N), boxes of 64 columns x KP rows, 128-byte swizzle
+  CUtensorMap tmap_b;  // B factor (M x r), boxes of kb_row bytes x 128 rows, matching swizzle
   uint8_t* q;
   void* scale;
   int8_t* zp;
@@ -82,6 +84,8 @@ struct alignas(64) DevWeight {
   int scale_mode;      // MX E8M0 rounding
   int scale_dt;        // INT8 scale dtype
   int use_tma;         // code tiles move by bulk tensor copies (swizzled rows)
+  int use_tma_a;       // A tiles by bulk tensor copies (else cp.async into the same layout)
+  int use_tma_b;       // B strips by bulk tensor copies (else cp.async into the same layout)
 };
 
 struct LaunchParams {
@@ -616,10 +620,39 @@ __device__ __forceinline__ void fp8_encode_rtn(const float (&m)[32], float s, fl
   for (int w = 0; w < 8; ++w) out[w] = enc_fp8x4<E4M3>(q[4 * w], q[4 * w + 1], q[4 * w + 2], q[4 * w + 3]);
 }
 
+// Quantization parameters of the quantization block a thread is working in,
+// kept in registers while consecutive chunks stay in that block (per-row and
+// per-tensor layouts: for the whole work item), so the workspace and scale
+// loads are issued once per block rather than once per 32 columns.
+struct QpCache {
+  int qp = -1;
+  float s_in = 1.0f;   // input scale (ENCODE: saved by the REDUCE pass)
+  int z_in = 0;        // input zero point
+  float qmax = 0.0f;   // ENCODE: reduced max(|x|) or max(x, 0)
+  float nmin = 0.0f;   // ENCODE (INT8): reduced -min(x, 0)
+};
+
+template <int FMT, int PASS>
+__device__ __forceinline__ void qp_load(const DevWeight& W, int qp, QpCache& q) {
+  if (q.qp == qp) return;
+  q.qp = qp;
+  if (PASS == kEncode) {
+    q.s_in = W.old_scale[qp];
+    q.z_in = W.old_zp[qp];
+    q.qmax = __uint_as_float(W.qmax[qp]);
+    if (FMT == PIPER_FMT_INT8) q.nmin = __uint_as_float(W.qmin[qp]);
+  } else if (FMT == PIPER_FMT_INT8) {
+    q.s_in = load_scale_dt(W.scale, qp, W.scale_dt);
+    q.z_in = W.zp != nullptr ? static_cast<int>(W.zp[qp]) : 0;
+  } else {
+    q.s_in = reinterpret_cast<const float*>(W.scale)[qp];
+  }
+}
+
 // Input scale / zero point of each column of a chunk.
 template <int FMT, int PASS>
 __device__ __forceinline__ void affine_inputs(const DevWeight& W, const RowCtx& c, int col,
-                                              float (&scale_in)[32], int (&zp_in)[32]) {
+                                              float (&scale_in)[32], int (&zp_in)[32], QpCache& qc) {
   if (!c.valid) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -630,22 +663,11 @@ __device__ __forceinline__ void affine_inputs(const DevWeight& W, const RowCtx& 
   }
   const bool uniform = W.nq_row == 0 || W.group >= 32;
   if (uniform && (W.nq_row == 0 || (col % W.group) + 32 <= W.group)) {
-    const int qp = qparam_index(W, c.row, col);
-    float s;
-    int z = 0;
-    if (PASS == kEncode) {
-      s = W.old_scale[qp];
-      z = W.old_zp[qp];
-    } else if (FMT == PIPER_FMT_INT8) {
-      s = c.valid ? load_scale_dt(W.scale, qp, W.scale_dt) : 1.0f;
-      z = (W.zp != nullptr && c.valid) ? static_cast<int>(W.zp[qp]) : 0;
-    } else {
-      s = c.valid ? reinterpret_cast<const float*>(W.scale)[qp] : 1.0f;
-    }
+    qp_load<FMT, PASS>(W, qparam_index(W, c.row, col), qc);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      scale_in[i] = s;
-      zp_in[i] = z;
+      scale_in[i] = qc.s_in;
+      zp_in[i] = qc.z_in;
     }
     return;
   }
@@ -772,6 +794,9 @@ constexpr int kWsThreads = 384;
 constexpr int kEpiThreads = 256;
 constexpr int kLoadThreads = 64;  // warps 2-3
 constexpr int kMaxStages = 6;
+constexpr uint32_t kCtrlRegs = 56;
+constexpr uint32_t kEpiRegs = 224;
+static_assert(128 * kCtrlRegs + kEpiThreads * kEpiRegs <= kWsThreads * 168, "register split exceeds the launch");
 constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 
 template <int FMT>
@@ -830,6 +855,20 @@ __device__ __forceinline__ int64_t code_off(int c0) {
   else return c0;
 }
 
+// Row bytes of the B strip's swizzle atoms (K-major): the widest of 128 / 64 /
+// 32 bytes dividing KP * 2, so a strip is KP*2 / kb boxes of 128 rows x kb bytes.
+__host__ __device__ __forceinline__ int kb_row(int kp) {
+  return (kp * 2) % 128 == 0 ? 128 : ((kp * 2) % 64 == 0 ? 64 : 32);
+}
+__host__ __device__ __forceinline__ uint32_t swizzle_layout(int row_bytes) {
+  return row_bytes == 128 ? 2u : (row_bytes == 64 ? 4u : 6u);
+}
+// 16-byte chunk XOR of row r under the swizzle of `row_bytes`-byte rows.
+__device__ __forceinline__ uint32_t swizzle_xor(int r, int row_bytes) {
+  return row_bytes == 128 ? static_cast<uint32_t>(r & 7)
+                          : (row_bytes == 64 ? static_cast<uint32_t>((r >> 1) & 3) : static_cast<uint32_t>((r >> 2) & 1));
+}
+
 template <int FMT, int PASS, int BN, int CDT>
 __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_constant__ LaunchParams P) {
   using G = TileGeom<FMT, BN>;
@@ -863,7 +902,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bfull[i], kLoadThreads);
+      mbar_init(&bfull[i], 1 + kLoadThreads);
       mbar_init(&bempty[i], 1);
       mbar_init(&afull[i], 1);
       mbar_init(&aempty[i], kEpiThreads / 32);
@@ -879,36 +918,61 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  // Launch allocation 384 x 168 = 64512 registers: the control warpgroup
+  // (warps 0-3) keeps 56 per thread, the two epilogue warpgroups get 224
+  // (128 x 56 + 256 x 224 = 64512), which buys the epilogue more independent
+  // work in flight per thread.
+  if (warp < 4) {
+  regs_dec<kCtrlRegs>();
   if (warp == 0) {
     // ------------------------------------------------ code tiles (bulk tensor)
     if (lane == 0) {
-      uint32_t t = 0;
+      uint32_t t = 0, it = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x) {
+      for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x, ++it) {
         const ItemGeom g = item_geom<BN>(P, item);
         const DevWeight& W = P.w[g.wi];
+        const int KP = W.KP;
         if (W.use_tma) prefetch_tmap(&W.tmap);
+        // B strip of this item: KP*2 / kb boxes of 128 rows x kb bytes.
+        const int jb = it & 1;
+        if (it >= 2) {
+          ok = mbar_wait(&bempty[jb], ((it >> 1) - 1) & 1u, kStatusTimeoutMma);
+          if (!ok) break;
+        }
+        if (W.use_tma_b) {
+          const int kb = kb_row(KP);
+          const int nbox = KP * 2 / kb;
+          uint8_t* sBj = sB + jb * 128 * KPL * 2;
+          mbar_arrive_expect_tx(&bfull[jb], static_cast<uint32_t>(nbox * 128 * kb));
+          for (int j = 0; j < nbox; ++j) tma_load_2d(sBj + j * 128 * kb, &W.tmap_b, j * (kb / 2), g.row0, &bfull[jb]);
+        } else {
+          mbar_arrive(&bfull[jb]);
+        }
         for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
           const int s = t % S;
           if (t >= static_cast<uint32_t>(S)) {
             ok = mbar_wait(&empty[s], ((t / S) - 1) & 1u, kStatusTimeoutLoad);
             if (!ok) break;
           }
-          if (W.use_tma) {
-            const int c0 = g.col_begin + tile * BN;
-            const int64_t off = code_off<FMT>(c0);
-            int boxes = 0;
+          const int c0 = g.col_begin + tile * BN;
+          int boxes = 0;
+          const int64_t off = code_off<FMT>(c0);
+          if (W.use_tma)
             for (int j = 0; j < G::kBoxes; ++j) boxes += (off + j * G::kBoxRow < W.row_bytes) ? 1 : 0;
-            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(boxes * 128 * G::kBoxRow));
-            for (int j = 0; j < boxes; ++j) {
-              const int x = static_cast<int>(off + j * G::kBoxRow);
-              tma_load_2d(stage_codes(s) + j * 128 * G::kBoxRow, &W.tmap, is_gguf<FMT>() ? x / 8 : x, g.row0,
-                          &full[s]);
-            }
-          } else {
-            mbar_arrive(&full[s]);
+          const uint32_t a_bytes = W.use_tma_a ? static_cast<uint32_t>(BN * KP * 2) : 0u;
+          const uint32_t tx = static_cast<uint32_t>(boxes * 128 * G::kBoxRow) + a_bytes;
+          if (tx != 0u) mbar_arrive_expect_tx(&full[s], tx);
+          else mbar_arrive(&full[s]);
+          for (int j = 0; j < boxes; ++j) {
+            const int x = static_cast<int>(off + j * G::kBoxRow);
+            tma_load_2d(stage_codes(s) + j * 128 * G::kBoxRow, &W.tmap, is_gguf<FMT>() ? x / 8 : x, g.row0,
+                        &full[s]);
           }
+          // A tile: BN/64 boxes of 64 columns x KP rows (MN-major, 128-byte swizzle).
+          if (W.use_tma_a)
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(stage_a(s) + j * KP * 128, &W.tmap_a, c0 + j * 64, 0, &full[s]);
         }
       }
       // Loads still in flight after an early exit land before the CTA retires.
@@ -930,6 +994,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
         ok = mbar_wait(&bfull[jb], (it >> 1) & 1u, kStatusTimeoutLoad);
         if (!ok) break;
         const uint32_t a_base = smem_u32(sB + jb * 128 * KPL * 2);
+        const int kb = kb_row(KP);
+        const uint32_t a_layout = swizzle_layout(kb);
         for (int tile = 0; tile < g.n_tiles && ok; ++tile, ++t) {
           const int s = t % S;
           const int ab = t & 1;
@@ -940,8 +1006,12 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
           tc_fence_after();
           const uint32_t b_base = smem_u32(stage_a(s));
           for (int ks = 0; ks < KP / 16; ++ks) {
-            const uint64_t adesc = smem_desc(a_base + ks * 2 * 2048, 2048, 128);
-            const uint64_t bdesc = smem_desc(b_base + ks * 2 * (BN * 16), BN * 16, 128);
+            // B strip, K-major: 16 columns = 32 bytes inside a kb-byte swizzled row.
+            const int kbyte = ks * 32;
+            const uint64_t adesc =
+                smem_desc_sw(a_base + (kbyte / kb) * 128 * kb + (kbyte % kb), 16, 8 * kb, a_layout);
+            // A tile, MN-major: 64-column blocks KP*128 bytes apart, 8-row groups 1024 apart.
+            const uint64_t bdesc = smem_desc_sw(b_base + ks * 2048, KP * 128, 1024, 2u);
             umma_f16(tmem + ab * BN, adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
           }
           umma_commit(&afull[ab]);
@@ -968,14 +1038,18 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
         ok = mbar_wait(&bempty[jb], ((it >> 1) - 1) & 1u, kStatusTimeoutMma);
         if (!ok) break;
       }
-      {
+      if (!W.use_tma_b) {
+        // Same swizzled K-major layout the bulk tensor copy would produce.
         uint8_t* sBj = sB + jb * 128 * KPL * 2;
+        const int kb = kb_row(KP);
+        const int cpr = kb / 16;  // 16-byte chunks per row
         const bool vec = ((reinterpret_cast<uintptr_t>(W.b) | (W.r * 2)) & 15) == 0;
         for (int idx = lt; idx < 128 * (KP / 8); idx += kLoadThreads) {
           const int rt = idx & 127;
           const int kc = idx >> 7;
           const int row = g.row0 + rt;
-          uint8_t* dst = sBj + kc * 2048 + (rt >> 3) * 128 + (rt & 7) * 16;
+          uint8_t* dst = sBj + (kc / cpr) * 128 * kb + rt * kb +
+                         (((static_cast<uint32_t>(kc % cpr)) ^ swizzle_xor(rt, kb)) << 4);
           const uint16_t* brow = W.b + static_cast<int64_t>(row) * W.r;
           if (row < W.M && vec && kc * 8 + 8 <= W.r) {
             cp_async16(dst, brow + kc * 8);
@@ -990,9 +1064,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
             *reinterpret_cast<uint4*>(dst) = v;
           }
         }
-        __threadfence_block();  // plain smem stores of ragged rows precede the arrival
-        cp_async_mbar_arrive(&bfull[jb]);
       }
+      __threadfence_block();  // plain smem stores of ragged rows precede the arrival
+      cp_async_mbar_arrive(&bfull[jb]);
       const bool vec_a = ((reinterpret_cast<uintptr_t>(W.a) | (W.N * 2)) & 15) == 0;
       for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
         const int s = t % S;
@@ -1041,17 +1115,16 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
             }
           }
         }
-        // A tile (MN-major canonical): element (k, n) at (k/8)*(BN*16) + (n/8)*128 + (k%8)*16 + (n%8)*2.
-        {
+        // A tile when it cannot move by bulk tensor copies: the same MN-major
+        // layout, 64-column blocks of KP rows x 128 bytes, 128-byte swizzle.
+        if (!W.use_tma_a) {
           uint8_t* sA = stage_a(s);
           const int chunks = KP * BN / 8;
           for (int idx = lt; idx < chunks; idx += kLoadThreads) {
-            const int kk = idx & 7;
-            const int ng = (idx >> 3) % (BN / 8);
-            const int kg = idx / BN;
-            const int kr = kg * 8 + kk;
+            const int ng = idx % (BN / 8);
+            const int kr = idx / (BN / 8);
             const int n = c0 + ng * 8;
-            uint8_t* dst = sA + kg * (BN * 16) + ng * 128 + kk * 16;
+            uint8_t* dst = sA + (ng >> 3) * KP * 128 + kr * 128 + (((static_cast<uint32_t>(ng & 7)) ^ (kr & 7)) << 4);
             const uint16_t* ap = W.a + static_cast<int64_t>(kr) * W.N + n;
             if (kr < W.r && vec_a && n + 8 <= g.col_end) {
               cp_async16(dst, ap);
@@ -1072,8 +1145,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
       }
     }
     cp_async_wait_all();
+  }
   } else {
     // ---------------------------------------------------------------- epilogue
+    regs_inc<kEpiRegs>();
     const int e = tid - 128;
     const int rt = e & 127;         // tile row / tensor-memory lane of this thread
     const int wg = e >> 7;          // takes every other accumulator chunk
@@ -1090,6 +1165,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
       const int rows_here = min(128, W.M - g.row0);
       const bool tma = W.use_tma != 0;
 
+      QpCache qc;  // quantization block of this thread's row (FP8 / INT8)
       // Per-thread running reductions for REDUCE passes.
       float red_max = 0.0f, red_nmin = 0.0f;
       int red_qp = -1;
@@ -1129,6 +1205,20 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
         if (!ok) break;
         tc_fence_after();
         const uint32_t taddr = tmem + lane_off + ab * BN;
+        // Chunks kbeg, kbeg+2, ... < kend of the accumulator, each loaded from
+        // tensor memory while the previous one is being processed.
+        auto chunk_loop = [&](int kbeg, int kend, auto&& body) {
+          uint32_t cur[32];
+          if (kbeg < kend) tmem_ld32_async(taddr + 32 * kbeg, cur);
+          for (int k = kbeg; k < kend; k += 2) {
+            tmem_ld_wait(cur);
+            float acc[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(cur[i]);
+            if (k + 2 < kend) tmem_ld32_async(taddr + 32 * (k + 2), cur);
+            body(k, acc);
+          }
+        };
 
         RowCtx c;
         c.row = row;
@@ -1153,17 +1243,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
         {
       if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 ||
                     FMT == PIPER_FMT_MXFP4) {
-        for (int k = wg; k < tcols / 32; k += 2) {
-          float acc[32];
-          tmem_ld32(taddr + 32 * k, acc);
-          mx_chunk<FMT, CDT>(W, c, k, acc);
-        }
+        chunk_loop(wg, tcols / 32, [&](int k, const float (&acc)[32]) { mx_chunk<FMT, CDT>(W, c, k, acc); });
       } else if constexpr (FMT == PIPER_FMT_NVFP4) {
-        for (int k = wg; k < tcols / 32; k += 2) {
-          float acc[32];
-          tmem_ld32(taddr + 32 * k, acc);
+        chunk_loop(wg, tcols / 32, [&](int k, const float (&acc)[32]) {
           nvfp4_chunk<PASS, CDT>(W, c, k, acc, g_in, g_out, two_level, red_max);
-        }
+        });
         if ((tcols & 31) && ((tcols / 32) & 1) == wg) {  // trailing 16-column block
           float acc[32];
           const int k = tcols / 32;
@@ -1173,11 +1257,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
           if (PASS != kReduce) *reinterpret_cast<uint2*>(chunk_ptr(c, k)) = codes;
         }
       } else if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
-        for (int k = wg; k < tcols / 32; k += 2) {
-          float acc[32];
-          tmem_ld32(taddr + 32 * k, acc);
-          gguf_chunk<FMT, CDT>(W, c, k, acc);
-        }
+        chunk_loop(wg, tcols / 32, [&](int k, const float (&acc)[32]) { gguf_chunk<FMT, CDT>(W, c, k, acc); });
       } else {
         // ------------------------------------------- FP8 / INT8 (affine) paths
         constexpr bool kInt8 = FMT == PIPER_FMT_INT8;
@@ -1198,7 +1278,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
             for (int k = g0; k < g0 + gch; ++k) {
               float acc[32], merged[32];
               tmem_ld32(taddr + 32 * k, acc);
-              affine_inputs<FMT, PASS>(W, c, c0 + 32 * k, scale_in, zp_in);
+              affine_inputs<FMT, PASS>(W, c, c0 + 32 * k, scale_in, zp_in, qc);
               affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
@@ -1251,12 +1331,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
             }
           }
         } else {
-          for (int k = wg; k < nchunks; k += 2) {
-            float acc[32], merged[32], scale_in[32];
+          chunk_loop(wg, nchunks, [&](int k, const float (&acc)[32]) {
+            float merged[32], scale_in[32];
             int zp_in[32];
-            tmem_ld32(taddr + 32 * k, acc);
             const int col = c0 + 32 * k;
-            affine_inputs<FMT, PASS>(W, c, col, scale_in, zp_in);
+            affine_inputs<FMT, PASS>(W, c, col, scale_in, zp_in, qc);
             affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
             const int nvalid = min(32, tcols - 32 * k);
             if constexpr (PASS == kReduce) {
@@ -1323,11 +1402,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
               if (valid && uniform_chunk) {
                 // One quantization block covers the whole chunk (per-row / per-tensor).
                 const int qp = qparam_index(W, row, col);
-                const float qmx = __uint_as_float(W.qmax[qp]);
+                qp_load<FMT, PASS>(W, qp, qc);
+                const float qmx = qc.qmax;
                 const bool owner = W.nq_row == 0 ? (row == 0 && col == 0) : (col % W.group == 0);
                 if constexpr (kInt8) {
-                  const Int8Q q = int8_qparams<CDT>(-__uint_as_float(W.qmin[qp]), qmx, asym, qmin, qmax,
-                                                    W.scale_dt);
+                  const Int8Q q = int8_qparams<CDT>(-qc.nmin, qmx, asym, qmin, qmax, W.scale_dt);
                   if (owner) {
                     store_scale_dt(W.scale, qp, W.scale_dt, q.scale);
                     if (W.zp != nullptr) W.zp[qp] = static_cast<int8_t>(q.zp);
@@ -1389,7 +1468,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
               }
               store_chunks32(c, k, out);
             }
-          }
+          });
         }
       }
         }
@@ -1800,6 +1879,41 @@ void setup_tma(DevWeight& w, const piper_merge_desc& d, int bn) {
   w.use_tma = 1;
 }
 
+// Tensor maps of the LoRA factors for bulk tensor tiles in the swizzled UMMA
+// layouts: A (r x N, row-major) in boxes of 64 columns x KP rows with 128-byte
+// swizzle (MN-major operand); B (M x r, row-major) in boxes of kb_row(KP)
+// bytes x 128 rows with the matching swizzle (K-major operand). Rows past r
+// and columns past N read as zeros. Requires 16-byte aligned bases and row
+// pitches; otherwise the loader warps copy the same layouts with cp.async.
+void setup_tma_factors(DevWeight& w, const piper_merge_desc& d, int kp) {
+  w.use_tma_a = 0;
+  w.use_tma_b = 0;
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return;
+  const cuuint32_t estr[2] = {1u, 1u};
+  if ((d.cols * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(d.a) & 15) == 0 && d.cols >= 64) {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.cols), static_cast<cuuint64_t>(d.rank)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.cols * 2)};
+    const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(kp)};
+    if (enc(&w.tmap_a, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(d.a), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      w.use_tma_a = 1;
+  }
+  if ((d.rank * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(d.b) & 15) == 0) {
+    const int kb = pm::kb_row(kp);
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.rank), static_cast<cuuint64_t>(d.rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.rank * 2)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kb / 2), 128u};
+    const CUtensorMapSwizzle sw = kb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : (kb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+    if (enc(&w.tmap_b, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(d.b), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      w.use_tma_b = 1;
+  }
+}
+
 DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws, const Segment& seg) {
   DevWeight w;
   std::memset(&w, 0, sizeof(w));
@@ -1833,7 +1947,10 @@ DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws,
   w.scale_cols = d.format == PIPER_FMT_NVFP4 ? static_cast<int>(d.cols / 16) : static_cast<int>(d.cols / 32);
   w.scale_mode = d.scale_mode;
   w.scale_dt = d.scale_dtype;
-  if (std::getenv("PIPER_MERGE_NO_TMA") == nullptr) setup_tma(w, d, p.bn);
+  if (std::getenv("PIPER_MERGE_NO_TMA") == nullptr) {
+    setup_tma(w, d, p.bn);
+    setup_tma_factors(w, d, w.KP);
+  }
   return w;
 }
 

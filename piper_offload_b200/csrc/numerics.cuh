@@ -139,25 +139,38 @@ __device__ __forceinline__ float philox_uniform(PhiloxKey key, uint64_t offset) 
 }
 
 // ------------------------------------------------- stochastic terminal codes
+// The helpers below are branch-free: the uniform draw is computed for every
+// element (almost all are interior), so the 32 Philox chains of a chunk are
+// independent instruction streams the scheduler can interleave.
+
+// 1 / g for a power of two g in the normal range (exact).
+__device__ __forceinline__ float recip_pow2(float g) {
+  return __uint_as_float((254u << 23) - __float_as_uint(g));
+}
+
 // _stochastic_float8 (_triton_stochastic_quantization.py:132-175): `v` is the
-// clamped, normalized value; returns the E4M3/E5M2 code.
+// clamped, normalized value; returns the E4M3/E5M2 code. Neighbouring codes of
+// one sign are a power-of-two gap apart, so `(m - lo) / (hi - lo)` is an
+// exact quotient, computed as a product with the exact reciprocal.
 template <bool E4M3>
 __device__ __forceinline__ uint32_t sr_fp8(float v, float limit, PhiloxKey key, uint64_t off) {
   const float mag = fabsf(v);
   const uint32_t det = enc_fp8<E4M3>(mag);
   const float det_v = dec_fp8<E4M3>(det);
   const bool down = det_v > mag;
-  const uint32_t lo = (down ? det - 1u : det) & 0xFFu;
-  const uint32_t hi = (down ? det : det + 1u) & 0xFFu;
-  const float lov = dec_fp8<E4M3>(lo);
-  const float hiv = dec_fp8<E4M3>(hi);
-  const float p = hiv > lov ? div_full(mag - lov, hiv - lov) : 0.0f;
+  const uint32_t other = (down ? det - 1u : det + 1u) & 0xFFu;
+  const float other_v = dec_fp8<E4M3>(other);
+  const uint32_t lo = down ? other : det;
+  const uint32_t hi = down ? det : other;
+  const float lov = down ? other_v : det_v;
+  const float hiv = down ? det_v : other_v;
+  const float gap = hiv - lov;
+  // A NaN / infinite upper neighbour only occurs at |v| >= limit (not interior).
+  const float p = (gap > 0.0f && gap < 1e30f) ? (mag - lov) * recip_pow2(gap) : 0.0f;
+  const float u = philox_uniform(key, off);
   const uint32_t sign = (__float_as_uint(v) >> 24) & 0x80u;
-  if (mag < limit && p > 0.0f) {
-    const float u = philox_uniform(key, off);
-    return (u < p ? hi : lo) | sign;
-  }
-  return det | sign;
+  const bool interior = mag < limit && p > 0.0f;
+  return (interior ? (u < p ? hi : lo) : det) | sign;
 }
 
 // _stochastic_e2m1_code (_triton_stochastic_quantization.py:109-129).
@@ -169,27 +182,22 @@ __device__ __forceinline__ uint32_t sr_e2m1(float v, uint32_t det, PhiloxKey key
   const uint32_t uc = down ? nc : nc + 1u;
   const float lv = e2m1_mag(lc);
   const float uv = e2m1_mag(uc);
-  const float p = uv > lv ? div_full(mag - lv, uv - lv) : 0.0f;
-  if (mag > 0.0f && mag < 6.0f && p > 0.0f) {
-    const float u = philox_uniform(key, off);
-    return (u < p ? uc : lc) | ((__float_as_uint(v) >> 28) & 8u);
-  }
-  return det;
+  const float gap = uv - lv;  // 0.5, 1 or 2 inside (0, 6); <= 0 past the top code
+  const float p = gap > 0.0f ? (mag - lv) * recip_pow2(gap) : 0.0f;
+  const float u = philox_uniform(key, off);
+  const bool interior = mag > 0.0f && mag < 6.0f && p > 0.0f;
+  return interior ? ((u < p ? uc : lc) | ((__float_as_uint(v) >> 28) & 8u)) : det;
 }
 
 // _stochastic_round_to_int (_triton_stochastic_quantization.py:24-39);
 // returns the (possibly) re-rounded value as a float.
 __device__ __forceinline__ float sr_int(float v, float det, float qmin, float qmax, PhiloxKey key,
                                         uint64_t off) {
-  if (v > qmin && v < qmax) {
-    const float lower = floorf(v);
-    const float p = __fsub_rn(v, lower);
-    if (p > 0.0f) {
-      const float u = philox_uniform(key, off);
-      return __fadd_rn(lower, u < p ? 1.0f : 0.0f);
-    }
-  }
-  return det;
+  const float lower = floorf(v);
+  const float p = __fsub_rn(v, lower);
+  const float u = philox_uniform(key, off);
+  const bool interior = v > qmin && v < qmax && p > 0.0f;
+  return interior ? __fadd_rn(lower, u < p ? 1.0f : 0.0f) : det;
 }
 
 }  // namespace pm
