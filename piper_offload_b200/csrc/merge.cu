@@ -92,8 +92,10 @@ struct LaunchParams {
   DevWeight w[kMaxWeights];
   int n_weights;
   int n_items;  // work items over all weights; CTAs stride over them
-  int kp_max;   // shared-memory layout is sized for the largest padded rank
-  int stages;   // depth of the (codes, A tile, scales) ring
+  int kp_max;    // shared-memory layout is sized for the largest padded rank
+  int c_stages;  // ring of (code tile, scale bytes) stages, freed after the write-back
+  int a_stages;  // ring of A tiles, freed when the tensor core has read them
+  int b_bufs;    // B strips (1 or 2)
 };
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -151,6 +153,47 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
   return v;
+}
+
+// Balanced-tree reductions over a chunk. fmaxf / fminf are exact, commutative
+// and associative (NaN operands are ignored, -0 orders below +0), so a tree
+// gives the same value as the sequential fold while its dependency depth is
+// log2(N) instead of N.
+template <int N>
+__device__ __forceinline__ float tree_max_abs(const float (&m)[N]) {
+  float t[N / 2];
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) t[i] = fmaxf(fabsf(m[2 * i]), fabsf(m[2 * i + 1]));
+#pragma unroll
+  for (int w = N / 4; w >= 1; w /= 2) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) t[i] = fmaxf(t[2 * i], t[2 * i + 1]);
+  }
+  return t[0];
+}
+template <int N>
+__device__ __forceinline__ float tree_max(const float (&m)[N]) {
+  float t[N / 2];
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) t[i] = fmaxf(m[2 * i], m[2 * i + 1]);
+#pragma unroll
+  for (int w = N / 4; w >= 1; w /= 2) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) t[i] = fmaxf(t[2 * i], t[2 * i + 1]);
+  }
+  return t[0];
+}
+template <int N>
+__device__ __forceinline__ float tree_min(const float (&m)[N]) {
+  float t[N / 2];
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) t[i] = fminf(m[2 * i], m[2 * i + 1]);
+#pragma unroll
+  for (int w = N / 4; w >= 1; w /= 2) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) t[i] = fminf(t[2 * i], t[2 * i + 1]);
+  }
+  return t[0];
 }
 
 // ------------------------------------------------------------ MX scales
@@ -317,9 +360,7 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
   for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], W.strength, merged[i]);
 #pragma unroll
   for (int i = 0; i < 32; i += 2) bf16r2(merged[i], merged[i + 1]);
-  float amax = fabsf(merged[0]);
-#pragma unroll
-  for (int i = 1; i < 32; ++i) amax = fmaxf(amax, fabsf(merged[i]));
+  const float amax = tree_max_abs(merged);
   const MxScale s = mx_scale(amax, W.scale_mode, P::kTarget, P::kMax, P::kMbits);
   const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
   const PhiloxKey key{W.k0, W.k1};
@@ -389,9 +430,7 @@ __device__ __forceinline__ void nvfp4_block(const DevWeight& W, const RowCtx& c,
   }
 #pragma unroll
   for (int i = 0; i < 16; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
-  float amax = fabsf(m[0]);
-#pragma unroll
-  for (int i = 1; i < 16; ++i) amax = fmaxf(amax, fabsf(m[i]));
+  const float amax = tree_max_abs(m);
   if constexpr (PASS == kReduce) {
     if (c.valid) amax_acc = fmaxf(amax_acc, amax);
   } else {
@@ -597,6 +636,38 @@ __device__ __forceinline__ void affine_merged(const DevWeight& W, const RowCtx& 
   for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
 }
 
+// affine_merged for a chunk inside one quantization block (one scale / zero point).
+template <int FMT, int CDT>
+__device__ __forceinline__ void affine_merged_u(const DevWeight& W, const RowCtx& c, int k,
+                                                const float (&acc)[32], float s_in, int z_in,
+                                                float (&merged)[32]) {
+  uint32_t wv[8];
+  load_chunks32(c, k, wv);
+  if constexpr (FMT == PIPER_FMT_INT8) {
+    const float zf = static_cast<float>(z_in);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
+      merged[i] = __fmul_rn(__fsub_rn(qv, zf), s_in);
+    }
+  } else {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      float f[4];
+      dec_fp8x4<FMT == PIPER_FMT_FP8_E4M3>(wv[w], f);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) merged[4 * w + j] = __fmul_rn(f[j], s_in);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+  const float st = W.strength;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], st, merged[i]);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+}
+
 // FP8 codes of 32 merged values for one scale `s` (round to nearest).
 // The reference quotient is div.full(x, s); x * RN(1/s) is used unless some
 // element lands within 4 ulp of an FP8 rounding boundary.
@@ -728,9 +799,7 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
   const uint64_t off0 =
       W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
   if constexpr (kQ8) {
-    float amax = fabsf(merged[0]);
-#pragma unroll
-    for (int i = 1; i < 32; ++i) amax = fmaxf(amax, fabsf(merged[i]));
+    const float amax = tree_max_abs(merged);
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
     const unsigned short dh = __half_as_ushort(__float2half_rn(d));
@@ -790,13 +859,32 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
 // accumulators through afull/aempty; B strips through bfull/bempty. Every
 // wait is bounded (ptx.cuh); a role whose wait gives up stops issuing work and
 // the others then give up in turn, so the CTA always reaches its exit.
-constexpr int kWsThreads = 384;
-constexpr int kEpiThreads = 256;
+// Epilogue warpgroups per format (tile t -> warpgroup t % EW). Three give the
+// epilogue more warps in flight; GGUF keeps two so that its 256-column tiles
+// (the narrowest whose rows are 16-byte multiples) fit two accumulators, and
+// NVFP4 keeps two for its register-heavy two-level blocks.
+template <int FMT>
+__host__ __device__ constexpr int epi_wgs() {
+  return (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0 || FMT == PIPER_FMT_NVFP4) ? 2 : 3;
+}
+__host__ __device__ constexpr int epi_wgs_rt(int fmt) {
+  return (fmt == PIPER_FMT_GGUF_Q8_0 || fmt == PIPER_FMT_GGUF_Q4_0 || fmt == PIPER_FMT_NVFP4) ? 2 : 3;
+}
+template <int FMT>
+__host__ __device__ constexpr int ws_threads() { return 128 * (1 + epi_wgs<FMT>()); }
 constexpr int kLoadThreads = 64;  // warps 2-3
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 8;    // code stages
+constexpr int kMaxAStages = 4;
+constexpr int kMaxAcc = 8;        // accumulator buffers: 512 tensor-memory columns / BN
 constexpr uint32_t kCtrlRegs = 56;
-constexpr uint32_t kEpiRegs = 224;
-static_assert(128 * kCtrlRegs + kEpiThreads * kEpiRegs <= kWsThreads * 168, "register split exceeds the launch");
+// Registers per epilogue thread after the control warpgroup gives up its share
+// (launch allocation: threads x (65536 / threads rounded down to 8)).
+template <int FMT>
+__host__ __device__ constexpr uint32_t epi_regs() {
+  constexpr uint32_t threads = ws_threads<FMT>();
+  constexpr uint32_t launch = (65536u / threads) / 8u * 8u;
+  return ((threads * launch - 128u * kCtrlRegs) / (128u * epi_wgs<FMT>())) / 8u * 8u;
+}
 constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 
 template <int FMT>
@@ -817,13 +905,15 @@ struct TileGeom {
   static constexpr int kCodeSlot = align_up(128 * (kPadRS > kRowBytes ? kPadRS : kRowBytes), 1024);
 };
 
-__host__ __device__ constexpr int ws_stage_bytes(int code_slot, int kp, int bn) {
-  return align_up(code_slot + kp * bn * 2 + 128 * kScaleSlot, 1024);
+// Shared memory: code stages, A stages, B strips, then the barriers and the
+// TMEM slot (+1 KB of alignment slack for the dynamic shared-memory base).
+__host__ __device__ constexpr int ws_code_stage_bytes(int code_slot) {
+  return align_up(code_slot + 128 * kScaleSlot, 1024);
 }
-// Stages, then two B strips, then the barriers and the TMEM slot (+1 KB of
-// alignment slack for the dynamic shared-memory base).
-__host__ __device__ constexpr int ws_smem_bytes(int stage_bytes, int stages, int kp) {
-  return 1024 + stages * stage_bytes + 2 * 128 * kp * 2 + 256;
+__host__ __device__ constexpr int ws_a_stage_bytes(int kp, int bn) { return align_up(kp * bn * 2, 1024); }
+__host__ __device__ constexpr int ws_b_buf_bytes(int kp) { return 128 * kp * 2; }
+__host__ __device__ constexpr int ws_smem_bytes(int code_slot, int kp, int bn, int sc, int sa, int nbb) {
+  return 1024 + sc * ws_code_stage_bytes(code_slot) + sa * ws_a_stage_bytes(kp, bn) + nbb * ws_b_buf_bytes(kp) + 512;
 }
 
 struct ItemGeom {
@@ -870,48 +960,64 @@ __device__ __forceinline__ uint32_t swizzle_xor(int r, int row_bytes) {
 }
 
 template <int FMT, int PASS, int BN, int CDT>
-__global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_constant__ LaunchParams P) {
+__global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __grid_constant__ LaunchParams P) {
+  constexpr int kEpiWGs = epi_wgs<FMT>();
   using G = TileGeom<FMT, BN>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int KPL = P.kp_max;
-  const int S = P.stages;
-  const int kStageB = ws_stage_bytes(G::kCodeSlot, KPL, BN);
+  const int S = P.c_stages;
+  const int SA = P.a_stages;
+  const int NBB = P.b_bufs;
+  constexpr int kCodeStage = ws_code_stage_bytes(G::kCodeSlot);
+  const int kAStage = ws_a_stage_bytes(KPL, BN);
 
   uint8_t* base1k = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);
-  uint8_t* sStage = base1k;
-  uint8_t* sB = sStage + S * kStageB;  // two B strips
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + 2 * 128 * KPL * 2);
-  uint64_t* full = bars;                  // [kMaxStages]
-  uint64_t* empty = full + kMaxStages;    // [kMaxStages]
-  uint64_t* bfull = empty + kMaxStages;   // [2]
+  uint8_t* sCode = base1k;
+  uint8_t* sAst = sCode + S * kCodeStage;
+  uint8_t* sB = sAst + SA * kAStage;  // NBB B strips
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + NBB * ws_b_buf_bytes(KPL));
+  uint64_t* full = bars;                  // [kMaxStages] code tile (+ scales) landed
+  uint64_t* empty = full + kMaxStages;    // [kMaxStages] code stage written back
+  uint64_t* full_a = empty + kMaxStages;  // [kMaxAStages] A tile landed
+  uint64_t* empty_a = full_a + kMaxAStages;  // [kMaxAStages] A tile read by the tensor core
+  uint64_t* bfull = empty_a + kMaxAStages;   // [2]
   uint64_t* bempty = bfull + 2;           // [2]
-  uint64_t* afull = bempty + 2;           // [2]
-  uint64_t* aempty = afull + 2;           // [2]
-  uint64_t* mma_done = aempty + 2;
+  uint64_t* afull = bempty + 2;           // [kMaxAcc]
+  uint64_t* aempty = afull + kMaxAcc;     // [kMaxAcc]
+  uint64_t* mma_done = aempty + kMaxAcc;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-  auto stage_codes = [&](int s) { return sStage + s * kStageB; };
-  auto stage_a = [&](int s) { return sStage + s * kStageB + G::kCodeSlot; };
-  auto stage_scales = [&](int s) { return sStage + s * kStageB + G::kCodeSlot + KPL * BN * 2; };
+  auto stage_codes = [&](int s) { return sCode + s * kCodeStage; };
+  auto stage_scales = [&](int s) { return sCode + s * kCodeStage + G::kCodeSlot; };
+  auto stage_a = [&](int x) { return sAst + x * kAStage; };
 
   if (tid == 0) {
+    for (int i = 0; i < SA; ++i) {
+      mbar_init(&full_a[i], 1 + kLoadThreads);
+      mbar_init(&empty_a[i], 1);  // tcgen05.commit after the MMAs that read it
+    }
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1 + kLoadThreads);
-      mbar_init(&empty[i], 1);
+      // REDUCE stores nothing: each warp of the tile's warpgroup releases the stage.
+      mbar_init(&empty[i], PASS == kReduce ? 4 : 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bfull[i], 1 + kLoadThreads);
       mbar_init(&bempty[i], 1);
+    }
+    for (int i = 0; i < kMaxAcc; ++i) {
       mbar_init(&afull[i], 1);
-      mbar_init(&aempty[i], kEpiThreads / 32);
+      mbar_init(&aempty[i], 4);  // the four warps of the tile's warpgroup
     }
     mbar_init(mma_done, 1);
     fence_mbar_init();
   }
+  constexpr int NB = 512 / BN;  // accumulator buffers in the 512 tensor-memory columns
+  static_assert(NB >= kEpiWGs && NB <= kMaxAcc, "accumulator buffers per warpgroup");
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -935,50 +1041,60 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
         const int KP = W.KP;
         if (W.use_tma) prefetch_tmap(&W.tmap);
         // B strip of this item: KP*2 / kb boxes of 128 rows x kb bytes.
-        const int jb = it & 1;
-        if (it >= 2) {
-          ok = mbar_wait(&bempty[jb], ((it >> 1) - 1) & 1u, kStatusTimeoutMma);
+        const int jb = it % NBB;
+        if (it >= static_cast<uint32_t>(NBB)) {
+          ok = mbar_wait(&bempty[jb], ((it / NBB) - 1) & 1u, kStatusTimeoutMma);
           if (!ok) break;
         }
         if (W.use_tma_b) {
           const int kb = kb_row(KP);
           const int nbox = KP * 2 / kb;
-          uint8_t* sBj = sB + jb * 128 * KPL * 2;
+          uint8_t* sBj = sB + jb * ws_b_buf_bytes(KPL);
           mbar_arrive_expect_tx(&bfull[jb], static_cast<uint32_t>(nbox * 128 * kb));
           for (int j = 0; j < nbox; ++j) tma_load_2d(sBj + j * 128 * kb, &W.tmap_b, j * (kb / 2), g.row0, &bfull[jb]);
         } else {
           mbar_arrive(&bfull[jb]);
         }
         for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
+          const int c0 = g.col_begin + tile * BN;
+          // A tile: BN/64 boxes of 64 columns x KP rows (MN-major, 128-byte swizzle).
+          const int x = t % SA;
+          if (t >= static_cast<uint32_t>(SA)) {
+            ok = mbar_wait(&empty_a[x], ((t / SA) - 1) & 1u, kStatusTimeoutMma);
+            if (!ok) break;
+          }
+          if (W.use_tma_a) {
+            mbar_arrive_expect_tx(&full_a[x], static_cast<uint32_t>(BN * KP * 2));
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(stage_a(x) + j * KP * 128, &W.tmap_a, c0 + j * 64, 0, &full_a[x]);
+          } else {
+            mbar_arrive(&full_a[x]);
+          }
+          // Code tile.
           const int s = t % S;
           if (t >= static_cast<uint32_t>(S)) {
             ok = mbar_wait(&empty[s], ((t / S) - 1) & 1u, kStatusTimeoutLoad);
             if (!ok) break;
           }
-          const int c0 = g.col_begin + tile * BN;
           int boxes = 0;
           const int64_t off = code_off<FMT>(c0);
           if (W.use_tma)
             for (int j = 0; j < G::kBoxes; ++j) boxes += (off + j * G::kBoxRow < W.row_bytes) ? 1 : 0;
-          const uint32_t a_bytes = W.use_tma_a ? static_cast<uint32_t>(BN * KP * 2) : 0u;
-          const uint32_t tx = static_cast<uint32_t>(boxes * 128 * G::kBoxRow) + a_bytes;
-          if (tx != 0u) mbar_arrive_expect_tx(&full[s], tx);
+          if (boxes > 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(boxes * 128 * G::kBoxRow));
           else mbar_arrive(&full[s]);
           for (int j = 0; j < boxes; ++j) {
-            const int x = static_cast<int>(off + j * G::kBoxRow);
-            tma_load_2d(stage_codes(s) + j * 128 * G::kBoxRow, &W.tmap, is_gguf<FMT>() ? x / 8 : x, g.row0,
+            const int xb = static_cast<int>(off + j * G::kBoxRow);
+            tma_load_2d(stage_codes(s) + j * 128 * G::kBoxRow, &W.tmap, is_gguf<FMT>() ? xb / 8 : xb, g.row0,
                         &full[s]);
           }
-          // A tile: BN/64 boxes of 64 columns x KP rows (MN-major, 128-byte swizzle).
-          if (W.use_tma_a)
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(stage_a(s) + j * KP * 128, &W.tmap_a, c0 + j * 64, 0, &full[s]);
         }
       }
       // Loads still in flight after an early exit land before the CTA retires.
       const uint32_t issued = t;
       for (uint32_t u = issued > static_cast<uint32_t>(S) ? issued - S : 0u; u < issued; ++u)
         mbar_wait(&full[u % S], (u / S) & 1u, kStatusTimeoutLoad);
+      for (uint32_t u = issued > static_cast<uint32_t>(SA) ? issued - SA : 0u; u < issued; ++u)
+        mbar_wait(&full_a[u % SA], (u / SA) & 1u, kStatusTimeoutLoad);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -990,21 +1106,21 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
       for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x, ++it) {
         const ItemGeom g = item_geom<BN>(P, item);
         const int KP = P.w[g.wi].KP;
-        const int jb = it & 1;
-        ok = mbar_wait(&bfull[jb], (it >> 1) & 1u, kStatusTimeoutLoad);
+        const int jb = it % NBB;
+        ok = mbar_wait(&bfull[jb], (it / NBB) & 1u, kStatusTimeoutLoad);
         if (!ok) break;
-        const uint32_t a_base = smem_u32(sB + jb * 128 * KPL * 2);
+        const uint32_t a_base = smem_u32(sB + jb * ws_b_buf_bytes(KPL));
         const int kb = kb_row(KP);
         const uint32_t a_layout = swizzle_layout(kb);
         for (int tile = 0; tile < g.n_tiles && ok; ++tile, ++t) {
-          const int s = t % S;
-          const int ab = t & 1;
-          ok = mbar_wait(&full[s], (t / S) & 1u, kStatusTimeoutLoad);
-          if (ok && t >= 2) ok = mbar_wait(&aempty[ab], ((t >> 1) - 1) & 1u, kStatusTimeoutMma);
+          const int x = t % SA;
+          const int ab = t % NB;
+          ok = mbar_wait(&full_a[x], (t / SA) & 1u, kStatusTimeoutLoad);
+          if (ok && t >= static_cast<uint32_t>(NB)) ok = mbar_wait(&aempty[ab], ((t / NB) - 1) & 1u, kStatusTimeoutMma);
           if (!ok) break;
           fence_proxy_async_smem();  // cp.async-written operands -> tensor core
           tc_fence_after();
-          const uint32_t b_base = smem_u32(stage_a(s));
+          const uint32_t b_base = smem_u32(stage_a(x));
           for (int ks = 0; ks < KP / 16; ++ks) {
             // B strip, K-major: 16 columns = 32 bytes inside a kb-byte swizzled row.
             const int kbyte = ks * 32;
@@ -1015,6 +1131,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
             umma_f16(tmem + ab * BN, adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
           }
           umma_commit(&afull[ab]);
+          umma_commit(&empty_a[x]);  // the A stage is free once these MMAs complete
         }
         umma_commit(&bempty[jb]);  // the strip is free once these MMAs complete
       }
@@ -1033,14 +1150,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
       const int KP = W.KP;
       const int rows_here = min(128, W.M - g.row0);
       // B strip (K-major canonical): chunk kc of row t at kc*2048 + (t/8)*128 + (t%8)*16.
-      const int jb = it & 1;
-      if (it >= 2) {
-        ok = mbar_wait(&bempty[jb], ((it >> 1) - 1) & 1u, kStatusTimeoutMma);
+      const int jb = it % NBB;
+      if (it >= static_cast<uint32_t>(NBB)) {
+        ok = mbar_wait(&bempty[jb], ((it / NBB) - 1) & 1u, kStatusTimeoutMma);
         if (!ok) break;
       }
       if (!W.use_tma_b) {
         // Same swizzled K-major layout the bulk tensor copy would produce.
-        uint8_t* sBj = sB + jb * 128 * KPL * 2;
+        uint8_t* sBj = sB + jb * ws_b_buf_bytes(KPL);
         const int kb = kb_row(KP);
         const int cpr = kb / 16;  // 16-byte chunks per row
         const bool vec = ((reinterpret_cast<uintptr_t>(W.b) | (W.r * 2)) & 15) == 0;
@@ -1069,13 +1186,45 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
       cp_async_mbar_arrive(&bfull[jb]);
       const bool vec_a = ((reinterpret_cast<uintptr_t>(W.a) | (W.N * 2)) & 15) == 0;
       for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
+        const int c0 = g.col_begin + tile * BN;
+        const int ncols = min(BN, g.col_end - c0);
+        const int x = t % SA;
+        if (t >= static_cast<uint32_t>(SA)) {
+          ok = mbar_wait(&empty_a[x], ((t / SA) - 1) & 1u, kStatusTimeoutMma);
+          if (!ok) break;
+        }
+        // A tile when it cannot move by bulk tensor copies: the same MN-major
+        // layout, 64-column blocks of KP rows x 128 bytes, 128-byte swizzle.
+        if (!W.use_tma_a) {
+          uint8_t* sA = stage_a(x);
+          const int chunks = KP * BN / 8;
+          for (int idx = lt; idx < chunks; idx += kLoadThreads) {
+            const int ng = idx % (BN / 8);
+            const int kr = idx / (BN / 8);
+            const int n = c0 + ng * 8;
+            uint8_t* dst = sA + (ng >> 3) * KP * 128 + kr * 128 + (((static_cast<uint32_t>(ng & 7)) ^ (kr & 7)) << 4);
+            const uint16_t* ap = W.a + static_cast<int64_t>(kr) * W.N + n;
+            if (kr < W.r && vec_a && n + 8 <= g.col_end) {
+              cp_async16(dst, ap);
+            } else {
+              uint4 v = make_uint4(0u, 0u, 0u, 0u);
+              if (kr < W.r) {
+                uint16_t e[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) e[j] = (n + j < g.col_end) ? ap[j] : 0;
+                v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16), e[6] | (e[7] << 16));
+              }
+              *reinterpret_cast<uint4*>(dst) = v;
+            }
+          }
+        }
+        __threadfence_block();
+        cp_async_mbar_arrive(&full_a[x]);
         const int s = t % S;
         if (t >= static_cast<uint32_t>(S)) {
           ok = mbar_wait(&empty[s], ((t / S) - 1) & 1u, kStatusTimeoutLoad);
           if (!ok) break;
         }
-        const int c0 = g.col_begin + tile * BN;
-        const int ncols = min(BN, g.col_end - c0);
         if (!W.use_tma) {
           // Codes into the padded row layout (rows of kPadRS bytes).
           const int64_t off = code_off<FMT>(c0);
@@ -1115,31 +1264,6 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
             }
           }
         }
-        // A tile when it cannot move by bulk tensor copies: the same MN-major
-        // layout, 64-column blocks of KP rows x 128 bytes, 128-byte swizzle.
-        if (!W.use_tma_a) {
-          uint8_t* sA = stage_a(s);
-          const int chunks = KP * BN / 8;
-          for (int idx = lt; idx < chunks; idx += kLoadThreads) {
-            const int ng = idx % (BN / 8);
-            const int kr = idx / (BN / 8);
-            const int n = c0 + ng * 8;
-            uint8_t* dst = sA + (ng >> 3) * KP * 128 + kr * 128 + (((static_cast<uint32_t>(ng & 7)) ^ (kr & 7)) << 4);
-            const uint16_t* ap = W.a + static_cast<int64_t>(kr) * W.N + n;
-            if (kr < W.r && vec_a && n + 8 <= g.col_end) {
-              cp_async16(dst, ap);
-            } else {
-              uint4 v = make_uint4(0u, 0u, 0u, 0u);
-              if (kr < W.r) {
-                uint16_t e[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) e[j] = (n + j < g.col_end) ? ap[j] : 0;
-                v = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16), e[6] | (e[7] << 16));
-              }
-              *reinterpret_cast<uint4*>(dst) = v;
-            }
-          }
-        }
         __threadfence_block();
         cp_async_mbar_arrive(&full[s]);
       }
@@ -1148,10 +1272,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
   }
   } else {
     // ---------------------------------------------------------------- epilogue
-    regs_inc<kEpiRegs>();
+    regs_inc<epi_regs<FMT>()>();
     const int e = tid - 128;
     const int rt = e & 127;         // tile row / tensor-memory lane of this thread
-    const int wg = e >> 7;          // takes every other accumulator chunk
+    const int wg = e >> 7;          // processes tiles t with t % kEpiWGs == wg
+    const uint32_t bar_id = 1u + static_cast<uint32_t>(wg);  // this warpgroup's named barrier
     const uint32_t lane_off = static_cast<uint32_t>((e >> 5) & 3) * 32u << 16;
     uint32_t t = 0;
     int pending = -1;  // stage whose bulk store may still be reading it
@@ -1164,6 +1289,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
       const bool valid = row < W.M;
       const int rows_here = min(128, W.M - g.row0);
       const bool tma = W.use_tma != 0;
+      const int owner = static_cast<int>(t % kEpiWGs);  // warpgroup of the item's first tile
 
       QpCache qc;  // quantization block of this thread's row (FP8 / INT8)
       // Per-thread running reductions for REDUCE passes.
@@ -1184,7 +1310,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
         if (two_level) {
           if (PASS == kReduce) {
             g_in = *W.gscale;
-            if (local == 0 && e == 0) W.old_scale[0] = g_in;
+            if (local == 0 && rt == 0 && wg == owner) W.old_scale[0] = g_in;
           } else {
             g_in = W.old_scale[0];
             const float amax = __uint_as_float(*W.qmax);
@@ -1194,28 +1320,37 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
       }
 
       for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
+        if (static_cast<int>(t % kEpiWGs) != wg) continue;  // another warpgroup's tile
         const int s = t % S;
-        const int ab = t & 1;
+        const int ab = t % NB;
         const int c0 = g.col_begin + tile * BN;
         const int tcols = min(BN, g.col_end - c0);
         ok = mbar_wait(&full[s], (t / S) & 1u, kStatusTimeoutLoad);
-        if (ok) ok = mbar_wait(&afull[ab], (t >> 1) & 1u, kStatusTimeoutMma);
-        // One decision for all epilogue threads: the barriers below need them all.
-        ok = named_bar_and(1, kEpiThreads, ok);
+        if (ok) ok = mbar_wait(&afull[ab], (t / NB) & 1u, kStatusTimeoutMma);
+        // One decision for all threads that meet at a barrier below: the
+        // warpgroup when the tile is stored, each warp alone in REDUCE passes.
+        if constexpr (PASS == kReduce) ok = __all_sync(0xFFFFFFFFu, ok);
+        else ok = named_bar_and(bar_id, 128, ok);
         if (!ok) break;
+        if (rt == 0 && pending >= 0) {
+          // The previous tile's bulk store has long finished reading its stage.
+          bulk_wait_read_all();
+          mbar_arrive(&empty[pending]);
+          pending = -1;
+        }
         tc_fence_after();
         const uint32_t taddr = tmem + lane_off + ab * BN;
-        // Chunks kbeg, kbeg+2, ... < kend of the accumulator, each loaded from
-        // tensor memory while the previous one is being processed.
+        // Chunks kbeg .. kend-1 of the accumulator, each loaded from tensor
+        // memory while the previous one is being processed.
         auto chunk_loop = [&](int kbeg, int kend, auto&& body) {
           uint32_t cur[32];
           if (kbeg < kend) tmem_ld32_async(taddr + 32 * kbeg, cur);
-          for (int k = kbeg; k < kend; k += 2) {
+          for (int k = kbeg; k < kend; ++k) {
             tmem_ld_wait(cur);
             float acc[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(cur[i]);
-            if (k + 2 < kend) tmem_ld32_async(taddr + 32 * (k + 2), cur);
+            if (k + 1 < kend) tmem_ld32_async(taddr + 32 * (k + 1), cur);
             body(k, acc);
           }
         };
@@ -1243,12 +1378,12 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
         {
       if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 ||
                     FMT == PIPER_FMT_MXFP4) {
-        chunk_loop(wg, tcols / 32, [&](int k, const float (&acc)[32]) { mx_chunk<FMT, CDT>(W, c, k, acc); });
+        chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) { mx_chunk<FMT, CDT>(W, c, k, acc); });
       } else if constexpr (FMT == PIPER_FMT_NVFP4) {
-        chunk_loop(wg, tcols / 32, [&](int k, const float (&acc)[32]) {
+        chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) {
           nvfp4_chunk<PASS, CDT>(W, c, k, acc, g_in, g_out, two_level, red_max);
         });
-        if ((tcols & 31) && ((tcols / 32) & 1) == wg) {  // trailing 16-column block
+        if (tcols & 31) {  // trailing 16-column block
           float acc[32];
           const int k = tcols / 32;
           tmem_ld32(taddr + 32 * k, acc);
@@ -1257,7 +1392,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
           if (PASS != kReduce) *reinterpret_cast<uint2*>(chunk_ptr(c, k)) = codes;
         }
       } else if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
-        chunk_loop(wg, tcols / 32, [&](int k, const float (&acc)[32]) { gguf_chunk<FMT, CDT>(W, c, k, acc); });
+        chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) { gguf_chunk<FMT, CDT>(W, c, k, acc); });
       } else {
         // ------------------------------------------- FP8 / INT8 (affine) paths
         constexpr bool kInt8 = FMT == PIPER_FMT_INT8;
@@ -1271,20 +1406,24 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
         if constexpr (PASS == kLocal) {
           // Groups of W.group (multiple of 32, dividing the tile width) are local.
           const int gch = W.group / 32;
-          for (int g0 = wg * gch; g0 < nchunks; g0 += 2 * gch) {
+          for (int g0 = 0; g0 < nchunks; g0 += gch) {
             float gmax = 0.0f, gmin = 0.0f, gabs = 0.0f;
-            float scale_in[32];
-            int zp_in[32];
+            float s_in = 1.0f;
+            int z_in = 0;
+            if (valid) {
+              qp_load<FMT, PASS>(W, qparam_index(W, row, c0 + 32 * g0), qc);
+              s_in = qc.s_in;
+              z_in = qc.z_in;
+            }
             for (int k = g0; k < g0 + gch; ++k) {
               float acc[32], merged[32];
               tmem_ld32(taddr + 32 * k, acc);
-              affine_inputs<FMT, PASS>(W, c, c0 + 32 * k, scale_in, zp_in, qc);
-              affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                gabs = fmaxf(gabs, fabsf(merged[i]));
-                gmax = fmaxf(gmax, merged[i]);
-                gmin = fminf(gmin, merged[i]);
+              affine_merged_u<FMT, CDT>(W, c, k, acc, s_in, z_in, merged);
+              if constexpr (kInt8) {
+                gmax = fmaxf(gmax, tree_max(merged));
+                gmin = fminf(gmin, tree_min(merged));
+              } else {
+                gabs = fmaxf(gabs, tree_max_abs(merged));
               }
             }
             const int qp = qparam_index(W, row, c0 + 32 * g0);
@@ -1297,7 +1436,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
               for (int k = g0; k < g0 + gch; ++k) {
                 float acc[32], merged[32];
                 tmem_ld32(taddr + 32 * k, acc);
-                affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
+                affine_merged_u<FMT, CDT>(W, c, k, acc, s_in, z_in, merged);
                 uint32_t out[8];
                 const uint64_t off0 = W.offset_base +
                                       static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) +
@@ -1312,7 +1451,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
               for (int k = g0; k < g0 + gch; ++k) {
                 float acc[32], merged[32];
                 tmem_ld32(taddr + 32 * k, acc);
-                affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
+                affine_merged_u<FMT, CDT>(W, c, k, acc, s_in, z_in, merged);
                 uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
                 const uint64_t off0 = W.offset_base +
                                       static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) +
@@ -1331,13 +1470,25 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
             }
           }
         } else {
-          chunk_loop(wg, nchunks, [&](int k, const float (&acc)[32]) {
-            float merged[32], scale_in[32];
-            int zp_in[32];
+          chunk_loop(0, nchunks, [&](int k, const float (&acc)[32]) {
+            float merged[32];
             const int col = c0 + 32 * k;
-            affine_inputs<FMT, PASS>(W, c, col, scale_in, zp_in, qc);
-            affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
             const int nvalid = min(32, tcols - 32 * k);
+            if (W.nq_row == 0 || (W.group >= 32 && (col % W.group) + 32 <= W.group)) {
+              float s_in = 1.0f;
+              int z_in = 0;
+              if (valid) {
+                qp_load<FMT, PASS>(W, qparam_index(W, row, col), qc);
+                s_in = qc.s_in;
+                z_in = qc.z_in;
+              }
+              affine_merged_u<FMT, CDT>(W, c, k, acc, s_in, z_in, merged);
+            } else {
+              float scale_in[32];
+              int zp_in[32];
+              affine_inputs<FMT, PASS>(W, c, col, scale_in, zp_in, qc);
+              affine_merged<FMT, CDT>(W, c, k, acc, scale_in, zp_in, merged);
+            }
             if constexpr (PASS == kReduce) {
               const bool uniform_chunk =
                   W.nq_row == 0 || (W.group >= 32 && (col % W.group) + 32 <= W.group);
@@ -1356,15 +1507,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
                     W.old_scale[qp] = reinterpret_cast<const float*>(W.scale)[qp];
                   }
                 }
-                if (kInt8) {
-#pragma unroll
-                  for (int i = 0; i < 32; ++i) {
-                    red_max = fmaxf(red_max, merged[i]);
-                    red_nmin = fmaxf(red_nmin, -merged[i]);
-                  }
+                if constexpr (kInt8) {
+                  red_max = fmaxf(red_max, tree_max(merged));
+                  red_nmin = fmaxf(red_nmin, -tree_min(merged));
                 } else {
-#pragma unroll
-                  for (int i = 0; i < 32; ++i) red_max = fmaxf(red_max, fabsf(merged[i]));
+                  red_max = fmaxf(red_max, tree_max_abs(merged));
                 }
               } else if (valid) {
 #pragma unroll
@@ -1480,8 +1627,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
         // ---- write the tile back (in place) and release the stage.
         if (PASS != kReduce && tma) {
           fence_proxy_async_smem();
-          named_bar_sync(1, kEpiThreads);
-          if (e == 0) {
+          named_bar_sync(bar_id, 128);
+          if (rt == 0) {
             const int64_t off = code_off<FMT>(c0);
             for (int j = 0; j < G::kBoxes; ++j) {
               if (off + j * G::kBoxRow >= W.row_bytes) break;
@@ -1489,15 +1636,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
               tma_store_2d(&W.tmap, is_gguf<FMT>() ? x / 8 : x, g.row0, stage_codes(s) + j * 128 * G::kBoxRow);
             }
             bulk_commit();
-            if (pending >= 0) {
-              bulk_wait_read_1();
-              mbar_arrive(&empty[pending]);
-            }
             pending = s;
           }
+        } else if constexpr (PASS == kReduce) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
         } else {
-          named_bar_sync(1, kEpiThreads);
-          if (PASS != kReduce) {
+          named_bar_sync(bar_id, 128);
+          {
             // Coalesced write-back of the padded layout.
             const int64_t off = code_off<FMT>(c0);
             const int nbytes = static_cast<int>(code_off<FMT>(c0 + tcols) - off);
@@ -1506,7 +1652,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
             const int per = nbytes / gran;
             uint8_t* dst0 = W.q + static_cast<int64_t>(g.row0) * W.row_bytes + off;
             const uint8_t* base = stage_codes(s);
-            for (int k = e; k < rows_here * per; k += kEpiThreads) {
+            for (int k = rt; k < rows_here * per; k += 128) {
               const int r = k / per;
               const int i = k - r * per;
               const uint8_t* src = base + r * G::kPadRS + i * gran;
@@ -1515,9 +1661,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
               else if (gran == 4) *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(src);
               else *dst = *src;
             }
-            named_bar_sync(1, kEpiThreads);
+            named_bar_sync(bar_id, 128);
           }
-          if (e == 0) {
+          if (rt == 0) {
             if (pending >= 0) {
               bulk_wait_read_all();
               mbar_arrive(&empty[pending]);
@@ -1548,22 +1694,22 @@ __global__ void __launch_bounds__(kWsThreads, 1) merge_kernel(const __grid_const
       }
       // ---- NVFP4: zero swizzle padding columns and publish the new global scale.
       if constexpr (FMT == PIPER_FMT_NVFP4 && PASS == kLocal) {
-        if ((W.flags & PIPER_FLAG_SWIZZLED) && g.col_end == W.N && wg == 0) {
+        if ((W.flags & PIPER_FLAG_SWIZZLED) && g.col_end == W.N && wg == owner) {
           const int padded = align_up(W.scale_cols, 4);
           uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
           for (int pc = W.scale_cols; pc < padded; ++pc) scale8[swizzled_index(row, pc, W.scale_cols)] = 0u;
         }
-        if (two_level && local == 0 && e == 0) *W.gscale = g_out;
+        if (two_level && local == 0 && rt == 0 && wg == owner) *W.gscale = g_out;
       }
     }
-    if (e == 0) bulk_wait_all();  // bulk stores complete before the CTA exits
+    if (rt == 0) bulk_wait_all();  // bulk stores complete before the CTA exits
   }
 
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -1607,11 +1753,28 @@ int ws_code_slot(int fmt, int bn) {
   return pm::align_up(128 * std::max(rs, rb), 1024);
 }
 
-// Pipeline stages that fit in the per-CTA shared-memory limit.
-int ws_stages(int fmt, int bn, int kp) {
-  const int stage = pm::ws_stage_bytes(ws_code_slot(fmt, bn), kp, bn);
-  const int fixed = pm::ws_smem_bytes(0, 0, kp);
-  return std::min(pm::kMaxStages, (pm::kSmemLimit - fixed) / stage);
+// Shared-memory pipeline of one launch: code stages, A stages, B strips.
+struct PipeCfg {
+  int sc = 0, sa = 0, nbb = 0;
+};
+
+// Deepest rings that fit the per-CTA shared-memory limit, in order of
+// preference: many code stages (they hold the HBM traffic in flight), then A
+// stages (refilled as soon as the tensor core has read them), then a second B
+// strip (hides the strip load at item boundaries).
+PipeCfg plan_pipe(int fmt, int bn, int kp) {
+  const int cs = pm::ws_code_stage_bytes(ws_code_slot(fmt, bn));
+  const int as = pm::ws_a_stage_bytes(kp, bn);
+  const int bs = pm::ws_b_buf_bytes(kp);
+  const int avail = pm::kSmemLimit - 1024 - 512;
+  const int pref[][3] = {{2, 3, 6}, {2, 2, 6}, {1, 2, 6}, {2, 2, 4}, {1, 2, 4}, {1, 2, 3}, {1, 1, 2}};
+  for (const auto& q : pref) {
+    const int rest = avail - q[0] * bs - q[1] * as;
+    if (rest <= 0) continue;
+    const int sc = std::min(pm::kMaxStages, rest / cs);
+    if (sc >= q[2]) return {sc, q[1], q[0]};
+  }
+  return {};
 }
 
 struct Plan {
@@ -1712,9 +1875,12 @@ int validate(const piper_merge_desc& d, Plan& p) {
   // stages of (codes, A tile, scales) next to two B strips; 64-column tiles
   // (large ranks) may run with two.
   const int kp = pm::align_up(static_cast<int>(d.rank), 16);
-  if (ws_stages(d.format, 256, kp) >= 3) p.bn = 256;
-  else if (ws_stages(d.format, 128, kp) >= 3) p.bn = 128;
-  else if (ws_stages(d.format, 64, kp) >= 2) p.bn = 64;
+  auto fits = [&](int bn, int min_sc) {
+    return 512 / bn >= pm::epi_wgs_rt(d.format) && plan_pipe(d.format, bn, kp).sc >= min_sc;
+  };
+  if (fits(256, 4)) p.bn = 256;
+  else if (fits(128, 4)) p.bn = 128;
+  else if (fits(64, 2)) p.bn = 64;
   else return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(d.rank) + " is too large for the merge pipeline.");
   if ((d.format == PIPER_FMT_FP8_E4M3 || d.format == PIPER_FMT_FP8_E5M2 || d.format == PIPER_FMT_INT8) &&
       !p.two_pass && p.group > p.bn) {
@@ -1745,22 +1911,24 @@ constexpr int kMinSmem = 120 * 1024;
 template <int FMT, int PASS, int BN, int CDT>
 int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
   auto kern = pm::merge_kernel<FMT, PASS, BN, CDT>;
-  const int stages = ws_stages(FMT, BN, kp_max);
-  if (stages < 2)
+  const PipeCfg pc = plan_pipe(FMT, BN, kp_max);
+  if (pc.sc < 2)
     return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(kp_max) + " does not fit the shared-memory pipeline.");
-  const int stage_bytes = pm::ws_stage_bytes(pm::TileGeom<FMT, BN>::kCodeSlot, kp_max, BN);
-  const int smem = std::max(pm::ws_smem_bytes(stage_bytes, stages, kp_max), kMinSmem);
+  const int smem =
+      std::max(pm::ws_smem_bytes(pm::TileGeom<FMT, BN>::kCodeSlot, kp_max, BN, pc.sc, pc.sa, pc.nbb), kMinSmem);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess)
     return fail(PIPER_MERGE_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   lp.n_items = items;
   lp.kp_max = kp_max;
-  lp.stages = stages;
+  lp.c_stages = pc.sc;
+  lp.a_stages = pc.sa;
+  lp.b_bufs = pc.nbb;
   const int grid = std::min(items, sm_count());
   if (std::getenv("PIPER_MERGE_DEBUG") != nullptr)
-    std::fprintf(stderr, "[piper-merge] fmt=%d pass=%d bn=%d kp=%d stages=%d smem=%d items=%d grid=%d\n", FMT, PASS,
-                 BN, kp_max, stages, smem, items, grid);
-  kern<<<grid, pm::kWsThreads, smem, stream>>>(lp);
+    std::fprintf(stderr, "[piper-merge] fmt=%d pass=%d bn=%d kp=%d stages=%d/%d/%d smem=%d items=%d grid=%d\n", FMT,
+                 PASS, BN, kp_max, pc.sc, pc.sa, pc.nbb, smem, items, grid);
+  kern<<<grid, pm::ws_threads<FMT>(), smem, stream>>>(lp);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
@@ -1769,7 +1937,11 @@ int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
 
 template <int FMT, int PASS, int CDT>
 int launch_bn(int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
-  if (bn == 256) return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
+  if (bn == 256) {
+    // 256-column tiles leave two accumulator buffers: one per epilogue warpgroup at most.
+    if constexpr (512 / 256 >= pm::epi_wgs<FMT>()) return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
+    else return fail(PIPER_MERGE_EINVAL, "256-column tiles need at most two epilogue warpgroups.");
+  }
   if (bn == 128) return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
   return launch_t<FMT, PASS, 64, CDT>(lp, items, kp, s);
 }

@@ -133,8 +133,8 @@ __device__ __forceinline__ uint32_t philox_word0(PhiloxKey key, uint64_t offset)
 }
 
 __device__ __forceinline__ float philox_uniform(PhiloxKey key, uint64_t offset) {
-  int32_t x = static_cast<int32_t>(philox_word0(key, offset));
-  x = x < 0 ? -x - 1 : x;
+  const int32_t w = static_cast<int32_t>(philox_word0(key, offset));
+  const int32_t x = w ^ (w >> 31);  // x < 0 ? -x - 1 : x
   return __fmul_rn(__int2float_rn(x), __uint_as_float(0x2FFFFFFFu));
 }
 
@@ -149,28 +149,41 @@ __device__ __forceinline__ float recip_pow2(float g) {
 }
 
 // _stochastic_float8 (_triton_stochastic_quantization.py:132-175): `v` is the
-// clamped, normalized value; returns the E4M3/E5M2 code. Neighbouring codes of
-// one sign are a power-of-two gap apart, so `(m - lo) / (hi - lo)` is an
-// exact quotient, computed as a product with the exact reciprocal.
+// normalized value, already clamped to [-limit, limit] (a NaN became -limit);
+// returns the E4M3/E5M2 code.
+//
+// The reference rounds |v| to nearest, steps one code down when that code is
+// above |v|, and so takes lo = the largest code <= |v| and hi = lo + 1, then
+// p = (|v| - lo) / (hi - lo). In the normal range lo is |v| with its mantissa
+// truncated to 3 (2) bits, the gap is 2^(e-3) (2^(e-2)), and p is exactly the
+// dropped mantissa bits scaled by 2^-20 (2^-21); below the smallest normal the
+// codes are evenly spaced by 2^-9 (2^-16) and p is the fraction of |v| / gap.
+// Where the result is not stochastic (p == 0 or |v| == limit) |v| is on the
+// grid, so the reference's round-to-nearest code equals lo.
 template <bool E4M3>
 __device__ __forceinline__ uint32_t sr_fp8(float v, float limit, PhiloxKey key, uint64_t off) {
-  const float mag = fabsf(v);
-  const uint32_t det = enc_fp8<E4M3>(mag);
-  const float det_v = dec_fp8<E4M3>(det);
-  const bool down = det_v > mag;
-  const uint32_t other = (down ? det - 1u : det + 1u) & 0xFFu;
-  const float other_v = dec_fp8<E4M3>(other);
-  const uint32_t lo = down ? other : det;
-  const uint32_t hi = down ? det : other;
-  const float lov = down ? other_v : det_v;
-  const float hiv = down ? det_v : other_v;
-  const float gap = hiv - lov;
-  // A NaN / infinite upper neighbour only occurs at |v| >= limit (not interior).
-  const float p = (gap > 0.0f && gap < 1e30f) ? (mag - lov) * recip_pow2(gap) : 0.0f;
+  constexpr int kMant = E4M3 ? 3 : 2;
+  constexpr int kDrop = 23 - kMant;
+  constexpr uint32_t kMinNormal = E4M3 ? 0x3C800000u : 0x38800000u;  // 2^-6 / 2^-14
+  constexpr uint32_t kBiasFix = (127u - (E4M3 ? 7u : 15u)) << kMant;
+  constexpr float kSubScale = E4M3 ? 512.0f : 65536.0f;               // 1 / subnormal gap
+  const uint32_t bits = __float_as_uint(v);
+  const uint32_t abits = bits & 0x7FFFFFFFu;
+  const float mag = __uint_as_float(abits);
+  // normal range
+  const uint32_t lo_n = (abits >> kDrop) - kBiasFix;
+  const float p_n = __uint_as_float(0x3F800000u | ((abits << kMant) & 0x7FFFFFu)) - 1.0f;
+  // subnormal range (exact: scaling by a power of two, truncation, subtraction)
+  const float t = mag * kSubScale;
+  const float fl = truncf(t);
+  const uint32_t lo_s = __float_as_uint(fl + 8388608.0f) - 0x4B000000u;
+  const float p_s = t - fl;
+  const bool normal = abits >= kMinNormal;
+  const uint32_t lo = normal ? lo_n : lo_s;
+  const float p = normal ? p_n : p_s;
   const float u = philox_uniform(key, off);
-  const uint32_t sign = (__float_as_uint(v) >> 24) & 0x80u;
-  const bool interior = mag < limit && p > 0.0f;
-  return (interior ? (u < p ? hi : lo) : det) | sign;
+  const bool up = mag < limit && p > 0.0f && u < p;
+  return (lo + (up ? 1u : 0u)) | ((bits >> 24) & 0x80u);
 }
 
 // _stochastic_e2m1_code (_triton_stochastic_quantization.py:109-129).
