@@ -147,6 +147,19 @@ int piper_merge_float8(void* qdata, void* scale, const void* b, const void* a, i
                        uint64_t seed, uint64_t offset_base, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* piper_merge_float8 without a workspace argument. No counterpart in the
+ * reference: an addition for callers that cannot allocate device memory at
+ * merge time. The two-pass scratch comes from a fixed 1 MiB array in device
+ * memory (one per device): layouts that need more (more than 65,536
+ * quantization blocks, e.g. per-row weights above 65,536 rows) are rejected
+ * with PIPER_MERGE_EWORKSPACE. The first call on a device performs the setup
+ * (cudaGetSymbolAddress) and should come before any stream capture.
+ * Overlapping calls on one device race on the shared scratch. */
+int piper_merge_float8_noalloc(void* qdata, void* scale, const void* b, const void* a, int64_t rows,
+                               int64_t cols, int64_t rank, int64_t block_rows, int64_t block_cols,
+                               int32_t e5m2, int32_t compute_dtype, float strength, int32_t has_seed,
+                               uint64_t seed, uint64_t offset_base, void* stream);
+
 /* _triton_int8_lora.py:267 merge_int8_lora(qdata, scale, zero_point, block_size,
  * b, a, strength, *, asymmetric, reduce_range, rounding_seed). */
 int piper_merge_int8(void* qdata, void* scale, void* zero_point, const void* b, const void* a,

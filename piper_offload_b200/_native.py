@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "piper_merge_mx",
     "piper_merge_nvfp4",
     "piper_merge_float8",
+    "piper_merge_float8_noalloc",
     "piper_merge_int8",
     "piper_merge_gguf",
     "piper_merge_last_error",
@@ -135,6 +136,7 @@ def load() -> ctypes.CDLL:
             "piper_merge_mx",
             "piper_merge_nvfp4",
             "piper_merge_float8",
+            "piper_merge_float8_noalloc",
             "piper_merge_int8",
             "piper_merge_gguf",
             "piper_merge_device_status",

@@ -38,6 +38,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -2329,6 +2330,78 @@ int piper_merge_float8(void* qdata, void* scale, const void* b, const void* a, i
   d.seed = seed;
   d.offset_base = offset_base;
   return piper_merge_batch(&d, 1, workspace, workspace_bytes, stream);
+}
+
+// Per-row / per-tensor / wide-group FP8 merges keep 16 bytes of running state
+// per quantization block between their two passes. This variant takes that
+// scratch from a fixed array in device memory instead of a caller's buffer,
+// for callers that cannot allocate device memory at merge time: a C or C++
+// host embedding the library without PyTorch's caching allocator (it has no
+// device allocator of its own), or a process whose device memory a model cache
+// has already reserved, where a merge-time cudaMalloc could fail or force an
+// implicit device synchronization. It calls no allocating routine. The array
+// exists once per device (every device's copy of the module has its own), so
+// overlapping calls on one device, from several host threads or streams, race
+// on it. The first call on a device looks up the array's address
+// (cudaGetSymbolAddress, with that device current); make that first call
+// before any stream capture. Each call zeroes the blocks it uses on the stream
+// before the kernels read them, as the buffer-taking entry point does.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t{1} << 20;  // 65,536 quantization blocks
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+}  // namespace
+
+int piper_merge_float8_noalloc(void* qdata, void* scale, const void* b, const void* a, int64_t rows, int64_t cols,
+                               int64_t rank, int64_t block_rows, int64_t block_cols, int32_t e5m2,
+                               int32_t compute_dtype, float strength, int32_t has_seed, uint64_t seed,
+                               uint64_t offset_base, void* stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(PIPER_MERGE_EINVAL, "device " + std::to_string(dev) + " is beyond the static scratch table.");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (e != cudaSuccess || ptr == nullptr)
+        return fail(PIPER_MERGE_ECUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+      g_noalloc_ptr[dev] = ptr;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  piper_merge_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.format = e5m2 ? PIPER_FMT_FP8_E5M2 : PIPER_FMT_FP8_E4M3;
+  d.qdata = qdata;
+  d.scale = scale;
+  d.b = b;
+  d.a = a;
+  d.rows = rows;
+  d.cols = cols;
+  d.rank = rank;
+  d.block_rows = block_rows;
+  d.block_cols = block_cols;
+  d.compute_dtype = compute_dtype;
+  d.flags = has_seed ? PIPER_FLAG_STOCHASTIC : 0u;
+  d.strength = strength;
+  d.seed = seed;
+  d.offset_base = offset_base;
+  size_t need = 0;
+  const int rc = piper_merge_workspace_size(&d, 1, &need);
+  if (rc != PIPER_MERGE_OK) return rc;
+  if (need > kNoAllocScratchBytes)
+    return fail(PIPER_MERGE_EWORKSPACE,
+                "this layout needs " + std::to_string(need) + " bytes of scratch; the static scratch of " +
+                    "piper_merge_float8_noalloc holds " + std::to_string(kNoAllocScratchBytes) +
+                    " bytes (65536 quantization blocks). Use piper_merge_float8 with a workspace.");
+  return piper_merge_float8(qdata, scale, b, a, rows, cols, rank, block_rows, block_cols, e5m2, compute_dtype,
+                            strength, has_seed, seed, offset_base, scratch, kNoAllocScratchBytes, stream);
 }
 
 int piper_merge_int8(void* qdata, void* scale, void* zero_point, const void* b, const void* a, int64_t rows,
