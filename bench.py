@@ -419,31 +419,34 @@ def main() -> int:
         except Exception:  # noqa: BLE001
             pass
 
-    # End to end: pinned host codes -> device -> merge -> host, through the public API.
+    # End to end through the public API: every weight starts and ends in pinned
+    # host memory; streaming.merge_streamed moves each layer through a ring of
+    # three device slots, overlapping upload, merge and download on three streams.
     e2e = None
     if not args.no_e2e:
-        host = []
+        import copy
+
+        from piper_offload_b200.streaming import StreamedOp, merge_streamed, storages
+
+        host_ops = []
         h2d = d2h = 0
         for key, rows, cols, t, b, a in items:
-            hs = [s.detach().cpu().pin_memory() for s in storage_tensors(t)]
-            hf = [b.cpu().pin_memory(), a.cpu().pin_memory()]
-            host.append((hs, hf))
-            h2d += sum(x.numel() * x.element_size() for x in hs + hf)
-            d2h += sum(x.numel() * x.element_size() for x in hs)
+            ht = copy.copy(t)
+            for name, dt in storages(t):
+                setattr(ht, name, dt.detach().cpu().pin_memory())
+            hb, ha = b.cpu().pin_memory(), a.cpu().pin_memory()
+            host_ops.append((key, ht, hb, ha))
+            st = [x for _, x in storages(ht)]
+            h2d += sum(x.numel() * x.element_size() for x in st + [hb, ha])
+            d2h += sum(x.numel() * x.element_size() for x in st)
+        per_layer = len(CONFIGS[cfg][0])
+        layer_ops = [host_ops[i:i + per_layer] for i in range(0, len(host_ops), per_layer)]
         torch.cuda.synchronize(device)
 
         def e2e_step(stp: int):
-            ops = []
-            for (key, rows, cols, t, b, a), (hs, hf) in zip(items, host):
-                for dst, src in zip(storage_tensors(t), hs):
-                    dst.copy_(src, non_blocking=True)
-                b.copy_(hf[0], non_blocking=True)
-                a.copy_(hf[1], non_blocking=True)
-                ops.append((t, b, a, 1.0, derive_seed(key, stp) if stochastic else None))
-            AD.merge_lora_batch(ops, workspace=ws)
-            for (key, rows, cols, t, b, a), (hs, hf) in zip(items, host):
-                for dst, src in zip(hs, storage_tensors(t)):
-                    dst.copy_(src, non_blocking=True)
+            blocks = [[StreamedOp(ht, hb, ha, 1.0, derive_seed(key, stp) if stochastic else None)
+                       for key, ht, hb, ha in layer] for layer in layer_ops]
+            merge_streamed(blocks, device, depth=3, workspace=ws)
 
         e2e_step(step)
         torch.cuda.synchronize(device)
@@ -459,7 +462,8 @@ def main() -> int:
         e_ms = max_over_ranks(e_start.elapsed_time(e_end) / args.e2e_steps)
         e2e = {"value": total_bytes * world / (e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": args.e2e_steps,
-               "path": "pinned host -> H2D -> adapters.merge_lora_batch (C ABI) -> D2H, one stream"}
+               "path": "pinned host -> streaming.merge_streamed (per layer: upload / merge via C ABI / download "
+                       "on three streams, 3 device slots) -> pinned host"}
 
     if rank == 0:
         line = {

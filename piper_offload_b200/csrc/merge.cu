@@ -364,7 +364,7 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
   const float amax = tree_max_abs(merged);
   const MxScale s = mx_scale(amax, W.scale_mode, P::kTarget, P::kMax, P::kMbits);
   const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
-  const PhiloxKey key{W.k0, W.k1};
+  const PhiloxKey key = philox_key(W.k0, W.k1);
   const uint64_t off0 =
       W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
 #pragma unroll
@@ -387,7 +387,10 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
 #pragma unroll
       for (int w = 0; w < 8; ++w) out[w] = 0u;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) out[i >> 2] |= sr_fp8<kE4>(merged[i], P::kMax, key, off0 + i) << ((i & 3) * 8);
+      for (int w4 = 0; w4 < 8; ++w4) {
+        const float x[4] = {merged[4 * w4], merged[4 * w4 + 1], merged[4 * w4 + 2], merged[4 * w4 + 3]};
+        out[w4] = sr_fp8x4<kE4>(x, P::kMax, key, off0 + 4 * w4);
+      }
     } else {
 #pragma unroll
       for (int w = 0; w < 8; ++w)
@@ -472,7 +475,7 @@ __device__ __forceinline__ void nvfp4_block(const DevWeight& W, const RowCtx& c,
     for (int i = 0; i < 16; ++i) m[i] = fminf(fmaxf(m[i], -6.0f), 6.0f);
     uint32_t out[2] = {0u, 0u};
     if (sr) {
-      const PhiloxKey key{W.k0, W.k1};
+      const PhiloxKey key = philox_key(W.k0, W.k1);
       const uint64_t off0 =
           W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
 #pragma unroll
@@ -559,7 +562,7 @@ __device__ __forceinline__ void round_rt2(float& a, float& b, int dt) {
 }
 
 __device__ __forceinline__ void int8_encode32(const float (&m)[32], const Int8Q& q, int qmin, int qmax,
-                                              int scale_dt, bool sr, PhiloxKey key, uint64_t off0,
+                                              int scale_dt, bool sr, const PhiloxKey& key, uint64_t off0,
                                               uint32_t (&out)[8]) {
   float inv = div_full(1.0f, q.scale);
   inv = round_dt_rt(inv, scale_dt);
@@ -591,7 +594,7 @@ __device__ __forceinline__ void int8_encode32(const float (&m)[32], const Int8Q&
 }
 
 __device__ __forceinline__ uint32_t int8_encode(float v, const Int8Q& q, int qmin, int qmax,
-                                                int scale_dt, bool sr, PhiloxKey key,
+                                                int scale_dt, bool sr, const PhiloxKey& key,
                                                 uint64_t off) {
   const float inv = round_dt_rt(div_full(1.0f, q.scale), scale_dt);
   const float scaled = round_dt_rt(__fmul_rn(v, inv), scale_dt);
@@ -795,7 +798,7 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
 #pragma unroll
   for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
   const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
-  const PhiloxKey key{W.k0, W.k1};
+  const PhiloxKey key = philox_key(W.k0, W.k1);
   const int col = c.tile_col0 + 32 * k;
   const uint64_t off0 =
       W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
@@ -1402,7 +1405,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         const bool asym = (W.flags & PIPER_FLAG_ASYMMETRIC) != 0u;
         const int qmin = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? -64 : -128;
         const int qmax = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? 63 : 127;
-        const PhiloxKey key{W.k0, W.k1};
+        const PhiloxKey key = philox_key(W.k0, W.k1);
         const int nchunks = (tcols + 31) / 32;
         if constexpr (PASS == kLocal) {
           // Groups of W.group (multiple of 32, dividing the tile width) are local.
@@ -1459,9 +1462,12 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
                                       c0 + 32 * k;
                 if (W.flags & PIPER_FLAG_STOCHASTIC) {
 #pragma unroll
-                  for (int i = 0; i < 32; ++i) {
-                    const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
-                    out[i >> 2] |= sr_fp8<kE4>(x, kLimit, key, off0 + i) << ((i & 3) * 8);
+                  for (int w4 = 0; w4 < 8; ++w4) {
+                    float x[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                      x[j] = fminf(fmaxf(div_full(merged[4 * w4 + j], s), -kLimit), kLimit);
+                    out[w4] = sr_fp8x4<kE4>(x, kLimit, key, off0 + 4 * w4);
                   }
                 } else {
                   fp8_encode_rtn<kE4>(merged, s, kLimit, out);
@@ -1565,9 +1571,12 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
                   if (owner) reinterpret_cast<float*>(W.scale)[qp] = s;
                   if (sr_on) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                      const float x = fminf(fmaxf(div_full(merged[i], s), -kLimit), kLimit);
-                      out[i >> 2] |= sr_fp8<kE4>(x, kLimit, key, off0 + i) << ((i & 3) * 8);
+                    for (int w4 = 0; w4 < 8; ++w4) {
+                      float x[4];
+#pragma unroll
+                      for (int j = 0; j < 4; ++j)
+                        x[j] = fminf(fmaxf(div_full(merged[4 * w4 + j], s), -kLimit), kLimit);
+                      out[w4] = sr_fp8x4<kE4>(x, kLimit, key, off0 + 4 * w4);
                     }
                   } else {
                     fp8_encode_rtn<kE4>(merged, s, kLimit, out);

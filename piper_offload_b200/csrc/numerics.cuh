@@ -107,32 +107,42 @@ __device__ __forceinline__ float dec_e8m0(uint32_t code) {
 // Triton `tl.rand`: Philox4x32 with 10 rounds, key = (seed lo, seed hi),
 // counter = (offset lo, offset hi, 0, 0); output word 0 folded to a
 // non-negative int32 and scaled by the fp32 constant 0x2FFFFFFF.
+// Philox4x32-10 key schedule, computed once per chunk: round r uses
+// (k0 + r * 0x9E3779B9, k1 + r * 0xBB67AE85). The round keys are the same for
+// every element of a weight, so the element loop only multiplies and xors.
 struct PhiloxKey {
-  uint32_t k0, k1;
+  uint32_t k0[10], k1[10];
 };
 
-__device__ __forceinline__ uint32_t philox_word0(PhiloxKey key, uint64_t offset) {
+__device__ __forceinline__ PhiloxKey philox_key(uint32_t k0, uint32_t k1) {
+  PhiloxKey k;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    k.k0[r] = k0 + static_cast<uint32_t>(r) * 0x9E3779B9u;
+    k.k1[r] = k1 + static_cast<uint32_t>(r) * 0xBB67AE85u;
+  }
+  return k;
+}
+
+__device__ __forceinline__ uint32_t philox_word0(const PhiloxKey& key, uint64_t offset) {
   uint32_t c0 = static_cast<uint32_t>(offset);
   uint32_t c1 = static_cast<uint32_t>(offset >> 32);
   uint32_t c2 = 0u, c3 = 0u;
-  uint32_t k0 = key.k0, k1 = key.k1;
 #pragma unroll
   for (int round = 0; round < 10; ++round) {
     const uint32_t hb = __umulhi(0xCD9E8D57u, c2);
     const uint32_t lb = 0xCD9E8D57u * c2;
     const uint32_t ha = __umulhi(0xD2511F53u, c0);
     const uint32_t la = 0xD2511F53u * c0;
-    c0 = hb ^ c1 ^ k0;
-    c2 = ha ^ c3 ^ k1;
+    c0 = hb ^ c1 ^ key.k0[round];
+    c2 = ha ^ c3 ^ key.k1[round];
     c1 = lb;
     c3 = la;
-    k0 += 0x9E3779B9u;
-    k1 += 0xBB67AE85u;
   }
   return c0;
 }
 
-__device__ __forceinline__ float philox_uniform(PhiloxKey key, uint64_t offset) {
+__device__ __forceinline__ float philox_uniform(const PhiloxKey& key, uint64_t offset) {
   const int32_t w = static_cast<int32_t>(philox_word0(key, offset));
   const int32_t x = w ^ (w >> 31);  // x < 0 ? -x - 1 : x
   return __fmul_rn(__int2float_rn(x), __uint_as_float(0x2FFFFFFFu));
@@ -161,7 +171,7 @@ __device__ __forceinline__ float recip_pow2(float g) {
 // Where the result is not stochastic (p == 0 or |v| == limit) |v| is on the
 // grid, so the reference's round-to-nearest code equals lo.
 template <bool E4M3>
-__device__ __forceinline__ uint32_t sr_fp8(float v, float limit, PhiloxKey key, uint64_t off) {
+__device__ __forceinline__ uint32_t sr_fp8(float v, float limit, const PhiloxKey& key, uint64_t off) {
   constexpr int kMant = E4M3 ? 3 : 2;
   constexpr int kDrop = 23 - kMant;
   constexpr uint32_t kMinNormal = E4M3 ? 0x3C800000u : 0x38800000u;  // 2^-6 / 2^-14
@@ -186,8 +196,72 @@ __device__ __forceinline__ uint32_t sr_fp8(float v, float limit, PhiloxKey key, 
   return (lo + (up ? 1u : 0u)) | ((bits >> 24) & 0x80u);
 }
 
+// Four consecutive counters advanced round by round, so the four independent
+// multiply chains issue back to back.
+__device__ __forceinline__ void philox_word0_x4(const PhiloxKey& key, uint64_t offset, uint32_t (&w)[4]) {
+  uint32_t c0[4], c1[4], c2[4], c3[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint64_t o = offset + static_cast<uint64_t>(j);
+    c0[j] = static_cast<uint32_t>(o);
+    c1[j] = static_cast<uint32_t>(o >> 32);
+    c2[j] = 0u;
+    c3[j] = 0u;
+  }
+#pragma unroll
+  for (int round = 0; round < 10; ++round) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t hb = __umulhi(0xCD9E8D57u, c2[j]);
+      const uint32_t lb = 0xCD9E8D57u * c2[j];
+      const uint32_t ha = __umulhi(0xD2511F53u, c0[j]);
+      const uint32_t la = 0xD2511F53u * c0[j];
+      c0[j] = hb ^ c1[j] ^ key.k0[round];
+      c2[j] = ha ^ c3[j] ^ key.k1[round];
+      c1[j] = lb;
+      c3[j] = la;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) w[j] = c0[j];
+}
+
+// sr_fp8 for four consecutive elements (offsets off .. off+3), packed as the
+// little-endian bytes of one word; same arithmetic as sr_fp8.
+template <bool E4M3>
+__device__ __forceinline__ uint32_t sr_fp8x4(const float (&v)[4], float limit, const PhiloxKey& key, uint64_t off) {
+  constexpr int kMant = E4M3 ? 3 : 2;
+  constexpr int kDrop = 23 - kMant;
+  constexpr uint32_t kMinNormal = E4M3 ? 0x3C800000u : 0x38800000u;
+  constexpr uint32_t kBiasFix = (127u - (E4M3 ? 7u : 15u)) << kMant;
+  constexpr float kSubScale = E4M3 ? 512.0f : 65536.0f;
+  uint32_t r[4];
+  philox_word0_x4(key, off, r);
+  uint32_t word = 0u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t bits = __float_as_uint(v[j]);
+    const uint32_t abits = bits & 0x7FFFFFFFu;
+    const float mag = __uint_as_float(abits);
+    const uint32_t lo_n = (abits >> kDrop) - kBiasFix;
+    const float p_n = __uint_as_float(0x3F800000u | ((abits << kMant) & 0x7FFFFFu)) - 1.0f;
+    const float t = mag * kSubScale;
+    const float fl = truncf(t);
+    const uint32_t lo_s = __float_as_uint(fl + 8388608.0f) - 0x4B000000u;
+    const float p_s = t - fl;
+    const bool normal = abits >= kMinNormal;
+    const uint32_t lo = normal ? lo_n : lo_s;
+    const float p = normal ? p_n : p_s;
+    const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
+    const float u = __fmul_rn(__int2float_rn(x), __uint_as_float(0x2FFFFFFFu));
+    const bool up = mag < limit && p > 0.0f && u < p;
+    word |= ((lo + (up ? 1u : 0u)) | ((bits >> 24) & 0x80u)) << (8 * j);
+  }
+  return word;
+}
+
 // _stochastic_e2m1_code (_triton_stochastic_quantization.py:109-129).
-__device__ __forceinline__ uint32_t sr_e2m1(float v, uint32_t det, PhiloxKey key, uint64_t off) {
+__device__ __forceinline__ uint32_t sr_e2m1(float v, uint32_t det, const PhiloxKey& key, uint64_t off) {
   const float mag = fabsf(v);
   const uint32_t nc = det & 7u;
   const bool down = e2m1_mag(nc) > mag;
@@ -204,7 +278,7 @@ __device__ __forceinline__ uint32_t sr_e2m1(float v, uint32_t det, PhiloxKey key
 
 // _stochastic_round_to_int (_triton_stochastic_quantization.py:24-39);
 // returns the (possibly) re-rounded value as a float.
-__device__ __forceinline__ float sr_int(float v, float det, float qmin, float qmax, PhiloxKey key,
+__device__ __forceinline__ float sr_int(float v, float det, float qmin, float qmax, const PhiloxKey& key,
                                         uint64_t off) {
   const float lower = floorf(v);
   const float p = __fsub_rn(v, lower);
