@@ -262,7 +262,7 @@ namespace pm {
 // ------------------------------------------------- bulk tensor (TMA) copies
 // 2-D tile load into shared memory, completion counted on `bar` (expect_tx).
 // `tmap` is the generic address of a CUtensorMap kernel parameter. The
-// innermost coordinate x must be a multiple of 16 bytes. No multicast.
+// innermost coordinate x must be a multiple of 16 bytes. Every load here targets this CTA only.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
