@@ -51,7 +51,11 @@ namespace pm {
 constexpr int kMaxWeights = 24;
 constexpr int kMaxRank = 256;
 
-enum Pass : int { kLocal = 0, kReduce = 1, kEncode = 2 };
+// kLocal: scales local to a tile, one pass. kReduce / kEncode: the two
+// launches of layouts whose scales need a reduction across CTAs (per-tensor,
+// wide groups, NVFP4 global scale). kFused: per-row layouts in one launch;
+// each CTA reduces, then encodes, whole 128-row strips.
+enum Pass : int { kLocal = 0, kReduce = 1, kEncode = 2, kFused = 3 };
 
 // Device-side descriptor of one weight (or a row range of one weight).
 struct alignas(64) DevWeight {
@@ -916,8 +920,12 @@ __host__ __device__ constexpr int ws_code_stage_bytes(int code_slot) {
 }
 __host__ __device__ constexpr int ws_a_stage_bytes(int kp, int bn) { return align_up(kp * bn * 2, 1024); }
 __host__ __device__ constexpr int ws_b_buf_bytes(int kp) { return 128 * kp * 2; }
+// The tail holds the mbarriers (512 B) and, for fused per-row passes, each
+// epilogue warpgroup's partial row maxima for two items (2 x 3 x 128 float2).
+constexpr int kTailBytes = 512 + 2 * 3 * 128 * 8;
 __host__ __device__ constexpr int ws_smem_bytes(int code_slot, int kp, int bn, int sc, int sa, int nbb) {
-  return 1024 + sc * ws_code_stage_bytes(code_slot) + sa * ws_a_stage_bytes(kp, bn) + nbb * ws_b_buf_bytes(kp) + 512;
+  return 1024 + sc * ws_code_stage_bytes(code_slot) + sa * ws_a_stage_bytes(kp, bn) + nbb * ws_b_buf_bytes(kp) +
+         kTailBytes;
 }
 
 struct ItemGeom {
@@ -992,7 +1000,9 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
   uint64_t* afull = bempty + 2;           // [kMaxAcc]
   uint64_t* aempty = afull + kMaxAcc;     // [kMaxAcc]
   uint64_t* mma_done = aempty + kMaxAcc;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* rmax_bar = mma_done + 1;      // [2] partial row maxima published (fused per-row)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rmax_bar + 2);
+  float2* rpart = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + 512);  // [2][kEpiWGs][128]
   auto stage_codes = [&](int s) { return sCode + s * kCodeStage; };
   auto stage_scales = [&](int s) { return sCode + s * kCodeStage + G::kCodeSlot; };
   auto stage_a = [&](int x) { return sAst + x * kAStage; };
@@ -1004,8 +1014,9 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
     }
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1 + kLoadThreads);
-      // REDUCE stores nothing: each warp of the tile's warpgroup releases the stage.
-      mbar_init(&empty[i], PASS == kReduce ? 4 : 1);
+      // REDUCE steps store nothing: each warp of the tile's warpgroup releases
+      // the stage (fused passes release stored stages with four arrivals too).
+      mbar_init(&empty[i], (PASS == kReduce || PASS == kFused) ? 4 : 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bfull[i], 1 + kLoadThreads);
@@ -1016,6 +1027,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
       mbar_init(&aempty[i], 4);  // the four warps of the tile's warpgroup
     }
     mbar_init(mma_done, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&rmax_bar[i], kEpiWGs);
     fence_mbar_init();
   }
   constexpr int NB = 512 / BN;  // accumulator buffers in the 512 tensor-memory columns
@@ -1059,7 +1071,10 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         } else {
           mbar_arrive(&bfull[jb]);
         }
-        for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
+        // Fused per-row passes visit every column tile twice: reduce, then encode.
+        const int n_steps = PASS == kFused ? 2 * g.n_tiles : g.n_tiles;
+        for (int st = 0; st < n_steps; ++st, ++t) {
+          const int tile = st < g.n_tiles ? st : st - g.n_tiles;
           const int c0 = g.col_begin + tile * BN;
           // A tile: BN/64 boxes of 64 columns x KP rows (MN-major, 128-byte swizzle).
           const int x = t % SA;
@@ -1116,7 +1131,10 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         const uint32_t a_base = smem_u32(sB + jb * ws_b_buf_bytes(KPL));
         const int kb = kb_row(KP);
         const uint32_t a_layout = swizzle_layout(kb);
-        for (int tile = 0; tile < g.n_tiles && ok; ++tile, ++t) {
+        // Fused per-row passes visit every column tile twice: reduce, then encode.
+        const int n_steps = PASS == kFused ? 2 * g.n_tiles : g.n_tiles;
+        for (int st = 0; st < n_steps && ok; ++st, ++t) {
+          const int tile = st < g.n_tiles ? st : st - g.n_tiles;
           const int x = t % SA;
           const int ab = t % NB;
           ok = mbar_wait(&full_a[x], (t / SA) & 1u, kStatusTimeoutLoad);
@@ -1189,7 +1207,10 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
       __threadfence_block();  // plain smem stores of ragged rows precede the arrival
       cp_async_mbar_arrive(&bfull[jb]);
       const bool vec_a = ((reinterpret_cast<uintptr_t>(W.a) | (W.N * 2)) & 15) == 0;
-      for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
+      // Fused per-row passes visit every column tile twice: reduce, then encode.
+      const int n_steps = PASS == kFused ? 2 * g.n_tiles : g.n_tiles;
+      for (int st = 0; st < n_steps; ++st, ++t) {
+        const int tile = st < g.n_tiles ? st : st - g.n_tiles;
         const int c0 = g.col_begin + tile * BN;
         const int ncols = min(BN, g.col_end - c0);
         const int x = t % SA;
@@ -1283,9 +1304,12 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
     const uint32_t bar_id = 1u + static_cast<uint32_t>(wg);  // this warpgroup's named barrier
     const uint32_t lane_off = static_cast<uint32_t>((e >> 5) & 3) * 32u << 16;
     uint32_t t = 0;
-    int pending = -1;  // stage whose bulk store may still be reading it
+    uint32_t it_e = 0;  // items done by this CTA (fused passes: parity of the row-maxima slot)
+    int pending = -1;   // stage whose bulk store may still be reading it
+    // Stages are released by four arrivals when warps release them one by one.
+    constexpr uint32_t kStoreRelease = PASS == kFused ? 4u : 1u;
     bool ok = true;
-    for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x) {
+    for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x, ++it_e) {
       const ItemGeom g = item_geom<BN>(P, item);
       const DevWeight& W = P.w[g.wi];
       const int local = item - W.item_begin;
@@ -1323,13 +1347,68 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         }
       }
 
-      for (int tile = 0; tile < g.n_tiles; ++tile, ++t) {
+      // Fused per-row passes: the row's input scale / zero point are read once,
+      // before any warpgroup can publish (and so before the new scale is
+      // written); the new qparams follow from the combined row maxima.
+      float f_s_in = 1.0f;
+      int f_z_in = 0;
+      bool fq_ready = false;
+      float f_s = 1.0f;
+      Int8Q f_q;
+      f_q.scale = 1.0f;
+      f_q.zp = 0;
+      if constexpr (PASS == kFused) {
+        if (valid) {
+          qp_load<FMT, kReduce>(W, row, qc);
+          f_s_in = qc.s_in;
+          f_z_in = qc.z_in;
+        }
+      }
+
+      // Fused per-row passes visit every column tile twice: reduce, then encode.
+      const int n_steps = PASS == kFused ? 2 * g.n_tiles : g.n_tiles;
+      for (int st = 0; st < n_steps; ++st, ++t) {
+        const int tile = st < g.n_tiles ? st : st - g.n_tiles;
+        const bool enc_phase = PASS == kFused && st >= g.n_tiles;
+        if constexpr (PASS == kFused) {
+          if (st == g.n_tiles) {
+            // Publish this warpgroup's partial row maxima (zero when it saw no
+            // tile of the strip) for the encode steps of every warpgroup.
+            rpart[((it_e & 1u) * kEpiWGs + wg) * 128 + rt] = make_float2(red_max, red_nmin);
+            named_bar_sync(bar_id, 128);
+            if (rt == 0) mbar_arrive(&rmax_bar[it_e & 1u]);
+          }
+        }
         if (static_cast<int>(t % kEpiWGs) != wg) continue;  // another warpgroup's tile
+        if (enc_phase && !fq_ready) {
+          ok = mbar_wait(&rmax_bar[it_e & 1u], (it_e >> 1) & 1u, kStatusTimeoutLoad);
+          float amax = 0.0f, nmin = 0.0f;
+#pragma unroll
+          for (int w = 0; w < kEpiWGs; ++w) {
+            const float2 v = rpart[((it_e & 1u) * kEpiWGs + w) * 128 + rt];
+            amax = fmaxf(amax, v.x);
+            nmin = fmaxf(nmin, v.y);
+          }
+          if constexpr (FMT == PIPER_FMT_INT8) {
+            const bool asym = (W.flags & PIPER_FLAG_ASYMMETRIC) != 0u;
+            const int qlo = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? -64 : -128;
+            const int qhi = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? 63 : 127;
+            f_q = int8_qparams<CDT>(-nmin, amax, asym, qlo, qhi, W.scale_dt);
+            if (valid && tile == 0) {
+              store_scale_dt(W.scale, row, W.scale_dt, f_q.scale);
+              if (W.zp != nullptr) W.zp[row] = static_cast<int8_t>(f_q.zp);
+            }
+          } else if constexpr (FMT == PIPER_FMT_FP8_E4M3 || FMT == PIPER_FMT_FP8_E5M2) {
+            f_s = fp8_new_scale<CDT>(amax, FMT == PIPER_FMT_FP8_E4M3 ? 448.0f : 57344.0f);
+            if (valid && tile == 0) reinterpret_cast<float*>(W.scale)[row] = f_s;
+          }
+          fq_ready = true;
+        }
         const int s = t % S;
         const int ab = t % NB;
         const int c0 = g.col_begin + tile * BN;
         const int tcols = min(BN, g.col_end - c0);
-        ok = mbar_wait(&full[s], (t / S) & 1u, kStatusTimeoutLoad);
+        if (ok) ok = mbar_wait(&full[s], (t / S) & 1u, kStatusTimeoutLoad);
         if (ok) ok = mbar_wait(&afull[ab], (t / NB) & 1u, kStatusTimeoutMma);
         // One decision for all threads that meet at a barrier below: the
         // warpgroup when the tile is stored, each warp alone in REDUCE passes.
@@ -1339,7 +1418,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         if (rt == 0 && pending >= 0) {
           // The previous tile's bulk store has long finished reading its stage.
           bulk_wait_read_all();
-          mbar_arrive(&empty[pending]);
+          mbar_arrive_cnt(&empty[pending], kStoreRelease);
           pending = -1;
         }
         tc_fence_after();
@@ -1407,7 +1486,51 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         const int qmax = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? 63 : 127;
         const PhiloxKey key = philox_key(W.k0, W.k1);
         const int nchunks = (tcols + 31) / 32;
-        if constexpr (PASS == kLocal) {
+        if constexpr (PASS == kFused) {
+          // Per-row layout: one quantization block per row, qparams on chip.
+          chunk_loop(0, nchunks, [&](int k, const float (&acc)[32]) {
+            float merged[32];
+            affine_merged_u<FMT, CDT>(W, c, k, acc, f_s_in, f_z_in, merged);
+            const int nvalid = min(32, tcols - 32 * k);
+            if (nvalid < 32) {
+              // Columns past the row end are zero, which leaves the maxima unchanged.
+#pragma unroll
+              for (int i = 0; i < 32; ++i) merged[i] = i < nvalid ? merged[i] : 0.0f;
+            }
+            if (!enc_phase) {
+              if (valid) {
+                if constexpr (kInt8) {
+                  red_max = fmaxf(red_max, tree_max(merged));
+                  red_nmin = fmaxf(red_nmin, -tree_min(merged));
+                } else {
+                  red_max = fmaxf(red_max, tree_max_abs(merged));
+                }
+              }
+            } else {
+              uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+              if (valid) {
+                const uint64_t off0 =
+                    W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + c0 + 32 * k;
+                const bool sr_on = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+                if constexpr (kInt8) {
+                  int8_encode32(merged, f_q, qmin, qmax, W.scale_dt, sr_on, key, off0, out);
+                } else if (sr_on) {
+#pragma unroll
+                  for (int w4 = 0; w4 < 8; ++w4) {
+                    float x[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                      x[j] = fminf(fmaxf(div_full(merged[4 * w4 + j], f_s), -kLimit), kLimit);
+                    out[w4] = sr_fp8x4<kE4>(x, kLimit, key, off0 + 4 * w4);
+                  }
+                } else {
+                  fp8_encode_rtn<kE4>(merged, f_s, kLimit, out);
+                }
+              }
+              store_chunks32(c, k, out);
+            }
+          });
+        } else if constexpr (PASS == kLocal) {
           // Groups of W.group (multiple of 32, dividing the tile width) are local.
           const int gch = W.group / 32;
           for (int g0 = 0; g0 < nchunks; g0 += gch) {
@@ -1635,7 +1758,8 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         if (lane == 0) mbar_arrive(&aempty[ab]);
 
         // ---- write the tile back (in place) and release the stage.
-        if (PASS != kReduce && tma) {
+        const bool stores = PASS == kLocal || PASS == kEncode || enc_phase;
+        if (stores && tma) {
           fence_proxy_async_smem();
           named_bar_sync(bar_id, 128);
           if (rt == 0) {
@@ -1648,7 +1772,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
             bulk_commit();
             pending = s;
           }
-        } else if constexpr (PASS == kReduce) {
+        } else if (!stores) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[s]);
         } else {
@@ -1676,10 +1800,10 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
           if (rt == 0) {
             if (pending >= 0) {
               bulk_wait_read_all();
-              mbar_arrive(&empty[pending]);
+              mbar_arrive_cnt(&empty[pending], kStoreRelease);
               pending = -1;
             }
-            mbar_arrive(&empty[s]);
+            mbar_arrive_cnt(&empty[s], kStoreRelease);
           }
         }
       }
@@ -1776,7 +1900,7 @@ PipeCfg plan_pipe(int fmt, int bn, int kp) {
   const int cs = pm::ws_code_stage_bytes(ws_code_slot(fmt, bn));
   const int as = pm::ws_a_stage_bytes(kp, bn);
   const int bs = pm::ws_b_buf_bytes(kp);
-  const int avail = pm::kSmemLimit - 1024 - 512;
+  const int avail = pm::kSmemLimit - 1024 - pm::kTailBytes;
   const int pref[][3] = {{2, 3, 6}, {2, 2, 6}, {1, 2, 6}, {2, 2, 4}, {1, 2, 4}, {1, 2, 3}, {1, 1, 2}};
   for (const auto& q : pref) {
     const int rest = avail - q[0] * bs - q[1] * as;
@@ -1790,6 +1914,7 @@ PipeCfg plan_pipe(int fmt, int bn, int kp) {
 struct Plan {
   int bn = 128;
   bool two_pass = false;
+  bool fused = false;  // per-row FP8 / INT8: one kFused launch, no workspace
   int nq = 0;          // quantization blocks held in the workspace
   int nq_row = 0;      // blocks per row (0 = per tensor)
   int group = 0;
@@ -1867,6 +1992,8 @@ int validate(const piper_merge_desc& d, Plan& p) {
         p.nq_row = static_cast<int>(d.cols / g);
         if (g < d.cols && (g == 32 || g == 64 || g == 128 || g == 256)) {
           // groups are local to a tile: encoded in one pass
+        } else if (g == d.cols) {
+          p.fused = true;  // per-row: each CTA reduces then encodes its strips, one launch
         } else {
           p.two_pass = true;
           p.nq = static_cast<int>(d.rows * p.nq_row);
@@ -1893,7 +2020,7 @@ int validate(const piper_merge_desc& d, Plan& p) {
   else if (fits(64, 2)) p.bn = 64;
   else return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(d.rank) + " is too large for the merge pipeline.");
   if ((d.format == PIPER_FMT_FP8_E4M3 || d.format == PIPER_FMT_FP8_E5M2 || d.format == PIPER_FMT_INT8) &&
-      !p.two_pass && p.group > p.bn) {
+      !p.two_pass && !p.fused && p.group > p.bn) {
     p.two_pass = true;  // the group no longer fits one tile
     p.nq = static_cast<int>(d.rows * p.nq_row);
   }
@@ -1969,7 +2096,8 @@ int launch_fmt(int fmt, int bn, LaunchParams& lp, int items, int kp, cudaStream_
       if constexpr (PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP4, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_NVFP4:
-      if constexpr (PASS != pm::kEncode && CDT == pm::kBF16) return launch_bn<PIPER_FMT_NVFP4, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr ((PASS == pm::kLocal || PASS == pm::kReduce) && CDT == pm::kBF16)
+        return launch_bn<PIPER_FMT_NVFP4, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_FP8_E4M3: return launch_bn<PIPER_FMT_FP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
     case PIPER_FMT_FP8_E5M2: return launch_bn<PIPER_FMT_FP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
@@ -1990,10 +2118,12 @@ int launch(int pass, int cdt, int fmt, int bn, LaunchParams& lp, int items, int 
   if (cdt == PIPER_DT_BF16) {
     if (pass == pm::kLocal) return launch_fmt<pm::kLocal, pm::kBF16>(fmt, bn, lp, items, kp, s);
     if (pass == pm::kReduce) return launch_fmt<pm::kReduce, pm::kBF16>(fmt, bn, lp, items, kp, s);
+    if (pass == pm::kFused) return launch_fmt<pm::kFused, pm::kBF16>(fmt, bn, lp, items, kp, s);
     return launch_fmt<pm::kEncode, pm::kBF16>(fmt, bn, lp, items, kp, s);
   }
   if (pass == pm::kLocal) return launch_fmt<pm::kLocal, pm::kF16>(fmt, bn, lp, items, kp, s);
   if (pass == pm::kReduce) return launch_fmt<pm::kReduce, pm::kF16>(fmt, bn, lp, items, kp, s);
+  if (pass == pm::kFused) return launch_fmt<pm::kFused, pm::kF16>(fmt, bn, lp, items, kp, s);
   return launch_fmt<pm::kEncode, pm::kF16>(fmt, bn, lp, items, kp, s);
 }
 
@@ -2161,7 +2291,8 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
     const Plan& p = plans[segs[i].desc];
     DevWeight w = make_dev_weight(d, p, ws, segs[i]);
     const int col_tiles = static_cast<int>((d.cols + p.bn - 1) / p.bn);
-    const int ci = std::max(1, (col_tiles + tiles_per_item - 1) / tiles_per_item);
+    // Fused per-row passes need whole rows in one item.
+    const int ci = p.fused ? 1 : std::max(1, (col_tiles + tiles_per_item - 1) / tiles_per_item);
     const int tiles_each = (col_tiles + ci - 1) / ci;
     w.item_cols = tiles_each * p.bn;
     w.col_items = (col_tiles + tiles_each - 1) / tiles_each;
@@ -2176,6 +2307,8 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
     if (rc) return rc;
     const int second = d0.format == PIPER_FMT_NVFP4 ? pm::kLocal : pm::kEncode;
     rc = launch(second, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
+  } else if (p0.fused) {
+    rc = launch(pm::kFused, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
   } else {
     rc = launch(pm::kLocal, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
   }
@@ -2184,7 +2317,7 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
 
 bool same_kernel(const piper_merge_desc& a, const Plan& pa, const piper_merge_desc& b, const Plan& pb) {
   return a.format == b.format && a.compute_dtype == b.compute_dtype && pa.bn == pb.bn &&
-         pa.two_pass == pb.two_pass;
+         pa.two_pass == pb.two_pass && pa.fused == pb.fused;
 }
 
 int plan_all(const piper_merge_desc* descs, int count, std::vector<Plan>& plans, size_t& ws_total) {

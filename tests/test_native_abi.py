@@ -74,18 +74,21 @@ def test_invalid_descriptors_are_rejected_on_host(kw, match):
 
 def test_workspace_sizes():
     assert nat.workspace_bytes([_desc(format=nat.FMT_MXFP8_E4M3)]) == 0
-    per_row = nat.workspace_bytes([_desc()])  # 64 row blocks x 16 bytes
-    assert per_row == 1024
+    # per-row layouts keep their row maxima on chip (one fused launch): no workspace
+    assert nat.workspace_bytes([_desc()]) == 0
+    # groups wider than a tile: 64 rows x 2 blocks x 16 bytes
+    assert nat.workspace_bytes([_desc(cols=1024, block_cols=512)]) == 2048
     per_tensor = nat.workspace_bytes([_desc(block_rows=64, block_cols=256)])
     assert per_tensor == 256
     grouped_local = nat.workspace_bytes([_desc(block_cols=64)])
     assert grouped_local == 0
-    two = nat.workspace_bytes([_desc(), _desc(block_rows=64, block_cols=256)])
-    assert two == 1024 + 256
+    two = nat.workspace_bytes([_desc(cols=1024, block_cols=512), _desc(block_rows=64, block_cols=256)])
+    assert two == 2048 + 256
 
 
 def test_workspace_too_small_is_reported():
-    d = _desc()
+    # A per-tensor layout needs workspace; the call is rejected before any launch.
+    d = _desc(block_rows=64, block_cols=256)
     arr = (nat.MergeDesc * 1)(d)
     rc = nat.load().piper_merge_batch(arr, 1, ctypes.c_void_p(0x100000), 16, None)
     assert rc == nat.EWORKSPACE

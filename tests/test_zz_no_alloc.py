@@ -34,13 +34,18 @@ def _bind():
 
 
 @pytest.mark.parametrize("seed", [None, 0x9C3EA68DBAC91AAD])
-@pytest.mark.parametrize("rows,cols,layout", [(300, 512, "row"), (70, 130, "row"), (256, 1024, "tensor")])
+@pytest.mark.parametrize("rows,cols,layout", [(300, 512, "row"), (70, 130, "row"), (256, 1024, "tensor"),
+                                             (200, 1024, "group512")])
 def test_noalloc_matches_workspace_entry(cuda_device, seed, rows, cols, layout):
     fn, ref = _bind()
     w = S.normal((rows, cols), 0.02, seed=rows + cols, device=cuda_device)
-    q = S.quantize_fp8(w, per_tensor=layout == "tensor")
+    if layout == "group512":
+        q = S.quantize_fp8(w, group=512)
+        block = (1, 512)
+    else:
+        q = S.quantize_fp8(w, per_tensor=layout == "tensor")
+        block = (1, cols) if layout == "row" else (rows, cols)
     b, a = S.lora_factors(rows, cols, 16, 0.01, seed=rows * 3 + 1, device=cuda_device)
-    block = (1, cols) if layout == "row" else (rows, cols)
     ref_q, ref_s = q.qdata.clone(), q.scale.clone()
     new_q, new_s = q.qdata.clone(), q.scale.clone()
     ws = torch.zeros(1 << 20, dtype=torch.uint8, device=cuda_device)
@@ -63,13 +68,15 @@ def test_noalloc_matches_workspace_entry(cuda_device, seed, rows, cols, layout):
 
 def test_noalloc_rejects_layout_beyond_static_scratch(cuda_device):
     fn, _ = _bind()
-    rows, cols = 70000, 16  # per-row: 70,000 quantization blocks > 65,536
+    # Groups of 512 columns are wider than a tile, so their maxima go through
+    # the scratch: 70,000 rows x 2 groups = 140,000 quantization blocks > 65,536.
+    rows, cols, group = 70000, 1024, 512
     q = torch.zeros((rows, cols), dtype=torch.uint8, device=cuda_device)
-    s = torch.ones((rows, 1), dtype=torch.float32, device=cuda_device)
+    s = torch.ones((rows, cols // group), dtype=torch.float32, device=cuda_device)
     b = torch.zeros((rows, 16), dtype=torch.bfloat16, device=cuda_device)
     a = torch.zeros((16, cols), dtype=torch.bfloat16, device=cuda_device)
     before = q.clone()
-    rc = fn(q.data_ptr(), s.data_ptr(), b.data_ptr(), a.data_ptr(), rows, cols, 16, 1, cols, 0, nat.DT_BF16, 1.0,
+    rc = fn(q.data_ptr(), s.data_ptr(), b.data_ptr(), a.data_ptr(), rows, cols, 16, 1, group, 0, nat.DT_BF16, 1.0,
             0, 0, 0, torch.cuda.current_stream(cuda_device).cuda_stream)
     assert rc == nat.EWORKSPACE
     assert b"static scratch" in nat.load().piper_merge_last_error()
