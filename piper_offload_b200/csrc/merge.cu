@@ -1074,7 +1074,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         // Fused per-row passes visit every column tile twice: reduce, then encode.
         const int n_steps = PASS == kFused ? 2 * g.n_tiles : g.n_tiles;
         for (int st = 0; st < n_steps; ++st, ++t) {
-          const int tile = st < g.n_tiles ? st : st - g.n_tiles;
+          const int tile = st < g.n_tiles ? st : 2 * g.n_tiles - 1 - st;  // encode sweep runs backwards: L2-hot tiles first
           const int c0 = g.col_begin + tile * BN;
           // A tile: BN/64 boxes of 64 columns x KP rows (MN-major, 128-byte swizzle).
           const int x = t % SA;
@@ -1134,7 +1134,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         // Fused per-row passes visit every column tile twice: reduce, then encode.
         const int n_steps = PASS == kFused ? 2 * g.n_tiles : g.n_tiles;
         for (int st = 0; st < n_steps && ok; ++st, ++t) {
-          const int tile = st < g.n_tiles ? st : st - g.n_tiles;
+          const int tile = st < g.n_tiles ? st : 2 * g.n_tiles - 1 - st;  // encode sweep runs backwards: L2-hot tiles first
           const int x = t % SA;
           const int ab = t % NB;
           ok = mbar_wait(&full_a[x], (t / SA) & 1u, kStatusTimeoutLoad);
@@ -1210,7 +1210,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
       // Fused per-row passes visit every column tile twice: reduce, then encode.
       const int n_steps = PASS == kFused ? 2 * g.n_tiles : g.n_tiles;
       for (int st = 0; st < n_steps; ++st, ++t) {
-        const int tile = st < g.n_tiles ? st : st - g.n_tiles;
+        const int tile = st < g.n_tiles ? st : 2 * g.n_tiles - 1 - st;  // encode sweep runs backwards: L2-hot tiles first
         const int c0 = g.col_begin + tile * BN;
         const int ncols = min(BN, g.col_end - c0);
         const int x = t % SA;
@@ -1368,7 +1368,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
       // Fused per-row passes visit every column tile twice: reduce, then encode.
       const int n_steps = PASS == kFused ? 2 * g.n_tiles : g.n_tiles;
       for (int st = 0; st < n_steps; ++st, ++t) {
-        const int tile = st < g.n_tiles ? st : st - g.n_tiles;
+        const int tile = st < g.n_tiles ? st : 2 * g.n_tiles - 1 - st;  // encode sweep runs backwards: L2-hot tiles first
         const bool enc_phase = PASS == kFused && st >= g.n_tiles;
         if constexpr (PASS == kFused) {
           if (st == g.n_tiles) {
@@ -1394,15 +1394,19 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
             const int qlo = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? -64 : -128;
             const int qhi = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? 63 : 127;
             f_q = int8_qparams<CDT>(-nmin, amax, asym, qlo, qhi, W.scale_dt);
-            if (valid && tile == 0) {
-              store_scale_dt(W.scale, row, W.scale_dt, f_q.scale);
-              if (W.zp != nullptr) W.zp[row] = static_cast<int8_t>(f_q.zp);
-            }
           } else if constexpr (FMT == PIPER_FMT_FP8_E4M3 || FMT == PIPER_FMT_FP8_E5M2) {
             f_s = fp8_new_scale<CDT>(amax, FMT == PIPER_FMT_FP8_E4M3 ? 448.0f : 57344.0f);
-            if (valid && tile == 0) reinterpret_cast<float*>(W.scale)[row] = f_s;
           }
           fq_ready = true;
+        }
+        if (enc_phase && tile == 0 && valid) {
+          // The warpgroup that encodes the row's first tile writes its new qparams.
+          if constexpr (FMT == PIPER_FMT_INT8) {
+            store_scale_dt(W.scale, row, W.scale_dt, f_q.scale);
+            if (W.zp != nullptr) W.zp[row] = static_cast<int8_t>(f_q.zp);
+          } else if constexpr (FMT == PIPER_FMT_FP8_E4M3 || FMT == PIPER_FMT_FP8_E5M2) {
+            reinterpret_cast<float*>(W.scale)[row] = f_s;
+          }
         }
         const int s = t % S;
         const int ab = t % NB;
