@@ -212,6 +212,29 @@ def test_batched_multi_weight_launch(cuda_device):
         assert d.scale_mismatch == 0, (cs.fmt, d)
 
 
+def test_batched_mixed_tma_and_fallback_weights(cuda_device):
+    """One fused launch over per-row weights whose codes and factors move by
+    bulk tensor copies (aligned rows) and weights that need the cp.async
+    fallback (130-column rows, rank 7), alternating, RTN and stochastic."""
+    specs = [("fp8_row", 300, 512, 32), ("fp8_row", 70, 130, 7), ("fp8_row", 256, 1024, 16),
+             ("fp8_row", 35, 69, 7), ("int8_row", 200, 512, 16), ("int8_row", 35, 69, 7)]
+    cases = [Case(f, r, c, k, seed=SEED if i % 3 == 1 else None).build(data_seed=50 + i) for i, (f, r, c, k) in
+             enumerate(specs)]
+    wants = [cs.run_oracle() for cs in cases]
+    descs, keep = [], []
+    for cs in cases:
+        d, held = _desc_for(cs, cuda_device)
+        descs.append(d)
+        keep.append(held)
+    _native.merge_batch(descs, cuda_device)
+    torch.cuda.synchronize(cuda_device)
+    assert _native.device_status(cuda_device) == 0
+    for cs, held, want in zip(cases, keep, wants):
+        d = compare(cs, _collect(cs, held), want)
+        assert d.code_mismatch <= math.floor(TIE_FRACTION * d.n) and d.max_step <= 1, (cs.fmt, cs.rows, cs.cols, d)
+        assert d.scale_mismatch == 0, (cs.fmt, cs.rows, cs.cols, d)
+
+
 def _desc_for(cs: Case, dev):
     from merge_cases import f32np  # noqa: F401
 
