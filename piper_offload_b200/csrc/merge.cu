@@ -775,25 +775,62 @@ __device__ __forceinline__ float roundf_away(float x) {  // gguf.quants.np_round
   return x > 0.0f ? b : (x < 0.0f ? -b : 0.0f * x);
 }
 
+// Signed byte b of `w` (xor 0x80 already applied) as a float, exactly:
+// 2^23 + (b ^ 0x80) assembled by a byte permute, minus 2^23 + 128.
+__device__ __forceinline__ float sbyte_to_float(uint32_t wx, int b) {
+  return __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u + static_cast<uint32_t>(b))) - 8388736.0f;
+}
+// Byte b of `w` (a value 0..15) minus 8 as a float, exactly.
+__device__ __forceinline__ float nibble_to_float_m8(uint32_t w, int b) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + static_cast<uint32_t>(b))) - 8388616.0f;
+}
+// Low byte of an integer-valued float in [-2^22, 2^22] (two's complement), exactly.
+__device__ __forceinline__ uint32_t float_int_bits(float q) { return __float_as_uint(q + 12582912.0f); }
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
+}
+
+// One GGUF block (32 elements) of a tile row. Blocks start at even byte
+// offsets, so a block is read and written as the 4-byte words that cover it
+// (9 for Q8_0, 5 for Q4_0); the 2 bytes of a neighbouring block that share a
+// word are written back unchanged (this thread owns the whole row segment).
 template <int FMT, int CDT>
 __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, int k,
                                            const float (&acc)[32]) {
   constexpr bool kQ8 = FMT == PIPER_FMT_GGUF_Q8_0;
   constexpr int kTS = kQ8 ? 34 : 18;
-  uint8_t* blk = c.srow + kTS * k;
-  const unsigned short dbits = static_cast<unsigned short>(blk[0] | (blk[1] << 8));
-  const float d_in = round_dt<CDT>(__half2float(__ushort_as_half(dbits)));
-  float merged[32];
+  constexpr int kWords = kQ8 ? 9 : 5;
+  constexpr int kCodeWords = kQ8 ? 8 : 4;
+  const int byte0 = kTS * k;
+  const bool odd = (byte0 & 2) != 0;  // the block starts in the high half of its first word
+  uint32_t* wp = reinterpret_cast<uint32_t*>(c.srow + (byte0 & ~3));
+  uint32_t w[kWords];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    float qv;
-    if constexpr (kQ8) {
-      qv = static_cast<float>(static_cast<int8_t>(blk[2 + i]));
-    } else {
-      const uint32_t byte = blk[2 + (i & 15)];
-      qv = static_cast<float>(static_cast<int>(i < 16 ? (byte & 0xFu) : (byte >> 4)) - 8);
+  for (int j = 0; j < kWords; ++j) w[j] = wp[j];
+  const uint32_t dbits = odd ? (w[0] >> 16) : (w[0] & 0xFFFFu);
+  uint32_t cw[kCodeWords];
+#pragma unroll
+  for (int j = 0; j < kCodeWords; ++j) cw[j] = odd ? w[j + 1] : __funnelshift_r(w[j], w[j + 1], 16);
+  const float d_in = round_dt<CDT>(__half2float(__ushort_as_half(static_cast<unsigned short>(dbits))));
+  float merged[32];
+  if constexpr (kQ8) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t x = cw[j] ^ 0x80808080u;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) merged[4 * j + b] = __fmul_rn(d_in, sbyte_to_float(x, b));
     }
-    merged[i] = __fmul_rn(d_in, qv);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t lo = cw[j] & 0x0F0F0F0Fu;         // elements 4j .. 4j+3
+      const uint32_t hi = (cw[j] >> 4) & 0x0F0F0F0Fu;  // elements 16+4j .. 16+4j+3
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        merged[4 * j + b] = __fmul_rn(d_in, nibble_to_float_m8(lo, b));
+        merged[16 + 4 * j + b] = __fmul_rn(d_in, nibble_to_float_m8(hi, b));
+      }
+    }
   }
 #pragma unroll
   for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
@@ -806,20 +843,24 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
   const int col = c.tile_col0 + 32 * k;
   const uint64_t off0 =
       W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
+  uint32_t ow[kCodeWords];
+  uint32_t dh;
   if constexpr (kQ8) {
     const float amax = tree_max_abs(merged);
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-    const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+    dh = __half_as_ushort(__float2half_rn(d));
+    uint32_t qb[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const float x = __fmul_rn(merged[i], id);
       float q = roundf_away(x);
       if (sr) q = sr_int(x, q, -127.0f, 127.0f, key, off0 + i);
       q = fminf(fmaxf(q, -128.0f), 127.0f);
-      blk[2 + i] = static_cast<uint8_t>(static_cast<int8_t>(static_cast<int>(q)));
+      qb[i] = float_int_bits(q);
     }
-    *reinterpret_cast<unsigned short*>(blk) = dh;  // blocks start at even offsets
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ow[j] = pack_low_bytes(qb[4 * j], qb[4 * j + 1], qb[4 * j + 2], qb[4 * j + 3]);
   } else {
     int imax = 0;
     float best = fabsf(merged[0]);
@@ -836,37 +877,51 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
     for (int i = 1; i < 32; ++i) mx = (i == imax) ? merged[i] : mx;
     const float d = __fdiv_rn(mx, -8.0f);
     const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-    const unsigned short dh = __half_as_ushort(__float2half_rn(d));
-    uint32_t q[32];
+    dh = __half_as_ushort(__float2half_rn(d));
+    uint32_t qb[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const float x = __fmul_rn(merged[i], id);
       float qf = truncf(__fadd_rn(x, 8.5f));
       if (sr) qf = sr_int(__fadd_rn(x, 8.0f), qf, 0.0f, 15.0f, key, off0 + i);
       qf = fminf(fmaxf(qf, 0.0f), 15.0f);
-      q[i] = static_cast<uint32_t>(qf);
+      qb[i] = float_int_bits(qf);
     }
+    // byte j = element j (low nibble) | element j+16 (high nibble)
 #pragma unroll
-    for (int j = 0; j < 16; ++j) blk[2 + j] = static_cast<uint8_t>(q[j] | (q[j + 16] << 4));
-    *reinterpret_cast<unsigned short*>(blk) = dh;
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t lo = pack_low_bytes(qb[4 * j], qb[4 * j + 1], qb[4 * j + 2], qb[4 * j + 3]);
+      const uint32_t hi = pack_low_bytes(qb[16 + 4 * j], qb[16 + 4 * j + 1], qb[16 + 4 * j + 2], qb[16 + 4 * j + 3]);
+      ow[j] = lo | (hi << 4);
+    }
+  }
+  if (odd) {
+    wp[0] = (w[0] & 0xFFFFu) | (dh << 16);
+#pragma unroll
+    for (int j = 0; j < kCodeWords; ++j) wp[j + 1] = ow[j];
+  } else {
+    wp[0] = dh | (ow[0] << 16);
+#pragma unroll
+    for (int j = 1; j < kCodeWords; ++j) wp[j] = __funnelshift_l(ow[j - 1], ow[j], 16);
+    wp[kCodeWords] = (w[kCodeWords] & 0xFFFF0000u) | (ow[kCodeWords - 1] >> 16);
   }
 }
 
-// ============================================================== the kernel
 // ================================================================== kernel
-// Warp-specialised persistent kernel, one CTA per SM (384 threads):
-//   warp 0      code tiles by 2-D bulk tensor copies (one elected lane);
-//   warp 1      tcgen05.mma of the rank-r update into a double-buffered TMEM
-//               accumulator (one elected lane), plus TMEM allocation;
-//   warps 2-3   A tiles, per-tile scale bytes and the B strip by cp.async
-//               (and code tiles of weights whose rows cannot use the TMA);
-//   warps 4-11  epilogue: two warpgroups, thread e owns tile row (e & 127) and
-//               every other 32-column chunk; decode, merge, re-scale, encode
+// Warp-specialised persistent kernel, one CTA per SM, 128 x (1 + EW) threads:
+//   warp 0      (one lane) the B strip of each item, and per tile the A tile
+//               and the code tile, by 2-D bulk tensor copies;
+//   warp 1      (one lane) TMEM allocation and tcgen05.mma of the rank-r
+//               update into one of 512 / BN TMEM accumulators per tile;
+//   warps 2-3   per-row scale bytes, and the cp.async fallback for factors or
+//               code tiles whose alignment rules out bulk tensor copies;
+//   warps 4..   EW epilogue warpgroups; tile t goes to warpgroup t % EW, whose
+//               thread i owns tile row i: decode, merge, re-scale and encode
 //               in place in shared memory, then one bulk tensor store.
-// Stages of (codes, A tile, scales) circulate through full/empty mbarriers;
-// accumulators through afull/aempty; B strips through bfull/bempty. Every
-// wait is bounded (ptx.cuh); a role whose wait gives up stops issuing work and
-// the others then give up in turn, so the CTA always reaches its exit.
+// Code stages, A stages, B strips and accumulators circulate through their own
+// full / empty mbarrier pairs. Every wait is bounded (ptx.cuh); a role whose
+// wait gives up stops issuing work and the others then give up in turn, so
+// the CTA always reaches its exit.
 // Epilogue warpgroups per format (tile t -> warpgroup t % EW). Three give the
 // epilogue more warps in flight; GGUF keeps two so that its 256-column tiles
 // (the narrowest whose rows are 16-byte multiples) fit two accumulators, and
@@ -1133,8 +1188,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         const uint32_t a_layout = swizzle_layout(kb);
         // Fused per-row passes visit every column tile twice: reduce, then encode.
         const int n_steps = PASS == kFused ? 2 * g.n_tiles : g.n_tiles;
-        for (int st = 0; st < n_steps && ok; ++st, ++t) {
-          const int tile = st < g.n_tiles ? st : 2 * g.n_tiles - 1 - st;  // encode sweep runs backwards: L2-hot tiles first
+        for (int st = 0; st < n_steps && ok; ++st, ++t) {  // the MMA needs no column: its A tile is staged
           const int x = t % SA;
           const int ab = t % NB;
           ok = mbar_wait(&full_a[x], (t / SA) & 1u, kStatusTimeoutLoad);
