@@ -177,6 +177,13 @@ int piper_merge_gguf(void* raw, const void* b, const void* a, int64_t rows, int6
                      int32_t has_seed, uint64_t seed, uint64_t offset_base, void* stream);
 
 /* Message of the calling thread's last failed call ("" if none). */
+/* Self-test of the failure path, no counterpart in the reference: enqueues a
+ * one-thread kernel that waits on a barrier nothing arrives on. Its bounded
+ * wait gives up after the kernels' wait limit (2 s), sets the device status
+ * word (read it with piper_merge_device_status) and returns; the context stays
+ * usable. */
+int piper_merge_selftest_timeout(void* stream);
+
 const char* piper_merge_last_error(void);
 
 /* Reads and clears the device-side error word of the current device (nonzero

@@ -57,6 +57,7 @@ EXPORTED_SYMBOLS = (
     "piper_merge_device_status",
     "piper_merge_version",
     "piper_merge_launches",
+    "piper_merge_selftest_timeout",
 )
 
 
@@ -140,6 +141,7 @@ def load() -> ctypes.CDLL:
             "piper_merge_int8",
             "piper_merge_gguf",
             "piper_merge_device_status",
+            "piper_merge_selftest_timeout",
         ):
             getattr(lib, name).restype = ctypes.c_int
         _lib = lib

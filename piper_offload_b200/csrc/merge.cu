@@ -1906,6 +1906,18 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
 }
 
 
+
+// Self-test of the bounded waits: one thread waits on an mbarrier that nothing
+// arrives on. The wait gives up after kWaitLimitNs, records kStatusTimeoutLoad
+// in the status word and the kernel returns; nothing faults or hangs.
+__global__ void selftest_wait_kernel() {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait(&bar, 0u, kStatusTimeoutLoad);
+  }
+}
 }  // namespace pm
 
 
@@ -2655,6 +2667,13 @@ int piper_merge_gguf(void* raw, const void* b, const void* a, int64_t rows, int6
 }
 
 const char* piper_merge_last_error(void) { return g_last_error.c_str(); }
+
+int piper_merge_selftest_timeout(void* stream) {
+  pm::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("self-test launch: ") + cudaGetErrorString(e));
+  return PIPER_MERGE_OK;
+}
 
 int piper_merge_device_status(void* stream, uint32_t* status) {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));

@@ -3,11 +3,13 @@ arguments before touching the device."""
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import re
 from pathlib import Path
 
 import pytest
+import torch
 
 from piper_offload_b200 import _native as nat
 
@@ -100,3 +102,31 @@ def test_convenience_entry_points_validate():
     assert lib.piper_merge_mx(1, 1, 1, 1, 32, 64, 16, 5, 0, 0, 0, 1.0, 0, 0, 0, None) == nat.EINVAL
     assert lib.piper_merge_gguf(1, 1, 1, 32, 64, 16, 3, 0, 1.0, 0, 0, 0, None) == nat.EINVAL
     assert lib.piper_merge_float8(1, 1, 1, 1, 0, 64, 16, 1, 64, 0, 0, 1.0, 0, 0, 0, None, 0, None) == nat.EINVAL
+
+
+class _FailingLib:
+    """Stands in for the C-ABI library: validation succeeds, the launch reports a CUDA error."""
+
+    def piper_merge_workspace_size(self, arr, count, out):
+        return nat.OK
+
+    def piper_merge_batch(self, arr, count, ws, ws_bytes, stream):
+        return nat.ECUDA
+
+    def piper_merge_last_error(self):
+        return b"injected launch failure"
+
+
+def test_injected_launch_error_raises_and_mutates_nothing(monkeypatch):
+    # merge_batch surfaces a failing C-ABI return as RuntimeError with the
+    # library's message; the (CPU) storages handed in are untouched.
+    monkeypatch.setattr(nat, "load", lambda: _FailingLib())
+    monkeypatch.setattr(nat, "current_stream_handle", lambda dev: None)
+    monkeypatch.setattr(torch.cuda, "device", lambda dev: contextlib.nullcontext())
+    q = torch.arange(64, dtype=torch.uint8)
+    before = q.clone()
+    d = _desc()
+    d.qdata = q.data_ptr()
+    with pytest.raises(RuntimeError, match="injected launch failure"):
+        nat.merge_batch([d], torch.device("cpu"))
+    assert torch.equal(q, before)
