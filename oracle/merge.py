@@ -20,6 +20,7 @@ from .numerics import (
     decode_e8m0,
     e2m1_value,
     encode_e2m1,
+    f16_round,
     fdiv,
     fdiv_t,
     fma_f32,
@@ -42,8 +43,13 @@ FLT_MIN = np.float32(1.1754943508222875e-38)
 
 
 def lora_delta(b: np.ndarray, a: np.ndarray) -> np.ndarray:
-    """fp32 ``B @ A``; correctly rounded (tie class: GPU summation order)."""
-    return (np.asarray(b, np.float64) @ np.asarray(a, np.float64)).astype(np.float32)
+    """fp32 ``B @ A``; correctly rounded (tie class: GPU summation order).
+
+    The reference accumulates into ``tl.zeros`` (``accumulator += tl.dot(b, a)``),
+    so an all-zero sum is +0.0 whatever the signs of its products.
+    """
+    acc = (np.asarray(b, np.float64) @ np.asarray(a, np.float64)).astype(np.float32)
+    return (np.float32(0.0) + acc).astype(np.float32)
 
 
 def merged_values(base: np.ndarray, acc: np.ndarray, strength: float, compute: str) -> np.ndarray:
@@ -409,7 +415,15 @@ def merge_int8(qdata, scale, zero_point, block_size, b, a, strength, *, asymmetr
                else np.asarray(zero_point, np.int8).reshape(-1).astype(np.int64))
     qidx = np.arange(M * N, dtype=np.int64) // block_numel
     base = round_to_compute(flat_q - zp_flat[qidx].astype(np.float32), compute)
-    base = round_to_compute((base * s_flat[qidx]).astype(np.float32), compute)
+    sv_in = s_flat[qidx]
+    if {compute, qparam} == {"bf16", "f16"}:
+        # ``base * scale`` (:80) with one bf16 and one fp16 operand: Triton
+        # converts both to fp16 and rounds the product to fp16
+        # (triton/language/semantic.py, computation_type_impl).
+        prod = f16_round((f16_round(base) * f16_round(sv_in)).astype(np.float32))
+    else:
+        prod = (base * sv_in).astype(np.float32)
+    base = round_to_compute(prod, compute)
     acc = lora_delta(b, a).reshape(-1)
     dense = merged_values(base, acc, strength, compute)
     blocks = dense.reshape(nq, block_numel)

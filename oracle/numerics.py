@@ -171,10 +171,15 @@ def e2m1_value(code: np.ndarray) -> np.ndarray:
 
 
 def decode_e2m1(code: np.ndarray) -> np.ndarray:
-    """Signed value of a 4-bit code (``_decode_fp4``)."""
+    """Signed value of a 4-bit code (``_decode_fp4``, ``_triton_nvfp4_lora.py:24-52``,
+    ``_triton_mx_lora.py:40-64``).
+
+    The sign is applied as ``-magnitude``, which Triton lowers to ``0.0 - x``
+    (``triton/language/semantic.py`` ``minus``), so code 8 decodes to +0.0.
+    """
     code = np.asarray(code, dtype=np.int64)
     mag = E2M1_VALUES[code & 7]
-    return np.where((code & 8) != 0, -mag, mag).astype(np.float32)
+    return np.where((code & 8) != 0, np.float32(0.0) - mag, mag).astype(np.float32)
 
 
 def encode_e2m1(x: np.ndarray) -> np.ndarray:

@@ -612,6 +612,27 @@ __device__ __forceinline__ uint32_t int8_encode(float v, const Int8Q& q, int qmi
   return static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu;
 }
 
+// INT8 `base * scale` (_triton_int8_lora.py:80) with one operand bf16 and the
+// other fp16 runs in fp16: Triton converts both operands to fp16 and rounds the
+// product to fp16 (semantic.computation_type_impl). For fp16 factors with a
+// bf16 scale the scale is first rounded to fp16 (int8_f16_scale); for bf16
+// factors with an fp16 scale the product is rounded to fp16 before the bf16
+// cast (int8_half_product). q - zp is exact in fp16 either way.
+template <int CDT>
+__device__ __forceinline__ bool int8_f16_scale(int scale_dt) {
+  return CDT == kF16 && scale_dt == kBF16;
+}
+
+template <int CDT>
+__device__ __forceinline__ void int8_half_product(int scale_dt, float (&m)[32]) {
+  if constexpr (CDT == kBF16) {
+    if (scale_dt == kF16) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) f16r2(m[i], m[i + 1]);
+    }
+  }
+}
+
 // Decode + merge 32 columns of an FP8/INT8 row chunk. Columns >= N are
 // garbage and excluded by the callers.
 template <int FMT, int CDT>
@@ -621,12 +642,15 @@ __device__ __forceinline__ void affine_merged(const DevWeight& W, const RowCtx& 
   uint32_t wv[8];
   load_chunks32(c, k, wv);
   if constexpr (FMT == PIPER_FMT_INT8) {
+    const bool f16_scale = int8_f16_scale<CDT>(W.scale_dt);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
       // q - zp is an integer in [-255, 255]: exact in bf16 / fp16.
-      merged[i] = __fmul_rn(__fsub_rn(qv, static_cast<float>(zp_in[i])), scale_in[i]);
+      const float s = f16_scale ? f16r(scale_in[i]) : scale_in[i];
+      merged[i] = __fmul_rn(__fsub_rn(qv, static_cast<float>(zp_in[i])), s);
     }
+    int8_half_product<CDT>(W.scale_dt, merged);
   } else {
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
@@ -653,11 +677,13 @@ __device__ __forceinline__ void affine_merged_u(const DevWeight& W, const RowCtx
   load_chunks32(c, k, wv);
   if constexpr (FMT == PIPER_FMT_INT8) {
     const float zf = static_cast<float>(z_in);
+    const float s = int8_f16_scale<CDT>(W.scale_dt) ? f16r(s_in) : s_in;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
-      merged[i] = __fmul_rn(__fsub_rn(qv, zf), s_in);
+      merged[i] = __fmul_rn(__fsub_rn(qv, zf), s);
     }
+    int8_half_product<CDT>(W.scale_dt, merged);
   } else {
 #pragma unroll
     for (int w = 0; w < 8; ++w) {

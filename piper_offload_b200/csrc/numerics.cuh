@@ -343,12 +343,16 @@ __device__ __forceinline__ uint32_t enc_fp8x4(float a, float b, float c, float d
   return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 
-// Two E2M1 codes (low nibble first) of one byte to fp32.
+// Two E2M1 codes (low nibble first) of one byte to fp32. The reference applies
+// the sign as `-magnitude`, which Triton lowers to `0.0 - magnitude`, so code 8
+// decodes to +0.0 there; the f16x2 add of +0 gives the same (-0 + +0 = +0, every
+// other value unchanged).
 __device__ __forceinline__ void dec_e2m1x2(uint32_t byte, float& a, float& b) {
   uint32_t h;
-  asm("{\n\t.reg .b8 t0, t1;\n\tmov.b16 {t0, t1}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t0;\n\t}"
+  asm("{\n\t.reg .b8 t0, t1;\n\tmov.b16 {t0, t1}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t0;\n\t"
+      "add.rn.f16x2 %0, %0, %2;\n\t}"
       : "=r"(h)
-      : "h"(static_cast<uint16_t>(byte & 0xFFu)));
+      : "h"(static_cast<uint16_t>(byte & 0xFFu)), "r"(0u));
   const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
   a = f.x;
   b = f.y;

@@ -1,0 +1,33 @@
+"""CPU: the oracle against the reference's own Triton merge kernels, bit for bit.
+
+The fixtures (``tests/golden/merge_reference.*``) were recorded from the four
+raw-buffer launchers of the reference (``merge_float8_lora``,
+``merge_int8_lora``, ``merge_nvfp4_lora``, ``merge_mx_lora_``) at the
+reference tests' shapes, across layouts, scale modes, swizzling, rounding
+modes, factor and scale dtypes, negative strengths and zero factors. Their
+divisions are IEEE, which the oracle computes without its GPU-division hook.
+"""
+
+from __future__ import annotations
+
+import pytest
+
+import reference_fixtures as rf
+
+CASES = rf.cases()
+
+
+def test_fixture_coverage():
+    launchers = {c["launcher"] for c in CASES}
+    assert launchers == {"float8", "int8", "nvfp4", "mx"}
+    assert {c["elem"] for c in CASES if c["launcher"] == "mx"} == {"e4m3", "e5m2", "e2m1"}
+    assert {c["scaling_mode"] for c in CASES if c["launcher"] == "mx"} == {0, 1, 2, 3}
+    assert any(c["seed"] is not None for c in CASES) and any(c["seed"] is None for c in CASES)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["id"] + "-" + rf.case_label(c) for c in CASES])
+def test_oracle_matches_reference_kernels(case):
+    got = rf.oracle(case)
+    want = rf.expected(case)
+    bad = {k: v[:8].tolist() for k, v in rf.mismatches(got, want).items() if v.size}
+    assert not bad, bad

@@ -1,0 +1,45 @@
+"""GPU: the sm_100a merge on the inputs the reference's own Triton kernels were recorded on.
+
+Each fixture case (``tests/golden/merge_reference.*``) runs through
+``piper_offload_b200.kernels``. Two checks, both exact:
+
+* against the oracle evaluated with the GPU's tensor-by-tensor division
+  (``oracle.gpu_division``): every code, scale, zero point and global scale;
+* against the reference's recorded outputs: the only differing elements are
+  those where the GPU's ``div.full`` quotient and the IEEE quotient of the
+  recording differ, i.e. exactly where the GPU-division oracle differs from
+  the recording.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import reference_fixtures as rf
+
+pytestmark = pytest.mark.gpu
+
+CASES = rf.cases()
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu_division(cuda_device):
+    from oracle import gpu_division
+
+    gpu_division.install()
+    yield
+    gpu_division.uninstall()
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["id"] + "-" + rf.case_label(c) for c in CASES])
+def test_native_matches_reference_kernels(case, cuda_device):
+    got = rf.native(case, cuda_device)
+    oracle = rf.oracle(case)
+    bad = {k: v[:8].tolist() for k, v in rf.mismatches(got, oracle).items() if v.size}
+    assert not bad, f"native vs GPU-division oracle: {bad}"
+    want = rf.expected(case)
+    vs_ref = rf.mismatches(got, want)
+    explained = rf.mismatches(oracle, want)
+    for k in want:
+        assert np.array_equal(vs_ref[k], explained[k]), (k, vs_ref[k][:8].tolist(), explained[k][:8].tolist())
