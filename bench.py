@@ -251,6 +251,60 @@ def cpu_baseline(cfg: str, steps: int, warmup: int, rows_per_step: int = 1024, c
 
 
 # ------------------------------------------------------------------ main
+def staging_bench(cfg: str, n_layers: int | None, steps: int, warmup: int) -> dict:
+    """``merge_lora()`` end to end with the LoRA factors in host memory (bf16,
+    pageable, as a checkpoint loader leaves them) and the weights on the GPU.
+
+    ``per_weight`` is the reference driver's sequence: for each weight, stage
+    for validation, validate, stage again, merge (``lora.py:406-413``,
+    ``:543-549``), four host-to-device copies and one launch per weight.
+    ``batched`` is ``transform.merge_lora``: one staging copy for the batch,
+    validation of every weight, one batched launch. Wall-clock per call, with
+    the device synchronized on both sides; median of ``steps`` calls.
+    """
+    import torch
+
+    from piper_offload_b200 import transform as TR
+
+    dev = torch.device("cuda", 0)
+    items = build_weights(cfg, dev, 0, n_layers)
+    weights = {key: t for key, _, _, t, _, _ in items}
+    lora = {key: (a.cpu(), b.cpu()) for key, _, _, _, b, a in items}
+    stochastic = CONFIGS[cfg][5]
+    del items
+
+    def per_weight():
+        for key, target in weights.items():
+            tr = TR.LoRATransform([TR.LoRAFactor(*lora[key])], stochastic_rounding=stochastic, target_key=key)
+            plan = tr._make_plan(target)
+            b, a, s = tr._stage(target, plan)
+            plan.adapter.validate_lora_merge(target, b, a, s, rounding_seed=tr._rounding_seed())
+            b, a, s = tr._stage(target, plan)
+            plan.adapter.merge_lora_(target, b, a, s, rounding_seed=tr._rounding_seed())
+
+    def batched():
+        TR.merge_lora(weights, [(lora, 1.0)], stochastic_rounding=stochastic)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        out = []
+        for _ in range(steps):
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize(dev)
+            out.append((time.perf_counter() - t0) * 1e3)
+        return statistics.median(out)
+
+    factor_bytes = sum((a.numel() + b.numel()) * a.element_size() for a, b in lora.values())
+    pw, bt = timed(per_weight), timed(batched)
+    return {"mode": "staging", "config": {"workload": CONFIGS[cfg][6], "weights": len(weights),
+                                          "factor_bytes": factor_bytes},
+            "per_weight_ms": round(pw, 3), "batched_ms": round(bt, 3),
+            "h2d_copies": {"per_weight": 4 * len(weights), "batched": 1}, "steps": steps, "warmup": warmup}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -266,8 +320,13 @@ def main() -> int:
                     help="override the layer count (small profiling case; the headline uses the config's)")
     ap.add_argument("--kernel-reps", type=int, default=5,
                     help="timed repetitions of the dominant-weight roofline leg")
+    ap.add_argument("--staging", action="store_true",
+                    help="time merge_lora() with host-resident factors: batched staging vs the per-weight driver")
     args = ap.parse_args()
     warmup = max(3, args.warmup)
+    if args.staging:
+        print(json.dumps(staging_bench(args.config, args.layers, args.steps, warmup)), flush=True)
+        return 0
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -268,3 +268,29 @@ def test_merge_lora_driver_rules(fake_adapter):
     assert n == 2
     b, a, s, seed = w["a"].calls[-1]
     assert a.shape == (3, 6) and seed == derive_seed("a", 0)
+
+
+def test_validated_transform_stages_once(fake_adapter, monkeypatch):
+    t = FakeTarget(4, 6)
+    tr = TR.LoRATransform([TR.LoRAFactor(torch.ones(2, 6), torch.ones(4, 2))])
+    calls = []
+    orig = TR.LoRATransform._stage
+    monkeypatch.setattr(TR.LoRATransform, "_stage", lambda self, x, plan: calls.append(1) or orig(self, x, plan))
+    tr.validate_target(t)
+    tr.apply_weight(t)
+    assert len(calls) == 1  # validation's staging is reused by the application
+    tr.apply_weight(t)
+    assert len(calls) == 2  # a further application stages afresh
+
+
+def test_stage_factors_matches_per_weight_staging(fake_adapter):
+    g = torch.Generator().manual_seed(3)
+    f1 = TR.LoRAFactor(torch.randn(2, 6, generator=g), torch.randn(4, 2, generator=g), strength=0.7)
+    f2 = TR.LoRAFactor(torch.randn(3, 6, generator=g), torch.randn(4, 3, generator=g), strength=-1.5)
+    pairs = [(TR.LoRATransform([f1]), FakeTarget(4, 6)), (TR.LoRATransform([f1, f2]), FakeTarget(4, 6)),
+             (TR.LoRATransform([f2]), FakeTarget(4, 6, dtype=torch.float16))]
+    staged = TR.stage_factors(pairs)
+    for (tr, x), (b, a, s) in zip(pairs, staged):
+        rb, ra, rs = tr._stage(x, tr._make_plan(x))
+        assert s == rs and b.dtype == rb.dtype and a.dtype == ra.dtype
+        assert torch.equal(b, rb) and torch.equal(a, ra)
