@@ -52,6 +52,10 @@ extern "C" {
 #define PIPER_FMT_INT8 6       /* TorchAO affine INT8 */
 #define PIPER_FMT_GGUF_Q8_0 7
 #define PIPER_FMT_GGUF_Q4_0 8
+#define PIPER_FMT_BNB8 9             /* bitsandbytes LLM.int8: int8 CB, fp32 SCB per row */
+#define PIPER_FMT_QUANTO_INT8 10     /* Quanto qint8 qbytes, scales in the compute dtype */
+#define PIPER_FMT_QUANTO_FP8_E4M3 11 /* Quanto qfloat8 qbytes */
+#define PIPER_FMT_QUANTO_FP8_E5M2 12
 
 /* ---- floating dtypes (factors = compute dtype; INT8 scales) ---- */
 #define PIPER_DT_BF16 0
@@ -80,7 +84,9 @@ extern "C" {
  * scale   MX: E8M0 bytes, rows x cols/32 or swizzled ((rows+127)/128*32) x
  *         ((cols+127)/128*16); NVFP4: E4M3 bytes, rows x cols/16 or swizzled
  *         ((rows+127)/128*32) x ((cols+63)/64*16); FP8: fp32, one per
- *         quantization block; INT8: `scale_dtype`, one per block; GGUF: unused.
+ *         quantization block; INT8: `scale_dtype`, one per block; BNB8: fp32
+ *         SCB, one per row; Quanto: `compute_dtype`, one per row or one per
+ *         tensor; GGUF: unused.
  * zero_point  INT8 only: int8 per block, or NULL (symmetric storage).
  * global_scale NVFP4 only: fp32 per-tensor scale (two-level), or NULL.
  * block_rows, block_cols  FP8/INT8 quantization block: (1, cols) per row,

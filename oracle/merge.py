@@ -388,6 +388,113 @@ def merge_float8(qdata, scale, block_size, b, a, strength, *, e4m3=True, seed=No
     return new_q, new_scale.reshape(scale.shape).astype(np.float32)
 
 
+def merge_static_float8(qdata, scale, b, a, strength, *, e4m3=True, seed=None, compute="bf16", offset_base=0):
+    """Static per-tensor FP8 merge (``merge_static_float8_lora``,
+    ``_triton_static_float8_lora.py:23-158``): the per-tensor layout of
+    :func:`merge_float8` (dense ``compute(fp8 * scale)``, tile maxima of
+    ``|merged|``, ``compute(amax / limit)`` with 0 -> 2**-23, ``merged / scale``
+    clamped, RTNE or stochastic FP8)."""
+    M = np.asarray(b).shape[0]
+    N = np.asarray(a).shape[1]
+    return merge_float8(qdata, np.asarray(scale, np.float32).reshape(1, 1), (M, N), b, a, strength, e4m3=e4m3,
+                        seed=seed, compute=compute, offset_base=offset_base)
+
+
+# ---------------------------------------------------------------------------
+# bitsandbytes LLM.int8: _triton_bnb8_lora.py:20-142.
+# ---------------------------------------------------------------------------
+
+
+def merge_bnb8(cb, scb, b, a, strength, *, seed=None, offset_base=0):
+    """bitsandbytes row-wise int8 merge (``merge_bnb8_lora``, ``_triton_bnb8_lora.py:145-242``).
+
+    ``cb`` int8 (M x N), ``scb`` fp32 (M,). fp16 arithmetic: ``normalized =
+    f16(cb / 127.0)`` (IEEE constant division), ``base = f16(normalized *
+    f16(scb))``, ``merged = f16(clamp(base + acc * strength, +-65504))``; the new
+    SCB is the row max of ``|merged|``; codes ``rint(merged / SCB * 127)`` (0
+    where SCB is 0) or stochastic, clamped to [-127, 127]. Returns ``(cb, scb)``.
+    """
+    from .numerics import f16_round
+
+    M = b.shape[0]
+    N = a.shape[1]
+    cbf = np.asarray(cb, np.int8).astype(np.float32)
+    normalized = f16_round((cbf / np.float32(127.0)).astype(np.float32))
+    s16 = f16_round(np.asarray(scb, np.float32).reshape(M, 1))
+    base = f16_round((normalized * s16).astype(np.float32))
+    acc = lora_delta(b, a)
+    merged = f16_round(clamp(fma_f32(acc, np.float32(strength), base), -65504.0, 65504.0))
+    new_scb = nanmax_reduce(np.abs(merged), axis=1).astype(np.float32)
+    safe = np.where(new_scb == 0.0, np.float32(1.0), new_scb).reshape(M, 1)
+    scaled = (fdiv_t(merged, safe) * np.float32(127.0)).astype(np.float32)
+    scaled = np.where(new_scb.reshape(M, 1) == 0.0, np.float32(0.0), scaled).astype(np.float32)
+    quant = rint_half_even(scaled).astype(np.float32)
+    if seed is not None:
+        quant = sr_round_to_int(scaled, quant, seed, logical_offsets(M, N, offset_base), -127, 127)
+    quant = np.clip(quant, -127, 127).astype(np.int8)
+    return quant, new_scb.reshape(np.shape(scb))
+
+
+# ---------------------------------------------------------------------------
+# Quanto qbytes: _triton_quanto_lora.py:28-168, 202-217.
+# ---------------------------------------------------------------------------
+
+
+def merge_quanto(qdata, scale, axis_kind, b, a, strength, *, storage="int8", seed=None, compute="bf16",
+                 offset_base=0):
+    """Quanto qint8 / qfloat8 merge (``_merge_quanto_qbytes_lora``, ``_triton_quanto_lora.py:220-314``).
+
+    ``storage`` is ``"int8"``, ``"e4m3"`` or ``"e5m2"``; ``qdata`` int8 or uint8
+    FP8 codes; ``scale`` holds compute-dtype values, one per tensor / row /
+    column (``axis_kind`` "tensor" / "row" / "column"). ``base = compute(q *
+    scale)`` (0 where the scale is 0), ``merged = compute(base + acc *
+    strength)``; the new scale is ``compute(amax * fp32(1 / qmax))`` (torch on
+    CUDA divides by a host scalar through its reciprocal), 0 -> fp32 eps;
+    ``s = merged / scale``; int8: ``rint(compute(s))`` or stochastic on ``s``,
+    clamp [-128, 127]; FP8: RTNE of ``clamp(compute(s))`` or stochastic FP8 of
+    ``clamp(s)``. Returns ``(qdata, scale)``.
+    """
+    M = b.shape[0]
+    N = a.shape[1]
+    if storage == "int8":
+        lp = np.asarray(qdata, np.int8).astype(np.float32)
+        qmax = np.float32(127.0)
+    else:
+        encode, decode, limit = fp8_codec(storage == "e4m3")
+        lp = decode(np.asarray(qdata, np.uint8))
+        qmax = np.float32(limit)
+    s_in = np.asarray(scale, np.float32)
+    shape_b = {"tensor": (1, 1), "row": (M, 1), "column": (1, N)}[axis_kind]
+    s_b = s_in.reshape(shape_b)
+    with np.errstate(invalid="ignore"):
+        prod = (lp * s_b).astype(np.float32)
+    base = round_to_compute(np.where(s_b == 0.0, np.float32(0.0), prod).astype(np.float32), compute)
+    acc = lora_delta(b, a)
+    merged = merged_values(base, acc, strength, compute)
+    absm = np.abs(merged)
+    if axis_kind == "tensor":
+        amax = nanmax_reduce(absm.reshape(-1), axis=0).reshape(1, 1)
+    elif axis_kind == "row":
+        amax = nanmax_reduce(absm, axis=1).reshape(M, 1)
+    else:
+        amax = nanmax_reduce(absm, axis=0).reshape(1, N)
+    inv = np.float32(np.float32(1.0) / qmax)
+    new_s = round_to_compute((amax * inv).astype(np.float32), compute)
+    new_s = np.where(new_s == 0.0, EPS_2_23, new_s).astype(np.float32)
+    ss = fdiv_t(merged, new_s)
+    offs = logical_offsets(M, N, offset_base)
+    if storage == "int8":
+        det = rint_half_even(round_to_compute(ss, compute)).astype(np.float32)
+        quant = det if seed is None else sr_round_to_int(ss, det, seed, offs, -128, 127)
+        new_q = np.clip(quant, -128, 127).astype(np.int8)
+    else:
+        if seed is None:
+            new_q = encode(clamp(round_to_compute(ss, compute), -qmax, qmax))
+        else:
+            new_q = sr_float8(clamp(ss, -qmax, qmax), seed, offs, storage == "e4m3", float(qmax))
+    return new_q, new_s.reshape(np.shape(scale)).astype(np.float32)
+
+
 # ---------------------------------------------------------------------------
 # Affine INT8: _triton_int8_lora.py:24-236.
 # ---------------------------------------------------------------------------

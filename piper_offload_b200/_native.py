@@ -34,6 +34,10 @@ FMT_FP8_E5M2 = 5
 FMT_INT8 = 6
 FMT_GGUF_Q8_0 = 7
 FMT_GGUF_Q4_0 = 8
+FMT_BNB8 = 9
+FMT_QUANTO_INT8 = 10
+FMT_QUANTO_FP8_E4M3 = 11
+FMT_QUANTO_FP8_E5M2 = 12
 
 DT_BF16 = 0
 DT_F16 = 1

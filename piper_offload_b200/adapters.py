@@ -21,6 +21,10 @@ adapter            reference gate / merge it replaces
 Int8Adapter        int8_adapter.py:144-188 gate, :350-410 merge (act_pre_scale
                    folding :59-141)
 Float8Adapter      float8_adapter.py:63-98 gate, :242-272 merge
+StaticFloat8Ada.   static_float8_adapter.py:113-248 (layout rules
+                   _torchao_static_float8.py:213-258)
+Bnb8Adapter        bnb8bit_adapter.py:92-121 gate, :285-315 merge
+QuantoAdapter      quanto_adapter.py:136-187 gate, :370-440 merge
 Nvfp4Adapter       nvfp4_adapter.py:57-117 gate, :255-290 merge
 MxAdapter          mx_adapter.py:90-137 gate, :274-309 merge
 GgufAdapter        new: gguf_adapter.py:160-284 has no merge capability
@@ -258,6 +262,224 @@ class Float8Adapter:
         nat.merge_batch([d], target.qdata.device)
 
 
+# ============================================================ static FP8
+class StaticFloat8Adapter:
+    """TorchAO ``PrototypeFloat8Tensor`` with a static activation scale
+    (``static_float8_adapter.py:113-248``): per-tensor FP8 weight, fp32 scale.
+    The merge rewrites ``qdata`` and ``scale`` and leaves ``act_quant_scale``."""
+
+    NAME = "torchao-static-float8"
+
+    @staticmethod
+    def matches(t: Any) -> bool:
+        return _has(t, "qdata", "scale", "act_quant_scale") and t.act_quant_scale is not None \
+            and getattr(t.qdata, "dtype", None) in _FP8_DTYPES
+
+    @staticmethod
+    def logical_shape(t: Any) -> tuple[int, ...]:
+        return tuple(t.qdata.shape)
+
+    @staticmethod
+    def compute_dtype(t: Any) -> torch.dtype:
+        return t.dtype
+
+    @classmethod
+    def _check(cls, t: Any, b: torch.Tensor, a: torch.Tensor) -> tuple:
+        label = "static FP8"
+        if not isinstance(t.act_quant_scale, torch.Tensor):
+            raise TypeError("PrototypeFloat8Tensor.act_quant_scale must be a tensor")
+        if t.act_quant_scale.numel() != 1:
+            raise ValueError("StaticFloat8Adapter supports a per-tensor activation scale containing exactly one value.")
+        if tuple(getattr(t, "block_size", t.qdata.shape)) != tuple(t.qdata.shape):
+            raise ValueError("StaticFloat8Adapter supports only the per-tensor FP8 weight layout used by TorchAO's "
+                             "static workflow; use Float8Tensor's dynamic activation path for other weight "
+                             "granularities.")
+        if t.qdata.ndim != 2:
+            raise ValueError(f"{label} merge expects a rank-two weight.")
+        if t.scale.dtype is not torch.float32 or t.scale.numel() != 1:
+            raise ValueError(f"{label} merge expects one float32 per-tensor scale.")
+        rows, cols = t.qdata.shape
+        rank, cdt = _factors(b, a, rows, cols, label)
+        dev = _cuda_same_device(label, t.qdata, t.scale, b, a)
+        if not t.qdata.is_contiguous():
+            raise ValueError(f"{label} merge requires contiguous qdata.")
+        return rows, cols, rank, cdt, dev
+
+    @classmethod
+    def validate_lora_merge(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                            rounding_seed: int | None = None) -> None:
+        _seed(rounding_seed)
+        cls._check(target, b, a)
+
+    @classmethod
+    def merge_desc(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                   rounding_seed: int | None = None, offset_base: int = 0, keep: list | None = None) -> nat.MergeDesc:
+        rows, cols, rank, cdt, _ = cls._check(target, b, a)
+        b = b.contiguous()
+        a = a.contiguous()
+        if keep is not None:
+            keep.extend([b, a])
+        seed, sflag = _seed(rounding_seed)
+        return K._desc(
+            qdata=target.qdata.data_ptr(), scale=target.scale.data_ptr(), b=b.data_ptr(), a=a.data_ptr(),
+            rows=rows, cols=cols, rank=rank, block_rows=rows, block_cols=cols,
+            format=nat.FMT_FP8_E5M2 if target.qdata.dtype is torch.float8_e5m2 else nat.FMT_FP8_E4M3,
+            compute_dtype=cdt, flags=sflag, strength=float(strength), seed=seed, offset_base=int(offset_base))
+
+    @classmethod
+    def merge_lora_(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                    rounding_seed: int | None = None, offset_base: int = 0) -> None:
+        keep: list = []
+        d = cls.merge_desc(target, b, a, strength, rounding_seed=rounding_seed, offset_base=offset_base, keep=keep)
+        nat.merge_batch([d], target.qdata.device)
+
+
+# ================================================= bitsandbytes LLM.int8
+class Bnb8Adapter:
+    """bitsandbytes ``Int8Params`` (``CB`` int8 rows, fp32 ``SCB`` per row);
+    ``bnb8bit_adapter.py:92-121`` gate, ``:285-315`` merge. LLM.int8 computes in fp16."""
+
+    NAME = "bitsandbytes-int8"
+
+    @staticmethod
+    def matches(t: Any) -> bool:
+        return _has(t, "CB", "SCB") and isinstance(t.CB, torch.Tensor) and t.CB.dtype is torch.int8
+
+    @staticmethod
+    def logical_shape(t: Any) -> tuple[int, ...]:
+        return tuple(t.CB.shape)
+
+    @staticmethod
+    def compute_dtype(t: Any) -> torch.dtype:
+        return torch.float16
+
+    @classmethod
+    def _check(cls, t: Any, b: torch.Tensor, a: torch.Tensor) -> tuple:
+        label = "bitsandbytes 8-bit"
+        if t.CB.ndim != 2:
+            raise ValueError(f"{label} merge expects a rank-two weight.")
+        if not isinstance(t.SCB, torch.Tensor) or t.SCB.dtype is not torch.float32:
+            raise ValueError(f"{label} merge expects float32 SCB.")
+        rows, cols = t.CB.shape
+        if t.SCB.numel() != rows:
+            raise ValueError(f"{label} merge expects one SCB value per row.")
+        rank, _ = _factors(b, a, rows, cols, label)
+        if b.dtype is not torch.float16 or a.dtype is not torch.float16:
+            raise ValueError(f"{label} merge expects float16 LoRA factors.")
+        dev = _cuda_same_device(label, t.CB, t.SCB, b, a)
+        if not t.CB.is_contiguous() or not t.SCB.is_contiguous():
+            raise ValueError(f"{label} merge requires contiguous CB and SCB.")
+        return rows, cols, rank, dev
+
+    @classmethod
+    def validate_lora_merge(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                            rounding_seed: int | None = None) -> None:
+        _seed(rounding_seed)
+        cls._check(target, b, a)
+
+    @classmethod
+    def merge_desc(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                   rounding_seed: int | None = None, offset_base: int = 0, keep: list | None = None) -> nat.MergeDesc:
+        rows, cols, rank, _ = cls._check(target, b, a)
+        b = b.contiguous()
+        a = a.contiguous()
+        if keep is not None:
+            keep.extend([b, a])
+        seed, sflag = _seed(rounding_seed)
+        return K._desc(qdata=target.CB.data_ptr(), scale=target.SCB.data_ptr(), b=b.data_ptr(), a=a.data_ptr(),
+                       rows=rows, cols=cols, rank=rank, block_rows=1, block_cols=cols, format=nat.FMT_BNB8,
+                       compute_dtype=nat.DT_F16, scale_dtype=nat.DT_F32, flags=sflag, strength=float(strength),
+                       seed=seed, offset_base=int(offset_base))
+
+    @classmethod
+    def merge_lora_(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                    rounding_seed: int | None = None, offset_base: int = 0) -> None:
+        keep: list = []
+        d = cls.merge_desc(target, b, a, strength, rounding_seed=rounding_seed, offset_base=offset_base, keep=keep)
+        nat.merge_batch([d], target.CB.device)
+
+
+# ================================================================ Quanto
+class QuantoAdapter:
+    """optimum-quanto ``WeightQBytesTensor`` (qint8 / qfloat8 ``_data``, ``_scale``
+    in the weight dtype); ``quanto_adapter.py:136-187`` gate, ``:370-440`` merge."""
+
+    NAME = "quanto-qbytes"
+
+    @staticmethod
+    def matches(t: Any) -> bool:
+        return _has(t, "_data", "_scale", "axis", "qtype")
+
+    @staticmethod
+    def logical_shape(t: Any) -> tuple[int, ...]:
+        return tuple(t.size())
+
+    @staticmethod
+    def compute_dtype(t: Any) -> torch.dtype:
+        return t.dtype
+
+    @classmethod
+    def _check(cls, t: Any, b: torch.Tensor, a: torch.Tensor) -> tuple:
+        label = "Quanto qbytes"
+        data, scale = t._data, t._scale
+        if data.ndim != 2 or tuple(data.shape) != tuple(t.size()):
+            raise ValueError("Quanto LoRA merge requires a rank-two weight whose qbytes storage matches its "
+                             "logical shape.")
+        if getattr(t.qtype, "bits", None) != 8:
+            raise ValueError("Quanto qbytes LoRA merge requires an 8-bit qtype.")
+        if getattr(t.qtype, "dtype", None) is not data.dtype:
+            raise ValueError("Quanto qbytes storage dtype does not match its qtype metadata.")
+        if not scale.dtype.is_floating_point:
+            raise ValueError("Quanto qbytes LoRA merge requires floating-point scales.")
+        rows, cols = data.shape
+        kind = K.quanto_scale_axis(t.axis, scale, rows, cols)
+        rank, cdt = _factors(b, a, rows, cols, label)
+        if scale.dtype is not b.dtype:
+            raise ValueError(f"{label} merge requires matching scale and factor dtypes.")
+        if kind == "column":
+            raise ValueError("Quanto qbytes merge on sm_100a supports a scalar scale or one scale per row "
+                             "(axis 0); last-axis scales are not supported.")
+        if data.dtype is torch.int8:
+            fmt = nat.FMT_QUANTO_INT8
+        elif data.dtype is torch.float8_e4m3fn:
+            fmt = nat.FMT_QUANTO_FP8_E4M3
+        elif data.dtype is torch.float8_e5m2:
+            fmt = nat.FMT_QUANTO_FP8_E5M2
+        else:
+            raise ValueError(f"Quanto qbytes merge supports qint8 and qfloat8 storage, got {data.dtype}.")
+        dev = _cuda_same_device(label, data, scale, b, a)
+        if not data.is_contiguous() or not scale.is_contiguous():
+            raise ValueError(f"{label} merge requires contiguous storage.")
+        return rows, cols, rank, cdt, fmt, kind, dev
+
+    @classmethod
+    def validate_lora_merge(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                            rounding_seed: int | None = None) -> None:
+        _seed(rounding_seed)
+        cls._check(target, b, a)
+
+    @classmethod
+    def merge_desc(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                   rounding_seed: int | None = None, offset_base: int = 0, keep: list | None = None) -> nat.MergeDesc:
+        rows, cols, rank, cdt, fmt, kind, _ = cls._check(target, b, a)
+        b = b.contiguous()
+        a = a.contiguous()
+        if keep is not None:
+            keep.extend([b, a])
+        seed, sflag = _seed(rounding_seed)
+        return K._desc(qdata=target._data.data_ptr(), scale=target._scale.data_ptr(), b=b.data_ptr(),
+                       a=a.data_ptr(), rows=rows, cols=cols, rank=rank, block_rows=rows if kind == "tensor" else 1,
+                       block_cols=cols, format=fmt, compute_dtype=cdt, scale_dtype=cdt, flags=sflag,
+                       strength=float(strength), seed=seed, offset_base=int(offset_base))
+
+    @classmethod
+    def merge_lora_(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                    rounding_seed: int | None = None, offset_base: int = 0) -> None:
+        keep: list = []
+        d = cls.merge_desc(target, b, a, strength, rounding_seed=rounding_seed, offset_base=offset_base, keep=keep)
+        nat.merge_batch([d], target._data.device)
+
+
 # =================================================================== NVFP4
 class Nvfp4Adapter:
     """TorchAO ``NVFP4Tensor`` (packed e2m1, e4m3 block scales, optional fp32 global scale)."""
@@ -483,7 +705,8 @@ class GgufAdapter:
 
 
 # ================================================================ registry
-_ADAPTERS: list[type] = [MxAdapter, Nvfp4Adapter, Float8Adapter, Int8Adapter, GgufAdapter]
+_ADAPTERS: list[type] = [MxAdapter, Nvfp4Adapter, StaticFloat8Adapter, Float8Adapter, Int8Adapter,
+                         Bnb8Adapter, QuantoAdapter, GgufAdapter]
 
 
 def register_adapter(adapter: type, *, first: bool = True) -> None:
@@ -501,8 +724,11 @@ def select_adapter(t: Any) -> type:
 
 
 def target_device(t: Any) -> torch.device:
-    raw = t.raw if hasattr(t, "raw") else getattr(t, "qdata", t)
-    return raw.device
+    for name in ("raw", "qdata", "CB", "_data"):
+        raw = getattr(t, name, None)
+        if isinstance(raw, torch.Tensor):
+            return raw.device
+    return t.device
 
 
 def merge_lora_batch(ops: Sequence[tuple], *, workspace: torch.Tensor | None = None) -> None:

@@ -87,7 +87,7 @@ struct alignas(64) DevWeight {
   int nq_row;          // FP8/INT8 quantization blocks per row (0 = per tensor)
   int scale_cols;      // MX: N/32, NVFP4: N/16
   int scale_mode;      // MX E8M0 rounding
-  int scale_dt;        // INT8 scale dtype
+  int scale_dt;        // stored scale dtype (INT8: as given; FP8: fp32, Quanto: the compute dtype)
   int use_tma;         // code tiles move by bulk tensor copies (swizzled rows)
   int use_tma_a;       // A tiles by bulk tensor copies (else cp.async into the same layout)
   int use_tma_b;       // B strips by bulk tensor copies (else cp.async into the same layout)
@@ -612,6 +612,104 @@ __device__ __forceinline__ uint32_t int8_encode(float v, const Int8Q& q, int qmi
   return static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu;
 }
 
+// ------------------------------------------------ bitsandbytes / Quanto flavors
+// bitsandbytes LLM.int8 (_triton_bnb8_lora.py) and Quanto qbytes
+// (_triton_quanto_lora.py) run on the INT8 / FP8 pipeline with their own
+// decode, scale and encode arithmetic, selected per weight at run time.
+enum Flavor { kTorchao = 0, kBnb = 1, kQuanto = 2 };
+
+// Kernel formats: the bitsandbytes / Quanto ids instantiate the INT8 / FP8
+// kernels with their flavor fixed at compile time.
+__host__ __device__ constexpr int base_fmt(int f) {
+  return f == PIPER_FMT_BNB8 || f == PIPER_FMT_QUANTO_INT8 ? PIPER_FMT_INT8
+         : f == PIPER_FMT_QUANTO_FP8_E4M3                 ? PIPER_FMT_FP8_E4M3
+         : f == PIPER_FMT_QUANTO_FP8_E5M2                 ? PIPER_FMT_FP8_E5M2
+                                                          : f;
+}
+__host__ __device__ constexpr int flavor_of(int f) {
+  return f == PIPER_FMT_BNB8 ? kBnb
+         : (f == PIPER_FMT_QUANTO_INT8 || f == PIPER_FMT_QUANTO_FP8_E4M3 || f == PIPER_FMT_QUANTO_FP8_E5M2) ? kQuanto
+                                                                                                             : kTorchao;
+}
+__host__ __device__ constexpr int kernel_fmt(int base, int flavor) {
+  return flavor == kBnb      ? PIPER_FMT_BNB8
+         : flavor == kQuanto ? (base == PIPER_FMT_INT8       ? PIPER_FMT_QUANTO_INT8
+                                : base == PIPER_FMT_FP8_E4M3 ? PIPER_FMT_QUANTO_FP8_E4M3
+                                                             : PIPER_FMT_QUANTO_FP8_E5M2)
+                             : base;
+}
+
+// New scale of a block from its max |x|. bitsandbytes: SCB = the row's max
+// |merged| (_triton_bnb8_lora.py:84-98). Quanto: (amax / qmax).to(dtype), 0 ->
+// fp32 eps (_triton_quanto_lora.py:202-217); torch divides a CUDA tensor by a
+// host scalar as a multiplication by the scalar's fp32 reciprocal.
+template <int CDT>
+__device__ __forceinline__ float flavor_scale(int flavor, float amax, float qmax) {
+  if (flavor == kBnb) return amax;
+  const float s = round_dt<CDT>(__fmul_rn(amax, __frcp_rn(qmax)));
+  return s == 0.0f ? 1.1920928955078125e-07f : s;
+}
+
+// INT8 codes of 32 merged values of one row for the bitsandbytes and Quanto
+// flavors. bitsandbytes (_triton_bnb8_lora.py:101-142): x = (v / SCB) * 127
+// (0 where SCB == 0), rint or stochastic, clamp [-127, 127]. Quanto qint8
+// (_triton_quanto_lora.py:107-168): s = v / scale, rint(dtype(s)) or
+// stochastic on s, clamp [-128, 127].
+template <int CDT>
+__device__ __forceinline__ void flavor_int8_encode32(int flavor, const float (&m)[32], float s, bool sr,
+                                                     const PhiloxKey& key, uint64_t off0, uint32_t (&out)[8]) {
+  const float lo = flavor == kBnb ? -127.0f : -128.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) out[w] = 0u;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float ss, x;
+    if (flavor == kBnb) {
+      ss = s == 0.0f ? 0.0f : __fmul_rn(div_full(m[i], s), 127.0f);
+      x = ss;
+    } else {
+      ss = div_full(m[i], s);
+      x = round_dt<CDT>(ss);
+    }
+    float qf = rintf(x);
+    if (sr) qf = sr_int(ss, qf, lo, 127.0f, key, off0 + i);
+    qf = fminf(fmaxf(qf, lo), 127.0f);
+    out[i >> 2] |= (static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu) << ((i & 3) * 8);
+  }
+}
+
+// FP8 codes for Quanto qfloat8 (_triton_quanto_lora.py:124-168): s = v / scale;
+// round to nearest: fp8(clamp(dtype(s))); stochastic: on clamp(s).
+template <bool E4M3, int CDT>
+__device__ __forceinline__ void quanto_fp8_encode32(const float (&m)[32], float s, float limit, bool sr,
+                                                    const PhiloxKey& key, uint64_t off0, uint32_t (&out)[8]) {
+#pragma unroll
+  for (int w4 = 0; w4 < 8; ++w4) {
+    float x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float q = div_full(m[4 * w4 + j], s);
+      x[j] = fminf(fmaxf(sr ? q : round_dt<CDT>(q), -limit), limit);
+    }
+    out[w4] = sr ? sr_fp8x4<E4M3>(x, limit, key, off0 + 4 * w4) : enc_fp8x4<E4M3>(x[0], x[1], x[2], x[3]);
+  }
+}
+
+// bitsandbytes decode + merge of 32 columns (_triton_bnb8_lora.py:20-81), fp16:
+// base = f16(f16(cb / 127) * f16(SCB)), merged = f16(clamp(base + acc * s, +-65504)).
+__device__ __forceinline__ void bnb8_merged(const uint32_t (&wv)[8], const float (&acc)[32], float s_in,
+                                            float strength, float (&merged)[32]) {
+  const float s16 = f16r(s_in);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
+    const float base = f16r(__fmul_rn(f16r(__fdiv_rn(qv, 127.0f)), s16));  // `cb / 127.0`: IEEE
+    merged[i] = fminf(fmaxf(fmaf(acc[i], strength, base), -65504.0f), 65504.0f);
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) f16r2(merged[i], merged[i + 1]);
+}
+
 // INT8 `base * scale` (_triton_int8_lora.py:80) with one operand bf16 and the
 // other fp16 runs in fp16: Triton converts both operands to fp16 and rounds the
 // product to fp16 (semantic.computation_type_impl). For fp16 factors with a
@@ -641,7 +739,7 @@ __device__ __forceinline__ void affine_merged(const DevWeight& W, const RowCtx& 
                                               const int* zp_in, float (&merged)[32]) {
   uint32_t wv[8];
   load_chunks32(c, k, wv);
-  if constexpr (FMT == PIPER_FMT_INT8) {
+  if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
     const bool f16_scale = int8_f16_scale<CDT>(W.scale_dt);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -655,7 +753,7 @@ __device__ __forceinline__ void affine_merged(const DevWeight& W, const RowCtx& 
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       float f[4];
-      dec_fp8x4<FMT == PIPER_FMT_FP8_E4M3>(wv[w], f);
+      dec_fp8x4<base_fmt(FMT) == PIPER_FMT_FP8_E4M3>(wv[w], f);
 #pragma unroll
       for (int j = 0; j < 4; ++j) merged[4 * w + j] = __fmul_rn(f[j], scale_in[4 * w + j]);
     }
@@ -675,7 +773,11 @@ __device__ __forceinline__ void affine_merged_u(const DevWeight& W, const RowCtx
                                                 float (&merged)[32]) {
   uint32_t wv[8];
   load_chunks32(c, k, wv);
-  if constexpr (FMT == PIPER_FMT_INT8) {
+  if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
+    if constexpr (flavor_of(FMT) == kBnb) {
+      bnb8_merged(wv, acc, s_in, W.strength, merged);
+      return;
+    }
     const float zf = static_cast<float>(z_in);
     const float s = int8_f16_scale<CDT>(W.scale_dt) ? f16r(s_in) : s_in;
 #pragma unroll
@@ -688,13 +790,20 @@ __device__ __forceinline__ void affine_merged_u(const DevWeight& W, const RowCtx
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       float f[4];
-      dec_fp8x4<FMT == PIPER_FMT_FP8_E4M3>(wv[w], f);
+      dec_fp8x4<base_fmt(FMT) == PIPER_FMT_FP8_E4M3>(wv[w], f);
 #pragma unroll
       for (int j = 0; j < 4; ++j) merged[4 * w + j] = __fmul_rn(f[j], s_in);
     }
   }
 #pragma unroll
   for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+  if constexpr (flavor_of(FMT) == kQuanto) {
+    if (s_in == 0.0f) {
+      // where(scale == 0, 0, q * scale): Quanto's FP8 codes are NaN under a zero scale (:90-94).
+#pragma unroll
+      for (int i = 0; i < 32; ++i) merged[i] = 0.0f;
+    }
+  }
   const float st = W.strength;
 #pragma unroll
   for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], st, merged[i]);
@@ -725,6 +834,23 @@ __device__ __forceinline__ void fp8_encode_rtn(const float (&m)[32], float s, fl
   for (int w = 0; w < 8; ++w) out[w] = enc_fp8x4<E4M3>(q[4 * w], q[4 * w + 1], q[4 * w + 2], q[4 * w + 3]);
 }
 
+// Stored scale of an FP8 / INT8 weight: TorchAO FP8 scales are fp32; INT8,
+// bitsandbytes and Quanto scales have the weight's scale dtype.
+template <int FMT>
+__device__ __forceinline__ float load_scale(const DevWeight& W, int64_t i) {
+  if constexpr (base_fmt(FMT) != PIPER_FMT_INT8 && flavor_of(FMT) == kTorchao)
+    return reinterpret_cast<const float*>(W.scale)[i];
+  else
+    return load_scale_dt(W.scale, i, W.scale_dt);
+}
+template <int FMT>
+__device__ __forceinline__ void store_scale(const DevWeight& W, int64_t i, float v) {
+  if constexpr (base_fmt(FMT) != PIPER_FMT_INT8 && flavor_of(FMT) == kTorchao)
+    reinterpret_cast<float*>(W.scale)[i] = v;
+  else
+    store_scale_dt(W.scale, i, W.scale_dt, v);
+}
+
 // Quantization parameters of the quantization block a thread is working in,
 // kept in registers while consecutive chunks stay in that block (per-row and
 // per-tensor layouts: for the whole work item), so the workspace and scale
@@ -745,12 +871,12 @@ __device__ __forceinline__ void qp_load(const DevWeight& W, int qp, QpCache& q) 
     q.s_in = W.old_scale[qp];
     q.z_in = W.old_zp[qp];
     q.qmax = __uint_as_float(W.qmax[qp]);
-    if (FMT == PIPER_FMT_INT8) q.nmin = __uint_as_float(W.qmin[qp]);
-  } else if (FMT == PIPER_FMT_INT8) {
+    if (base_fmt(FMT) == PIPER_FMT_INT8) q.nmin = __uint_as_float(W.qmin[qp]);
+  } else if (base_fmt(FMT) == PIPER_FMT_INT8) {
     q.s_in = load_scale_dt(W.scale, qp, W.scale_dt);
     q.z_in = W.zp != nullptr ? static_cast<int>(W.zp[qp]) : 0;
   } else {
-    q.s_in = reinterpret_cast<const float*>(W.scale)[qp];
+    q.s_in = load_scale<FMT>(W, qp);
   }
 }
 
@@ -783,7 +909,7 @@ __device__ __forceinline__ void affine_inputs(const DevWeight& W, const RowCtx& 
     if (PASS == kEncode) {
       scale_in[i] = W.old_scale[qp];
       zp_in[i] = W.old_zp[qp];
-    } else if (FMT == PIPER_FMT_INT8) {
+    } else if (base_fmt(FMT) == PIPER_FMT_INT8) {
       scale_in[i] = c.valid ? load_scale_dt(W.scale, qp, W.scale_dt) : 1.0f;
       zp_in[i] = (W.zp != nullptr && c.valid) ? static_cast<int>(W.zp[qp]) : 0;
     } else {
@@ -1406,7 +1532,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
       auto flush_reduce = [&]() {
         if (red_qp >= 0) {
           atomic_max_nonneg(&W.qmax[red_qp], red_max);
-          if (FMT == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[red_qp], red_nmin);
+          if (base_fmt(FMT) == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[red_qp], red_nmin);
         }
         red_max = 0.0f;
         red_nmin = 0.0f;
@@ -1469,23 +1595,30 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
             amax = fmaxf(amax, v.x);
             nmin = fmaxf(nmin, v.y);
           }
-          if constexpr (FMT == PIPER_FMT_INT8) {
+          if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
             const bool asym = (W.flags & PIPER_FLAG_ASYMMETRIC) != 0u;
             const int qlo = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? -64 : -128;
             const int qhi = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? 63 : 127;
-            f_q = int8_qparams<CDT>(-nmin, amax, asym, qlo, qhi, W.scale_dt);
-          } else if constexpr (FMT == PIPER_FMT_FP8_E4M3 || FMT == PIPER_FMT_FP8_E5M2) {
-            f_s = fp8_new_scale<CDT>(amax, FMT == PIPER_FMT_FP8_E4M3 ? 448.0f : 57344.0f);
+            if constexpr (flavor_of(FMT) == kTorchao) {
+              f_q = int8_qparams<CDT>(-nmin, amax, asym, qlo, qhi, W.scale_dt);
+            } else {
+              f_q.scale = flavor_scale<CDT>(flavor_of(FMT), fmaxf(amax, nmin), 127.0f);
+              f_q.zp = 0;
+            }
+          } else if constexpr (base_fmt(FMT) == PIPER_FMT_FP8_E4M3 || base_fmt(FMT) == PIPER_FMT_FP8_E5M2) {
+            const float lim = base_fmt(FMT) == PIPER_FMT_FP8_E4M3 ? 448.0f : 57344.0f;
+            if constexpr (flavor_of(FMT) == kQuanto) f_s = flavor_scale<CDT>(kQuanto, amax, lim);
+            else f_s = fp8_new_scale<CDT>(amax, lim);
           }
           fq_ready = true;
         }
         if (enc_phase && tile == 0 && valid) {
           // The warpgroup that encodes the row's first tile writes its new qparams.
-          if constexpr (FMT == PIPER_FMT_INT8) {
+          if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
             store_scale_dt(W.scale, row, W.scale_dt, f_q.scale);
             if (W.zp != nullptr) W.zp[row] = static_cast<int8_t>(f_q.zp);
-          } else if constexpr (FMT == PIPER_FMT_FP8_E4M3 || FMT == PIPER_FMT_FP8_E5M2) {
-            reinterpret_cast<float*>(W.scale)[row] = f_s;
+          } else if constexpr (base_fmt(FMT) == PIPER_FMT_FP8_E4M3 || base_fmt(FMT) == PIPER_FMT_FP8_E5M2) {
+            store_scale<FMT>(W, row, f_s);
           }
         }
         const int s = t % S;
@@ -1562,8 +1695,9 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
         chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) { gguf_chunk<FMT, CDT>(W, c, k, acc); });
       } else {
         // ------------------------------------------- FP8 / INT8 (affine) paths
-        constexpr bool kInt8 = FMT == PIPER_FMT_INT8;
-        constexpr bool kE4 = FMT == PIPER_FMT_FP8_E4M3;
+        constexpr bool kInt8 = base_fmt(FMT) == PIPER_FMT_INT8;
+        constexpr bool kE4 = base_fmt(FMT) == PIPER_FMT_FP8_E4M3;
+        constexpr int kFlv = flavor_of(FMT);
         constexpr float kLimit = kE4 ? 448.0f : 57344.0f;
         const bool asym = (W.flags & PIPER_FLAG_ASYMMETRIC) != 0u;
         const int qmin = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? -64 : -128;
@@ -1597,7 +1731,10 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
                     W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + c0 + 32 * k;
                 const bool sr_on = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
                 if constexpr (kInt8) {
-                  int8_encode32(merged, f_q, qmin, qmax, W.scale_dt, sr_on, key, off0, out);
+                  if constexpr (kFlv != kTorchao) flavor_int8_encode32<CDT>(kFlv, merged, f_q.scale, sr_on, key, off0, out);
+                  else int8_encode32(merged, f_q, qmin, qmax, W.scale_dt, sr_on, key, off0, out);
+                } else if constexpr (kFlv == kQuanto) {
+                  quanto_fp8_encode32<kE4, CDT>(merged, f_s, kLimit, sr_on, key, off0, out);
                 } else if (sr_on) {
 #pragma unroll
                   for (int w4 = 0; w4 < 8; ++w4) {
@@ -1718,7 +1855,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
                     W.old_scale[qp] = load_scale_dt(W.scale, qp, W.scale_dt);
                     W.old_zp[qp] = W.zp != nullptr ? static_cast<int>(W.zp[qp]) : 0;
                   } else {
-                    W.old_scale[qp] = reinterpret_cast<const float*>(W.scale)[qp];
+                    W.old_scale[qp] = load_scale<FMT>(W, qp);
                   }
                 }
                 if constexpr (kInt8) {
@@ -1740,7 +1877,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
                           W.old_scale[qp] = load_scale_dt(W.scale, qp, W.scale_dt);
                           W.old_zp[qp] = W.zp != nullptr ? static_cast<int>(W.zp[qp]) : 0;
                         } else {
-                          W.old_scale[qp] = reinterpret_cast<const float*>(W.scale)[qp];
+                          W.old_scale[qp] = load_scale<FMT>(W, qp);
                         }
                       }
                     }
@@ -1767,16 +1904,26 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
                 const float qmx = qc.qmax;
                 const bool owner = W.nq_row == 0 ? (row == 0 && col == 0) : (col % W.group == 0);
                 if constexpr (kInt8) {
-                  const Int8Q q = int8_qparams<CDT>(-qc.nmin, qmx, asym, qmin, qmax, W.scale_dt);
+                  Int8Q q;
+                  if constexpr (kFlv == kTorchao) {
+                    q = int8_qparams<CDT>(-qc.nmin, qmx, asym, qmin, qmax, W.scale_dt);
+                  } else {
+                    q.scale = flavor_scale<CDT>(kFlv, fmaxf(qmx, qc.nmin), 127.0f);
+                    q.zp = 0;
+                  }
                   if (owner) {
                     store_scale_dt(W.scale, qp, W.scale_dt, q.scale);
                     if (W.zp != nullptr) W.zp[qp] = static_cast<int8_t>(q.zp);
                   }
-                  int8_encode32(merged, q, qmin, qmax, W.scale_dt, sr_on, key, off0, out);
+                  if constexpr (kFlv == kTorchao) int8_encode32(merged, q, qmin, qmax, W.scale_dt, sr_on, key, off0, out);
+                  else flavor_int8_encode32<CDT>(kFlv, merged, q.scale, sr_on, key, off0, out);
                 } else {
-                  const float s = fp8_new_scale<CDT>(qmx, kLimit);
-                  if (owner) reinterpret_cast<float*>(W.scale)[qp] = s;
-                  if (sr_on) {
+                  const float s = kFlv == kQuanto ? flavor_scale<CDT>(kQuanto, qmx, kLimit)
+                                                  : fp8_new_scale<CDT>(qmx, kLimit);
+                  if (owner) store_scale<FMT>(W, qp, s);
+                  if constexpr (kFlv == kQuanto) {
+                    quanto_fp8_encode32<kE4, CDT>(merged, s, kLimit, sr_on, key, off0, out);
+                  } else if (sr_on) {
 #pragma unroll
                     for (int w4 = 0; w4 < 8; ++w4) {
                       float x[4];
@@ -1903,7 +2050,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
             const float n = warp_max(red_nmin);
             if (lane == 0) {
               atomic_max_nonneg(&W.qmax[0], m);
-              if (FMT == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[0], n);
+              if (base_fmt(FMT) == PIPER_FMT_INT8) atomic_max_nonneg(&W.qmin[0], n);
             }
           } else {
             flush_reduce();
@@ -2014,6 +2161,7 @@ struct Plan {
   int nq = 0;          // quantization blocks held in the workspace
   int nq_row = 0;      // blocks per row (0 = per tensor)
   int group = 0;
+  int flavor = 0;      // pm::Flavor of an FP8 / INT8 weight
   size_t ws_off = 0;
 };
 
@@ -2027,6 +2175,47 @@ int64_t row_bytes_of(const piper_merge_desc& d) {
     case PIPER_FMT_GGUF_Q4_0: return d.cols / 32 * 18;
     default: return d.cols;
   }
+}
+
+// bitsandbytes LLM.int8 and Quanto qbytes weights run on the INT8 / FP8
+// kernels with their own arithmetic (pm::Flavor); TorchAO FP8 scales are fp32.
+// Rewrites `d` to the kernel's format and stored scale dtype.
+int normalize(piper_merge_desc& d, int& flavor) {
+  flavor = pm::kTorchao;
+  const bool per_row = d.block_rows == 1 && d.block_cols == d.cols;
+  const bool per_tensor = d.block_rows == d.rows && d.block_cols == d.cols;
+  switch (d.format) {
+    case PIPER_FMT_FP8_E4M3:
+    case PIPER_FMT_FP8_E5M2:
+      d.scale_dtype = PIPER_DT_F32;
+      break;
+    case PIPER_FMT_BNB8:  // _triton_bnb8_lora.py:145-190
+      if (d.compute_dtype != PIPER_DT_F16)
+        return fail(PIPER_MERGE_EINVAL, "bitsandbytes 8-bit merge expects float16 LoRA factors.");
+      if (!per_row) return fail(PIPER_MERGE_EINVAL, "bitsandbytes 8-bit merge expects one SCB value per row.");
+      if (d.zero_point != nullptr || (d.flags & (PIPER_FLAG_ASYMMETRIC | PIPER_FLAG_REDUCE_RANGE)))
+        return fail(PIPER_MERGE_EINVAL, "bitsandbytes 8-bit storage is symmetric over [-127, 127].");
+      d.format = PIPER_FMT_INT8;
+      d.scale_dtype = PIPER_DT_F32;
+      flavor = pm::kBnb;
+      break;
+    case PIPER_FMT_QUANTO_INT8:  // _triton_quanto_lora.py:184-200, 220-343
+    case PIPER_FMT_QUANTO_FP8_E4M3:
+    case PIPER_FMT_QUANTO_FP8_E5M2:
+      if (!per_row && !per_tensor)
+        return fail(PIPER_MERGE_EINVAL, "Quanto qbytes merge on sm_100a supports a scalar scale or one scale per "
+                                        "row (axis 0); last-axis scales are not supported.");
+      if (d.zero_point != nullptr || (d.flags & (PIPER_FLAG_ASYMMETRIC | PIPER_FLAG_REDUCE_RANGE)))
+        return fail(PIPER_MERGE_EINVAL, "Quanto qbytes storage is symmetric.");
+      d.format = d.format == PIPER_FMT_QUANTO_INT8 ? PIPER_FMT_INT8
+                 : d.format == PIPER_FMT_QUANTO_FP8_E4M3 ? PIPER_FMT_FP8_E4M3 : PIPER_FMT_FP8_E5M2;
+      d.scale_dtype = d.compute_dtype;  // scales share the factors' dtype
+      flavor = pm::kQuanto;
+      break;
+    default:
+      break;
+  }
+  return PIPER_MERGE_OK;
 }
 
 // Argument checks mirror the reference launchers (e.g. _triton_mx_lora.py:348-393).
@@ -2144,7 +2333,7 @@ constexpr int kMinSmem = 120 * 1024;
 template <int FMT, int PASS, int BN, int CDT>
 int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
   auto kern = pm::merge_kernel<FMT, PASS, BN, CDT>;
-  const PipeCfg pc = plan_pipe(FMT, BN, kp_max);
+  const PipeCfg pc = plan_pipe(pm::base_fmt(FMT), BN, kp_max);
   if (pc.sc < 2)
     return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(kp_max) + " does not fit the shared-memory pipeline.");
   const int smem =
@@ -2198,6 +2387,18 @@ int launch_fmt(int fmt, int bn, LaunchParams& lp, int items, int kp, cudaStream_
     case PIPER_FMT_FP8_E4M3: return launch_bn<PIPER_FMT_FP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
     case PIPER_FMT_FP8_E5M2: return launch_bn<PIPER_FMT_FP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
     case PIPER_FMT_INT8: return launch_bn<PIPER_FMT_INT8, PASS, CDT>(bn, lp, items, kp, s);
+    case PIPER_FMT_BNB8:  // per-row, fp16 only
+      if constexpr (PASS == pm::kFused && CDT == pm::kF16) return launch_bn<PIPER_FMT_BNB8, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_QUANTO_INT8:  // per-row (fused) or per-tensor (reduce + encode)
+      if constexpr (PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_INT8, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_QUANTO_FP8_E4M3:
+      if constexpr (PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_FP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_QUANTO_FP8_E5M2:
+      if constexpr (PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_FP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
+      break;
     case PIPER_FMT_GGUF_Q8_0:
       if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_GGUF_Q8_0, PASS, CDT>(bn, lp, items, kp, s);
       break;
@@ -2397,33 +2598,40 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
     kp_max = std::max(kp_max, w.KP);
     lp.w[i] = w;
   }
+  const int kfmt = pm::kernel_fmt(d0.format, p0.flavor);
   int rc;
   if (p0.two_pass) {
-    rc = launch(pm::kReduce, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
+    rc = launch(pm::kReduce, d0.compute_dtype, kfmt, p0.bn, lp, items, kp_max, stream);
     if (rc) return rc;
     const int second = d0.format == PIPER_FMT_NVFP4 ? pm::kLocal : pm::kEncode;
-    rc = launch(second, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
+    rc = launch(second, d0.compute_dtype, kfmt, p0.bn, lp, items, kp_max, stream);
   } else if (p0.fused) {
-    rc = launch(pm::kFused, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
+    rc = launch(pm::kFused, d0.compute_dtype, kfmt, p0.bn, lp, items, kp_max, stream);
   } else {
-    rc = launch(pm::kLocal, d0.compute_dtype, d0.format, p0.bn, lp, items, kp_max, stream);
+    rc = launch(pm::kLocal, d0.compute_dtype, kfmt, p0.bn, lp, items, kp_max, stream);
   }
   return rc;
 }
 
 bool same_kernel(const piper_merge_desc& a, const Plan& pa, const piper_merge_desc& b, const Plan& pb) {
   return a.format == b.format && a.compute_dtype == b.compute_dtype && pa.bn == pb.bn &&
-         pa.two_pass == pb.two_pass && pa.fused == pb.fused;
+         pa.two_pass == pb.two_pass && pa.fused == pb.fused && pa.flavor == pb.flavor;
 }
 
-int plan_all(const piper_merge_desc* descs, int count, std::vector<Plan>& plans, size_t& ws_total) {
+int plan_all(const piper_merge_desc* in, int count, std::vector<piper_merge_desc>& descs,
+             std::vector<Plan>& plans, size_t& ws_total) {
   if (count < 0) return fail(PIPER_MERGE_EINVAL, "negative descriptor count.");
-  if (count > 0 && descs == nullptr) return fail(PIPER_MERGE_EINVAL, "null descriptor array.");
+  if (count > 0 && in == nullptr) return fail(PIPER_MERGE_EINVAL, "null descriptor array.");
+  descs.assign(in, in + count);
   plans.assign(count, Plan());
   ws_total = 0;
   for (int i = 0; i < count; ++i) {
-    int rc = validate(descs[i], plans[i]);
+    int flavor = pm::kTorchao;
+    int rc = normalize(descs[i], flavor);
     if (rc) return rc;
+    rc = validate(descs[i], plans[i]);
+    if (rc) return rc;
+    plans[i].flavor = flavor;
     plans[i].ws_off = ws_total;
     ws_total += scratch_bytes(plans[i].nq);
   }
@@ -2435,20 +2643,22 @@ int plan_all(const piper_merge_desc* descs, int count, std::vector<Plan>& plans,
 // ================================================================= C ABI
 extern "C" {
 
-int piper_merge_workspace_size(const piper_merge_desc* descs, int32_t count, size_t* bytes) {
+int piper_merge_workspace_size(const piper_merge_desc* in, int32_t count, size_t* bytes) {
+  std::vector<piper_merge_desc> descs;
   std::vector<Plan> plans;
   size_t total = 0;
-  int rc = plan_all(descs, count, plans, total);
+  int rc = plan_all(in, count, descs, plans, total);
   if (rc) return rc;
   if (bytes) *bytes = total;
   return PIPER_MERGE_OK;
 }
 
-int piper_merge_batch(const piper_merge_desc* descs, int32_t count, void* workspace,
+int piper_merge_batch(const piper_merge_desc* in, int32_t count, void* workspace,
                       size_t workspace_bytes, void* stream_ptr) {
+  std::vector<piper_merge_desc> descs;
   std::vector<Plan> plans;
   size_t total = 0;
-  int rc = plan_all(descs, count, plans, total);
+  int rc = plan_all(in, count, descs, plans, total);
   if (rc) return rc;
   if (total > 0 && (workspace == nullptr || workspace_bytes < total))
     return fail(PIPER_MERGE_EWORKSPACE, "workspace of " + std::to_string(workspace_bytes) +
@@ -2488,7 +2698,7 @@ int piper_merge_batch(const piper_merge_desc* descs, int32_t count, void* worksp
                   static_cast<int>(group.size()) >= pm::kMaxWeights ||
                   (p.two_pass && group_bytes + bytes > kL2GroupBytes));
     if (flush) {
-      rc = run_group(descs, plans, ws, group, stream);
+      rc = run_group(descs.data(), plans, ws, group, stream);
       if (rc) return rc;
       group.clear();
       group_bytes = 0;
@@ -2496,7 +2706,7 @@ int piper_merge_batch(const piper_merge_desc* descs, int32_t count, void* worksp
     group.push_back(s);
     group_bytes += bytes;
   }
-  return run_group(descs, plans, ws, group, stream);
+  return run_group(descs.data(), plans, ws, group, stream);
 }
 
 int piper_merge_mx(void* qdata, void* scale, const void* b, const void* a, int64_t rows, int64_t cols,

@@ -318,6 +318,56 @@ def merge_float8_lora(
     return qdata, scale
 
 
+def merge_static_float8_lora(
+    qdata: torch.Tensor,
+    scale: torch.Tensor,
+    b: torch.Tensor,
+    a: torch.Tensor,
+    strength: float,
+    *,
+    rounding_seed: int | None = None,
+    offset_base: int = 0,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Static per-tensor FP8 merge in place (``merge_static_float8_lora``,
+    ``_triton_static_float8_lora.py:174-295``); returns ``(qdata, scale)``.
+
+    The reference's arithmetic is the per-tensor layout of the scaled-FP8
+    merge: ``base = compute(fp8 * scale)``, ``merged = compute(base + acc *
+    strength)``, ``scale = compute(amax / limit)`` (0 becomes 2**-23), codes
+    ``fp8(clamp(merged / scale))`` or the stochastic FP8 rounding
+    (``:23-158``), so it runs as one per-tensor FP8 descriptor.
+    """
+    if qdata.device.type != "cuda":
+        raise ValueError("static-FP8 merge requires CUDA tensors.")
+    if qdata.dtype not in (torch.float8_e4m3fn, torch.float8_e5m2):
+        raise ValueError(f"static-FP8 merge supports E4M3FN and E5M2 storage, got {qdata.dtype}.")
+    cdt = _factor_dt(b, a, allowed=(torch.float16, torch.bfloat16, torch.float32))
+    if qdata.ndim != 2 or b.ndim != 2 or a.ndim != 2:
+        raise ValueError("static-FP8 merge expects rank-two tensors.")
+    _same_device(qdata, scale, b, a)
+    if scale.dtype is not torch.float32 or scale.numel() != 1:
+        raise ValueError("static-FP8 merge expects one float32 per-tensor scale.")
+    rows, cols = qdata.shape
+    rank = a.shape[0]
+    if rows == 0 or cols == 0 or rank == 0:
+        raise ValueError("static-FP8 merge requires non-empty weight and factors.")
+    if tuple(b.shape) != (rows, rank) or a.shape[1] != cols:
+        raise ValueError("LoRA factors do not match the FP8 weight shape.")
+    if not qdata.is_contiguous():
+        raise ValueError("static-FP8 merge requires contiguous storage for an in-place update.")
+    b = b.contiguous()
+    a = a.contiguous()
+    seed, sflag = _seed_fields(rounding_seed)
+    d = _desc(
+        qdata=qdata.data_ptr(), scale=scale.data_ptr(), b=b.data_ptr(), a=a.data_ptr(),
+        rows=rows, cols=cols, rank=rank, block_rows=rows, block_cols=cols,
+        format=nat.FMT_FP8_E5M2 if qdata.dtype is torch.float8_e5m2 else nat.FMT_FP8_E4M3,
+        compute_dtype=cdt, flags=sflag, strength=float(strength), seed=seed, offset_base=int(offset_base),
+    )
+    nat.merge_batch([d], qdata.device)
+    return qdata, scale
+
+
 # -------------------------------------------------------------------- INT8
 def int8_block_numel(shape: tuple[int, int], block_size: tuple[int, int]) -> int:
     """``_block_numel`` (``_triton_int8_lora.py:251-264``)."""
@@ -392,6 +442,118 @@ def merge_int8_lora(
     nat.merge_batch([d], qdata.device)
     zp_out = zero_point if zero_point is not None else torch.zeros_like(scale, dtype=torch.int8)
     return qdata, scale, zp_out
+
+
+# ----------------------------------------------------- bitsandbytes LLM.int8
+def merge_bnb8_lora(
+    cb: torch.Tensor,
+    scb: torch.Tensor,
+    b: torch.Tensor,
+    a: torch.Tensor,
+    strength: float,
+    *,
+    rounding_seed: int | None = None,
+    offset_base: int = 0,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """bitsandbytes row-wise int8 merge in place (``merge_bnb8_lora``,
+    ``_triton_bnb8_lora.py:145-242``); returns ``(CB, SCB)``.
+
+    ``base = f16(f16(CB / 127) * f16(SCB))``, ``merged = f16(clamp(base + acc *
+    strength, +-65504))``, ``SCB = row max |merged|``, codes ``rint((merged /
+    SCB) * 127)`` (0 where SCB is 0) or stochastic, clamped to [-127, 127].
+    """
+    if cb.device.type != "cuda":
+        raise ValueError("BNB8 merge requires CUDA tensors.")
+    if cb.dtype is not torch.int8 or scb.dtype is not torch.float32:
+        raise ValueError("BNB8 merge expects int8 CB and float32 SCB tensors.")
+    if b.dtype is not torch.float16 or a.dtype is not torch.float16:
+        raise ValueError("BNB8 merge expects float16 LoRA factors.")
+    if cb.ndim != 2 or b.ndim != 2 or a.ndim != 2:
+        raise ValueError("BNB8 merge expects rank-two tensors.")
+    _same_device(cb, scb, b, a)
+    rows, cols = cb.shape
+    rank = a.shape[0]
+    if rows == 0 or cols == 0 or rank == 0:
+        raise ValueError("BNB8 merge requires non-empty tensors.")
+    if scb.numel() != rows:
+        raise ValueError("BNB8 merge expects one SCB value per row.")
+    if tuple(b.shape) != (rows, rank) or a.shape[1] != cols:
+        raise ValueError("LoRA factors do not match the BNB8 weight shape.")
+    if not cb.is_contiguous() or not scb.is_contiguous():
+        raise ValueError("BNB8 merge requires contiguous storage for an in-place update.")
+    b = b.contiguous()
+    a = a.contiguous()
+    seed, sflag = _seed_fields(rounding_seed)
+    d = _desc(qdata=cb.data_ptr(), scale=scb.data_ptr(), b=b.data_ptr(), a=a.data_ptr(), rows=rows, cols=cols,
+              rank=rank, block_rows=1, block_cols=cols, format=nat.FMT_BNB8, compute_dtype=nat.DT_F16,
+              scale_dtype=nat.DT_F32, flags=sflag, strength=float(strength), seed=seed,
+              offset_base=int(offset_base))
+    nat.merge_batch([d], cb.device)
+    return cb, scb
+
+
+# ---------------------------------------------------------------- Quanto
+def quanto_scale_axis(axis: int | None, scale: torch.Tensor, rows: int, cols: int) -> str:
+    """``_scale_axis_id`` (``_triton_quanto_lora.py:184-199``): "tensor", "row" or "column"."""
+    if axis is None and scale.numel() == 1:
+        return "tensor"
+    if axis == 0 and scale.numel() == rows:
+        return "row"
+    if axis in (-1, 1) and scale.numel() == cols:
+        return "column"
+    raise ValueError("Quanto qbytes merge expects a scalar scale, one scale per row for axis 0, "
+                     "or one scale per column for the last axis.")
+
+
+def _merge_quanto(qdata, scale, axis, b, a, strength, *, fmt: int, rounding_seed, offset_base):
+    if qdata.device.type != "cuda":
+        raise ValueError("Quanto qbytes merge requires CUDA tensors.")
+    if scale.dtype is not b.dtype or b.dtype is not a.dtype:
+        raise ValueError("Quanto qbytes merge requires matching scale and factor dtypes.")
+    cdt = _factor_dt(b, a, allowed=(torch.float16, torch.bfloat16, torch.float32))
+    if qdata.ndim != 2 or b.ndim != 2 or a.ndim != 2:
+        raise ValueError("Quanto qbytes merge expects rank-two tensors.")
+    _same_device(qdata, scale, b, a)
+    rows, cols = qdata.shape
+    rank = a.shape[0]
+    if rows == 0 or cols == 0 or rank == 0:
+        raise ValueError("Quanto qbytes merge requires non-empty tensors.")
+    if tuple(b.shape) != (rows, rank) or a.shape[1] != cols:
+        raise ValueError("LoRA factors do not match the Quanto weight shape.")
+    kind = quanto_scale_axis(axis, scale, rows, cols)
+    if kind == "column":
+        raise ValueError("Quanto qbytes merge on sm_100a supports a scalar scale or one scale per row "
+                         "(axis 0); last-axis scales are not supported.")
+    if not qdata.is_contiguous() or not scale.is_contiguous():
+        raise ValueError("Quanto qbytes merge requires contiguous storage for an in-place update.")
+    b = b.contiguous()
+    a = a.contiguous()
+    brows = rows if kind == "tensor" else 1
+    seed, sflag = _seed_fields(rounding_seed)
+    d = _desc(qdata=qdata.data_ptr(), scale=scale.data_ptr(), b=b.data_ptr(), a=a.data_ptr(), rows=rows,
+              cols=cols, rank=rank, block_rows=brows, block_cols=cols, format=fmt, compute_dtype=cdt,
+              scale_dtype=cdt, flags=sflag, strength=float(strength), seed=seed, offset_base=int(offset_base))
+    nat.merge_batch([d], qdata.device)
+    return qdata, scale
+
+
+def merge_quanto_qint8_lora(qdata, scale, axis, b, a, strength, *, rounding_seed=None, offset_base=0):
+    """Quanto qint8 merge in place (``merge_quanto_qint8_lora``, ``_triton_quanto_lora.py:317-342``);
+    returns ``(qdata, scale)``: ``base = dtype(q * scale)`` (0 under a zero scale), the absmax
+    scale ``dtype(amax / 127)`` (0 -> fp32 eps), codes ``rint(dtype(x / scale))`` or stochastic."""
+    if qdata.dtype is not torch.int8:
+        raise ValueError("Quanto qint8 merge expects int8 storage.")
+    return _merge_quanto(qdata, scale, axis, b, a, strength, fmt=nat.FMT_QUANTO_INT8,
+                         rounding_seed=rounding_seed, offset_base=offset_base)
+
+
+def merge_quanto_qfloat8_lora(qdata, scale, axis, b, a, strength, *, rounding_seed=None, offset_base=0):
+    """Quanto qfloat8 merge in place (``merge_quanto_qfloat8_lora``, ``_triton_quanto_lora.py:345-377``)."""
+    if qdata.dtype not in (torch.float8_e4m3fn, torch.float8_e5m2):
+        raise ValueError(f"Quanto qfloat8 merge expects E4M3FN or E5M2 storage, got {qdata.dtype}.")
+    fmt = nat.FMT_QUANTO_FP8_E5M2 if qdata.dtype is torch.float8_e5m2 else nat.FMT_QUANTO_FP8_E4M3
+    return _merge_quanto(qdata, scale, axis, b, a, strength, fmt=fmt, rounding_seed=rounding_seed,
+                         offset_base=offset_base)
 
 
 # -------------------------------------------------------------------- GGUF

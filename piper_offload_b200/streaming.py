@@ -28,7 +28,7 @@ import torch
 
 from .adapters import merge_lora_batch
 
-STORAGE_NAMES = ("qdata", "scale", "zero_point", "per_tensor_scale", "raw")
+STORAGE_NAMES = ("qdata", "scale", "zero_point", "per_tensor_scale", "raw", "CB", "SCB", "_data", "_scale")
 
 
 @dataclass

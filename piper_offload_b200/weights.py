@@ -43,6 +43,79 @@ class Float8Weight:
 
 
 @dataclass
+class StaticFloat8Weight:
+    """TorchAO's calibrated ``PrototypeFloat8Tensor``: per-tensor FP8 weight plus
+    a static activation scale that a merge leaves alone
+    (``static_float8_adapter.py:241-248``)."""
+
+    qdata: torch.Tensor
+    scale: torch.Tensor
+    act_quant_scale: torch.Tensor
+    block_size: tuple[int, int] = ()
+    dtype: torch.dtype = torch.bfloat16
+
+    def __post_init__(self) -> None:
+        if not self.block_size:
+            self.block_size = tuple(self.qdata.shape)
+
+    @property
+    def shape(self) -> torch.Size:
+        return self.qdata.shape
+
+
+@dataclass
+class Bnb8Weight:
+    """bitsandbytes ``Int8Params`` before its first forward: row-major int8
+    ``CB`` and one fp32 ``SCB`` per row (``bnb8bit_adapter.py:1-35``)."""
+
+    CB: torch.Tensor
+    SCB: torch.Tensor
+
+    @property
+    def shape(self) -> torch.Size:
+        return self.CB.shape
+
+
+@dataclass(frozen=True)
+class QuantoQType:
+    """The parts of an optimum-quanto ``qtype`` the merge reads."""
+
+    name: str
+    bits: int
+    is_floating_point: bool
+    dtype: torch.dtype
+    qmax: float
+
+
+QINT8 = QuantoQType("qint8", 8, False, torch.int8, 127.0)
+QFLOAT8_E4M3 = QuantoQType("qfloat8_e4m3fn", 8, True, torch.float8_e4m3fn, 448.0)
+QFLOAT8_E5M2 = QuantoQType("qfloat8_e5m2", 8, True, torch.float8_e5m2, 57344.0)
+
+
+@dataclass
+class QuantoWeight:
+    """optimum-quanto ``WeightQBytesTensor``: ``_data`` codes, ``_scale`` in the
+    compute dtype, ``axis`` (None, 0 or -1) and ``qtype`` (``quanto_adapter.py:1-30``)."""
+
+    _data: torch.Tensor
+    _scale: torch.Tensor
+    axis: int | None
+    qtype: QuantoQType
+    dtype: torch.dtype | None = None
+
+    def __post_init__(self) -> None:
+        if self.dtype is None:
+            self.dtype = self._scale.dtype
+
+    @property
+    def shape(self) -> torch.Size:
+        return self._data.shape
+
+    def size(self) -> torch.Size:
+        return self._data.shape
+
+
+@dataclass
 class NVFP4Weight:
     qdata: torch.Tensor
     scale: torch.Tensor

@@ -2,10 +2,14 @@
 
 Usage: ``python tests/golden/make_merge_golden.py /path/to/piper-offload``
 
-The four raw-buffer launchers of Piper Offload 0.2.5 --
+The raw-buffer launchers of Piper Offload 0.2.5 --
 ``merge_float8_lora`` (``_triton_float8_lora.py:486``), ``merge_int8_lora``
-(``_triton_int8_lora.py:267``), ``merge_nvfp4_lora`` (``_triton_nvfp4_lora.py:515``)
-and ``merge_mx_lora_`` (``_triton_mx_lora.py:333``) -- run unmodified under the
+(``_triton_int8_lora.py:267``), ``merge_nvfp4_lora`` (``_triton_nvfp4_lora.py:515``),
+``merge_mx_lora_`` (``_triton_mx_lora.py:333``), ``merge_static_float8_lora``
+(``_triton_static_float8_lora.py:174``), ``merge_bnb8_lora``
+(``_triton_bnb8_lora.py:145``) and ``merge_quanto_qint8_lora`` /
+``merge_quanto_qfloat8_lora`` (``_triton_quanto_lora.py:317, 345``) -- run
+unmodified under the
 Triton CPU interpreter (``TRITON_INTERPRET=1``, triton 3.6). Their inputs and
 outputs go to ``merge_reference.npz`` with one manifest entry per case in
 ``merge_reference.json``.
@@ -23,8 +27,12 @@ instruction computes:
   fp32 (the fixtures use factors whose dot products are exact in any order);
 * binary arithmetic on two bf16 tensors (``base * scale`` in the INT8 kernel):
   computed on decoded values and rounded once to bf16, as ``mul.rn.bf16`` does;
-* ``libdevice.llrint``: absent from the interpreter; ``numpy.rint``
-  (round half to even, the ``cvt.rni`` default mode).
+* ``libdevice.llrint`` / ``libdevice.rint``: absent from the interpreter;
+  ``numpy.rint`` (round half to even, the ``cvt.rni`` default mode);
+* Quanto's torch-side scale recompute (``_absmax_scale``) runs on CPU tensors
+  here, where torch divides ``amax / qmax``; on CUDA tensors torch multiplies
+  by the fp32 reciprocal of the host scalar, which this script applies (a GPU
+  test checks that torch behaviour on the device).
 
 Unary and reduction operations on bf16/fp8 tensors, which none of these kernels
 use, raise instead of running on bit patterns. The launchers' CUDA-device check
@@ -150,7 +158,7 @@ def patch_interpreter() -> None:
 
 
 class _Libdevice:
-    """``libdevice.llrint``: round half to even, to int64."""
+    """``libdevice.llrint`` (to int64) and ``libdevice.rint``: round half to even."""
 
     @staticmethod
     def llrint(x):
@@ -161,10 +169,38 @@ class _Libdevice:
         ty = x.type.with_element_ty(tl.int64) if x.type.is_block() else tl.int64
         return tl.core.tensor(ti.TensorHandle(data, tl.int64), ty)
 
+    @staticmethod
+    def rint(x):
+        import triton.language as tl
+        from triton.runtime import interpreter as ti
 
-def lift_device_check(mod, fname: str) -> None:
+        return tl.core.tensor(ti.TensorHandle(np.rint(x.handle.data), x.dtype), x.type)
+
+
+def _cuda_absmax_scale(quanto):
+    """Quanto's ``_absmax_scale`` (``_triton_quanto_lora.py:202-217``) as it runs on
+    CUDA tensors: there ``amax / qmax`` (a tensor over a host scalar) is computed
+    by torch as ``amax * fp32(1 / qmax)``; on the CPU tensors of this script torch
+    would divide. Every other step is the reference's."""
+
+    def absmax_scale(dense, scale, scale_axis, qmax):
+        if scale_axis == quanto._AXIS_ROW:
+            amax = dense.abs().amax(dim=1, keepdim=True)
+        elif scale_axis == quanto._AXIS_COLUMN:
+            amax = dense.abs().amax(dim=0, keepdim=True)
+        else:
+            amax = dense.abs().amax()
+        inv = torch.tensor(float(np.float32(1.0) / np.float32(qmax)), dtype=torch.float32)
+        output = (amax.float() * inv).to(dense.dtype).to(dtype=scale.dtype).reshape(scale.shape)
+        eps = torch.finfo(torch.float32).eps
+        return torch.where(output == 0, torch.full_like(output, eps), output)
+
+    return absmax_scale
+
+
+def lift_device_check(mod, fname: str, tensor: str = "qdata") -> None:
     src = inspect.getsource(getattr(mod, fname))
-    needle = 'qdata.device.type != "cuda"'
+    needle = f'{tensor}.device.type != "cuda"'
     if src.count(needle) != 1:
         raise RuntimeError(f"{mod.__name__}.{fname}: device check not found")
     code = compile(src.replace(needle, "False"), mod.__file__, "exec",
@@ -180,13 +216,19 @@ def load_reference(src: Path):
     from piper_offload import _triton_float8_lora as f8
     from piper_offload import _triton_int8_lora as i8
     from piper_offload import _triton_mx_lora as mx
+    from piper_offload import _triton_bnb8_lora as bnb8
     from piper_offload import _triton_nvfp4_lora as n4
+    from piper_offload import _triton_quanto_lora as qo
+    from piper_offload import _triton_static_float8_lora as sf8
 
     for mod, fname in ((f8, "_validate_inputs"), (i8, "merge_int8_lora"), (n4, "_validate_inputs"),
-                       (mx, "merge_mx_lora_")):
+                       (mx, "merge_mx_lora_"), (sf8, "merge_static_float8_lora"), (qo, "_merge_quanto_qbytes_lora")):
         lift_device_check(mod, fname)
-    i8.libdevice = _Libdevice
-    return f8, i8, n4, mx
+    lift_device_check(bnb8, "merge_bnb8_lora", tensor="cb")
+    for mod in (i8, bnb8, qo):
+        mod.libdevice = _Libdevice
+    qo._absmax_scale = _cuda_absmax_scale(qo)
+    return {"float8": f8, "int8": i8, "nvfp4": n4, "mx": mx, "static_float8": sf8, "bnb8": bnb8, "quanto": qo}
 
 
 # ---------------------------------------------------------------------- inputs
@@ -361,14 +403,86 @@ def gen_mx(mx, w: Writer, g) -> None:
     one(19, 96, 7, "e2m1", 1, True, SEED, zero_b=True)
 
 
+def gen_static_float8(sf8, w: Writer, g) -> None:
+    def one(rows, cols, rank, e4m3, seed, dt, strength=1.0, zero_b=False):
+        fdt = torch.float8_e4m3fn if e4m3 else torch.float8_e5m2
+        limit = torch.finfo(fdt).max
+        base = torch.randn(rows, cols, generator=g) * 0.02
+        s = (base.abs().amax() / limit).reshape(()).float()
+        q = (base / s).clamp(-limit, limit).to(fdt)
+        b, a = exact_factors(g, rows, cols, rank, DTYPES[dt], zero_b=zero_b)
+        oq, os_ = sf8.merge_static_float8_lora(q.clone(), s.clone(), b, a, strength, rounding_seed=seed)
+        w.add({"launcher": "static_float8", "rows": rows, "cols": cols, "rank": rank, "e4m3": e4m3, "seed": seed,
+               "dtype": dt, "strength": strength},
+              qdata=q, scale=s, b=b, a=a, out_qdata=oq, out_scale=os_)
+
+    for e4m3 in (True, False):
+        for seed in (None, SEED):
+            one(70, 130, 7, e4m3, seed, "bf16")
+    one(70, 130, 7, True, SEED, "f16", strength=-0.75)
+    one(70, 130, 7, True, None, "bf16", zero_b=True)
+
+
+def gen_bnb8(bnb8, w: Writer, g) -> None:
+    def one(rows, cols, rank, seed, strength=1.0, zero_b=False, zero_row=False):
+        cb = torch.randint(-127, 128, (rows, cols), generator=g, dtype=torch.int8)
+        scb = (torch.rand(rows, generator=g) * 0.05 + 0.01).float()
+        if zero_row:
+            cb[3] = 0
+            scb[3] = 0.0
+        b, a = exact_factors(g, rows, cols, rank, torch.float16, exp=9, zero_b=zero_b)
+        if zero_row:
+            b[3] = 0
+        ocb, oscb = bnb8.merge_bnb8_lora(cb.clone(), scb.clone(), b, a, strength, rounding_seed=seed)
+        w.add({"launcher": "bnb8", "rows": rows, "cols": cols, "rank": rank, "seed": seed, "dtype": "f16",
+               "strength": strength},
+              qdata=cb, scale=scb, b=b, a=a, out_qdata=ocb, out_scale=oscb)
+
+    for seed in (None, SEED):
+        one(35, 69, 7, seed)
+        one(35, 69, 19, seed, zero_row=True)
+    one(16, 64, 7, SEED, strength=-1.25)
+    one(35, 69, 7, None, zero_b=True)
+
+
+def gen_quanto(qo, w: Writer, g) -> None:
+    def one(rows, cols, rank, storage, axis, seed, dt, strength=1.0, zero_scale=False):
+        if storage == "int8":
+            q = torch.randint(-128, 128, (rows, cols), generator=g, dtype=torch.int8)
+            qmax = 127.0
+        else:
+            fdt = torch.float8_e4m3fn if storage == "e4m3" else torch.float8_e5m2
+            qmax = torch.finfo(fdt).max
+            q = (torch.randn(rows, cols, generator=g) * qmax / 4).clamp(-qmax, qmax).to(fdt)
+        sshape = {None: (), 0: (rows, 1), -1: (1, cols)}[axis]
+        scale = (torch.rand(sshape, generator=g) * 2e-4 + 5e-5).to(DTYPES[dt])
+        if zero_scale and axis == 0:
+            scale[2] = 0.0
+        b, a = exact_factors(g, rows, cols, rank, DTYPES[dt], exp=9)
+        fn = qo.merge_quanto_qint8_lora if storage == "int8" else qo.merge_quanto_qfloat8_lora
+        oq, os_ = fn(q.clone(), scale.clone(), axis, b, a, strength, rounding_seed=seed)
+        w.add({"launcher": "quanto", "rows": rows, "cols": cols, "rank": rank, "storage": storage, "axis": axis,
+               "seed": seed, "dtype": dt, "strength": strength},
+              qdata=q, scale=scale, b=b, a=a, out_qdata=oq, out_scale=os_)
+
+    for storage in ("int8", "e4m3", "e5m2"):
+        for axis in (None, 0, -1):
+            for seed in (None, SEED):
+                one(35, 69, 7, storage, axis, seed, "bf16")
+        one(35, 69, 7, storage, 0, SEED, "f16", strength=-0.75, zero_scale=True)
+
+
 def main() -> None:
     ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PIPER_OFFLOAD_SRC", ""))
-    f8, i8, n4, mx = load_reference(ref / "src")
+    mods = load_reference(ref / "src")
     w = Writer()
-    gen_float8(f8, w, torch.Generator().manual_seed(80))
-    gen_int8(i8, w, torch.Generator().manual_seed(81))
-    gen_nvfp4(n4, w, torch.Generator().manual_seed(82))
-    gen_mx(mx, w, torch.Generator().manual_seed(83))
+    gen_float8(mods["float8"], w, torch.Generator().manual_seed(80))
+    gen_int8(mods["int8"], w, torch.Generator().manual_seed(81))
+    gen_nvfp4(mods["nvfp4"], w, torch.Generator().manual_seed(82))
+    gen_mx(mods["mx"], w, torch.Generator().manual_seed(83))
+    gen_static_float8(mods["static_float8"], w, torch.Generator().manual_seed(84))
+    gen_bnb8(mods["bnb8"], w, torch.Generator().manual_seed(85))
+    gen_quanto(mods["quanto"], w, torch.Generator().manual_seed(86))
     w.save()
     print(f"{len(w.cases)} reference merge cases written to", HERE)
 

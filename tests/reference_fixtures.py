@@ -1,7 +1,7 @@
 """Reference-kernel fixtures: load them, and run the oracle or the sm_100a path on their inputs.
 
 ``tests/golden/merge_reference.{npz,json}`` hold the inputs and outputs of the
-reference's four Triton merge launchers, recorded by
+reference's Triton merge launchers, recorded by
 ``tests/golden/make_merge_golden.py``. Every case's factors are small-integer
 multiples of a power of two, so the rank-r dot product is exact in any
 summation order and the outputs are a bit-level target for any correct
@@ -40,8 +40,9 @@ def arr(case: dict, name: str) -> np.ndarray | None:
 
 
 def case_label(case: dict) -> str:
-    keys = [k for k in ("launcher", "rows", "cols", "rank", "e4m3", "elem", "block", "scaling_mode", "swizzled",
-                        "two_level", "asymmetric", "reduce_range", "dtype", "scale_dtype", "strength") if k in case]
+    keys = [k for k in ("launcher", "rows", "cols", "rank", "e4m3", "elem", "storage", "axis", "block",
+                        "scaling_mode", "swizzled", "two_level", "asymmetric", "reduce_range", "dtype", "scale_dtype",
+                        "strength") if k in case]
     sr = "sr" if case["seed"] is not None else "rtn"
     return "-".join(str(case[k]) for k in keys) + "-" + sr
 
@@ -64,8 +65,10 @@ def expected(case: dict) -> dict:
     if case["launcher"] == "int8":
         out["scale"] = _float_values(sc, case["scale_dtype"]).reshape(-1)
         out["zp"] = arr(case, "out_zero_point").reshape(-1)
-    elif case["launcher"] == "float8":
+    elif case["launcher"] in ("float8", "static_float8", "bnb8"):
         out["scale"] = sc.astype(np.float32).reshape(-1)
+    elif case["launcher"] == "quanto":
+        out["scale"] = _float_values(sc, case["dtype"]).reshape(-1)
     else:
         out["scale"] = sc.reshape(-1).view(np.uint8)
     g = arr(case, "out_per_tensor_scale")
@@ -84,6 +87,18 @@ def oracle(case: dict) -> dict:
     if L == "float8":
         nq, ns = om.merge_float8(q.view(np.uint8), arr(case, "scale"), tuple(case["block"]), b, a, s,
                                  e4m3=case["e4m3"], **kw)
+        return {"q": nq.reshape(-1).view(np.uint8), "scale": np.asarray(ns, np.float32).reshape(-1)}
+    if L == "static_float8":
+        nq, ns = om.merge_static_float8(q.view(np.uint8), arr(case, "scale"), b, a, s, e4m3=case["e4m3"], **kw)
+        return {"q": nq.reshape(-1).view(np.uint8), "scale": np.asarray(ns, np.float32).reshape(-1)}
+    if L == "bnb8":
+        nq, ns = om.merge_bnb8(q, arr(case, "scale"), b, a, s, seed=case["seed"])
+        return {"q": nq.reshape(-1).view(np.uint8), "scale": np.asarray(ns, np.float32).reshape(-1)}
+    if L == "quanto":
+        kind = {None: "tensor", 0: "row", -1: "column"}[case["axis"]]
+        qa = q if case["storage"] == "int8" else q.view(np.uint8)
+        nq, ns = om.merge_quanto(qa, _float_values(arr(case, "scale"), case["dtype"]), kind, b, a, s,
+                                 storage=case["storage"], **kw)
         return {"q": nq.reshape(-1).view(np.uint8), "scale": np.asarray(ns, np.float32).reshape(-1)}
     if L == "int8":
         sdt = case["scale_dtype"]
@@ -126,6 +141,26 @@ def native(case: dict, device) -> dict:
         sc = dev(arr(case, "scale"))
         K.merge_float8_lora(q, sc, tuple(case["block"]), b, a, s, **kw)
         return {"q": q.view(torch.uint8).cpu().numpy().reshape(-1), "scale": sc.cpu().numpy().reshape(-1)}
+    if L == "static_float8":
+        q = dev(arr(case, "qdata"), torch.float8_e4m3fn if case["e4m3"] else torch.float8_e5m2)
+        sc = dev(arr(case, "scale"))
+        K.merge_static_float8_lora(q, sc, b, a, s, **kw)
+        return {"q": q.view(torch.uint8).cpu().numpy().reshape(-1), "scale": sc.cpu().numpy().reshape(-1)}
+    if L == "bnb8":
+        q = dev(arr(case, "qdata"))
+        sc = dev(arr(case, "scale"))
+        K.merge_bnb8_lora(q, sc, b, a, s, **kw)
+        return {"q": q.cpu().numpy().reshape(-1).view(np.uint8), "scale": sc.cpu().numpy().reshape(-1)}
+    if L == "quanto":
+        if case["storage"] == "int8":
+            q = dev(arr(case, "qdata"))
+            fn = K.merge_quanto_qint8_lora
+        else:
+            q = dev(arr(case, "qdata"), torch.float8_e4m3fn if case["storage"] == "e4m3" else torch.float8_e5m2)
+            fn = K.merge_quanto_qfloat8_lora
+        sc = dev(arr(case, "scale"), fdt)
+        fn(q, sc, case["axis"], b, a, s, **kw)
+        return {"q": q.view(torch.uint8).cpu().numpy().reshape(-1), "scale": sc.float().cpu().numpy().reshape(-1)}
     if L == "int8":
         q = dev(arr(case, "qdata"))
         sdt = TORCH_DT[case["scale_dtype"]]

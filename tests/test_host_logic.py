@@ -136,6 +136,53 @@ def test_adapter_selection_and_shapes():
         AD.select_adapter(torch.zeros(3))
 
 
+def test_static_float8_adapter_selection_and_layout_rules():
+    q = torch.zeros(4, 32, dtype=torch.float8_e4m3fn)
+    st = WT.StaticFloat8Weight(q, torch.ones(()), torch.ones(()))
+    assert AD.select_adapter(st) is AD.StaticFloat8Adapter  # ahead of the dynamic Float8Tensor adapter
+    assert st.block_size == (4, 32) and AD.StaticFloat8Adapter.logical_shape(st) == (4, 32)
+    b, a = torch.zeros(4, 2, dtype=torch.bfloat16), torch.zeros(2, 32, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="exactly one value"):
+        AD.StaticFloat8Adapter.validate_lora_merge(WT.StaticFloat8Weight(q, torch.ones(()), torch.ones(2)), b, a, 1.0)
+    with pytest.raises(ValueError, match="per-tensor FP8 weight layout"):
+        AD.StaticFloat8Adapter.validate_lora_merge(WT.StaticFloat8Weight(q, torch.ones(()), torch.ones(()), (1, 32)),
+                                                   b, a, 1.0)
+    with pytest.raises(ValueError, match="CUDA"):
+        AD.StaticFloat8Adapter.validate_lora_merge(st, b, a, 1.0)
+    with pytest.raises(ValueError, match="CUDA"):
+        K.merge_static_float8_lora(q, torch.ones(()), b, a, 1.0)
+
+
+def test_bnb8_and_quanto_adapter_rules():
+    cb = torch.zeros(4, 32, dtype=torch.int8)
+    bnb = WT.Bnb8Weight(cb, torch.ones(4))
+    assert AD.select_adapter(bnb) is AD.Bnb8Adapter and AD.Bnb8Adapter.compute_dtype(bnb) is torch.float16
+    f16 = (torch.zeros(4, 2, dtype=torch.float16), torch.zeros(2, 32, dtype=torch.float16))
+    bf16 = (torch.zeros(4, 2, dtype=torch.bfloat16), torch.zeros(2, 32, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="float16 LoRA factors"):
+        AD.Bnb8Adapter.validate_lora_merge(bnb, *bf16, 1.0)
+    with pytest.raises(ValueError, match="one SCB value per row"):
+        AD.Bnb8Adapter.validate_lora_merge(WT.Bnb8Weight(cb, torch.ones(3)), *f16, 1.0)
+    with pytest.raises(ValueError, match="CUDA"):
+        AD.Bnb8Adapter.validate_lora_merge(bnb, *f16, 1.0)
+    qrow = WT.QuantoWeight(cb, torch.ones(4, 1, dtype=torch.bfloat16), 0, WT.QINT8)
+    assert AD.select_adapter(qrow) is AD.QuantoAdapter and AD.QuantoAdapter.compute_dtype(qrow) is torch.bfloat16
+    with pytest.raises(ValueError, match="CUDA"):
+        AD.QuantoAdapter.validate_lora_merge(qrow, *bf16, 1.0)
+    qcol = WT.QuantoWeight(cb, torch.ones(1, 32, dtype=torch.bfloat16), -1, WT.QINT8)
+    with pytest.raises(ValueError, match="last-axis"):
+        AD.QuantoAdapter.validate_lora_merge(qcol, *bf16, 1.0)
+    with pytest.raises(ValueError, match="matching scale and factor dtypes"):
+        AD.QuantoAdapter.validate_lora_merge(qrow, *f16, 1.0)
+    with pytest.raises(ValueError, match="qtype metadata"):
+        AD.QuantoAdapter.validate_lora_merge(WT.QuantoWeight(cb, torch.ones(4, 1, dtype=torch.bfloat16), 0,
+                                                             WT.QFLOAT8_E4M3), *bf16, 1.0)
+    with pytest.raises(ValueError, match="scalar scale, one scale per row"):
+        K.quanto_scale_axis(0, torch.ones(3), 4, 32)
+    assert K.quanto_scale_axis(None, torch.ones(()), 4, 32) == "tensor"
+    assert K.quanto_scale_axis(-1, torch.ones(1, 32), 4, 32) == "column"
+
+
 def test_mx_scaling_mode_resolution():
     mx = WT.MXWeight(torch.zeros(1, 32, dtype=torch.float8_e4m3fn), torch.zeros(1, 1), torch.float8_e4m3fn)
     assert AD.mx_scaling_mode_id(mx) == 0

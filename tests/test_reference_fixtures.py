@@ -1,8 +1,10 @@
 """CPU: the oracle against the reference's own Triton merge kernels, bit for bit.
 
-The fixtures (``tests/golden/merge_reference.*``) were recorded from the four
+The fixtures (``tests/golden/merge_reference.*``) were recorded from the
 raw-buffer launchers of the reference (``merge_float8_lora``,
-``merge_int8_lora``, ``merge_nvfp4_lora``, ``merge_mx_lora_``) at the
+``merge_int8_lora``, ``merge_nvfp4_lora``, ``merge_mx_lora_``,
+``merge_static_float8_lora``, ``merge_bnb8_lora``, ``merge_quanto_qint8_lora``,
+``merge_quanto_qfloat8_lora``) at the
 reference tests' shapes, across layouts, scale modes, swizzling, rounding
 modes, factor and scale dtypes, negative strengths and zero factors. Their
 divisions are IEEE, which the oracle computes without its GPU-division hook.
@@ -19,7 +21,7 @@ CASES = rf.cases()
 
 def test_fixture_coverage():
     launchers = {c["launcher"] for c in CASES}
-    assert launchers == {"float8", "int8", "nvfp4", "mx"}
+    assert launchers == {"float8", "int8", "nvfp4", "mx", "static_float8", "bnb8", "quanto"}
     assert {c["elem"] for c in CASES if c["launcher"] == "mx"} == {"e4m3", "e5m2", "e2m1"}
     assert {c["scaling_mode"] for c in CASES if c["launcher"] == "mx"} == {0, 1, 2, 3}
     assert any(c["seed"] is not None for c in CASES) and any(c["seed"] is None for c in CASES)
