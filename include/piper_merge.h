@@ -182,7 +182,30 @@ int piper_merge_gguf(void* raw, const void* b, const void* a, int64_t rows, int6
                      int64_t rank, int32_t quant_type, int32_t compute_dtype, float strength,
                      int32_t has_seed, uint64_t seed, uint64_t offset_base, void* stream);
 
-/* Message of the calling thread's last failed call ("" if none). */
+/* _triton_static_float8_lora.py:174 merge_static_float8_lora(qdata, scale, b, a,
+ * strength, *, rounding_seed): per-tensor FP8 with one fp32 scale. `workspace`
+ * >= piper_merge_workspace_size() of the equivalent per-tensor descriptor (256 B). */
+int piper_merge_static_float8(void* qdata, void* scale, const void* b, const void* a, int64_t rows,
+                              int64_t cols, int64_t rank, int32_t e5m2, int32_t compute_dtype,
+                              float strength, int32_t has_seed, uint64_t seed, uint64_t offset_base,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* _triton_bnb8_lora.py:145 merge_bnb8_lora(cb, scb, b, a, strength, *,
+ * rounding_seed): int8 CB rows x cols, fp32 SCB per row, fp16 factors. */
+int piper_merge_bnb8(void* cb, void* scb, const void* b, const void* a, int64_t rows, int64_t cols,
+                     int64_t rank, float strength, int32_t has_seed, uint64_t seed,
+                     uint64_t offset_base, void* stream);
+
+/* _triton_quanto_lora.py:317 / :345 merge_quanto_qint8_lora /
+ * merge_quanto_qfloat8_lora(qdata, scale, axis, b, a, strength, *,
+ * rounding_seed). storage: 0 = qint8, 1 = qfloat8 e4m3, 2 = qfloat8 e5m2;
+ * per_row: 1 for axis 0 (one scale per row), 0 for a scalar scale (workspace
+ * >= 256 B). Scales and factors share `compute_dtype`. */
+int piper_merge_quanto(void* qdata, void* scale, const void* b, const void* a, int64_t rows,
+                       int64_t cols, int64_t rank, int32_t storage, int32_t per_row,
+                       int32_t compute_dtype, float strength, int32_t has_seed, uint64_t seed,
+                       uint64_t offset_base, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Self-test of the failure path, no counterpart in the reference: enqueues a
  * one-thread kernel that waits on a barrier nothing arrives on. Its bounded
  * wait gives up after the kernels' wait limit (2 s), sets the device status
@@ -190,6 +213,7 @@ int piper_merge_gguf(void* raw, const void* b, const void* a, int64_t rows, int6
  * usable. */
 int piper_merge_selftest_timeout(void* stream);
 
+/* Message of the calling thread's last failed call ("" if none). */
 const char* piper_merge_last_error(void);
 
 /* Reads and clears the device-side error word of the current device (nonzero

@@ -57,6 +57,9 @@ EXPORTED_SYMBOLS = (
     "piper_merge_float8_noalloc",
     "piper_merge_int8",
     "piper_merge_gguf",
+    "piper_merge_static_float8",
+    "piper_merge_bnb8",
+    "piper_merge_quanto",
     "piper_merge_last_error",
     "piper_merge_device_status",
     "piper_merge_version",
@@ -129,6 +132,9 @@ def load() -> ctypes.CDLL:
         lib.piper_merge_float8.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, f32, i32, u64, u64, vp, sz, vp]
         lib.piper_merge_int8.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, i32, i32, f32, i32, u64, u64, vp, sz, vp]
         lib.piper_merge_gguf.argtypes = [vp, vp, vp, i64, i64, i64, i32, i32, f32, i32, u64, u64, vp]
+        lib.piper_merge_static_float8.argtypes = [vp, vp, vp, vp, i64, i64, i64, i32, i32, f32, i32, u64, u64, vp, sz, vp]
+        lib.piper_merge_bnb8.argtypes = [vp, vp, vp, vp, i64, i64, i64, f32, i32, u64, u64, vp]
+        lib.piper_merge_quanto.argtypes = [vp, vp, vp, vp, i64, i64, i64, i32, i32, i32, f32, i32, u64, u64, vp, sz, vp]
         lib.piper_merge_last_error.restype = ctypes.c_char_p
         lib.piper_merge_last_error.argtypes = []
         lib.piper_merge_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32)]
@@ -144,6 +150,9 @@ def load() -> ctypes.CDLL:
             "piper_merge_float8_noalloc",
             "piper_merge_int8",
             "piper_merge_gguf",
+            "piper_merge_static_float8",
+            "piper_merge_bnb8",
+            "piper_merge_quanto",
             "piper_merge_device_status",
             "piper_merge_selftest_timeout",
         ):

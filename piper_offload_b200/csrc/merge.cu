@@ -2880,6 +2880,65 @@ int piper_merge_int8(void* qdata, void* scale, void* zero_point, const void* b, 
   return piper_merge_batch(&d, 1, workspace, workspace_bytes, stream);
 }
 
+int piper_merge_static_float8(void* qdata, void* scale, const void* b, const void* a, int64_t rows,
+                              int64_t cols, int64_t rank, int32_t e5m2, int32_t compute_dtype,
+                              float strength, int32_t has_seed, uint64_t seed, uint64_t offset_base,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  return piper_merge_float8(qdata, scale, b, a, rows, cols, rank, rows, cols, e5m2, compute_dtype, strength,
+                            has_seed, seed, offset_base, workspace, workspace_bytes, stream);
+}
+
+int piper_merge_bnb8(void* cb, void* scb, const void* b, const void* a, int64_t rows, int64_t cols,
+                     int64_t rank, float strength, int32_t has_seed, uint64_t seed,
+                     uint64_t offset_base, void* stream) {
+  piper_merge_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.format = PIPER_FMT_BNB8;
+  d.qdata = cb;
+  d.scale = scb;
+  d.b = b;
+  d.a = a;
+  d.rows = rows;
+  d.cols = cols;
+  d.rank = rank;
+  d.block_rows = 1;
+  d.block_cols = cols;
+  d.compute_dtype = PIPER_DT_F16;
+  d.scale_dtype = PIPER_DT_F32;
+  d.flags = has_seed ? PIPER_FLAG_STOCHASTIC : 0u;
+  d.strength = strength;
+  d.seed = seed;
+  d.offset_base = offset_base;
+  return piper_merge_batch(&d, 1, nullptr, 0, stream);
+}
+
+int piper_merge_quanto(void* qdata, void* scale, const void* b, const void* a, int64_t rows,
+                       int64_t cols, int64_t rank, int32_t storage, int32_t per_row,
+                       int32_t compute_dtype, float strength, int32_t has_seed, uint64_t seed,
+                       uint64_t offset_base, void* workspace, size_t workspace_bytes, void* stream) {
+  if (storage < 0 || storage > 2)
+    return fail(PIPER_MERGE_EINVAL, "Quanto storage must be 0 (qint8), 1 (qfloat8 e4m3) or 2 (qfloat8 e5m2).");
+  piper_merge_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.format = storage == 0 ? PIPER_FMT_QUANTO_INT8 : (storage == 1 ? PIPER_FMT_QUANTO_FP8_E4M3 : PIPER_FMT_QUANTO_FP8_E5M2);
+  d.qdata = qdata;
+  d.scale = scale;
+  d.b = b;
+  d.a = a;
+  d.rows = rows;
+  d.cols = cols;
+  d.rank = rank;
+  d.block_rows = per_row ? 1 : rows;
+  d.block_cols = cols;
+  d.compute_dtype = compute_dtype;
+  d.scale_dtype = compute_dtype;
+  d.flags = has_seed ? PIPER_FLAG_STOCHASTIC : 0u;
+  d.strength = strength;
+  d.seed = seed;
+  d.offset_base = offset_base;
+  return piper_merge_batch(&d, 1, workspace, workspace_bytes, stream);
+}
+
 int piper_merge_gguf(void* raw, const void* b, const void* a, int64_t rows, int64_t cols, int64_t rank,
                      int32_t quant_type, int32_t compute_dtype, float strength, int32_t has_seed,
                      uint64_t seed, uint64_t offset_base, void* stream) {

@@ -102,6 +102,26 @@ def test_convenience_entry_points_validate():
     assert lib.piper_merge_mx(1, 1, 1, 1, 32, 64, 16, 5, 0, 0, 0, 1.0, 0, 0, 0, None) == nat.EINVAL
     assert lib.piper_merge_gguf(1, 1, 1, 32, 64, 16, 3, 0, 1.0, 0, 0, 0, None) == nat.EINVAL
     assert lib.piper_merge_float8(1, 1, 1, 1, 0, 64, 16, 1, 64, 0, 0, 1.0, 0, 0, 0, None, 0, None) == nat.EINVAL
+    # new formats: argument errors are reported before anything is enqueued
+    assert lib.piper_merge_static_float8(1, 1, 1, 1, 0, 64, 16, 0, 0, 1.0, 0, 0, 0, None, 0, None) == nat.EINVAL
+    assert lib.piper_merge_quanto(1, 1, 1, 1, 32, 64, 16, 3, 1, 0, 1.0, 0, 0, 0, None, 0, None) == nat.EINVAL
+    assert b"storage" in lib.piper_merge_last_error()
+    assert lib.piper_merge_bnb8(1, 1, 1, 1, 32, 64, 0, 1.0, 0, 0, 0, None) == nat.EINVAL
+
+
+def test_new_format_validation_messages():
+    # bitsandbytes: fp16 factors only; Quanto: per-row or per-tensor only.
+    d = _desc(format=nat.FMT_BNB8, compute_dtype=nat.DT_BF16, block_rows=1, block_cols=256)
+    assert nat.load().piper_merge_workspace_size((nat.MergeDesc * 1)(d), 1, ctypes.byref(ctypes.c_size_t())) == nat.EINVAL
+    assert b"float16" in nat.load().piper_merge_last_error()
+    d = _desc(format=nat.FMT_QUANTO_INT8, block_rows=1, block_cols=64)
+    assert nat.load().piper_merge_workspace_size((nat.MergeDesc * 1)(d), 1, ctypes.byref(ctypes.c_size_t())) == nat.EINVAL
+    assert b"last-axis" in nat.load().piper_merge_last_error()
+    # per-tensor Quanto and static FP8 take the two-pass workspace; per-row needs none
+    assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_FP8_E4M3, block_rows=64, block_cols=256)]) == 256
+    assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_INT8, block_rows=1, block_cols=256)]) == 0
+    assert nat.workspace_bytes([_desc(format=nat.FMT_BNB8, compute_dtype=nat.DT_F16, block_rows=1,
+                                      block_cols=256)]) == 0
 
 
 class _FailingLib:
