@@ -436,6 +436,188 @@ def merge_bnb8(cb, scb, b, a, strength, *, seed=None, offset_base=0):
 
 
 # ---------------------------------------------------------------------------
+# bitsandbytes 4-bit (NF4 / FP4): _triton_bnb4_lora.py:28-375.
+# ---------------------------------------------------------------------------
+
+BNB4_BLOCK = 64
+BNB4_NESTED_BLOCK = 256
+# Ordered FP4 magnitude levels and thresholds (_triton_bnb4_lora.py:53-105).
+_FP4_LEVELS = np.array([0.0, 0.0052083334885537624, 0.1666666716337204, 0.25, 0.3333333432674408, 0.5,
+                        0.6666666865348816, 1.0], dtype=np.float32)
+_FP4_THRESHOLDS = np.array([0.0026041667442768812, 0.08593750256113708, 0.2083333358168602, 0.2916666716337204,
+                            0.4166666716337204, 0.5833333432674408, 0.8333333432674408], dtype=np.float32)
+_FP4_STORE_TO_LEVEL = np.array([0, 1, 6, 7, 4, 5, 2, 3], dtype=np.int64)  # _fp4_storage_to_level
+
+
+def _fp4_level_to_store(level):
+    level = np.asarray(level, np.int64)
+    return np.where(level < 2, level, np.where(level < 4, level + 4, np.where(level < 6, level, level - 4)))
+
+
+def sorted_code_lower_bound(values, code, max_index: int):
+    """Index reached by the reference's binary search (``:29-50``): the number of
+    entries among ``code[0:max_index]`` that are ``< value``."""
+    values = np.asarray(values, np.float32)
+    code = np.asarray(code, np.float32)
+    low = np.zeros(values.shape, np.int64)
+    high = np.full(values.shape, max_index, np.int64)
+    steps = int(max_index).bit_length()
+    for _ in range(steps):
+        middle = (low + high) // 2
+        right = code[middle] < values
+        low = np.where(right, middle + 1, low)
+        high = np.where(right, high, middle)
+    return low
+
+
+def nearest_sorted_code(values, code, max_index: int):
+    """``_nearest_sorted_code`` (``_triton_bnb4_lora.py:29-50``)."""
+    values = np.asarray(values, np.float32)
+    code = np.asarray(code, np.float32)
+    upper_index = sorted_code_lower_bound(values, code, max_index)
+    lower_index = np.maximum(upper_index - 1, 0)
+    lower = code[lower_index]
+    upper = code[upper_index]
+    choose_lower = np.abs((values - lower).astype(np.float32)) <= np.abs((values - upper).astype(np.float32))
+    return np.where(choose_lower, lower_index, upper_index)
+
+
+def stochastic_sorted_code(values, deterministic, code, seed, offsets, max_index: int):
+    """``_stochastic_sorted_code`` (``_triton_stochastic_quantization.py:43-79``)."""
+    values = np.asarray(values, np.float32)
+    code = np.asarray(code, np.float32)
+    upper_index = sorted_code_lower_bound(values, code, max_index)
+    upper = code[upper_index]
+    exact = upper == values
+    lower_index = np.where(exact, upper_index, np.maximum(upper_index - 1, 0))
+    lower = code[lower_index]
+    width = (upper - lower).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        prob = np.where(width > 0.0, fdiv_t((values - lower).astype(np.float32), np.where(width > 0, width, 1.0)),
+                        np.float32(0.0)).astype(np.float32)
+    u = philox_uniform(seed, offsets)
+    chosen = np.where(u < prob, upper_index, lower_index)
+    interior = (values > code[0]) & (values < code[max_index]) & ~exact
+    return np.where(interior, chosen, np.asarray(deterministic, np.int64))
+
+
+def nearest_fp4_code(values):
+    """``_nearest_fp4_code`` (``_triton_bnb4_lora.py:53-75``)."""
+    values = np.asarray(values, np.float32)
+    mag = np.abs(values)
+    level = (mag[..., None] > _FP4_THRESHOLDS).sum(axis=-1).astype(np.int64)
+    code = _fp4_level_to_store(level)
+    return np.where((values < 0.0) & (level != 0), code + 8, code)
+
+
+def stochastic_fp4_code(values, deterministic, seed, offsets):
+    """``_stochastic_fp4_code`` (``_triton_bnb4_lora.py:135-160``)."""
+    values = np.asarray(values, np.float32)
+    deterministic = np.asarray(deterministic, np.int64)
+    mag = np.abs(values)
+    nearest_level = _FP4_STORE_TO_LEVEL[deterministic & 7]
+    nearest = _FP4_LEVELS[nearest_level]
+    down = nearest > mag
+    lower_level = np.where(down, nearest_level - 1, nearest_level)
+    upper_level = np.where(down, nearest_level, nearest_level + 1)
+    lower = _FP4_LEVELS[np.clip(lower_level, 0, 7)]
+    upper = _FP4_LEVELS[np.clip(upper_level, 0, 7)]
+    width = (upper - lower).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        prob = np.where(upper > lower, fdiv_t((mag - lower).astype(np.float32), np.where(width > 0, width, 1.0)),
+                        np.float32(0.0)).astype(np.float32)
+    level = np.where(philox_uniform(seed, offsets) < prob, upper_level, lower_level)
+    sign = np.where((values < 0.0) & (level != 0), 8, 0)
+    chosen = _fp4_level_to_store(level) + sign
+    interior = (mag > 0.0) & (mag < 1.0) & (prob > 0.0)
+    return np.where(interior, chosen, deterministic)
+
+
+def unpack_bnb4(packed, rows: int, cols: int) -> np.ndarray:
+    """Code index of every element: element 2j is the high nibble of byte j (``:217-226``)."""
+    p = np.asarray(packed, np.uint8).reshape(rows, cols // 2).astype(np.int64)
+    out = np.empty((rows, cols), np.int64)
+    out[:, 0::2] = p >> 4
+    out[:, 1::2] = p & 15
+    return out
+
+
+def pack_bnb4(codes) -> np.ndarray:
+    codes = np.asarray(codes, np.int64)
+    return ((codes[:, 0::2] << 4) | codes[:, 1::2]).astype(np.uint8)
+
+
+def bnb4_nested_quantize(raw_absmax, nested_code):
+    """Nested (double) quantization of the new block maxima (``:316-375``, ``:399-431``).
+
+    ``offset = sum(raw) / n``; per 256-block: ``nested = max |raw - offset|``,
+    code ``nearest(clamp((raw - offset) / nested, -1, 1))`` over the 256-entry
+    table. The reference sums in Triton's reduction order; here the sum is
+    exact and rounded once (tie class: fp32 summation order of the mean).
+    """
+    raw = np.asarray(raw_absmax, np.float32).reshape(-1)
+    n = raw.size
+    offset = np.float32(np.float32(np.sum(raw.astype(np.float64))) / np.float32(n))
+    centered = (raw - offset).astype(np.float32)
+    nblk = (n + BNB4_NESTED_BLOCK - 1) // BNB4_NESTED_BLOCK
+    pad = np.zeros(nblk * BNB4_NESTED_BLOCK, np.float32)
+    pad[:n] = np.abs(centered)
+    nested_absmax = nanmax_reduce(pad.reshape(nblk, BNB4_NESTED_BLOCK), axis=1).astype(np.float32)
+    safe = np.where(nested_absmax == 0.0, np.float32(1.0), nested_absmax)
+    scaled = clamp(fdiv_t(centered, np.repeat(safe, BNB4_NESTED_BLOCK)[:n]), -1.0, 1.0)
+    q = nearest_sorted_code(scaled, nested_code, 255).astype(np.uint8)
+    return q, nested_absmax, offset
+
+
+def merge_bnb4(packed, absmax, code, b, a, strength, *, quant_type="nf4", nested_absmax=None, nested_code=None,
+               offset=None, seed=None, compute="bf16", offset_base=0):
+    """bitsandbytes blockwise 4-bit merge (``merge_bnb4_lora``, ``_triton_bnb4_lora.py:434-604``).
+
+    Blocks of 64 values along each row. ``absmax`` fp32 per block, or uint8
+    codes of the nested quantization (``nested_absmax`` fp32 per 256 blocks,
+    ``nested_code`` 256 fp32, ``offset`` fp32). ``base = compute(code[q] *
+    scale)`` with ``scale = nested_code[c] * nested_absmax + offset`` (one fused
+    multiply-add) when nested; ``merged = compute(base + acc * strength)``;
+    new block scale ``max |merged|``; ``clamp(merged / scale, -1, 1)`` encoded
+    to the nearest NF4 table entry (ties to the lower) or the FP4 thresholds,
+    or stochastically. Returns ``(packed, absmax[, nested_absmax, offset])``.
+    """
+    M = b.shape[0]
+    N = a.shape[1]
+    nb = N // BNB4_BLOCK
+    code = np.asarray(code, np.float32)
+    idx = unpack_bnb4(packed, M, N)
+    base = code[idx]
+    if nested_absmax is not None:
+        q = np.asarray(absmax, np.uint8).reshape(M, nb).astype(np.int64)
+        flat = np.arange(M * nb).reshape(M, nb) // BNB4_NESTED_BLOCK
+        ns = np.asarray(nested_absmax, np.float32).reshape(-1)[flat]
+        scales = fma_f32(np.asarray(nested_code, np.float32)[q], ns, np.float32(offset))
+    else:
+        scales = np.asarray(absmax, np.float32).reshape(M, nb)
+    base = round_to_compute((base * np.repeat(scales, BNB4_BLOCK, axis=1)).astype(np.float32), compute)
+    acc = lora_delta(b, a)
+    merged = merged_values(base, acc, strength, compute)
+    out_scale = nanmax_reduce(np.abs(merged).reshape(M, nb, BNB4_BLOCK), axis=2).astype(np.float32)
+    safe = np.where(out_scale == 0.0, np.float32(1.0), out_scale)
+    normalized = clamp(fdiv_t(merged, np.repeat(safe, BNB4_BLOCK, axis=1)), -1.0, 1.0)
+    offs = logical_offsets(M, N, offset_base)
+    if quant_type == "nf4":
+        codes = nearest_sorted_code(normalized, code, 15)
+        if seed is not None:
+            codes = stochastic_sorted_code(normalized, codes, code, seed, offs, 15)
+    else:
+        codes = nearest_fp4_code(normalized)
+        if seed is not None:
+            codes = stochastic_fp4_code(normalized, codes, seed, offs)
+    new_packed = pack_bnb4(codes).reshape(np.shape(packed))
+    if nested_absmax is None:
+        return new_packed, out_scale.reshape(np.shape(absmax))
+    q, nabs, off = bnb4_nested_quantize(out_scale, nested_code)
+    return new_packed, q.reshape(np.shape(absmax)), nabs.reshape(np.shape(nested_absmax)), off
+
+
+# ---------------------------------------------------------------------------
 # Quanto qbytes: _triton_quanto_lora.py:28-168, 202-217.
 # ---------------------------------------------------------------------------
 

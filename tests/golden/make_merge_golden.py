@@ -216,6 +216,7 @@ def load_reference(src: Path):
     from piper_offload import _triton_float8_lora as f8
     from piper_offload import _triton_int8_lora as i8
     from piper_offload import _triton_mx_lora as mx
+    from piper_offload import _triton_bnb4_lora as bnb4
     from piper_offload import _triton_bnb8_lora as bnb8
     from piper_offload import _triton_nvfp4_lora as n4
     from piper_offload import _triton_quanto_lora as qo
@@ -225,10 +226,12 @@ def load_reference(src: Path):
                        (mx, "merge_mx_lora_"), (sf8, "merge_static_float8_lora"), (qo, "_merge_quanto_qbytes_lora")):
         lift_device_check(mod, fname)
     lift_device_check(bnb8, "merge_bnb8_lora", tensor="cb")
+    lift_device_check(bnb4, "merge_bnb4_lora", tensor="packed")
     for mod in (i8, bnb8, qo):
         mod.libdevice = _Libdevice
     qo._absmax_scale = _cuda_absmax_scale(qo)
-    return {"float8": f8, "int8": i8, "nvfp4": n4, "mx": mx, "static_float8": sf8, "bnb8": bnb8, "quanto": qo}
+    return {"float8": f8, "int8": i8, "nvfp4": n4, "mx": mx, "static_float8": sf8, "bnb8": bnb8, "quanto": qo,
+            "bnb4": bnb4}
 
 
 # ---------------------------------------------------------------------- inputs
@@ -472,6 +475,49 @@ def gen_quanto(qo, w: Writer, g) -> None:
         one(35, 69, 7, storage, 0, SEED, "f16", strength=-0.75, zero_scale=True)
 
 
+def bnb4_tables(g):
+    """Synthetic sorted code tables with few significant bits, so that the
+    nested scale ``code * absmax + offset`` is exact with or without a fused
+    multiply-add."""
+    inner = torch.randperm(2047, generator=g)[:13].sort().values.float() / 1024.0 - 1.0 + 1.0 / 1024.0
+    code = torch.cat([torch.tensor([-1.0, 0.0, 1.0]), inner]).unique().sort().values
+    while code.numel() < 16:
+        code = torch.cat([code, torch.tensor([float(code.numel()) / 4096.0])]).unique().sort().values
+    nested = torch.round(torch.linspace(-1.0, 1.0, 256) * 1024.0) / 1024.0
+    return code[:16].float().contiguous(), nested.float().contiguous()
+
+
+def gen_bnb4(bnb4, w: Writer, g) -> None:
+    code, nested_code = bnb4_tables(g)
+
+    def one(rows, cols, rank, quant_type, seed, dt, nested=False, strength=1.0, zero_b=False):
+        nblk = rows * cols // 64
+        packed = torch.randint(0, 256, (rows * cols // 2, 1), generator=g, dtype=torch.uint8)
+        if nested:
+            absmax = torch.randint(0, 256, (nblk,), generator=g, dtype=torch.uint8)
+            nabs = (torch.randint(64, 4096, ((nblk + 255) // 256,), generator=g).float() * 2.0**-14)
+            offset = torch.tensor(float(torch.randint(1, 4096, (1,), generator=g)) * 2.0**-16)
+        else:
+            absmax = torch.rand(nblk, generator=g) * 0.05 + 0.005
+            nabs = offset = None
+        b, a = exact_factors(g, rows, cols, rank, DTYPES[dt], exp=9, zero_b=zero_b)
+        out = bnb4.merge_bnb4_lora(packed.clone(), absmax.clone(), code, nabs, nested_code if nested else None,
+                                   offset, (rows, cols), 64, quant_type, b, a, strength, rounding_seed=seed)
+        w.add({"launcher": "bnb4", "rows": rows, "cols": cols, "rank": rank, "quant_type": quant_type,
+               "nested": nested, "seed": seed, "dtype": dt, "strength": strength},
+              qdata=packed, scale=absmax, code=code, nested_absmax=nabs,
+              nested_code=nested_code if nested else None, offset=offset, b=b, a=a,
+              out_qdata=out[0], out_scale=out[1], out_nested_absmax=out[2], out_offset=out[3])
+
+    for quant_type in ("nf4", "fp4"):
+        for seed in (None, SEED):
+            one(19, 128, 13, quant_type, seed, "bf16")
+            one(24, 256, 40, quant_type, seed, "f16")
+        one(40, 512, 7, quant_type, None, "bf16", nested=True)
+        one(40, 512, 7, quant_type, None, "f16", nested=True, strength=-0.5)
+        one(19, 128, 13, quant_type, SEED, "bf16", zero_b=True)
+
+
 def main() -> None:
     ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PIPER_OFFLOAD_SRC", ""))
     mods = load_reference(ref / "src")
@@ -483,6 +529,7 @@ def main() -> None:
     gen_static_float8(mods["static_float8"], w, torch.Generator().manual_seed(84))
     gen_bnb8(mods["bnb8"], w, torch.Generator().manual_seed(85))
     gen_quanto(mods["quanto"], w, torch.Generator().manual_seed(86))
+    gen_bnb4(mods["bnb4"], w, torch.Generator().manual_seed(87))
     w.save()
     print(f"{len(w.cases)} reference merge cases written to", HERE)
 

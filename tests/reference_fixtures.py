@@ -40,7 +40,8 @@ def arr(case: dict, name: str) -> np.ndarray | None:
 
 
 def case_label(case: dict) -> str:
-    keys = [k for k in ("launcher", "rows", "cols", "rank", "e4m3", "elem", "storage", "axis", "block",
+    keys = [k for k in ("launcher", "rows", "cols", "rank", "e4m3", "elem", "storage", "axis", "quant_type", "nested",
+                        "block",
                         "scaling_mode", "swizzled", "two_level", "asymmetric", "reduce_range", "dtype", "scale_dtype",
                         "strength") if k in case]
     sr = "sr" if case["seed"] is not None else "rtn"
@@ -69,6 +70,11 @@ def expected(case: dict) -> dict:
         out["scale"] = sc.astype(np.float32).reshape(-1)
     elif case["launcher"] == "quanto":
         out["scale"] = _float_values(sc, case["dtype"]).reshape(-1)
+    elif case["launcher"] == "bnb4":
+        out["scale"] = sc.reshape(-1).view(np.uint8) if case["nested"] else sc.astype(np.float32).reshape(-1)
+        if case["nested"]:
+            out["nested_absmax"] = arr(case, "out_nested_absmax").astype(np.float32).reshape(-1)
+            out["offset"] = arr(case, "out_offset").astype(np.float32).reshape(-1)
     else:
         out["scale"] = sc.reshape(-1).view(np.uint8)
     g = arr(case, "out_per_tensor_scale")
@@ -91,6 +97,20 @@ def oracle(case: dict) -> dict:
     if L == "static_float8":
         nq, ns = om.merge_static_float8(q.view(np.uint8), arr(case, "scale"), b, a, s, e4m3=case["e4m3"], **kw)
         return {"q": nq.reshape(-1).view(np.uint8), "scale": np.asarray(ns, np.float32).reshape(-1)}
+    if L == "bnb4":
+        nested = case["nested"]
+        res = om.merge_bnb4(q, arr(case, "scale"), arr(case, "code"), b, a, s, quant_type=case["quant_type"],
+                            nested_absmax=arr(case, "nested_absmax") if nested else None,
+                            nested_code=arr(case, "nested_code") if nested else None,
+                            offset=float(arr(case, "offset")) if nested else None, **kw)
+        out = {"q": np.asarray(res[0], np.uint8).reshape(-1)}
+        if nested:
+            out["scale"] = np.asarray(res[1], np.uint8).reshape(-1)
+            out["nested_absmax"] = np.asarray(res[2], np.float32).reshape(-1)
+            out["offset"] = np.asarray([res[3]], np.float32)
+        else:
+            out["scale"] = np.asarray(res[1], np.float32).reshape(-1)
+        return out
     if L == "bnb8":
         nq, ns = om.merge_bnb8(q, arr(case, "scale"), b, a, s, seed=case["seed"])
         return {"q": nq.reshape(-1).view(np.uint8), "scale": np.asarray(ns, np.float32).reshape(-1)}

@@ -21,7 +21,7 @@ CASES = rf.cases()
 
 def test_fixture_coverage():
     launchers = {c["launcher"] for c in CASES}
-    assert launchers == {"float8", "int8", "nvfp4", "mx", "static_float8", "bnb8", "quanto"}
+    assert launchers == {"float8", "int8", "nvfp4", "mx", "static_float8", "bnb8", "quanto", "bnb4"}
     assert {c["elem"] for c in CASES if c["launcher"] == "mx"} == {"e4m3", "e5m2", "e2m1"}
     assert {c["scaling_mode"] for c in CASES if c["launcher"] == "mx"} == {0, 1, 2, 3}
     assert any(c["seed"] is not None for c in CASES) and any(c["seed"] is None for c in CASES)
