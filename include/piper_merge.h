@@ -56,6 +56,8 @@ extern "C" {
 #define PIPER_FMT_QUANTO_INT8 10     /* Quanto qint8 qbytes, scales in the compute dtype */
 #define PIPER_FMT_QUANTO_FP8_E4M3 11 /* Quanto qfloat8 qbytes */
 #define PIPER_FMT_QUANTO_FP8_E5M2 12
+#define PIPER_FMT_BNB4_NF4 13        /* bitsandbytes 4-bit, NF4 code selection */
+#define PIPER_FMT_BNB4_FP4 14        /* bitsandbytes 4-bit, FP4 code selection */
 
 /* ---- floating dtypes (factors = compute dtype; INT8 scales) ---- */
 #define PIPER_DT_BF16 0
@@ -86,11 +88,16 @@ extern "C" {
  *         ((rows+127)/128*32) x ((cols+63)/64*16); FP8: fp32, one per
  *         quantization block; INT8: `scale_dtype`, one per block; BNB8: fp32
  *         SCB, one per row; Quanto: `compute_dtype`, one per row or one per
- *         tensor; GGUF: unused.
+ *         tensor; BNB4: fp32 absmax per 64-value block, or uint8 codes of the
+ *         nested quantization; GGUF: unused.
  * zero_point  INT8 only: int8 per block, or NULL (symmetric storage).
  * global_scale NVFP4 only: fp32 per-tensor scale (two-level), or NULL.
  * block_rows, block_cols  FP8/INT8 quantization block: (1, cols) per row,
  *         (rows, cols) per tensor, (1, g) per group with g | cols.
+ * codebook BNB4 only: 16 fp32 code values (bitsandbytes QuantState.code).
+ * nested_absmax, nested_code, nested_offset  BNB4 nested absmax only: fp32
+ *         per 256 blocks (updated), 256 fp32 code values, fp32 offset (updated);
+ *         NULL otherwise. The first 4-bit value of byte j is its high nibble.
  * offset_base is added to every logical element offset row*cols+col before it
  *         keys the stochastic stream (0 reproduces the reference; a row shard
  *         passes its first element's global offset to draw the unsharded stream).
@@ -115,6 +122,10 @@ typedef struct piper_merge_desc {
   float strength;
   uint64_t seed;
   uint64_t offset_base;
+  const void* codebook;
+  void* nested_absmax;
+  const void* nested_code;
+  void* nested_offset;
 } piper_merge_desc;
 
 /* Bytes of device workspace `piper_merge_batch` needs for these descriptors.
@@ -205,6 +216,16 @@ int piper_merge_quanto(void* qdata, void* scale, const void* b, const void* a, i
                        int64_t cols, int64_t rank, int32_t storage, int32_t per_row,
                        int32_t compute_dtype, float strength, int32_t has_seed, uint64_t seed,
                        uint64_t offset_base, void* workspace, size_t workspace_bytes, void* stream);
+
+/* _triton_bnb4_lora.py:434 merge_bnb4_lora(packed, absmax, code, nested_absmax,
+ * nested_code, offset, logical_shape, 64, quant_type, b, a, strength, *,
+ * rounding_seed). nf4: 1 for NF4, 0 for FP4. Nested absmax (nested_absmax !=
+ * NULL) needs workspace (piper_merge_workspace_size) and round-to-nearest. */
+int piper_merge_bnb4(void* packed, void* absmax, const void* code, void* nested_absmax,
+                     const void* nested_code, void* nested_offset, const void* b, const void* a,
+                     int64_t rows, int64_t cols, int64_t rank, int32_t nf4, int32_t compute_dtype,
+                     float strength, int32_t has_seed, uint64_t seed, uint64_t offset_base,
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* Self-test of the failure path, no counterpart in the reference: enqueues a
  * one-thread kernel that waits on a barrier nothing arrives on. Its bounded

@@ -38,6 +38,8 @@ FMT_BNB8 = 9
 FMT_QUANTO_INT8 = 10
 FMT_QUANTO_FP8_E4M3 = 11
 FMT_QUANTO_FP8_E5M2 = 12
+FMT_BNB4_NF4 = 13
+FMT_BNB4_FP4 = 14
 
 DT_BF16 = 0
 DT_F16 = 1
@@ -60,6 +62,7 @@ EXPORTED_SYMBOLS = (
     "piper_merge_static_float8",
     "piper_merge_bnb8",
     "piper_merge_quanto",
+    "piper_merge_bnb4",
     "piper_merge_last_error",
     "piper_merge_device_status",
     "piper_merge_version",
@@ -91,6 +94,10 @@ class MergeDesc(ctypes.Structure):
         ("strength", ctypes.c_float),
         ("seed", ctypes.c_uint64),
         ("offset_base", ctypes.c_uint64),
+        ("codebook", ctypes.c_void_p),
+        ("nested_absmax", ctypes.c_void_p),
+        ("nested_code", ctypes.c_void_p),
+        ("nested_offset", ctypes.c_void_p),
     ]
 
 
@@ -135,6 +142,8 @@ def load() -> ctypes.CDLL:
         lib.piper_merge_static_float8.argtypes = [vp, vp, vp, vp, i64, i64, i64, i32, i32, f32, i32, u64, u64, vp, sz, vp]
         lib.piper_merge_bnb8.argtypes = [vp, vp, vp, vp, i64, i64, i64, f32, i32, u64, u64, vp]
         lib.piper_merge_quanto.argtypes = [vp, vp, vp, vp, i64, i64, i64, i32, i32, i32, f32, i32, u64, u64, vp, sz, vp]
+        lib.piper_merge_bnb4.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i32, i32, f32, i32, u64, u64,
+                                         vp, sz, vp]
         lib.piper_merge_last_error.restype = ctypes.c_char_p
         lib.piper_merge_last_error.argtypes = []
         lib.piper_merge_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32)]
@@ -153,6 +162,7 @@ def load() -> ctypes.CDLL:
             "piper_merge_static_float8",
             "piper_merge_bnb8",
             "piper_merge_quanto",
+            "piper_merge_bnb4",
             "piper_merge_device_status",
             "piper_merge_selftest_timeout",
         ):

@@ -25,6 +25,7 @@ StaticFloat8Ada.   static_float8_adapter.py:113-248 (layout rules
                    _torchao_static_float8.py:213-258)
 Bnb8Adapter        bnb8bit_adapter.py:92-121 gate, :285-315 merge
 QuantoAdapter      quanto_adapter.py:136-187 gate, :370-440 merge
+Bnb4Adapter        bnb4bit_adapter.py:100-160 gate (plain / nested absmax)
 Nvfp4Adapter       nvfp4_adapter.py:57-117 gate, :255-290 merge
 MxAdapter          mx_adapter.py:90-137 gate, :274-309 merge
 GgufAdapter        new: gguf_adapter.py:160-284 has no merge capability
@@ -399,6 +400,57 @@ class Bnb8Adapter:
         nat.merge_batch([d], target.CB.device)
 
 
+# ================================================= bitsandbytes 4-bit
+class Bnb4Adapter:
+    """bitsandbytes ``Params4bit`` (NF4 / FP4, plain or nested absmax);
+    ``bnb4bit_adapter.py:100-160`` gate. The merge runs in the quant state's dtype."""
+
+    NAME = "bitsandbytes-4bit"
+
+    @staticmethod
+    def matches(t: Any) -> bool:
+        qs = getattr(t, "quant_state", None)
+        return qs is not None and hasattr(qs, "quant_type") and isinstance(getattr(t, "data", None), torch.Tensor)
+
+    @staticmethod
+    def logical_shape(t: Any) -> tuple[int, ...]:
+        return tuple(t.quant_state.shape)
+
+    @staticmethod
+    def compute_dtype(t: Any) -> torch.dtype:
+        return t.quant_state.dtype
+
+    @classmethod
+    def _desc(cls, t: Any, b, a, strength, rounding_seed, offset_base, keep) -> nat.MergeDesc:
+        qs = t.quant_state
+        st2 = qs.state2
+        if st2 is not None and getattr(st2, "blocksize", 256) != 256:
+            raise ValueError("Nested BNB4 scale metadata has an unsupported layout.")
+        _cuda_same_device("bitsandbytes 4-bit", t.data, qs.absmax, b, a)
+        return K.bnb4_desc(t.data, qs.absmax, qs.code, None if st2 is None else st2.absmax,
+                           None if st2 is None else st2.code, qs.offset if st2 is not None else None,
+                           tuple(qs.shape), qs.blocksize, qs.quant_type, b, a, strength, rounding_seed=rounding_seed,
+                           offset_base=offset_base, keep=keep)
+
+    @classmethod
+    def validate_lora_merge(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                            rounding_seed: int | None = None) -> None:
+        _seed(rounding_seed)
+        cls._desc(target, b, a, strength, rounding_seed, 0, None)
+
+    @classmethod
+    def merge_desc(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                   rounding_seed: int | None = None, offset_base: int = 0, keep: list | None = None) -> nat.MergeDesc:
+        return cls._desc(target, b, a, strength, rounding_seed, offset_base, keep)
+
+    @classmethod
+    def merge_lora_(cls, target: Any, b: torch.Tensor, a: torch.Tensor, strength: float, *,
+                    rounding_seed: int | None = None, offset_base: int = 0) -> None:
+        keep: list = []
+        d = cls.merge_desc(target, b, a, strength, rounding_seed=rounding_seed, offset_base=offset_base, keep=keep)
+        nat.merge_batch([d], target.data.device)
+
+
 # ================================================================ Quanto
 class QuantoAdapter:
     """optimum-quanto ``WeightQBytesTensor`` (qint8 / qfloat8 ``_data``, ``_scale``
@@ -706,7 +758,7 @@ class GgufAdapter:
 
 # ================================================================ registry
 _ADAPTERS: list[type] = [MxAdapter, Nvfp4Adapter, StaticFloat8Adapter, Float8Adapter, Int8Adapter,
-                         Bnb8Adapter, QuantoAdapter, GgufAdapter]
+                         Bnb8Adapter, QuantoAdapter, Bnb4Adapter, GgufAdapter]
 
 
 def register_adapter(adapter: type, *, first: bool = True) -> None:
@@ -724,7 +776,7 @@ def select_adapter(t: Any) -> type:
 
 
 def target_device(t: Any) -> torch.device:
-    for name in ("raw", "qdata", "CB", "_data"):
+    for name in ("raw", "qdata", "CB", "_data", "data"):
         raw = getattr(t, name, None)
         if isinstance(raw, torch.Tensor):
             return raw.device

@@ -88,6 +88,10 @@ struct alignas(64) DevWeight {
   int scale_cols;      // MX: N/32, NVFP4: N/16
   int scale_mode;      // MX E8M0 rounding
   int scale_dt;        // stored scale dtype (INT8: as given; FP8: fp32, Quanto: the compute dtype)
+  const float* code16; // BNB4: 16-entry code table
+  const float* ncode;  // BNB4 nested: 256-entry code table of the block maxima (else null)
+  const float* nabs;   // BNB4 nested: fp32 maximum per 256 blocks
+  const float* noff;   // BNB4 nested: fp32 offset
   int use_tma;         // code tiles move by bulk tensor copies (swizzled rows)
   int use_tma_a;       // A tiles by bulk tensor copies (else cp.async into the same layout)
   int use_tma_b;       // B strips by bulk tensor copies (else cp.async into the same layout)
@@ -108,7 +112,9 @@ __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / 
 // Code bytes for `cols` columns of one row.
 template <int FMT>
 __host__ __device__ constexpr int code_bytes(int cols) {
-  if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) return cols / 2;
+  if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4 || FMT == PIPER_FMT_BNB4_NF4 ||
+                FMT == PIPER_FMT_BNB4_FP4)
+    return cols / 2;
   else if constexpr (FMT == PIPER_FMT_GGUF_Q8_0) return cols / 32 * 34;
   else if constexpr (FMT == PIPER_FMT_GGUF_Q4_0) return cols / 32 * 18;
   else return cols;
@@ -919,6 +925,188 @@ __device__ __forceinline__ void affine_inputs(const DevWeight& W, const RowCtx& 
   }
 }
 
+// ================================================ bitsandbytes 4-bit epilogue
+// One 64-value block of _merge_quantize_kernel (_triton_bnb4_lora.py:163-313):
+// base = compute(code[q] * absmax) (nested absmax: nested_code[c] * nested
+// absmax + offset, one fused multiply-add), merged = compute(base + acc * s),
+// new absmax = max |merged|, x = clamp(merged / absmax, -1, 1) encoded to the
+// nearest table entry (NF4, ties to the lower index; _nearest_sorted_code
+// :29-50) or by the FP4 thresholds (_nearest_fp4_code :53-75), or
+// stochastically (_stochastic_sorted_code, _stochastic_fp4_code :135-160).
+// `lut` holds code[lane & 15] and `lvl` the FP4 level value of lane & 7: table
+// reads are full-warp shuffles, so the whole warp runs this together and every
+// lookup is evaluated unconditionally (never under a per-lane condition).
+__device__ __forceinline__ float lane_lut(float lut, int idx) { return __shfl_sync(0xFFFFFFFFu, lut, idx); }
+
+__device__ __forceinline__ int fp4_level_to_store(int level) {
+  return level < 2 ? level : (level < 4 ? level + 4 : (level < 6 ? level : level - 4));
+}
+
+template <int FMT, int CDT>
+__device__ __forceinline__ void bnb4_block(const DevWeight& W, const RowCtx& c, int col, const float (&acc0)[32],
+                                           const float (&acc1)[32], float lut, float lvl, const PhiloxKey& key,
+                                           uint32_t (&wv)[8]) {
+  constexpr bool kNf4 = FMT == PIPER_FMT_BNB4_NF4;
+  const int64_t bi = static_cast<int64_t>(c.row) * (W.N >> 6) + (col >> 6);
+  float scale = 0.0f;
+  if (c.valid) {
+    if (W.ncode != nullptr) {
+      const uint32_t q = reinterpret_cast<const uint8_t*>(W.scale)[bi];
+      scale = fmaf(__ldg(W.ncode + q), __ldg(W.nabs + (bi >> 8)), __ldg(W.noff));
+    } else {
+      scale = reinterpret_cast<const float*>(W.scale)[bi];
+    }
+  }
+  float m[64];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const uint32_t byte = (wv[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+    m[2 * j] = lane_lut(lut, static_cast<int>(byte >> 4));
+    m[2 * j + 1] = lane_lut(lut, static_cast<int>(byte & 15u));
+  }
+#pragma unroll
+  for (int i = 0; i < 64; ++i) m[i] = __fmul_rn(m[i], scale);
+#pragma unroll
+  for (int i = 0; i < 64; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    m[i] = fmaf(acc0[i], W.strength, m[i]);
+    m[32 + i] = fmaf(acc1[i], W.strength, m[32 + i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 64; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(m[i]));
+  if (c.valid) {
+    if (W.ncode != nullptr) W.qmax[bi] = __float_as_uint(amax);  // raw maxima for the nested pass
+    else reinterpret_cast<float*>(W.scale)[bi] = amax;
+  }
+  const float safe = amax == 0.0f ? 1.0f : amax;
+  const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;  // uniform across the warp
+  const float code_first = lane_lut(lut, 0);
+  const float code_last = lane_lut(lut, 15);
+  const uint64_t off0 = W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) wv[w] = 0u;
+#pragma unroll 4
+  for (int i = 0; i < 64; ++i) {
+    const float v = fminf(fmaxf(div_full(m[i], safe), -1.0f), 1.0f);
+    int code;
+    if constexpr (kNf4) {
+      int low = 0, high = 15;
+#pragma unroll
+      for (int st = 0; st < 4; ++st) {
+        const int mid = (low + high) >> 1;
+        const bool right = lane_lut(lut, mid) < v;
+        low = right ? mid + 1 : low;
+        high = right ? high : mid;
+      }
+      const int ui = low;
+      const int li = max(ui - 1, 0);
+      const float up = lane_lut(lut, ui);
+      const float lo = lane_lut(lut, li);
+      code = fabsf(__fsub_rn(v, lo)) <= fabsf(__fsub_rn(v, up)) ? li : ui;
+      if (sr) {
+        const bool exact = up == v;
+        const int li2 = exact ? ui : li;
+        const float lo2 = lane_lut(lut, li2);
+        const float width = __fsub_rn(up, lo2);
+        const float prob = width > 0.0f ? div_full(__fsub_rn(v, lo2), width) : 0.0f;
+        const int chosen = philox_uniform(key, off0 + i) < prob ? ui : li2;
+        const bool interior = (v > code_first) & (v < code_last) & !exact;
+        code = interior ? chosen : code;
+      }
+    } else {
+      const float mag = fabsf(v);
+      const int level = (mag > 0.0026041667442768812f) + (mag > 0.08593750256113708f) +
+                        (mag > 0.2083333358168602f) + (mag > 0.2916666716337204f) + (mag > 0.4166666716337204f) +
+                        (mag > 0.5833333432674408f) + (mag > 0.8333333432674408f);
+      code = fp4_level_to_store(level) + ((v < 0.0f && level != 0) ? 8 : 0);
+      if (sr) {
+        // _fp4_storage_to_level of the nearest code: the level itself.
+        const float nearest = lane_lut(lvl, level);
+        const bool down = nearest > mag;
+        const int lol = down ? level - 1 : level;
+        const int upl = down ? level : level + 1;
+        const float lo = lane_lut(lvl, max(lol, 0));
+        const float up = lane_lut(lvl, min(upl, 7));
+        const float prob = up > lo ? div_full(__fsub_rn(mag, lo), __fsub_rn(up, lo)) : 0.0f;
+        const int lv = philox_uniform(key, off0 + i) < prob ? upl : lol;
+        const int chosen = fp4_level_to_store(lv) + ((v < 0.0f && lv != 0) ? 8 : 0);
+        const bool interior = mag > 0.0f && mag < 1.0f && prob > 0.0f;
+        code = interior ? chosen : code;
+      }
+    }
+    const int j = i >> 1;
+    wv[j >> 2] |= static_cast<uint32_t>(code & 15) << ((j & 3) * 8 + ((i & 1) ? 0 : 4));
+  }
+}
+
+// Nested quantization of the new block maxima (_triton_bnb4_lora.py:316-375,
+// :399-431): offset = mean of the maxima; per 256 blocks the maximum of
+// |x - offset| and the nearest code of (x - offset) / maximum in the
+// 256-entry table. The mean is summed in fp64 in a fixed order and rounded
+// once; the reference sums in Triton's fp32 reduction order.
+__global__ void __launch_bounds__(1024) bnb4_offset_kernel(const uint32_t* __restrict__ raw, int64_t n,
+                                                           float* __restrict__ off) {
+  __shared__ double part[32];
+  double s = 0.0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += static_cast<double>(__uint_as_float(raw[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xFFFFFFFFu, s, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_down_sync(0xFFFFFFFFu, t, o);
+    if (threadIdx.x == 0) *off = __fdiv_rn(__double2float_rn(t), static_cast<float>(n));  // `/ TOTAL_VALUES`
+  }
+}
+
+__global__ void __launch_bounds__(256) bnb4_nested_kernel(const uint32_t* __restrict__ raw, int64_t n,
+                                                          const float* __restrict__ off,
+                                                          const float* __restrict__ ncode, uint8_t* __restrict__ qabs,
+                                                          float* __restrict__ nabs) {
+  __shared__ float tbl[256];
+  tbl[threadIdx.x] = ncode[threadIdx.x];
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int64_t nblk = (n + 255) / 256;
+  if (w >= nblk) return;
+  const float o = *off;
+  float cen[8];
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int64_t i = w * 256 + lane + 32 * j;
+    cen[j] = i < n ? __fsub_rn(__uint_as_float(raw[i]), o) : 0.0f;
+    mx = fmaxf(mx, fabsf(cen[j]));
+  }
+#pragma unroll
+  for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, x));
+  const float safe = mx == 0.0f ? 1.0f : mx;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int64_t i = w * 256 + lane + 32 * j;
+    if (i >= n) continue;
+    const float v = fminf(fmaxf(div_full(cen[j], safe), -1.0f), 1.0f);
+    int low = 0, high = 255;
+#pragma unroll
+    for (int st = 0; st < 8; ++st) {
+      const int mid = (low + high) >> 1;
+      const bool right = tbl[mid] < v;
+      low = right ? mid + 1 : low;
+      high = right ? high : mid;
+    }
+    const int li = max(low - 1, 0);
+    qabs[i] = static_cast<uint8_t>(fabsf(__fsub_rn(v, tbl[li])) <= fabsf(__fsub_rn(v, tbl[low])) ? li : low);
+  }
+  if (lane == 0) nabs[w] = mx;
+}
+
 // ============================================================ GGUF epilogue
 __device__ __forceinline__ float roundf_away(float x) {  // gguf.quants.np_roundf
   const float a = fabsf(x);
@@ -1080,10 +1268,16 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
 // NVFP4 keeps two for its register-heavy two-level blocks.
 template <int FMT>
 __host__ __device__ constexpr int epi_wgs() {
-  return (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0 || FMT == PIPER_FMT_NVFP4) ? 2 : 3;
+  return (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0 || FMT == PIPER_FMT_NVFP4 ||
+          FMT == PIPER_FMT_BNB4_NF4 || FMT == PIPER_FMT_BNB4_FP4)
+             ? 2
+             : 3;
 }
 __host__ __device__ constexpr int epi_wgs_rt(int fmt) {
-  return (fmt == PIPER_FMT_GGUF_Q8_0 || fmt == PIPER_FMT_GGUF_Q4_0 || fmt == PIPER_FMT_NVFP4) ? 2 : 3;
+  return (fmt == PIPER_FMT_GGUF_Q8_0 || fmt == PIPER_FMT_GGUF_Q4_0 || fmt == PIPER_FMT_NVFP4 ||
+          fmt == PIPER_FMT_BNB4_NF4 || fmt == PIPER_FMT_BNB4_FP4)
+             ? 2
+             : 3;
 }
 template <int FMT>
 __host__ __device__ constexpr int ws_threads() { return 128 * (1 + epi_wgs<FMT>()); }
@@ -1160,7 +1354,9 @@ __device__ __forceinline__ ItemGeom item_geom(const LaunchParams& P, int item) {
 template <int FMT>
 __device__ __forceinline__ int64_t code_off(int c0) {
   if constexpr (is_gguf<FMT>()) return code_bytes<FMT>(c0);
-  else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4) return c0 / 2;
+  else if constexpr (FMT == PIPER_FMT_MXFP4 || FMT == PIPER_FMT_NVFP4 || FMT == PIPER_FMT_BNB4_NF4 ||
+                     FMT == PIPER_FMT_BNB4_FP4)
+    return c0 / 2;
   else return c0;
 }
 
@@ -1691,6 +1887,27 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
           nvfp4_block<PASS, CDT>(W, c, c0 + 32 * k, acc, g_in, g_out, two_level, red_max, codes);
           if (PASS != kReduce) *reinterpret_cast<uint2*>(chunk_ptr(c, k)) = codes;
         }
+      } else if constexpr (FMT == PIPER_FMT_BNB4_NF4 || FMT == PIPER_FMT_BNB4_FP4) {
+        constexpr float kFp4Levels[8] = {0.0f, 0.0052083334885537624f, 0.1666666716337204f, 0.25f,
+                                         0.3333333432674408f, 0.5f, 0.6666666865348816f, 1.0f};
+        const float lut = __ldg(W.code16 + (lane & 15));
+        float lvl = kFp4Levels[0];
+#pragma unroll
+        for (int q = 1; q < 8; ++q) lvl = (lane & 7) == q ? kFp4Levels[q] : lvl;
+        const PhiloxKey key = philox_key(W.k0, W.k1);
+        for (int k = 0; k < tcols / 32; k += 2) {
+          float acc0[32], acc1[32];
+          tmem_ld32(taddr + 32 * k, acc0);
+          tmem_ld32(taddr + 32 * (k + 1), acc1);
+          uint32_t wv[8];
+          const uint4 lo = *reinterpret_cast<const uint4*>(chunk_ptr(c, k));
+          const uint4 hi = *reinterpret_cast<const uint4*>(chunk_ptr(c, k + 1));
+          wv[0] = lo.x; wv[1] = lo.y; wv[2] = lo.z; wv[3] = lo.w;
+          wv[4] = hi.x; wv[5] = hi.y; wv[6] = hi.z; wv[7] = hi.w;
+          bnb4_block<FMT, CDT>(W, c, c0 + 32 * k, acc0, acc1, lut, lvl, key, wv);
+          *reinterpret_cast<uint4*>(chunk_ptr(c, k)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          *reinterpret_cast<uint4*>(chunk_ptr(c, k + 1)) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+        }
       } else if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
         chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) { gguf_chunk<FMT, CDT>(W, c, k, acc); });
       } else {
@@ -2116,7 +2333,9 @@ constexpr int64_t kL2GroupBytes = 48ll << 20;
 int host_code_bytes(int fmt, int cols) {
   switch (fmt) {
     case PIPER_FMT_MXFP4:
-    case PIPER_FMT_NVFP4: return cols / 2;
+    case PIPER_FMT_NVFP4:
+    case PIPER_FMT_BNB4_NF4:
+    case PIPER_FMT_BNB4_FP4: return cols / 2;
     case PIPER_FMT_GGUF_Q8_0: return cols / 32 * 34;
     case PIPER_FMT_GGUF_Q4_0: return cols / 32 * 18;
     default: return cols;
@@ -2170,7 +2389,9 @@ bool is_fp_dt(int dt) { return dt == PIPER_DT_BF16 || dt == PIPER_DT_F16 || dt =
 int64_t row_bytes_of(const piper_merge_desc& d) {
   switch (d.format) {
     case PIPER_FMT_MXFP4:
-    case PIPER_FMT_NVFP4: return d.cols / 2;
+    case PIPER_FMT_NVFP4:
+    case PIPER_FMT_BNB4_NF4:
+    case PIPER_FMT_BNB4_FP4: return d.cols / 2;
     case PIPER_FMT_GGUF_Q8_0: return d.cols / 32 * 34;
     case PIPER_FMT_GGUF_Q4_0: return d.cols / 32 * 18;
     default: return d.cols;
@@ -2286,6 +2507,21 @@ int validate(const piper_merge_desc& d, Plan& p) {
       }
       break;
     }
+    case PIPER_FMT_BNB4_NF4:
+    case PIPER_FMT_BNB4_FP4:  // _triton_bnb4_lora.py:434-540
+      if (d.cols % 64 != 0) return fail(PIPER_MERGE_EINVAL, "BNB4 merge requires row-aligned 64-value blocks.");
+      if (d.scale == nullptr || d.codebook == nullptr)
+        return fail(PIPER_MERGE_EINVAL, "BNB4 merge requires absmax and a 16-value float32 codebook.");
+      if (d.nested_absmax != nullptr) {
+        if (d.nested_code == nullptr || d.nested_offset == nullptr)
+          return fail(PIPER_MERGE_EINVAL, "Nested BNB4 merge requires its codebook and offset.");
+        if (d.flags & PIPER_FLAG_STOCHASTIC)
+          return fail(PIPER_MERGE_EINVAL,
+                      "BNB4 stochastic merge does not support nested scales because their final effective values "
+                      "are unavailable during terminal-code selection.");
+        p.nq = static_cast<int>(d.rows * (d.cols / 64));  // raw block maxima for the nested pass
+      }
+      break;
     case PIPER_FMT_GGUF_Q8_0:
     case PIPER_FMT_GGUF_Q4_0:
       if (d.cols % 32 != 0) return fail(PIPER_MERGE_EINVAL, "GGUF merge requires columns divisible by 32.");
@@ -2398,6 +2634,12 @@ int launch_fmt(int fmt, int bn, LaunchParams& lp, int items, int kp, cudaStream_
       break;
     case PIPER_FMT_QUANTO_FP8_E5M2:
       if constexpr (PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_FP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_BNB4_NF4:
+      if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_BNB4_NF4, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_BNB4_FP4:
+      if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_BNB4_FP4, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_GGUF_Q8_0:
       if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_GGUF_Q8_0, PASS, CDT>(bn, lp, items, kp, s);
@@ -2556,6 +2798,10 @@ DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws,
   w.scale_cols = d.format == PIPER_FMT_NVFP4 ? static_cast<int>(d.cols / 16) : static_cast<int>(d.cols / 32);
   w.scale_mode = d.scale_mode;
   w.scale_dt = d.scale_dtype;
+  w.code16 = static_cast<const float*>(d.codebook);
+  w.ncode = static_cast<const float*>(d.nested_code);
+  w.nabs = static_cast<const float*>(d.nested_absmax);
+  w.noff = static_cast<const float*>(d.nested_offset);
   if (std::getenv("PIPER_MERGE_NO_TMA") == nullptr) {
     setup_tma(w, d, p.bn);
     setup_tma_factors(w, d, w.KP);
@@ -2610,7 +2856,24 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
   } else {
     rc = launch(pm::kLocal, d0.compute_dtype, kfmt, p0.bn, lp, items, kp_max, stream);
   }
-  return rc;
+  if (rc) return rc;
+  // bitsandbytes nested absmax: re-quantize the new block maxima.
+  for (const Segment& sg : segs) {
+    const piper_merge_desc& d = descs[sg.desc];
+    const Plan& p = plans[sg.desc];
+    if ((d.format != PIPER_FMT_BNB4_NF4 && d.format != PIPER_FMT_BNB4_FP4) || d.nested_absmax == nullptr) continue;
+    const uint32_t* raw = reinterpret_cast<const uint32_t*>(ws + p.ws_off);
+    const int64_t n = d.rows * (d.cols / 64);
+    pm::bnb4_offset_kernel<<<1, 1024, 0, stream>>>(raw, n, static_cast<float*>(d.nested_offset));
+    const int64_t nblk = (n + 255) / 256;
+    pm::bnb4_nested_kernel<<<static_cast<unsigned>((nblk + 7) / 8), 256, 0, stream>>>(
+        raw, n, static_cast<const float*>(d.nested_offset), static_cast<const float*>(d.nested_code),
+        static_cast<uint8_t*>(d.scale), static_cast<float*>(d.nested_absmax));
+    g_launches.fetch_add(2, std::memory_order_relaxed);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("nested BNB4 launch: ") + cudaGetErrorString(e));
+  }
+  return PIPER_MERGE_OK;
 }
 
 bool same_kernel(const piper_merge_desc& a, const Plan& pa, const piper_merge_desc& b, const Plan& pb) {
@@ -2936,6 +3199,33 @@ int piper_merge_quanto(void* qdata, void* scale, const void* b, const void* a, i
   d.strength = strength;
   d.seed = seed;
   d.offset_base = offset_base;
+  return piper_merge_batch(&d, 1, workspace, workspace_bytes, stream);
+}
+
+int piper_merge_bnb4(void* packed, void* absmax, const void* code, void* nested_absmax,
+                     const void* nested_code, void* nested_offset, const void* b, const void* a,
+                     int64_t rows, int64_t cols, int64_t rank, int32_t nf4, int32_t compute_dtype,
+                     float strength, int32_t has_seed, uint64_t seed, uint64_t offset_base,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  piper_merge_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.format = nf4 ? PIPER_FMT_BNB4_NF4 : PIPER_FMT_BNB4_FP4;
+  d.qdata = packed;
+  d.scale = absmax;
+  d.b = b;
+  d.a = a;
+  d.rows = rows;
+  d.cols = cols;
+  d.rank = rank;
+  d.compute_dtype = compute_dtype;
+  d.flags = has_seed ? PIPER_FLAG_STOCHASTIC : 0u;
+  d.strength = strength;
+  d.seed = seed;
+  d.offset_base = offset_base;
+  d.codebook = code;
+  d.nested_absmax = nested_absmax;
+  d.nested_code = nested_code;
+  d.nested_offset = nested_offset;
   return piper_merge_batch(&d, 1, workspace, workspace_bytes, stream);
 }
 

@@ -556,6 +556,108 @@ def merge_quanto_qfloat8_lora(qdata, scale, axis, b, a, strength, *, rounding_se
                          offset_base=offset_base)
 
 
+# ------------------------------------------------------- bitsandbytes 4-bit
+BNB4_BLOCK = 64
+BNB4_NESTED_BLOCK = 256
+
+
+def bnb4_desc(packed, absmax, code, nested_absmax, nested_code, offset, logical_shape, blocksize, quant_type, b, a,
+              strength, *, rounding_seed=None, offset_base=0, keep: list | None = None) -> nat.MergeDesc:
+    """Validate a bitsandbytes 4-bit merge (``_triton_bnb4_lora.py:449-540``) and build its descriptor."""
+    if packed.device.type != "cuda":
+        raise ValueError("BNB4 merge requires CUDA tensors.")
+    if packed.dtype is not torch.uint8:
+        raise ValueError("BNB4 merge expects a raw uint8 packed view.")
+    if quant_type not in ("nf4", "fp4"):
+        raise ValueError("BNB4 merge supports NF4 and FP4.")
+    if code.dtype is not torch.float32 or code.numel() != 16:
+        raise ValueError("BNB4 merge expects a 16-value float32 codebook.")
+    if b.dtype is not a.dtype:
+        raise ValueError("BNB4 merge requires matching factor dtypes.")
+    cdt = _factor_dt(b, a, allowed=(torch.float16, torch.bfloat16, torch.float32))
+    if b.ndim != 2 or a.ndim != 2:
+        raise ValueError("BNB4 merge expects rank-two factors.")
+    rows, cols = logical_shape
+    rank = a.shape[0]
+    numel = rows * cols
+    num_blocks = (numel + blocksize - 1) // blocksize
+    nested = nested_absmax is not None
+    if rows == 0 or cols == 0 or rank == 0:
+        raise ValueError("BNB4 merge requires non-empty tensors.")
+    if numel % 2 != 0 or packed.numel() != numel // 2:
+        raise ValueError("BNB4 merge requires exact two-values-per-byte storage.")
+    if blocksize != BNB4_BLOCK:
+        raise ValueError("BNB4 merge expects the standard 64-value blocks.")
+    if cols % blocksize != 0:
+        raise ValueError("BNB4 merge requires row-aligned 64-value blocks.")
+    if tuple(b.shape) != (rows, rank) or a.shape[1] != cols:
+        raise ValueError("LoRA factors do not match the BNB4 weight shape.")
+    if absmax.numel() != num_blocks:
+        raise ValueError("BNB4 absmax shape does not match the logical weight.")
+    _same_device(packed, absmax, code, b, a)
+    if nested:
+        if nested_code is None or offset is None:
+            raise ValueError("Nested BNB4 merge requires its codebook and offset.")
+        if (absmax.dtype is not torch.uint8 or nested_absmax.dtype is not torch.float32
+                or nested_absmax.numel() != (num_blocks + BNB4_NESTED_BLOCK - 1) // BNB4_NESTED_BLOCK
+                or nested_code.dtype is not torch.float32 or nested_code.numel() != 256
+                or offset.dtype is not torch.float32 or offset.numel() != 1):
+            raise ValueError("Nested BNB4 scale metadata has an unsupported layout.")
+        _same_device(packed, nested_absmax, nested_code, offset)
+        if rounding_seed is not None:
+            raise ValueError("BNB4 stochastic merge does not support nested scales because their final effective "
+                             "values are unavailable during terminal-code selection.")
+    elif absmax.dtype is not torch.float32:
+        raise ValueError("Non-nested BNB4 merge expects float32 absmax values.")
+    for t in (packed, absmax, nested_absmax, offset):
+        if t is not None and not t.is_contiguous():
+            raise ValueError("BNB4 merge requires contiguous storage for an in-place update.")
+    b = b.contiguous()
+    a = a.contiguous()
+    code = code.contiguous()
+    nested_code = nested_code.contiguous() if nested_code is not None else None
+    if keep is not None:
+        keep.extend([b, a, code, nested_code])
+    seed, sflag = _seed_fields(rounding_seed)
+    return _desc(qdata=packed.data_ptr(), scale=absmax.data_ptr(), b=b.data_ptr(), a=a.data_ptr(), rows=rows,
+              cols=cols, rank=rank, format=nat.FMT_BNB4_NF4 if quant_type == "nf4" else nat.FMT_BNB4_FP4,
+              compute_dtype=cdt, flags=sflag, strength=float(strength), seed=seed, offset_base=int(offset_base),
+              codebook=code.data_ptr(), nested_absmax=_ptr(nested_absmax), nested_code=_ptr(nested_code),
+              nested_offset=_ptr(offset))
+
+
+def merge_bnb4_lora(
+    packed: torch.Tensor,
+    absmax: torch.Tensor,
+    code: torch.Tensor,
+    nested_absmax: torch.Tensor | None,
+    nested_code: torch.Tensor | None,
+    offset: torch.Tensor | None,
+    logical_shape: tuple[int, int],
+    blocksize: int,
+    quant_type: str,
+    b: torch.Tensor,
+    a: torch.Tensor,
+    strength: float,
+    *,
+    rounding_seed: int | None = None,
+    offset_base: int = 0,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None, torch.Tensor | None]:
+    """bitsandbytes blockwise 4-bit merge in place (``merge_bnb4_lora``,
+    ``_triton_bnb4_lora.py:434-604``); returns ``(packed, absmax, nested_absmax, offset)``.
+
+    64-value blocks along rows, the first value of a byte in its high nibble.
+    Plain absmax is fp32 per block; nested absmax is uint8 codes of
+    ``nested_code`` scaled by ``nested_absmax`` (fp32 per 256 blocks) plus
+    ``offset``, re-quantized after the merge (round-to-nearest only).
+    """
+    keep: list = []
+    d = bnb4_desc(packed, absmax, code, nested_absmax, nested_code, offset, logical_shape, blocksize, quant_type, b,
+                  a, strength, rounding_seed=rounding_seed, offset_base=offset_base, keep=keep)
+    nat.merge_batch([d], packed.device)
+    return packed, absmax, nested_absmax, offset
+
+
 # -------------------------------------------------------------------- GGUF
 GGUF_Q8_0 = 8
 GGUF_Q4_0 = 2

@@ -116,6 +116,38 @@ class QuantoWeight:
 
 
 @dataclass
+class Bnb4State:
+    """The parts of a bitsandbytes ``QuantState`` the merge reads
+    (``bnb4bit_adapter.py:100-160``); ``state2`` / ``offset`` for nested absmax."""
+
+    absmax: torch.Tensor
+    code: torch.Tensor
+    shape: tuple[int, int]
+    quant_type: str = "nf4"
+    blocksize: int = 64
+    dtype: torch.dtype = torch.bfloat16
+    state2: "Bnb4State | None" = None
+    offset: torch.Tensor | None = None
+
+    @property
+    def nested(self) -> bool:
+        return self.state2 is not None
+
+
+@dataclass
+class Bnb4Weight:
+    """bitsandbytes ``Params4bit``: packed uint8 ``data`` (two values per byte,
+    the first in the high nibble) and its ``quant_state``."""
+
+    data: torch.Tensor
+    quant_state: Bnb4State
+
+    @property
+    def shape(self) -> torch.Size:
+        return torch.Size(self.quant_state.shape)
+
+
+@dataclass
 class NVFP4Weight:
     qdata: torch.Tensor
     scale: torch.Tensor

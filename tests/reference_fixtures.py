@@ -166,6 +166,20 @@ def native(case: dict, device) -> dict:
         sc = dev(arr(case, "scale"))
         K.merge_static_float8_lora(q, sc, b, a, s, **kw)
         return {"q": q.view(torch.uint8).cpu().numpy().reshape(-1), "scale": sc.cpu().numpy().reshape(-1)}
+    if L == "bnb4":
+        nested = case["nested"]
+        q = dev(arr(case, "qdata"))
+        sc = dev(arr(case, "scale"))
+        nabs = dev(arr(case, "nested_absmax")) if nested else None
+        off = dev(arr(case, "offset")).reshape(()) if nested else None
+        K.merge_bnb4_lora(q, sc, dev(arr(case, "code")), nabs, dev(arr(case, "nested_code")) if nested else None, off,
+                          (case["rows"], case["cols"]), 64, case["quant_type"], b, a, s, **kw)
+        out = {"q": q.cpu().numpy().reshape(-1)}
+        out["scale"] = sc.cpu().numpy().reshape(-1).view(np.uint8) if nested else sc.cpu().numpy().reshape(-1)
+        if nested:
+            out["nested_absmax"] = nabs.cpu().numpy().reshape(-1)
+            out["offset"] = off.cpu().numpy().reshape(-1)
+        return out
     if L == "bnb8":
         q = dev(arr(case, "qdata"))
         sc = dev(arr(case, "scale"))

@@ -183,6 +183,18 @@ def test_bnb8_and_quanto_adapter_rules():
     assert K.quanto_scale_axis(-1, torch.ones(1, 32), 4, 32) == "column"
 
 
+def test_bnb4_adapter_rules():
+    code = torch.linspace(-1, 1, 16)
+    qs = WT.Bnb4State(torch.ones(8), code, (4, 128))
+    w4 = WT.Bnb4Weight(torch.zeros(256, 1, dtype=torch.uint8), qs)
+    assert AD.select_adapter(w4) is AD.Bnb4Adapter and AD.Bnb4Adapter.logical_shape(w4) == (4, 128)
+    b, a = torch.zeros(4, 2, dtype=torch.bfloat16), torch.zeros(2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        AD.Bnb4Adapter.validate_lora_merge(w4, b, a, 1.0)
+    with pytest.raises(ValueError, match="CUDA"):
+        K.merge_bnb4_lora(w4.data, qs.absmax, code, None, None, None, (4, 128), 64, "nf4", b, a, 1.0)
+
+
 def test_mx_scaling_mode_resolution():
     mx = WT.MXWeight(torch.zeros(1, 32, dtype=torch.float8_e4m3fn), torch.zeros(1, 1), torch.float8_e4m3fn)
     assert AD.mx_scaling_mode_id(mx) == 0

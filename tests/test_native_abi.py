@@ -109,6 +109,22 @@ def test_convenience_entry_points_validate():
     assert lib.piper_merge_bnb8(1, 1, 1, 1, 32, 64, 0, 1.0, 0, 0, 0, None) == nat.EINVAL
 
 
+def test_bnb4_validation_messages():
+    lib = nat.load()
+    size = ctypes.c_size_t()
+    d = _desc(format=nat.FMT_BNB4_NF4, cols=96, codebook=0x5000)
+    assert lib.piper_merge_workspace_size((nat.MergeDesc * 1)(d), 1, ctypes.byref(size)) == nat.EINVAL
+    assert b"64-value blocks" in lib.piper_merge_last_error()
+    d = _desc(format=nat.FMT_BNB4_FP4, codebook=0x5000, nested_absmax=0x6000, nested_code=0x7000,
+              nested_offset=0x8000, flags=nat.FLAG_STOCHASTIC)
+    assert lib.piper_merge_workspace_size((nat.MergeDesc * 1)(d), 1, ctypes.byref(size)) == nat.EINVAL
+    assert b"nested" in lib.piper_merge_last_error()
+    d = _desc(format=nat.FMT_BNB4_NF4, codebook=0x5000, nested_absmax=0x6000, nested_code=0x7000,
+              nested_offset=0x8000)
+    assert nat.workspace_bytes([d]) == 64 * 256 // 64 * 16  # raw block maxima for the nested pass
+    assert nat.workspace_bytes([_desc(format=nat.FMT_BNB4_NF4, codebook=0x5000)]) == 0
+
+
 def test_new_format_validation_messages():
     # bitsandbytes: fp16 factors only; Quanto: per-row or per-tensor only.
     d = _desc(format=nat.FMT_BNB8, compute_dtype=nat.DT_BF16, block_rows=1, block_cols=256)

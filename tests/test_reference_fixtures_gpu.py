@@ -39,8 +39,6 @@ def _unsupported(case) -> bool:
 
 @pytest.mark.parametrize("case", CASES, ids=[c["id"] + "-" + rf.case_label(c) for c in CASES])
 def test_native_matches_reference_kernels(case, cuda_device):
-    if case["launcher"] == "bnb4":
-        pytest.skip("bitsandbytes 4-bit has no sm_100a path yet")
     if _unsupported(case):
         with pytest.raises(ValueError, match="last-axis"):
             rf.native(case, cuda_device)
