@@ -87,8 +87,8 @@ extern "C" {
  *         ((cols+127)/128*16); NVFP4: E4M3 bytes, rows x cols/16 or swizzled
  *         ((rows+127)/128*32) x ((cols+63)/64*16); FP8: fp32, one per
  *         quantization block; INT8: `scale_dtype`, one per block; BNB8: fp32
- *         SCB, one per row; Quanto: `compute_dtype`, one per row or one per
- *         tensor; BNB4: fp32 absmax per 64-value block, or uint8 codes of the
+ *         SCB, one per row; Quanto: `compute_dtype`, one per tensor, row
+ *         (block (1, cols)) or column (block (rows, 1)); BNB4: fp32 absmax per 64-value block, or uint8 codes of the
  *         nested quantization; GGUF: unused.
  * zero_point  INT8 only: int8 per block, or NULL (symmetric storage).
  * global_scale NVFP4 only: fp32 per-tensor scale (two-level), or NULL.
@@ -210,8 +210,10 @@ int piper_merge_bnb8(void* cb, void* scb, const void* b, const void* a, int64_t 
 /* _triton_quanto_lora.py:317 / :345 merge_quanto_qint8_lora /
  * merge_quanto_qfloat8_lora(qdata, scale, axis, b, a, strength, *,
  * rounding_seed). storage: 0 = qint8, 1 = qfloat8 e4m3, 2 = qfloat8 e5m2;
- * per_row: 1 for axis 0 (one scale per row), 0 for a scalar scale (workspace
- * >= 256 B). Scales and factors share `compute_dtype`. */
+ * per_row: 1 for axis 0 (one scale per row), 0 for a scalar scale. Per-column
+ * (last-axis) scales go through piper_merge_batch with block (rows, 1). The
+ * scalar and per-column layouts need workspace (piper_merge_workspace_size).
+ * Scales and factors share `compute_dtype`. */
 int piper_merge_quanto(void* qdata, void* scale, const void* b, const void* a, int64_t rows,
                        int64_t cols, int64_t rank, int32_t storage, int32_t per_row,
                        int32_t compute_dtype, float strength, int32_t has_seed, uint64_t seed,

@@ -488,9 +488,6 @@ class QuantoAdapter:
         rank, cdt = _factors(b, a, rows, cols, label)
         if scale.dtype is not b.dtype:
             raise ValueError(f"{label} merge requires matching scale and factor dtypes.")
-        if kind == "column":
-            raise ValueError("Quanto qbytes merge on sm_100a supports a scalar scale or one scale per row "
-                             "(axis 0); last-axis scales are not supported.")
         if data.dtype is torch.int8:
             fmt = nat.FMT_QUANTO_INT8
         elif data.dtype is torch.float8_e4m3fn:
@@ -519,9 +516,10 @@ class QuantoAdapter:
         if keep is not None:
             keep.extend([b, a])
         seed, sflag = _seed(rounding_seed)
+        brows, bcols = K.QUANTO_BLOCK[kind](rows, cols)
         return K._desc(qdata=target._data.data_ptr(), scale=target._scale.data_ptr(), b=b.data_ptr(),
-                       a=a.data_ptr(), rows=rows, cols=cols, rank=rank, block_rows=rows if kind == "tensor" else 1,
-                       block_cols=cols, format=fmt, compute_dtype=cdt, scale_dtype=cdt, flags=sflag,
+                       a=a.data_ptr(), rows=rows, cols=cols, rank=rank, block_rows=brows,
+                       block_cols=bcols, format=fmt, compute_dtype=cdt, scale_dtype=cdt, flags=sflag,
                        strength=float(strength), seed=seed, offset_base=int(offset_base))
 
     @classmethod

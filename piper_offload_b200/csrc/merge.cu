@@ -92,6 +92,7 @@ struct alignas(64) DevWeight {
   const float* ncode;  // BNB4 nested: 256-entry code table of the block maxima (else null)
   const float* nabs;   // BNB4 nested: fp32 maximum per 256 blocks
   const float* noff;   // BNB4 nested: fp32 offset
+  int col_axis;        // Quanto last-axis scales: one per column (two-pass, workspace per column)
   int use_tma;         // code tiles move by bulk tensor copies (swizzled rows)
   int use_tma_a;       // A tiles by bulk tensor copies (else cp.async into the same layout)
   int use_tma_b;       // B strips by bulk tensor copies (else cp.async into the same layout)
@@ -1107,6 +1108,85 @@ __global__ void __launch_bounds__(256) bnb4_nested_kernel(const uint32_t* __rest
   if (lane == 0) nabs[w] = mx;
 }
 
+// ====================================================== Quanto last-axis scales
+// One scale per column (_triton_quanto_lora.py:202-217 with dim=0). REDUCE: each
+// column's max |merged| over a warp's 32 rows by one warp reduction, then one
+// atomic per column; row 0 saves the input scales. ENCODE: the column scales
+// dtype(amax * fp32(1 / qmax)) and the codes of _quantize_qbytes_kernel
+// (:107-168). The whole warp runs this together (warp reductions).
+template <int FMT, int PASS, int CDT>
+__device__ __forceinline__ void quanto_column_chunk(const DevWeight& W, const RowCtx& c, int k, int col, int nvalid,
+                                                    const float (&acc)[32], int lane, const PhiloxKey& key) {
+  constexpr bool kInt8 = base_fmt(FMT) == PIPER_FMT_INT8;
+  constexpr bool kE4 = base_fmt(FMT) == PIPER_FMT_FP8_E4M3;
+  constexpr float kQmax = kInt8 ? 127.0f : (kE4 ? 448.0f : 57344.0f);
+  uint32_t wv[8];
+  load_chunks32(c, k, wv);
+  float s_in[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int cc = min(col + i, W.N - 1);
+    s_in[i] = PASS == kReduce ? load_scale<FMT>(W, cc) : W.old_scale[cc];
+  }
+  float m[32];
+  if constexpr (kInt8) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) m[i] = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
+  } else {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      float f[4];
+      dec_fp8x4<kE4>(wv[w], f);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) m[4 * w + j] = f[j];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) m[i] = s_in[i] == 0.0f ? 0.0f : __fmul_rn(m[i], s_in[i]);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) m[i] = fmaf(acc[i], W.strength, m[i]);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+  if constexpr (PASS == kReduce) {
+    uint32_t mine = 0u;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const uint32_t v = (c.valid && i < nvalid) ? __float_as_uint(fabsf(m[i])) : 0u;
+      const uint32_t r = __reduce_max_sync(0xFFFFFFFFu, v);  // non-negative floats order like their bits
+      mine = lane == i ? r : mine;
+    }
+    if (lane < nvalid && mine != 0u) atomicMax(&W.qmax[col + lane], mine);
+    if (c.valid && c.row == 0) {
+      for (int i = 0; i < nvalid; ++i) W.old_scale[col + i] = s_in[i];
+    }
+  } else {
+    uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    if (c.valid) {
+      const uint64_t off0 = W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
+      const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+      for (int i = 0; i < nvalid; ++i) {
+        const float s = flavor_scale<CDT>(kQuanto, __uint_as_float(W.qmax[col + i]), kQmax);
+        if (c.row == 0) store_scale<FMT>(W, col + i, s);
+        const float ss = div_full(m[i], s);
+        uint32_t code;
+        if constexpr (kInt8) {
+          float qf = rintf(round_dt<CDT>(ss));
+          if (sr) qf = sr_int(ss, qf, -128.0f, 127.0f, key, off0 + i);
+          qf = fminf(fmaxf(qf, -128.0f), 127.0f);
+          code = static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu;
+        } else {
+          code = sr ? sr_fp8<kE4>(fminf(fmaxf(ss, -kQmax), kQmax), kQmax, key, off0 + i)
+                    : enc_fp8<kE4>(fminf(fmaxf(round_dt<CDT>(ss), -kQmax), kQmax));
+        }
+        out[i >> 2] |= code << ((i & 3) * 8);
+      }
+    }
+    store_chunks32(c, k, out);
+  }
+}
+
 // ============================================================ GGUF epilogue
 __device__ __forceinline__ float roundf_away(float x) {  // gguf.quants.np_roundf
   const float a = fabsf(x);
@@ -2042,6 +2122,12 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
             float merged[32];
             const int col = c0 + 32 * k;
             const int nvalid = min(32, tcols - 32 * k);
+            if constexpr (kFlv == kQuanto) {
+              if (W.col_axis) {
+                quanto_column_chunk<FMT, PASS, CDT>(W, c, k, col, nvalid, acc, lane, key);
+                return;
+              }
+            }
             if (W.nq_row == 0 || (W.group >= 32 && (col % W.group) + 32 <= W.group)) {
               float s_in = 1.0f;
               int z_in = 0;
@@ -2381,6 +2467,7 @@ struct Plan {
   int nq_row = 0;      // blocks per row (0 = per tensor)
   int group = 0;
   int flavor = 0;      // pm::Flavor of an FP8 / INT8 weight
+  bool col_axis = false;  // Quanto last-axis scales
   size_t ws_off = 0;
 };
 
@@ -2401,10 +2488,12 @@ int64_t row_bytes_of(const piper_merge_desc& d) {
 // bitsandbytes LLM.int8 and Quanto qbytes weights run on the INT8 / FP8
 // kernels with their own arithmetic (pm::Flavor); TorchAO FP8 scales are fp32.
 // Rewrites `d` to the kernel's format and stored scale dtype.
-int normalize(piper_merge_desc& d, int& flavor) {
+int normalize(piper_merge_desc& d, int& flavor, bool& col_axis) {
   flavor = pm::kTorchao;
+  col_axis = false;
   const bool per_row = d.block_rows == 1 && d.block_cols == d.cols;
   const bool per_tensor = d.block_rows == d.rows && d.block_cols == d.cols;
+  const bool per_col = d.block_rows == d.rows && d.block_cols == 1;
   switch (d.format) {
     case PIPER_FMT_FP8_E4M3:
     case PIPER_FMT_FP8_E5M2:
@@ -2423,9 +2512,14 @@ int normalize(piper_merge_desc& d, int& flavor) {
     case PIPER_FMT_QUANTO_INT8:  // _triton_quanto_lora.py:184-200, 220-343
     case PIPER_FMT_QUANTO_FP8_E4M3:
     case PIPER_FMT_QUANTO_FP8_E5M2:
-      if (!per_row && !per_tensor)
-        return fail(PIPER_MERGE_EINVAL, "Quanto qbytes merge on sm_100a supports a scalar scale or one scale per "
-                                        "row (axis 0); last-axis scales are not supported.");
+      if (!per_row && !per_tensor && !per_col)
+        return fail(PIPER_MERGE_EINVAL, "Quanto qbytes merge expects a scalar scale, one scale per row for axis 0, "
+                                        "or one scale per column for the last axis.");
+      if (per_col) {  // two passes over the whole weight, one workspace slot per column
+        col_axis = true;
+        d.block_rows = d.rows;
+        d.block_cols = d.cols;
+      }
       if (d.zero_point != nullptr || (d.flags & (PIPER_FLAG_ASYMMETRIC | PIPER_FLAG_REDUCE_RANGE)))
         return fail(PIPER_MERGE_EINVAL, "Quanto qbytes storage is symmetric.");
       d.format = d.format == PIPER_FMT_QUANTO_INT8 ? PIPER_FMT_INT8
@@ -2802,6 +2896,7 @@ DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws,
   w.ncode = static_cast<const float*>(d.nested_code);
   w.nabs = static_cast<const float*>(d.nested_absmax);
   w.noff = static_cast<const float*>(d.nested_offset);
+  w.col_axis = p.col_axis ? 1 : 0;
   if (std::getenv("PIPER_MERGE_NO_TMA") == nullptr) {
     setup_tma(w, d, p.bn);
     setup_tma_factors(w, d, w.KP);
@@ -2878,7 +2973,7 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
 
 bool same_kernel(const piper_merge_desc& a, const Plan& pa, const piper_merge_desc& b, const Plan& pb) {
   return a.format == b.format && a.compute_dtype == b.compute_dtype && pa.bn == pb.bn &&
-         pa.two_pass == pb.two_pass && pa.fused == pb.fused && pa.flavor == pb.flavor;
+         pa.two_pass == pb.two_pass && pa.fused == pb.fused && pa.flavor == pb.flavor;  // col_axis is per weight
 }
 
 int plan_all(const piper_merge_desc* in, int count, std::vector<piper_merge_desc>& descs,
@@ -2890,11 +2985,16 @@ int plan_all(const piper_merge_desc* in, int count, std::vector<piper_merge_desc
   ws_total = 0;
   for (int i = 0; i < count; ++i) {
     int flavor = pm::kTorchao;
-    int rc = normalize(descs[i], flavor);
+    bool col_axis = false;
+    int rc = normalize(descs[i], flavor, col_axis);
     if (rc) return rc;
     rc = validate(descs[i], plans[i]);
     if (rc) return rc;
     plans[i].flavor = flavor;
+    if (col_axis) {
+      plans[i].col_axis = true;
+      plans[i].nq = static_cast<int>(descs[i].cols);
+    }
     plans[i].ws_off = ws_total;
     ws_total += scratch_bytes(plans[i].nq);
   }

@@ -505,6 +505,10 @@ def quanto_scale_axis(axis: int | None, scale: torch.Tensor, rows: int, cols: in
                      "or one scale per column for the last axis.")
 
 
+# Quantization block (rows, cols) of each Quanto scale layout in the C ABI.
+QUANTO_BLOCK = {"tensor": lambda r, c: (r, c), "row": lambda r, c: (1, c), "column": lambda r, c: (r, 1)}
+
+
 def _merge_quanto(qdata, scale, axis, b, a, strength, *, fmt: int, rounding_seed, offset_base):
     if qdata.device.type != "cuda":
         raise ValueError("Quanto qbytes merge requires CUDA tensors.")
@@ -521,17 +525,14 @@ def _merge_quanto(qdata, scale, axis, b, a, strength, *, fmt: int, rounding_seed
     if tuple(b.shape) != (rows, rank) or a.shape[1] != cols:
         raise ValueError("LoRA factors do not match the Quanto weight shape.")
     kind = quanto_scale_axis(axis, scale, rows, cols)
-    if kind == "column":
-        raise ValueError("Quanto qbytes merge on sm_100a supports a scalar scale or one scale per row "
-                         "(axis 0); last-axis scales are not supported.")
     if not qdata.is_contiguous() or not scale.is_contiguous():
         raise ValueError("Quanto qbytes merge requires contiguous storage for an in-place update.")
     b = b.contiguous()
     a = a.contiguous()
-    brows = rows if kind == "tensor" else 1
+    brows, bcols = QUANTO_BLOCK[kind](rows, cols)
     seed, sflag = _seed_fields(rounding_seed)
     d = _desc(qdata=qdata.data_ptr(), scale=scale.data_ptr(), b=b.data_ptr(), a=a.data_ptr(), rows=rows,
-              cols=cols, rank=rank, block_rows=brows, block_cols=cols, format=fmt, compute_dtype=cdt,
+              cols=cols, rank=rank, block_rows=brows, block_cols=bcols, format=fmt, compute_dtype=cdt,
               scale_dtype=cdt, flags=sflag, strength=float(strength), seed=seed, offset_base=int(offset_base))
     nat.merge_batch([d], qdata.device)
     return qdata, scale

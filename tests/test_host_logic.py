@@ -170,8 +170,9 @@ def test_bnb8_and_quanto_adapter_rules():
     with pytest.raises(ValueError, match="CUDA"):
         AD.QuantoAdapter.validate_lora_merge(qrow, *bf16, 1.0)
     qcol = WT.QuantoWeight(cb, torch.ones(1, 32, dtype=torch.bfloat16), -1, WT.QINT8)
-    with pytest.raises(ValueError, match="last-axis"):
+    with pytest.raises(ValueError, match="CUDA"):
         AD.QuantoAdapter.validate_lora_merge(qcol, *bf16, 1.0)
+    assert K.QUANTO_BLOCK["column"](4, 32) == (4, 1) and K.QUANTO_BLOCK["row"](4, 32) == (1, 32)
     with pytest.raises(ValueError, match="matching scale and factor dtypes"):
         AD.QuantoAdapter.validate_lora_merge(qrow, *f16, 1.0)
     with pytest.raises(ValueError, match="qtype metadata"):

@@ -132,7 +132,9 @@ def test_new_format_validation_messages():
     assert b"float16" in nat.load().piper_merge_last_error()
     d = _desc(format=nat.FMT_QUANTO_INT8, block_rows=1, block_cols=64)
     assert nat.load().piper_merge_workspace_size((nat.MergeDesc * 1)(d), 1, ctypes.byref(ctypes.c_size_t())) == nat.EINVAL
-    assert b"last-axis" in nat.load().piper_merge_last_error()
+    assert b"last axis" in nat.load().piper_merge_last_error()
+    # last-axis scales: one workspace slot (16 B) per column
+    assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_INT8, block_rows=64, block_cols=1)]) == 256 * 16
     # per-tensor Quanto and static FP8 take the two-pass workspace; per-row needs none
     assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_FP8_E4M3, block_rows=64, block_cols=256)]) == 256
     assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_INT8, block_rows=1, block_cols=256)]) == 0

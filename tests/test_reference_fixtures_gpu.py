@@ -32,17 +32,8 @@ def _gpu_division(cuda_device):
     gpu_division.uninstall()
 
 
-def _unsupported(case) -> bool:
-    # Quanto's last-axis (per-column) scales have no sm_100a path: the launcher raises.
-    return case["launcher"] == "quanto" and case["axis"] == -1
-
-
 @pytest.mark.parametrize("case", CASES, ids=[c["id"] + "-" + rf.case_label(c) for c in CASES])
 def test_native_matches_reference_kernels(case, cuda_device):
-    if _unsupported(case):
-        with pytest.raises(ValueError, match="last-axis"):
-            rf.native(case, cuda_device)
-        return
     got = rf.native(case, cuda_device)
     oracle = rf.oracle(case)
     bad = {k: v[:8].tolist() for k, v in rf.mismatches(got, oracle).items() if v.size}
