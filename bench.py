@@ -11,7 +11,13 @@ than the 126 MB L2, so no flush is needed between steps.
 Metric: weight GB/s = (codes + scales read + codes + scales written) / time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
-                    [--config fp8|int8|nvfp4|mxfp8|mxfp4|q8_0|q4_0] [--rtn]
+                    [--config fp8|int8|nvfp4|mxfp8|mxfp4|q8_0|q4_0|static_fp8|bnb8|
+                              quanto_int8|quanto_fp8|nf4|nf4_nested] [--rtn] [--staging]
+
+The last six configs run the reference's other Triton merges (static FP8,
+bitsandbytes 8- and 4-bit, Quanto) on the same Llama-3-8B-shaped stack; they
+are not BASELINE configs. ``nf4*`` report no ``e2e`` (the 4-bit quant state is
+not streamed).
 
 Under ``torch.distributed.run`` each rank merges its own copy of the model
 (weak scaling, no data-path collective); the step time is the max over ranks.
@@ -52,11 +58,21 @@ CONFIGS = {
     "mxfp4": (DIT_12B, 57, 128, 0.005, 0.02, False, "MXFP4 FLOOR, DiT-12B 57 blocks, r128, RTN"),
     "q8_0": (LLAMA_70B, 80, 16, 0.01, 0.015, False, "GGUF Q8_0, 70B-shaped x80, r16, RTN"),
     "q4_0": (LLAMA_70B, 80, 16, 0.01, 0.015, False, "GGUF Q4_0, 70B-shaped x80, r16, RTN"),
+    # Formats beyond BASELINE's configs (the reference's other Triton merges), on the config-2 stack.
+    "static_fp8": (LLAMA3_8B, 32, 32, 0.01, 0.02, True, "static per-tensor FP8 e4m3, Llama-3-8B x32, r32, SR"),
+    "bnb8": (LLAMA3_8B, 32, 16, 0.01, 0.02, False, "bitsandbytes LLM.int8, Llama-3-8B x32, r16, fp16, RTN"),
+    "quanto_int8": (LLAMA3_8B, 32, 32, 0.01, 0.02, False, "Quanto qint8 per-row, Llama-3-8B x32, r32, RTN"),
+    "quanto_fp8": (LLAMA3_8B, 32, 32, 0.01, 0.02, False, "Quanto qfloat8 e4m3 per-row, Llama-3-8B x32, r32, RTN"),
+    "nf4": (LLAMA3_8B, 32, 64, 0.005, 0.02, False, "bitsandbytes NF4, plain absmax, Llama-3-8B x32, r64, RTN"),
+    "nf4_nested": (LLAMA3_8B, 32, 64, 0.005, 0.02, False,
+                   "bitsandbytes NF4, nested absmax, Llama-3-8B x32, r64, RTN"),
 }
 # Algorithmic bytes per element (read + write) and per-row scale bytes.
 BYTES_PER_ELEM = {"fp8": 2.0, "int8": 2.0, "nvfp4": 1.125, "mxfp8": 2.0625, "mxfp4": 1.0625,
-                  "q8_0": 2.125, "q4_0": 1.125}
-ROW_SCALE_BYTES = {"fp8": 8, "int8": 4}  # fp32 / bf16 row scale read + written
+                  "q8_0": 2.125, "q4_0": 1.125, "static_fp8": 2.0, "bnb8": 2.0, "quanto_int8": 2.0,
+                  "quanto_fp8": 2.0, "nf4": 1.125, "nf4_nested": 1.03125}
+# fp32 / bf16 row scale read + written
+ROW_SCALE_BYTES = {"fp8": 8, "int8": 4, "bnb8": 8, "quanto_int8": 4, "quanto_fp8": 4}
 
 FALLBACK_HBM_GBS = 6650.0
 
@@ -171,11 +187,25 @@ def build_weights(cfg: str, device, seed_base: int, n_layers: int | None = None)
             q = S.quantize_mx(w, elem)
             edt = torch.float8_e4m3fn if cfg == "mxfp8" else torch.float4_e2m1fn_x2
             t = WT.MXWeight(q.qdata, q.scale.view(torch.float8_e8m0fnu), edt)
+        elif cfg == "static_fp8":
+            q = S.quantize_fp8(w, per_tensor=True)
+            t = WT.StaticFloat8Weight(q.qdata, q.scale.reshape(()), torch.ones((), device=device))
+        elif cfg == "bnb8":
+            t = WT.Bnb8Weight(*S.quantize_bnb8(w))
+        elif cfg in ("quanto_int8", "quanto_fp8"):
+            storage = "int8" if cfg == "quanto_int8" else "e4m3"
+            data, qscale = S.quantize_quanto(w, storage, axis=0)
+            t = WT.QuantoWeight(data, qscale, 0, WT.QINT8 if storage == "int8" else WT.QFLOAT8_E4M3)
+        elif cfg in ("nf4", "nf4_nested"):
+            packed, absmax, code, nabs, ncode, off = S.quantize_bnb4(w, nested=cfg == "nf4_nested")
+            st2 = None if nabs is None else WT.Bnb4State(nabs, ncode, (1, 1), blocksize=256, dtype=torch.float32)
+            t = WT.Bnb4Weight(packed, WT.Bnb4State(absmax, code, (rows, cols), "nf4", 64, torch.bfloat16, st2, off))
         else:
             q = S.quantize_gguf(w, 8 if cfg == "q8_0" else 2)
             t = WT.GGUFWeight(q.qdata, 8 if cfg == "q8_0" else 2)
         del w
-        b, a = S.lora_factors(rows, cols, rank, lora_std, seed=s + 1, device=device)
+        fdt = torch.float16 if cfg == "bnb8" else torch.bfloat16
+        b, a = S.lora_factors(rows, cols, rank, lora_std, seed=s + 1, device=device, dtype=fdt)
         items.append((key, rows, cols, t, b, a))
     torch.cuda.synchronize(device)
     return items
@@ -197,12 +227,23 @@ def _oracle_chunk(args):
 
     from oracle import merge as om
 
-    cfg, q, scale, b, a, seed, offset_base = args
+    cfg, q, scale, b, a, seed, offset_base, extra = args
     t0 = time.perf_counter()
     if cfg == "fp8":
         om.merge_float8(q, scale, (1, a.shape[1]), b, a, 1.0, seed=seed, offset_base=offset_base)
+    elif cfg == "static_fp8":
+        om.merge_static_float8(q, scale, b, a, 1.0, seed=seed, offset_base=offset_base)
     elif cfg == "int8":
         om.merge_int8(q, scale, None, (1, a.shape[1]), b, a, 1.0, seed=seed, offset_base=offset_base)
+    elif cfg == "bnb8":
+        om.merge_bnb8(q, scale.reshape(-1), b, a, 1.0, seed=seed, offset_base=offset_base)
+    elif cfg in ("quanto_int8", "quanto_fp8"):
+        om.merge_quanto(q, scale, "row", b, a, 1.0, storage="int8" if cfg == "quanto_int8" else "e4m3", seed=seed,
+                        offset_base=offset_base)
+    elif cfg in ("nf4", "nf4_nested"):
+        code, nabs, ncode, off = extra
+        om.merge_bnb4(q, scale, code, b, a, 1.0, nested_absmax=nabs, nested_code=ncode, offset=off, seed=seed,
+                      offset_base=offset_base)
     else:
         raise ValueError(cfg)
     return time.perf_counter() - t0, int(np.asarray(q).size)
@@ -217,21 +258,39 @@ def cpu_baseline(cfg: str, steps: int, warmup: int, rows_per_step: int = 1024, c
 
     from piper_offload_b200 import synthetic as S
 
-    if cfg not in ("fp8", "int8"):
-        cfg_eff = "fp8"
-    else:
-        cfg_eff = cfg
+    ported = ("fp8", "int8", "static_fp8", "bnb8", "quanto_int8", "quanto_fp8", "nf4", "nf4_nested")
+    cfg_eff = cfg if cfg in ported else "fp8"
     _, _, rank, lora_std, base_std, stochastic, _ = CONFIGS[cfg]
     cores = max(1, min(os.cpu_count() or 1, 32))
     chunk = max(16, rows_per_step // cores)
     w = S.normal((rows_per_step, cols), base_std, seed=11, device="cpu")
-    q = S.quantize_fp8(w) if cfg_eff == "fp8" else S.quantize_int8_per_row(w)
     b, a = S.lora_factors(rows_per_step, cols, rank, lora_std, seed=12, device="cpu")
-    qn = q.qdata.view(torch.uint8).numpy() if cfg_eff == "fp8" else q.qdata.numpy()
-    sn = q.scale.float().numpy()
+    extra = None
+    if cfg_eff in ("fp8", "static_fp8"):
+        q = S.quantize_fp8(w, per_tensor=cfg_eff == "static_fp8")
+        qn, sn = q.qdata.view(torch.uint8).numpy(), q.scale.float().numpy()
+    elif cfg_eff == "int8":
+        q = S.quantize_int8_per_row(w)
+        qn, sn = q.qdata.numpy(), q.scale.float().numpy()
+    elif cfg_eff == "bnb8":
+        cb, scb = S.quantize_bnb8(w)
+        qn, sn = cb.numpy(), scb.numpy().reshape(-1, 1)
+    elif cfg_eff in ("quanto_int8", "quanto_fp8"):
+        data, qs = S.quantize_quanto(w, "int8" if cfg_eff == "quanto_int8" else "e4m3", axis=0)
+        qn = data.numpy() if cfg_eff == "quanto_int8" else data.view(torch.uint8).numpy()
+        sn = qs.float().numpy()
+    else:
+        packed, absmax, code, nabs, ncode, off = S.quantize_bnb4(w, nested=cfg_eff == "nf4_nested")
+        qn = packed.numpy().reshape(rows_per_step, cols // 2)
+        sn = absmax.numpy().reshape(rows_per_step, cols // 64)
+        extra = (code.numpy(), None if nabs is None else nabs.numpy(), None if ncode is None else ncode.numpy(),
+                 None if off is None else float(off))
     bn, an = b.float().numpy(), a.float().numpy()
     seed = 0x9C3EA68DBAC91AAD if stochastic else None
-    tasks = [(cfg_eff, qn[r:r + chunk], sn[r:r + chunk], bn[r:r + chunk], an, seed, r * cols)
+    if cfg_eff == "static_fp8":
+        sn = np.repeat(sn.reshape(1, 1), rows_per_step, axis=0)  # one scale per chunk
+    tasks = [(cfg_eff, qn[r:r + chunk], sn[r:r + chunk].reshape(-1) if cfg_eff.startswith("nf4") else
+              (sn[r] if cfg_eff == "static_fp8" else sn[r:r + chunk]), bn[r:r + chunk], an, seed, r * cols, extra)
              for r in range(0, rows_per_step, chunk)]
     ctx = mp.get_context("spawn")
     times = []
@@ -245,7 +304,7 @@ def cpu_baseline(cfg: str, steps: int, warmup: int, rows_per_step: int = 1024, c
     nbytes = algorithmic_bytes(cfg_eff, rows_per_step, cols)
     t = statistics.median(times)
     return {"value": nbytes / t / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"{rows_per_step}x{cols} {cfg_eff} per-row{' SR' if stochastic else ' RTN'} rows of one weight, "
+            "sample": f"{rows_per_step}x{cols} {cfg_eff}{' SR' if stochastic else ' RTN'} rows of one weight, "
                       f"{len(tasks)} row chunks over {cores} spawned processes (numpy restatement, not reference code)",
             "ms_per_sample": t * 1e3}
 
@@ -482,7 +541,7 @@ def main() -> int:
     # host memory; streaming.merge_streamed moves each layer through a ring of
     # three device slots, overlapping upload, merge and download on three streams.
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and not cfg.startswith("nf4"):  # bitsandbytes 4-bit state is not streamed
         import copy
 
         from piper_offload_b200.streaming import StreamedOp, merge_streamed, storages

@@ -186,3 +186,79 @@ def quantize_gguf(w: torch.Tensor, quant_type: int) -> QuantizedWeight:
     dh = d.to(torch.float16).view(torch.uint8).view(-1, 2)
     raw = torch.cat([dh, packed], dim=1)
     return QuantizedWeight(raw.reshape(rows, cols // 32 * 18).contiguous(), None, None, None, rows, cols)
+
+
+# ------------------------------------------------ bitsandbytes and Quanto layouts
+def quantize_bnb8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """bitsandbytes LLM.int8 row-wise storage: ``CB = round(w * 127 / SCB)``, ``SCB = row max |w|`` (fp32)."""
+    wf = w.float()
+    scb = wf.abs().amax(dim=1).clamp_min(1e-12)
+    cb = torch.round(wf * 127.0 / scb[:, None]).clamp(-127, 127).to(torch.int8)
+    return cb.contiguous(), scb.contiguous()
+
+
+def quantize_quanto(w: torch.Tensor, storage: str, axis: int | None = 0,
+                    dtype: torch.dtype = torch.bfloat16) -> tuple[torch.Tensor, torch.Tensor]:
+    """Quanto qbytes: absmax scale (``dtype``) per row (axis 0), per column (axis -1) or per tensor."""
+    wf = w.float()
+    qmax = 127.0 if storage == "int8" else torch.finfo(torch.float8_e4m3fn if storage == "e4m3"
+                                                       else torch.float8_e5m2).max
+    if axis == 0:
+        amax = wf.abs().amax(dim=1, keepdim=True)
+    elif axis == -1:
+        amax = wf.abs().amax(dim=0, keepdim=True)
+    else:
+        amax = wf.abs().amax()
+    scale = (amax.clamp_min(1e-12) / qmax).to(dtype)
+    x = wf / scale.float()
+    if storage == "int8":
+        data = torch.round(x).clamp(-128, 127).to(torch.int8)
+    else:
+        data = x.clamp(-qmax, qmax).to(torch.float8_e4m3fn if storage == "e4m3" else torch.float8_e5m2)
+    return data.contiguous(), scale.contiguous()
+
+
+def nf4_style_table(device) -> torch.Tensor:
+    """A 16-entry NF4-style table: normal quantiles scaled to [-1, 1] with an exact zero
+    (the construction of the QLoRA paper; synthetic, for benchmarking)."""
+    pos = torch.erfinv(torch.linspace(0.0, 0.9677, 9)[1:] * 1.0).double()  # 8 positive quantiles
+    neg = -torch.erfinv(torch.linspace(0.0, 0.9677, 8)[1:] * 1.0).double()  # 7 negative quantiles
+    vals = torch.cat([neg / neg.abs().max(), torch.zeros(1, dtype=torch.float64), pos / pos.max()])
+    return vals.sort().values.float().to(device).contiguous()
+
+
+def _nearest_index(x: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    return (x[..., None] - table).abs().argmin(dim=-1)
+
+
+def quantize_bnb4(w: torch.Tensor, *, nested: bool = False):
+    """bitsandbytes 4-bit blockwise storage (64-value blocks along rows, first value of a
+    byte in its high nibble) with an NF4-style table; nested absmax quantized with a
+    256-entry table. Returns ``(packed (numel/2, 1) uint8, absmax, code, nested_absmax,
+    nested_code, offset)``."""
+    rows, cols = w.shape
+    dev = w.device
+    code = nf4_style_table(dev)
+    blocks = w.float().reshape(rows, cols // 64, 64)
+    absmax = blocks.abs().amax(dim=2).clamp_min(1e-12)
+    idx = torch.empty(rows, cols // 64, 64, dtype=torch.int64, device=dev)
+    for r0 in range(0, rows, 1024):  # bounded temporary
+        idx[r0:r0 + 1024] = _nearest_index(blocks[r0:r0 + 1024] / absmax[r0:r0 + 1024, :, None], code)
+    idx = idx.reshape(rows, cols)
+    packed = ((idx[:, 0::2] << 4) | idx[:, 1::2]).to(torch.uint8).reshape(-1, 1).contiguous()
+    if not nested:
+        return packed, absmax.reshape(-1).contiguous(), code, None, None, None
+    flat = absmax.reshape(-1)
+    offset = flat.mean().reshape(())
+    centered = flat - offset
+    nblk = (flat.numel() + 255) // 256
+    pad = torch.zeros(nblk * 256, device=dev)
+    pad[:flat.numel()] = centered.abs()
+    nested_absmax = pad.reshape(nblk, 256).amax(dim=1).clamp_min(1e-12)
+    nested_code = torch.linspace(-1.0, 1.0, 256, device=dev)
+    scaled = centered / nested_absmax.repeat_interleave(256)[:flat.numel()]
+    q = torch.empty(flat.numel(), dtype=torch.uint8, device=dev)
+    for i0 in range(0, flat.numel(), 1 << 16):
+        q[i0:i0 + (1 << 16)] = _nearest_index(scaled[i0:i0 + (1 << 16)], nested_code).to(torch.uint8)
+    return packed, q.contiguous(), code, nested_absmax.contiguous(), nested_code.contiguous(), \
+        offset.float().contiguous()
