@@ -280,18 +280,25 @@ def cpu_baseline(cfg: str, steps: int, warmup: int, rows_per_step: int = 1024, c
         qn = data.numpy() if cfg_eff == "quanto_int8" else data.view(torch.uint8).numpy()
         sn = qs.float().numpy()
     else:
-        packed, absmax, code, nabs, ncode, off = S.quantize_bnb4(w, nested=cfg_eff == "nf4_nested")
-        qn = packed.numpy().reshape(rows_per_step, cols // 2)
-        sn = absmax.numpy().reshape(rows_per_step, cols // 64)
-        extra = (code.numpy(), None if nabs is None else nabs.numpy(), None if ncode is None else ncode.numpy(),
-                 None if off is None else float(off))
+        # 4-bit: each row chunk is its own weight, so a nested chunk carries its own nested state.
+        nested = cfg_eff == "nf4_nested"
+        qn, sn, extra = [], [], []
+        for r in range(0, rows_per_step, chunk):
+            packed, absmax, code, nabs, ncode, off = S.quantize_bnb4(w[r:r + chunk], nested=nested)
+            qn.append(packed.numpy().reshape(-1, cols // 2))
+            sn.append(absmax.numpy().reshape(-1))
+            extra.append((code.numpy(), None if nabs is None else nabs.numpy(),
+                          None if ncode is None else ncode.numpy(), None if off is None else float(off)))
     bn, an = b.float().numpy(), a.float().numpy()
     seed = 0x9C3EA68DBAC91AAD if stochastic else None
     if cfg_eff == "static_fp8":
         sn = np.repeat(sn.reshape(1, 1), rows_per_step, axis=0)  # one scale per chunk
-    tasks = [(cfg_eff, qn[r:r + chunk], sn[r:r + chunk].reshape(-1) if cfg_eff.startswith("nf4") else
-              (sn[r] if cfg_eff == "static_fp8" else sn[r:r + chunk]), bn[r:r + chunk], an, seed, r * cols, extra)
-             for r in range(0, rows_per_step, chunk)]
+    if cfg_eff.startswith("nf4"):
+        tasks = [(cfg_eff, qn[j], sn[j], bn[r:r + chunk], an, seed, r * cols, extra[j])
+                 for j, r in enumerate(range(0, rows_per_step, chunk))]
+    else:
+        tasks = [(cfg_eff, qn[r:r + chunk], sn[r] if cfg_eff == "static_fp8" else sn[r:r + chunk], bn[r:r + chunk],
+                  an, seed, r * cols, extra) for r in range(0, rows_per_step, chunk)]
     ctx = mp.get_context("spawn")
     times = []
     with ctx.Pool(cores) as pool:
@@ -444,14 +451,13 @@ def main() -> int:
 
     # Device-resident path: descriptors built once through the adapters, then
     # one piper_merge_batch call per step with that step's seeds.
-    ws = torch.empty(64 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     keep: list = []
     descs = [AD.select_adapter(t).merge_desc(t, b, a, 1.0, rounding_seed=0 if stochastic else None, keep=keep)
              for key, rows, cols, t, b, a in items]
     arr = (_native.MergeDesc * len(descs))(*descs)
     need = _native.workspace_bytes(descs)
-    assert need <= ws.numel(), need
+    ws = torch.empty(max(64 << 20, need), dtype=torch.uint8, device=device)
     ws_ptr, ws_len = ws.data_ptr(), ws.numel()
     lib = _native.load()
     total_steps = warmup + args.steps

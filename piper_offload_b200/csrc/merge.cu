@@ -704,13 +704,16 @@ __device__ __forceinline__ void quanto_fp8_encode32(const float (&m)[32], float 
 
 // bitsandbytes decode + merge of 32 columns (_triton_bnb8_lora.py:20-81), fp16:
 // base = f16(f16(cb / 127) * f16(SCB)), merged = f16(clamp(base + acc * s, +-65504)).
+// `cb / 127.0` is an IEEE division; for every int8 code f16(cb * fp32(1 / 127))
+// equals f16(cb / 127) (all 256 codes checked), so the decode multiplies.
 __device__ __forceinline__ void bnb8_merged(const uint32_t (&wv)[8], const float (&acc)[32], float s_in,
                                             float strength, float (&merged)[32]) {
   const float s16 = f16r(s_in);
+  const float inv127 = __frcp_rn(127.0f);
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
-    const float base = f16r(__fmul_rn(f16r(__fdiv_rn(qv, 127.0f)), s16));  // `cb / 127.0`: IEEE
+    const float base = f16r(__fmul_rn(f16r(__fmul_rn(qv, inv127)), s16));
     merged[i] = fminf(fmaxf(fmaf(acc[i], strength, base), -65504.0f), 65504.0f);
   }
 #pragma unroll
@@ -934,150 +937,182 @@ __device__ __forceinline__ void affine_inputs(const DevWeight& W, const RowCtx& 
 // nearest table entry (NF4, ties to the lower index; _nearest_sorted_code
 // :29-50) or by the FP4 thresholds (_nearest_fp4_code :53-75), or
 // stochastically (_stochastic_sorted_code, _stochastic_fp4_code :135-160).
-// `lut` holds code[lane & 15] and `lvl` the FP4 level value of lane & 7: table
-// reads are full-warp shuffles, so the whole warp runs this together and every
-// lookup is evaluated unconditionally (never under a per-lane condition).
+// Per-lane tables (code[lane & 15], FP4 level values) are read with full-warp
+// shuffles, so the whole warp runs these helpers together and every lookup is
+// evaluated unconditionally (never under a per-lane condition).
 __device__ __forceinline__ float lane_lut(float lut, int idx) { return __shfl_sync(0xFFFFFFFFu, lut, idx); }
 
 __device__ __forceinline__ int fp4_level_to_store(int level) {
   return level < 2 ? level : (level < 4 ? level + 4 : (level < 6 ? level : level - 4));
 }
 
-template <int FMT, int CDT>
-__device__ __forceinline__ void bnb4_block(const DevWeight& W, const RowCtx& c, int col, const float (&acc0)[32],
-                                           const float (&acc1)[32], float lut, float lvl, const PhiloxKey& key,
-                                           uint32_t (&wv)[8]) {
-  constexpr bool kNf4 = FMT == PIPER_FMT_BNB4_NF4;
-  const int64_t bi = static_cast<int64_t>(c.row) * (W.N >> 6) + (col >> 6);
-  float scale = 0.0f;
-  if (c.valid) {
-    if (W.ncode != nullptr) {
-      const uint32_t q = reinterpret_cast<const uint8_t*>(W.scale)[bi];
-      scale = fmaf(__ldg(W.ncode + q), __ldg(W.nabs + (bi >> 8)), __ldg(W.noff));
-    } else {
-      scale = reinterpret_cast<const float*>(W.scale)[bi];
-    }
-  }
-  float m[64];
+// Decode + merge of 32 values (16 code bytes) of one 64-value block.
+template <int CDT>
+__device__ __forceinline__ void bnb4_merged32(const uint32_t (&wv)[4], float scale, float lut, float strength,
+                                              const float (&acc)[32], float (&m)[32]) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
+  for (int j = 0; j < 16; ++j) {
     const uint32_t byte = (wv[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
     m[2 * j] = lane_lut(lut, static_cast<int>(byte >> 4));
     m[2 * j + 1] = lane_lut(lut, static_cast<int>(byte & 15u));
   }
 #pragma unroll
-  for (int i = 0; i < 64; ++i) m[i] = __fmul_rn(m[i], scale);
+  for (int i = 0; i < 32; ++i) m[i] = __fmul_rn(m[i], scale);
 #pragma unroll
-  for (int i = 0; i < 64; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) m[i] = fmaf(acc[i], strength, m[i]);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+}
+
+// NF4 index of the reference's binary search (_nearest_sorted_code :29-50,
+// _stochastic_sorted_code): ui = first index in [0, 15] whose entry is not
+// below v. With a non-decreasing table (`tbl`, whole table in registers) that is
+// the count of tbl[0..14] below v: 15 independent compares.
+template <bool SR>
+__device__ __forceinline__ int nf4_code_sorted(float v, float lut, const float (&tbl)[16], const PhiloxKey& key,
+                                               uint64_t off) {
+  int ui = 0;
+#pragma unroll
+  for (int j = 0; j < 15; ++j) ui += tbl[j] < v ? 1 : 0;
+  const int li = max(ui - 1, 0);
+  const float up = lane_lut(lut, ui);
+  const float lo = lane_lut(lut, li);
+  int code = fabsf(__fsub_rn(v, lo)) <= fabsf(__fsub_rn(v, up)) ? li : ui;
+  if constexpr (SR) {
+    const bool exact = up == v;
+    const int li2 = exact ? ui : li;
+    const float lo2 = exact ? up : lo;
+    const float width = __fsub_rn(up, lo2);
+    const float prob = width > 0.0f ? div_full(__fsub_rn(v, lo2), width) : 0.0f;
+    const int chosen = philox_uniform(key, off) < prob ? ui : li2;
+    const bool interior = (v > tbl[0]) & (v < tbl[15]) & !exact;
+    code = interior ? chosen : code;
+  }
+  return code;
+}
+
+// The same with the table read by the 4-step binary search (any table order).
+__device__ __noinline__ int nf4_code_search(float v, const float* __restrict__ code16, bool sr, const PhiloxKey& key,
+                                            uint64_t off) {
+  int ui = 0, high = 15;
+  for (int st = 0; st < 4; ++st) {
+    const int mid = (ui + high) >> 1;
+    const bool right = __ldg(code16 + mid) < v;
+    ui = right ? mid + 1 : ui;
+    high = right ? high : mid;
+  }
+  const int li = max(ui - 1, 0);
+  const float up = __ldg(code16 + ui);
+  const float lo = __ldg(code16 + li);
+  int code = fabsf(__fsub_rn(v, lo)) <= fabsf(__fsub_rn(v, up)) ? li : ui;
+  if (sr) {
+    const bool exact = up == v;
+    const int li2 = exact ? ui : li;
+    const float lo2 = __ldg(code16 + li2);
+    const float width = __fsub_rn(up, lo2);
+    const float prob = width > 0.0f ? div_full(__fsub_rn(v, lo2), width) : 0.0f;
+    const int chosen = philox_uniform(key, off) < prob ? ui : li2;
+    const bool interior = (v > __ldg(code16)) & (v < __ldg(code16 + 15)) & !exact;
+    code = interior ? chosen : code;
+  }
+  return code;
+}
+
+// FP4 code (_nearest_fp4_code :53-75, _stochastic_fp4_code :135-160); `lvl`
+// holds the FP4 level value of lane & 7.
+template <bool SR>
+__device__ __forceinline__ int fp4_code(float v, float lvl, const PhiloxKey& key, uint64_t off) {
+  const float mag = fabsf(v);
+  const int level = (mag > 0.0026041667442768812f) + (mag > 0.08593750256113708f) + (mag > 0.2083333358168602f) +
+                    (mag > 0.2916666716337204f) + (mag > 0.4166666716337204f) + (mag > 0.5833333432674408f) +
+                    (mag > 0.8333333432674408f);
+  int code = fp4_level_to_store(level) + ((v < 0.0f && level != 0) ? 8 : 0);
+  if constexpr (SR) {
+    // _fp4_storage_to_level of the nearest code is the level itself.
+    const float nearest = lane_lut(lvl, level);
+    const bool down = nearest > mag;
+    const int lol = down ? level - 1 : level;
+    const int upl = down ? level : level + 1;
+    const float lo = lane_lut(lvl, max(lol, 0));
+    const float up = lane_lut(lvl, min(upl, 7));
+    const float prob = up > lo ? div_full(__fsub_rn(mag, lo), __fsub_rn(up, lo)) : 0.0f;
+    const int lv = philox_uniform(key, off) < prob ? upl : lol;
+    const int chosen = fp4_level_to_store(lv) + ((v < 0.0f && lv != 0) ? 8 : 0);
+    const bool interior = (mag > 0.0f) & (mag < 1.0f) & (prob > 0.0f);
+    code = interior ? chosen : code;
+  }
+  return code;
+}
+
+// Codes of 32 merged values (x = clamp(m / safe, -1, 1)) into 16 bytes, first
+// value of each byte in the high nibble. NF4 uses `lut` = code[lane & 15] and
+// the register table; FP4 uses `lut` = its level values.
+template <int FMT, bool SR>
+__device__ __forceinline__ void bnb4_encode32(const float (&m)[32], float safe, float lut, const float (&tbl)[16],
+                                              const PhiloxKey& key, uint64_t off0, uint32_t (&out)[4]) {
+#pragma unroll
+  for (int w = 0; w < 4; ++w) out[w] = 0u;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    m[i] = fmaf(acc0[i], W.strength, m[i]);
-    m[32 + i] = fmaf(acc1[i], W.strength, m[32 + i]);
-  }
-#pragma unroll
-  for (int i = 0; i < 64; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
-  float amax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(m[i]));
-  if (c.valid) {
-    if (W.ncode != nullptr) W.qmax[bi] = __float_as_uint(amax);  // raw maxima for the nested pass
-    else reinterpret_cast<float*>(W.scale)[bi] = amax;
-  }
-  const float safe = amax == 0.0f ? 1.0f : amax;
-  const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;  // uniform across the warp
-  const float code_first = lane_lut(lut, 0);
-  const float code_last = lane_lut(lut, 15);
-  const uint64_t off0 = W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
-#pragma unroll
-  for (int w = 0; w < 8; ++w) wv[w] = 0u;
-#pragma unroll 4
-  for (int i = 0; i < 64; ++i) {
     const float v = fminf(fmaxf(div_full(m[i], safe), -1.0f), 1.0f);
     int code;
-    if constexpr (kNf4) {
-      int low = 0, high = 15;
-#pragma unroll
-      for (int st = 0; st < 4; ++st) {
-        const int mid = (low + high) >> 1;
-        const bool right = lane_lut(lut, mid) < v;
-        low = right ? mid + 1 : low;
-        high = right ? high : mid;
-      }
-      const int ui = low;
-      const int li = max(ui - 1, 0);
-      const float up = lane_lut(lut, ui);
-      const float lo = lane_lut(lut, li);
-      code = fabsf(__fsub_rn(v, lo)) <= fabsf(__fsub_rn(v, up)) ? li : ui;
-      if (sr) {
-        const bool exact = up == v;
-        const int li2 = exact ? ui : li;
-        const float lo2 = lane_lut(lut, li2);
-        const float width = __fsub_rn(up, lo2);
-        const float prob = width > 0.0f ? div_full(__fsub_rn(v, lo2), width) : 0.0f;
-        const int chosen = philox_uniform(key, off0 + i) < prob ? ui : li2;
-        const bool interior = (v > code_first) & (v < code_last) & !exact;
-        code = interior ? chosen : code;
-      }
-    } else {
-      const float mag = fabsf(v);
-      const int level = (mag > 0.0026041667442768812f) + (mag > 0.08593750256113708f) +
-                        (mag > 0.2083333358168602f) + (mag > 0.2916666716337204f) + (mag > 0.4166666716337204f) +
-                        (mag > 0.5833333432674408f) + (mag > 0.8333333432674408f);
-      code = fp4_level_to_store(level) + ((v < 0.0f && level != 0) ? 8 : 0);
-      if (sr) {
-        // _fp4_storage_to_level of the nearest code: the level itself.
-        const float nearest = lane_lut(lvl, level);
-        const bool down = nearest > mag;
-        const int lol = down ? level - 1 : level;
-        const int upl = down ? level : level + 1;
-        const float lo = lane_lut(lvl, max(lol, 0));
-        const float up = lane_lut(lvl, min(upl, 7));
-        const float prob = up > lo ? div_full(__fsub_rn(mag, lo), __fsub_rn(up, lo)) : 0.0f;
-        const int lv = philox_uniform(key, off0 + i) < prob ? upl : lol;
-        const int chosen = fp4_level_to_store(lv) + ((v < 0.0f && lv != 0) ? 8 : 0);
-        const bool interior = mag > 0.0f && mag < 1.0f && prob > 0.0f;
-        code = interior ? chosen : code;
-      }
-    }
+    if constexpr (FMT == PIPER_FMT_BNB4_NF4) code = nf4_code_sorted<SR>(v, lut, tbl, key, off0 + i);
+    else code = fp4_code<SR>(v, lut, key, off0 + i);
     const int j = i >> 1;
-    wv[j >> 2] |= static_cast<uint32_t>(code & 15) << ((j & 3) * 8 + ((i & 1) ? 0 : 4));
+    out[j >> 2] |= static_cast<uint32_t>(code & 15) << ((j & 3) * 8 + ((i & 1) ? 0 : 4));
   }
 }
 
 // Nested quantization of the new block maxima (_triton_bnb4_lora.py:316-375,
 // :399-431): offset = mean of the maxima; per 256 blocks the maximum of
 // |x - offset| and the nearest code of (x - offset) / maximum in the
-// 256-entry table. The mean is summed in fp64 in a fixed order and rounded
-// once; the reference sums in Triton's fp32 reduction order.
-__global__ void __launch_bounds__(1024) bnb4_offset_kernel(const uint32_t* __restrict__ raw, int64_t n,
-                                                           float* __restrict__ off) {
-  __shared__ double part[32];
+// 256-entry table. The mean is summed in fp64 in a fixed order (kBnb4Parts
+// contiguous ranges, then their partial sums in index order) and rounded once;
+// the reference sums in Triton's fp32 reduction order.
+constexpr int kBnb4Parts = 64;
+
+__global__ void __launch_bounds__(256) bnb4_partial_kernel(const uint32_t* __restrict__ raw, int64_t n,
+                                                           double* __restrict__ part) {
+  __shared__ double red[8];
+  const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+  const int64_t b0 = static_cast<int64_t>(blockIdx.x) * per;
+  const int64_t b1 = min(n, b0 + per);
   double s = 0.0;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += static_cast<double>(__uint_as_float(raw[i]));
+  for (int64_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) s += static_cast<double>(__uint_as_float(raw[i]));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xFFFFFFFFu, s, o);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    double t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) t += __shfl_down_sync(0xFFFFFFFFu, t, o);
-    if (threadIdx.x == 0) *off = __fdiv_rn(__double2float_rn(t), static_cast<float>(n));  // `/ TOTAL_VALUES`
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < 8; ++w) t += red[w];
+    part[blockIdx.x] = t;
   }
 }
 
+// Every CTA folds the partial sums in the same order, so all see the same
+// offset; CTA 0 stores it.
 __global__ void __launch_bounds__(256) bnb4_nested_kernel(const uint32_t* __restrict__ raw, int64_t n,
-                                                          const float* __restrict__ off,
+                                                          const double* __restrict__ part, float* __restrict__ off,
                                                           const float* __restrict__ ncode, uint8_t* __restrict__ qabs,
                                                           float* __restrict__ nabs) {
   __shared__ float tbl[256];
+  __shared__ float s_off;
   tbl[threadIdx.x] = ncode[threadIdx.x];
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int b = 0; b < kBnb4Parts; ++b) t += part[b];
+    s_off = __fdiv_rn(__double2float_rn(t), static_cast<float>(n));  // `/ TOTAL_VALUES`
+    if (blockIdx.x == 0) *off = s_off;
+  }
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t w = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int64_t nblk = (n + 255) / 256;
   if (w >= nblk) return;
-  const float o = *off;
+  const float o = s_off;
   float cen[8];
   float mx = 0.0f;
 #pragma unroll
@@ -1968,25 +2003,86 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
           if (PASS != kReduce) *reinterpret_cast<uint2*>(chunk_ptr(c, k)) = codes;
         }
       } else if constexpr (FMT == PIPER_FMT_BNB4_NF4 || FMT == PIPER_FMT_BNB4_FP4) {
-        constexpr float kFp4Levels[8] = {0.0f, 0.0052083334885537624f, 0.1666666716337204f, 0.25f,
-                                         0.3333333432674408f, 0.5f, 0.6666666865348816f, 1.0f};
-        const float lut = __ldg(W.code16 + (lane & 15));
-        float lvl = kFp4Levels[0];
+        // One 64-value block of _merge_quantize_kernel (_triton_bnb4_lora.py:163-313)
+        // per pair of 32-column chunks: the block maximum from a first decode,
+        // then each chunk decoded again and encoded.
+        constexpr bool kNf4 = FMT == PIPER_FMT_BNB4_NF4;
+        // Decode table per lane; the encode table: NF4 the same, FP4 its level
+        // values (_fp4_level_value :78-105) per lane & 7.
+        const float dec = __ldg(W.code16 + (lane & 15));
+        const int l7 = lane & 7;
+        const float lut = kNf4 ? dec
+                               : (l7 == 0   ? 0.0f
+                                  : l7 == 1 ? 0.0052083334885537624f
+                                  : l7 == 2 ? 0.1666666716337204f
+                                  : l7 == 3 ? 0.25f
+                                  : l7 == 4 ? 0.3333333432674408f
+                                  : l7 == 5 ? 0.5f
+                                  : l7 == 6 ? 0.6666666865348816f
+                                            : 1.0f);
+        float tbl[16];
+        bool sorted = true;
 #pragma unroll
-        for (int q = 1; q < 8; ++q) lvl = (lane & 7) == q ? kFp4Levels[q] : lvl;
+        for (int j = 0; j < 16; ++j) tbl[j] = __ldg(W.code16 + j);
+#pragma unroll
+        for (int j = 0; j < 15; ++j) sorted = sorted && !(tbl[j + 1] < tbl[j]);
+        const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
         const PhiloxKey key = philox_key(W.k0, W.k1);
+        const int nbr = W.N >> 6;
         for (int k = 0; k < tcols / 32; k += 2) {
-          float acc0[32], acc1[32];
-          tmem_ld32(taddr + 32 * k, acc0);
-          tmem_ld32(taddr + 32 * (k + 1), acc1);
-          uint32_t wv[8];
-          const uint4 lo = *reinterpret_cast<const uint4*>(chunk_ptr(c, k));
-          const uint4 hi = *reinterpret_cast<const uint4*>(chunk_ptr(c, k + 1));
-          wv[0] = lo.x; wv[1] = lo.y; wv[2] = lo.z; wv[3] = lo.w;
-          wv[4] = hi.x; wv[5] = hi.y; wv[6] = hi.z; wv[7] = hi.w;
-          bnb4_block<FMT, CDT>(W, c, c0 + 32 * k, acc0, acc1, lut, lvl, key, wv);
-          *reinterpret_cast<uint4*>(chunk_ptr(c, k)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-          *reinterpret_cast<uint4*>(chunk_ptr(c, k + 1)) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+          const int col = c0 + 32 * k;
+          const int64_t bi = static_cast<int64_t>(row) * nbr + (col >> 6);
+          float scale = 0.0f;
+          if (valid) {
+            if (W.ncode != nullptr) {
+              const uint32_t q = reinterpret_cast<const uint8_t*>(W.scale)[bi];
+              scale = fmaf(__ldg(W.ncode + q), __ldg(W.nabs + (bi >> 8)), __ldg(W.noff));  // code * absmax + offset
+            } else {
+              scale = reinterpret_cast<const float*>(W.scale)[bi];
+            }
+          }
+          float amax = 0.0f;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint4 v4 = *reinterpret_cast<const uint4*>(chunk_ptr(c, k + h));
+            const uint32_t wq[4] = {v4.x, v4.y, v4.z, v4.w};
+            float acc[32], m[32];
+            tmem_ld32(taddr + 32 * (k + h), acc);
+            bnb4_merged32<CDT>(wq, scale, dec, W.strength, acc, m);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(m[i]));
+          }
+          if (valid) {
+            if (W.ncode != nullptr) W.qmax[bi] = __float_as_uint(amax);  // raw maxima for the nested pass
+            else reinterpret_cast<float*>(W.scale)[bi] = amax;
+          }
+          const float safe = amax == 0.0f ? 1.0f : amax;
+          for (int h = 0; h < 2; ++h) {  // codes still in shared memory: the chunk is rewritten below
+            const uint4 v4 = *reinterpret_cast<const uint4*>(chunk_ptr(c, k + h));
+            const uint32_t wq[4] = {v4.x, v4.y, v4.z, v4.w};
+            float acc[32], m[32];
+            tmem_ld32(taddr + 32 * (k + h), acc);
+            bnb4_merged32<CDT>(wq, scale, dec, W.strength, acc, m);
+            const uint64_t off0 =
+                W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + col + 32 * h;
+            uint32_t out[4];
+            if (kNf4 && !sorted) {  // uniform per item: the reference's binary search, element by element
+#pragma unroll
+              for (int w = 0; w < 4; ++w) out[w] = 0u;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float v = fminf(fmaxf(div_full(m[i], safe), -1.0f), 1.0f);
+                const int code = nf4_code_search(v, W.code16, sr, key, off0 + i);
+                const int j = i >> 1;
+                out[j >> 2] |= static_cast<uint32_t>(code & 15) << ((j & 3) * 8 + ((i & 1) ? 0 : 4));
+              }
+            } else if (sr) {
+              bnb4_encode32<FMT, true>(m, safe, lut, tbl, key, off0, out);
+            } else {
+              bnb4_encode32<FMT, false>(m, safe, lut, tbl, key, off0, out);
+            }
+            *reinterpret_cast<uint4*>(chunk_ptr(c, k + h)) = make_uint4(out[0], out[1], out[2], out[3]);
+          }
         }
       } else if constexpr (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0) {
         chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) { gguf_chunk<FMT, CDT>(W, c, k, acc); });
@@ -2613,7 +2709,8 @@ int validate(const piper_merge_desc& d, Plan& p) {
           return fail(PIPER_MERGE_EINVAL,
                       "BNB4 stochastic merge does not support nested scales because their final effective values "
                       "are unavailable during terminal-code selection.");
-        p.nq = static_cast<int>(d.rows * (d.cols / 64));  // raw block maxima for the nested pass
+        // raw block maxima for the nested pass, then the fp64 partial sums of their mean
+        p.nq = static_cast<int>(d.rows * (d.cols / 64)) + 2 * pm::kBnb4Parts + 2;
       }
       break;
     case PIPER_FMT_GGUF_Q8_0:
@@ -2642,9 +2739,14 @@ int validate(const piper_merge_desc& d, Plan& p) {
   return PIPER_MERGE_OK;
 }
 
-size_t scratch_bytes(int nq) {
-  // qmax, qmin, old_scale, old_zp: four words per quantization block, 256-byte aligned.
-  return nq == 0 ? 0 : (static_cast<size_t>(nq) * 16 + 255) / 256 * 256;
+// Workspace words per quantization block: qmax, qmin, old_scale, old_zp
+// (bitsandbytes 4-bit nested: the new block maximum only).
+int scratch_words(int format) {
+  return format == PIPER_FMT_BNB4_NF4 || format == PIPER_FMT_BNB4_FP4 ? 1 : 4;
+}
+
+size_t scratch_bytes(int nq, int words) {
+  return nq == 0 ? 0 : (static_cast<size_t>(nq) * 4 * words + 255) / 256 * 256;  // 256-byte aligned
 }
 
 int sm_count() {
@@ -2871,9 +2973,11 @@ DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws,
   if (p.nq > 0) {
     uint8_t* base = ws + p.ws_off;
     w.qmax = reinterpret_cast<uint32_t*>(base);
-    w.qmin = reinterpret_cast<uint32_t*>(base + 4 * static_cast<size_t>(p.nq));
-    w.old_scale = reinterpret_cast<float*>(base + 8 * static_cast<size_t>(p.nq));
-    w.old_zp = reinterpret_cast<int32_t*>(base + 12 * static_cast<size_t>(p.nq));
+    if (scratch_words(d.format) == 4) {
+      w.qmin = reinterpret_cast<uint32_t*>(base + 4 * static_cast<size_t>(p.nq));
+      w.old_scale = reinterpret_cast<float*>(base + 8 * static_cast<size_t>(p.nq));
+      w.old_zp = reinterpret_cast<int32_t*>(base + 12 * static_cast<size_t>(p.nq));
+    }
   }
   w.row_bytes = row_bytes_of(d);
   w.offset_base = d.offset_base;
@@ -2959,10 +3063,11 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
     if ((d.format != PIPER_FMT_BNB4_NF4 && d.format != PIPER_FMT_BNB4_FP4) || d.nested_absmax == nullptr) continue;
     const uint32_t* raw = reinterpret_cast<const uint32_t*>(ws + p.ws_off);
     const int64_t n = d.rows * (d.cols / 64);
-    pm::bnb4_offset_kernel<<<1, 1024, 0, stream>>>(raw, n, static_cast<float*>(d.nested_offset));
+    double* part = reinterpret_cast<double*>(ws + p.ws_off + (static_cast<size_t>(n) * 4 + 7) / 8 * 8);
+    pm::bnb4_partial_kernel<<<pm::kBnb4Parts, 256, 0, stream>>>(raw, n, part);
     const int64_t nblk = (n + 255) / 256;
     pm::bnb4_nested_kernel<<<static_cast<unsigned>((nblk + 7) / 8), 256, 0, stream>>>(
-        raw, n, static_cast<const float*>(d.nested_offset), static_cast<const float*>(d.nested_code),
+        raw, n, part, static_cast<float*>(d.nested_offset), static_cast<const float*>(d.nested_code),
         static_cast<uint8_t*>(d.scale), static_cast<float*>(d.nested_absmax));
     g_launches.fetch_add(2, std::memory_order_relaxed);
     const cudaError_t e = cudaGetLastError();
@@ -2996,7 +3101,7 @@ int plan_all(const piper_merge_desc* in, int count, std::vector<piper_merge_desc
       plans[i].nq = static_cast<int>(descs[i].cols);
     }
     plans[i].ws_off = ws_total;
-    ws_total += scratch_bytes(plans[i].nq);
+    ws_total += scratch_bytes(plans[i].nq, scratch_words(descs[i].format));
   }
   return PIPER_MERGE_OK;
 }

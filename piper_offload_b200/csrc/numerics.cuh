@@ -199,27 +199,57 @@ __device__ __forceinline__ uint32_t sr_fp8(float v, float limit, const PhiloxKey
 // Four consecutive counters advanced round by round, so the four independent
 // multiply chains issue back to back.
 __device__ __forceinline__ void philox_word0_x4(const PhiloxKey& key, uint64_t offset, uint32_t (&w)[4]) {
+  // Round 0 with counter words 2 and 3 zero: the second multiply is zero.
   uint32_t c0[4], c1[4], c2[4], c3[4];
+  const uint32_t hi0 = static_cast<uint32_t>(offset >> 32);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint64_t o = offset + static_cast<uint64_t>(j);
-    c0[j] = static_cast<uint32_t>(o);
-    c1[j] = static_cast<uint32_t>(o >> 32);
-    c2[j] = 0u;
-    c3[j] = 0u;
+    const uint32_t lo = static_cast<uint32_t>(o);
+    c0[j] = static_cast<uint32_t>(o >> 32) ^ key.k0[0];
+    c2[j] = __umulhi(0xD2511F53u, lo) ^ key.k1[0];
+    c1[j] = 0u;
+    c3[j] = 0xD2511F53u * lo;
+  }
+  // Round 1: word 0 is (offset >> 32) ^ key, the same for the four counters
+  // unless they straddle a multiple of 2^32, so its product is formed once.
+  uint32_t ha[4], la[4];
+  if (static_cast<uint32_t>((offset + 3u) >> 32) == hi0) {
+    const uint32_t h = __umulhi(0xD2511F53u, c0[0]);
+    const uint32_t l = 0xD2511F53u * c0[0];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ha[j] = h;
+      la[j] = l;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ha[j] = __umulhi(0xD2511F53u, c0[j]);
+      la[j] = 0xD2511F53u * c0[j];
+    }
   }
 #pragma unroll
-  for (int round = 0; round < 10; ++round) {
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t hb = __umulhi(0xCD9E8D57u, c2[j]);
+    const uint32_t lb = 0xCD9E8D57u * c2[j];
+    c0[j] = hb ^ c1[j] ^ key.k0[1];
+    c2[j] = ha[j] ^ c3[j] ^ key.k1[1];
+    c1[j] = lb;
+    c3[j] = la[j];
+  }
+#pragma unroll
+  for (int round = 2; round < 10; ++round) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t hb = __umulhi(0xCD9E8D57u, c2[j]);
       const uint32_t lb = 0xCD9E8D57u * c2[j];
-      const uint32_t ha = __umulhi(0xD2511F53u, c0[j]);
-      const uint32_t la = 0xD2511F53u * c0[j];
+      const uint32_t hm = __umulhi(0xD2511F53u, c0[j]);
+      const uint32_t lm = 0xD2511F53u * c0[j];
       c0[j] = hb ^ c1[j] ^ key.k0[round];
-      c2[j] = ha ^ c3[j] ^ key.k1[round];
+      c2[j] = hm ^ c3[j] ^ key.k1[round];
       c1[j] = lb;
-      c3[j] = la;
+      c3[j] = lm;
     }
   }
 #pragma unroll
@@ -237,25 +267,39 @@ __device__ __forceinline__ uint32_t sr_fp8x4(const float (&v)[4], float limit, c
   constexpr float kSubScale = E4M3 ? 512.0f : 65536.0f;
   uint32_t r[4];
   philox_word0_x4(key, off, r);
+  uint32_t lo[4];
+  float p[4];
+  bool sub = false;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t abits = __float_as_uint(v[j]) & 0x7FFFFFFFu;
+    lo[j] = (abits >> kDrop) - kBiasFix;
+    p[j] = __uint_as_float(0x3F800000u | ((abits << kMant) & 0x7FFFFFu)) - 1.0f;
+    sub |= abits < kMinNormal;
+  }
+  // Below the smallest normal (zero included) the codes are evenly spaced;
+  // that path runs only when a lane of the active part of the warp needs it.
+  if (__any_sync(__activemask(), sub)) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t abits = __float_as_uint(v[j]) & 0x7FFFFFFFu;
+      const float t = __uint_as_float(abits) * kSubScale;
+      const float fl = truncf(t);
+      if (abits < kMinNormal) {
+        lo[j] = __float_as_uint(fl + 8388608.0f) - 0x4B000000u;
+        p[j] = t - fl;
+      }
+    }
+  }
   uint32_t word = 0u;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t bits = __float_as_uint(v[j]);
-    const uint32_t abits = bits & 0x7FFFFFFFu;
-    const float mag = __uint_as_float(abits);
-    const uint32_t lo_n = (abits >> kDrop) - kBiasFix;
-    const float p_n = __uint_as_float(0x3F800000u | ((abits << kMant) & 0x7FFFFFu)) - 1.0f;
-    const float t = mag * kSubScale;
-    const float fl = truncf(t);
-    const uint32_t lo_s = __float_as_uint(fl + 8388608.0f) - 0x4B000000u;
-    const float p_s = t - fl;
-    const bool normal = abits >= kMinNormal;
-    const uint32_t lo = normal ? lo_n : lo_s;
-    const float p = normal ? p_n : p_s;
+    const float mag = __uint_as_float(bits & 0x7FFFFFFFu);
     const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
     const float u = __fmul_rn(__int2float_rn(x), __uint_as_float(0x2FFFFFFFu));
-    const bool up = mag < limit && p > 0.0f && u < p;
-    word |= ((lo + (up ? 1u : 0u)) | ((bits >> 24) & 0x80u)) << (8 * j);
+    const bool up = mag < limit && p[j] > 0.0f && u < p[j];
+    word |= ((lo[j] + (up ? 1u : 0u)) | ((bits >> 24) & 0x80u)) << (8 * j);
   }
   return word;
 }

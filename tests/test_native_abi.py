@@ -121,7 +121,8 @@ def test_bnb4_validation_messages():
     assert b"nested" in lib.piper_merge_last_error()
     d = _desc(format=nat.FMT_BNB4_NF4, codebook=0x5000, nested_absmax=0x6000, nested_code=0x7000,
               nested_offset=0x8000)
-    assert nat.workspace_bytes([d]) == 64 * 256 // 64 * 16  # raw block maxima for the nested pass
+    # raw block maxima for the nested pass, then 64 fp64 partial sums of their mean (256-byte aligned)
+    assert nat.workspace_bytes([d]) == (64 * 256 // 64 * 4 + 130 * 4 + 255) // 256 * 256
     assert nat.workspace_bytes([_desc(format=nat.FMT_BNB4_NF4, codebook=0x5000)]) == 0
 
 

@@ -172,3 +172,12 @@ def test_sr_int_probability_fixture():
     offs = np.arange(vals.size, dtype=np.uint64)
     out = om.sr_round_to_int(vals, det, 42, offs, -128, 127)
     assert abs(out.mean() - 0.3) < 0.005
+
+
+def test_bnb8_decode_multiply_equals_division_for_every_code():
+    # The kernel decodes bitsandbytes codes as f16(cb * fp32(1/127)); the reference
+    # computes f16(cb / 127.0) (_triton_bnb8_lora.py:67). Equal over the whole int8 domain.
+    q = np.arange(-128, 128, dtype=np.float32)
+    div = (q / np.float32(127.0)).astype(np.float32).astype(np.float16)
+    mul = (q * (np.float32(1.0) / np.float32(127.0))).astype(np.float32).astype(np.float16)
+    assert np.array_equal(div.view(np.uint16), mul.view(np.uint16))

@@ -56,3 +56,24 @@ def test_torch_cuda_divides_by_host_scalar_through_its_reciprocal(cuda_device):
         for qmax in (127.0, 448.0, 57344.0):
             inv = torch.tensor(float(np.float32(1.0) / np.float32(qmax)), dtype=torch.float32, device=cuda_device)
             assert torch.equal(x / qmax, (x.float() * inv).to(dt)), (dt, qmax)
+
+
+def test_bnb4_unsorted_table_follows_the_binary_search(cuda_device):
+    # NF4 code selection is the reference's binary search (_triton_bnb4_lora.py:29-50).
+    # For a sorted table the kernel counts entries instead; an unsorted table must
+    # still give the binary search's answer.
+    case = next(c for c in CASES if c["launcher"] == "bnb4" and c["quant_type"] == "nf4" and not c["nested"]
+                and c["seed"] is None)
+    code = rf.arr(case, "code").copy()
+    code[[3, 11]] = code[[11, 3]]
+    arrays = rf._load()[1]
+    key = f"{case['id']}.code"
+    saved = arrays[key]
+    arrays[key] = code
+    try:
+        got = rf.native(case, cuda_device)
+        want = rf.oracle(case)
+    finally:
+        arrays[key] = saved
+    bad = {k: v[:8].tolist() for k, v in rf.mismatches(got, want).items() if v.size}
+    assert not bad, bad
