@@ -580,8 +580,34 @@ __device__ __forceinline__ void int8_encode32(const float (&m)[32], const Int8Q&
   float x[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) x[i] = __fmul_rn(m[i], inv);
+  if (scale_dt == kBF16) {  // one dispatch per chunk
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) round_rt2(x[i], x[i + 1], scale_dt);
+    for (int i = 0; i < 32; i += 2) bf16r2(x[i], x[i + 1]);
+  } else if (scale_dt == kF16) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) f16r2(x[i], x[i + 1]);
+  }
+  if (!sr) {
+    // Round to nearest in the integer domain: for |x| < 2^22 the bits of
+    // x + 1.5 * 2^23 minus those of 1.5 * 2^23 are rint(x); a chunk holding a
+    // NaN or a larger value takes the general path below.
+    bool big = false;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) big |= !(fabsf(x[i]) < 4194304.0f);
+    if (!big) {
+      int qi[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int r = static_cast<int>(__float_as_uint(__fadd_rn(x[i], 12582912.0f)) - 0x4B400000u) + q.zp;
+        qi[i] = min(max(r, qmin), qmax);
+      }
+#pragma unroll
+      for (int w = 0; w < 8; ++w)
+        out[w] = __byte_perm(__byte_perm(qi[4 * w], qi[4 * w + 1], 0x0040), __byte_perm(qi[4 * w + 2], qi[4 * w + 3], 0x0040),
+                             0x5410);
+      return;
+    }
+  }
   const float zpf = static_cast<float>(q.zp);
 #pragma unroll
   for (int w = 0; w < 8; ++w) out[w] = 0u;
