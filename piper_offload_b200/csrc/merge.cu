@@ -692,6 +692,32 @@ template <int CDT>
 __device__ __forceinline__ void flavor_int8_encode32(int flavor, const float (&m)[32], float s, bool sr,
                                                      const PhiloxKey& key, uint64_t off0, uint32_t (&out)[8]) {
   const float lo = flavor == kBnb ? -127.0f : -128.0f;
+  if (!sr) {
+    // Round to nearest in the integer domain (see int8_encode32); a chunk
+    // holding a NaN or |x| >= 2^22 takes the general loop below.
+    float x[32];
+    bool big = false;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      x[i] = flavor == kBnb ? (s == 0.0f ? 0.0f : __fmul_rn(div_full(m[i], s), 127.0f))
+                            : round_dt<CDT>(div_full(m[i], s));
+      big |= !(fabsf(x[i]) < 4194304.0f);
+    }
+    if (!big) {
+      const int ilo = flavor == kBnb ? -127 : -128;
+      int qi[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int r = static_cast<int>(__float_as_uint(__fadd_rn(x[i], 12582912.0f)) - 0x4B400000u);
+        qi[i] = min(max(r, ilo), 127);
+      }
+#pragma unroll
+      for (int w = 0; w < 8; ++w)
+        out[w] = __byte_perm(__byte_perm(qi[4 * w], qi[4 * w + 1], 0x0040), __byte_perm(qi[4 * w + 2], qi[4 * w + 3], 0x0040),
+                             0x5410);
+      return;
+    }
+  }
 #pragma unroll
   for (int w = 0; w < 8; ++w) out[w] = 0u;
 #pragma unroll
@@ -1332,41 +1358,99 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
     const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
     dh = __half_as_ushort(__float2half_rn(d));
     uint32_t qb[32];
+    float x[32];
+    bool big = false;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const float x = __fmul_rn(merged[i], id);
-      float q = roundf_away(x);
-      if (sr) q = sr_int(x, q, -127.0f, 127.0f, key, off0 + i);
-      q = fminf(fmaxf(q, -128.0f), 127.0f);
-      qb[i] = float_int_bits(q);
+      x[i] = __fmul_rn(merged[i], id);
+      big |= !(fabsf(x[i]) < 4194304.0f);
+    }
+    if (!sr && !big) {
+      // Round half away from zero in the integer domain: t = trunc(|x|) from
+      // the bits of |x| + 2^23 added toward zero, plus 1 when |x| - t >= 0.5.
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = fabsf(x[i]);
+        const float y = __fadd_rz(a, 8388608.0f);
+        const float frac = __fsub_rn(a, __fsub_rn(y, 8388608.0f));
+        const int b = static_cast<int>(__float_as_uint(y) - 0x4B000000u) + (frac >= 0.5f ? 1 : 0);
+        qb[i] = static_cast<uint32_t>(min(max(x[i] < 0.0f ? -b : b, -128), 127));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float q = roundf_away(x[i]);
+        if (sr) q = sr_int(x[i], q, -127.0f, 127.0f, key, off0 + i);
+        q = fminf(fmaxf(q, -128.0f), 127.0f);
+        qb[i] = float_int_bits(q);
+      }
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) ow[j] = pack_low_bytes(qb[4 * j], qb[4 * j + 1], qb[4 * j + 2], qb[4 * j + 3]);
   } else {
-    int imax = 0;
-    float best = fabsf(merged[0]);
+    // The signed value of the first largest |x| (np.argmax): a pairwise tree
+    // that keeps the left value unless the right one is strictly larger gives
+    // the first maximum; a chunk holding a NaN scans in order as before.
+    bool has_nan = false;
 #pragma unroll
-    for (int i = 1; i < 32; ++i) {
-      const float a = fabsf(merged[i]);
-      if (a > best) {
-        best = a;
-        imax = i;
+    for (int i = 0; i < 32; ++i) has_nan |= merged[i] != merged[i];
+    float mx;
+    if (!has_nan) {
+      float av[32], sv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        av[i] = fabsf(merged[i]);
+        sv[i] = merged[i];
       }
-    }
-    float mx = merged[0];
 #pragma unroll
-    for (int i = 1; i < 32; ++i) mx = (i == imax) ? merged[i] : mx;
+      for (int st = 1; st < 32; st <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 2 * st) {
+          const bool r = av[i + st] > av[i];
+          av[i] = r ? av[i + st] : av[i];
+          sv[i] = r ? sv[i + st] : sv[i];
+        }
+      }
+      mx = sv[0];
+    } else {
+      int imax = 0;
+      float best = fabsf(merged[0]);
+      for (int i = 1; i < 32; ++i) {
+        const float a = fabsf(merged[i]);
+        if (a > best) {
+          best = a;
+          imax = i;
+        }
+      }
+      mx = merged[0];
+#pragma unroll
+      for (int i = 1; i < 32; ++i) mx = (i == imax) ? merged[i] : mx;
+    }
     const float d = __fdiv_rn(mx, -8.0f);
     const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
     dh = __half_as_ushort(__float2half_rn(d));
     uint32_t qb[32];
+    float y[32];
+    bool bad = false;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const float x = __fmul_rn(merged[i], id);
-      float qf = truncf(__fadd_rn(x, 8.5f));
-      if (sr) qf = sr_int(__fadd_rn(x, 8.0f), qf, 0.0f, 15.0f, key, off0 + i);
-      qf = fminf(fmaxf(qf, 0.0f), 15.0f);
-      qb[i] = float_int_bits(qf);
+      y[i] = __fadd_rn(__fmul_rn(merged[i], id), 8.5f);
+      bad |= !(y[i] >= 0.0f && y[i] < 4194304.0f);
+    }
+    if (!sr && !bad) {
+      // trunc(y) for 0 <= y < 2^22: the bits of y + 2^23 added toward zero.
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        qb[i] = min(__float_as_uint(__fadd_rz(y[i], 8388608.0f)) - 0x4B000000u, 15u);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float x = __fmul_rn(merged[i], id);
+        float qf = truncf(y[i]);
+        if (sr) qf = sr_int(__fadd_rn(x, 8.0f), qf, 0.0f, 15.0f, key, off0 + i);
+        qf = fminf(fmaxf(qf, 0.0f), 15.0f);
+        qb[i] = float_int_bits(qf);
+      }
     }
     // byte j = element j (low nibble) | element j+16 (high nibble)
 #pragma unroll
