@@ -379,6 +379,7 @@ def main() -> int:
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--config", default="fp8", choices=sorted(CONFIGS))
     ap.add_argument("--rtn", action="store_true", help="round-to-nearest instead of the config's rounding")
+    ap.add_argument("--sr", action="store_true", help="stochastic rounding instead of the config's rounding")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -399,7 +400,9 @@ def main() -> int:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     cfg = args.config
     _, _, lrank, _, _, cfg_sr, desc = CONFIGS[cfg]
-    stochastic = cfg_sr and not args.rtn
+    stochastic = (cfg_sr or args.sr) and not args.rtn
+    if stochastic != cfg_sr:
+        desc = desc.rsplit(", ", 1)[0] + (", SR" if stochastic else ", RTN")
     metric = "LoRA-merge weight GB/s (read+write)"
 
     if args.impl == "reference":

@@ -384,8 +384,10 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
     uint32_t out[4] = {0u, 0u, 0u, 0u};
     if (sr) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        out[i >> 3] |= (sr_e2m1(merged[i], enc_e2m1(merged[i]), key, off0 + i) & 0xFu) << ((i & 7) * 4);
+      for (int w = 0; w < 8; ++w) {
+        const float v[4] = {merged[4 * w], merged[4 * w + 1], merged[4 * w + 2], merged[4 * w + 3]};
+        out[w >> 1] |= sr_e2m1x4(v, key, off0 + 4 * w) << ((w & 1) * 16);
+      }
     } else {
 #pragma unroll
       for (int j = 0; j < 16; ++j) out[j >> 2] |= enc_e2m1x2(merged[2 * j], merged[2 * j + 1]) << ((j & 3) * 8);
@@ -490,8 +492,10 @@ __device__ __forceinline__ void nvfp4_block(const DevWeight& W, const RowCtx& c,
       const uint64_t off0 =
           W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        out[i >> 3] |= (sr_e2m1(m[i], enc_e2m1(m[i]), key, off0 + i) & 0xFu) << ((i & 7) * 4);
+      for (int w = 0; w < 4; ++w) {
+        const float v[4] = {m[4 * w], m[4 * w + 1], m[4 * w + 2], m[4 * w + 3]};
+        out[w >> 1] |= sr_e2m1x4(v, key, off0 + 4 * w) << ((w & 1) * 16);
+      }
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) out[j >> 2] |= enc_e2m1x2(m[2 * j], m[2 * j + 1]) << ((j & 3) * 8);

@@ -69,32 +69,6 @@ __device__ __forceinline__ float dec_fp8(uint32_t c) {
   else return dec_e5m2(c);
 }
 
-// ------------------------------------------------------------------ E2M1
-// Magnitudes of the low three code bits (_e2m1_value /
-// _triton_stochastic_quantization.py:82-106).
-__device__ __forceinline__ float e2m1_mag(uint32_t code) {
-  const uint32_t c = code & 7u;
-  // 0, .5, 1, 1.5, 2, 3, 4, 6
-  return c < 4u ? 0.5f * static_cast<float>(c) : (c == 7u ? 6.0f : static_cast<float>(c - 2u));
-}
-__device__ __forceinline__ float dec_e2m1(uint32_t code) {
-  const float m = e2m1_mag(code);
-  return (code & 8u) ? -m : m;
-}
-// Threshold ladder of _encode_fp4 (_triton_mx_lora.py:67-94); sign from the fp32 sign bit.
-__device__ __forceinline__ uint32_t enc_e2m1(float v) {
-  const float m = fabsf(v);
-  uint32_t c = m <= 0.25f ? 0u
-             : m < 0.75f  ? 1u
-             : m <= 1.25f ? 2u
-             : m < 1.75f  ? 3u
-             : m <= 2.5f  ? 4u
-             : m < 3.5f   ? 5u
-             : m <= 5.0f  ? 6u
-                          : 7u;
-  return c | ((__float_as_uint(v) >> 28) & 8u);
-}
-
 // E8M0 code -> fp32 (_e8m0_to_fp32, _triton_mx_lora.py:30-37).
 __device__ __forceinline__ float dec_e8m0(uint32_t code) {
   code &= 0xFFu;
@@ -152,11 +126,6 @@ __device__ __forceinline__ float philox_uniform(const PhiloxKey& key, uint64_t o
 // The helpers below are branch-free: the uniform draw is computed for every
 // element (almost all are interior), so the 32 Philox chains of a chunk are
 // independent instruction streams the scheduler can interleave.
-
-// 1 / g for a power of two g in the normal range (exact).
-__device__ __forceinline__ float recip_pow2(float g) {
-  return __uint_as_float((254u << 23) - __float_as_uint(g));
-}
 
 // _stochastic_float8 (_triton_stochastic_quantization.py:132-175): `v` is the
 // normalized value, already clamped to [-limit, limit] (a NaN became -limit);
@@ -304,20 +273,37 @@ __device__ __forceinline__ uint32_t sr_fp8x4(const float (&v)[4], float limit, c
   return word;
 }
 
-// _stochastic_e2m1_code (_triton_stochastic_quantization.py:109-129).
-__device__ __forceinline__ uint32_t sr_e2m1(float v, uint32_t det, const PhiloxKey& key, uint64_t off) {
-  const float mag = fabsf(v);
-  const uint32_t nc = det & 7u;
-  const bool down = e2m1_mag(nc) > mag;
-  const uint32_t lc = down ? nc - 1u : nc;
-  const uint32_t uc = down ? nc : nc + 1u;
-  const float lv = e2m1_mag(lc);
-  const float uv = e2m1_mag(uc);
-  const float gap = uv - lv;  // 0.5, 1 or 2 inside (0, 6); <= 0 past the top code
-  const float p = gap > 0.0f ? (mag - lv) * recip_pow2(gap) : 0.0f;
-  const float u = philox_uniform(key, off);
-  const bool interior = mag > 0.0f && mag < 6.0f && p > 0.0f;
-  return interior ? ((u < p ? uc : lc) | ((__float_as_uint(v) >> 28) & 8u)) : det;
+// _stochastic_e2m1_code (_triton_stochastic_quantization.py:109-129) for four
+// consecutive elements (offsets off .. off+3) of values already clamped to
+// [-6, 6], as four nibbles (element j in bits 4j .. 4j+3).
+// The lower code lc (largest magnitude <= |v|) and p = (|v| - lv) / gap follow
+// from the fp32 bits: below 0.5 lc = 0 and p = 2|v|; in [0.5, 1) lc = 1 and
+// p = 2|v| - 1; from 1 up, (bits >> 22) - 252 is 2e + 2 + the top mantissa bit
+// = lc and p is the mantissa below its top bit (all exact, as the reference's
+// p is). Where the rounding is not stochastic |v| lies on a code (p == 0) or
+// is 6, and the reference's round-to-nearest code is lc there (7 for 6).
+__device__ __forceinline__ uint32_t sr_e2m1x4(const float (&v)[4], const PhiloxKey& key, uint64_t off) {
+  uint32_t r[4];
+  philox_word0_x4(key, off, r);
+  uint32_t out = 0u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t bits = __float_as_uint(v[j]);
+    const uint32_t abits = bits & 0x7FFFFFFFu;
+    const float mag = __uint_as_float(abits);
+    const bool small = abits < 0x3F000000u;  // |v| < 0.5
+    const bool below1 = abits < 0x3F800000u;  // |v| < 1
+    const uint32_t lc = small ? 0u : min(max((abits >> 22) - 252u, 1u), 7u);
+    const float twice = __fmul_rn(mag, 2.0f);
+    const float p = small ? twice
+                    : below1 ? __fsub_rn(twice, 1.0f)
+                             : __fsub_rn(__uint_as_float(0x3F800000u | ((abits << 1) & 0x7FFFFFu)), 1.0f);
+    const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
+    const float u = __fmul_rn(__int2float_rn(x), __uint_as_float(0x2FFFFFFFu));
+    const bool up = mag < 6.0f && p > 0.0f && u < p;
+    out |= ((lc + (up ? 1u : 0u)) | ((bits >> 28) & 8u)) << (4 * j);
+  }
+  return out;
 }
 
 // _stochastic_round_to_int (_triton_stochastic_quantization.py:24-39);

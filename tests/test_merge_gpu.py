@@ -123,6 +123,68 @@ def test_fp8_group_256(cuda_device):
     check(Case("fp8_group", 130, 1024, 32, group=256, seed=SEED), cuda_device)
 
 
+def _nvfp4_special(fmt, *, strength=1.0, zero_b=False, neg_scales=False, nan_row=None, inf_row=None,
+                   seed=None):
+    cs = Case(fmt, 64, 256, 16, strength=strength, seed=seed).build()
+    b = cs.tensors["b"]
+    if zero_b:
+        b.zero_()
+    if nan_row is not None:
+        b[nan_row, :] = float("nan")
+    if inf_row is not None:
+        b[inf_row, :] = 0.0
+        b[inf_row, 0] = float("inf")
+    if neg_scales:
+        sc = cs.tensors["q"].scale.view(torch.uint8)
+        sc.view(-1)[::3] |= 0x80  # E4M3 block scales with the sign bit set: -0 bases
+    return cs
+
+
+def _check_built(cs: Case, dev, *, exact_rows=None, exact=False):
+    got = cs.run_native(dev)
+    torch.cuda.synchronize(dev)
+    want = cs.run_oracle()
+    d = compare(cs, got, want)
+    allowed = 0 if exact else math.floor(TIE_FRACTION * d.n)
+    assert d.max_step <= 1 and d.code_mismatch <= allowed, d
+    rows = slice(None) if exact else exact_rows
+    if rows is not None:
+        # Raw bytes: the code comparison above treats +0 and -0 (codes 0 and 8) alike.
+        assert np.array_equal(got["q"][rows], want["q"][rows]), "E2M1 bytes differ"
+        assert np.array_equal(got["scale"][rows], want["scale"][rows]), "block scales differ"
+    if want.get("global") is not None:
+        assert np.float32(got["global"]).tobytes() == np.float32(want["global"]).tobytes()
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "nvfp4_1l"])
+def test_nvfp4_zero_updates_keep_signed_bases(fmt, cuda_device):
+    """acc = 0 everywhere: the reference keeps each base, -0 included (negative block scales)."""
+    _check_built(_nvfp4_special(fmt, zero_b=True, neg_scales=True), cuda_device, exact=True)
+    _check_built(_nvfp4_special(fmt, zero_b=True, neg_scales=True, seed=SEED), cuda_device, exact=True)
+
+
+@pytest.mark.parametrize("fmt", ["mxfp4", "mxfp8"])
+def test_mx_sr_zero_updates_exact(fmt, cuda_device):
+    """Zero updates leave every normalized value on the code grid: no stochastic step."""
+    cs = Case(fmt, 64, 256, 16, seed=SEED).build()
+    cs.tensors["b"].zero_()
+    _check_built(cs, cuda_device, exact=True)
+
+
+@pytest.mark.parametrize("strength", [2.0 ** 70, 2.0 ** -70, -(2.0 ** 61)])
+@pytest.mark.parametrize("fmt", ["nvfp4", "nvfp4_1l"])
+def test_nvfp4_extreme_strengths(fmt, strength, cuda_device):
+    """Strengths outside [2^-60, 2^60] take the exact update-is-zero test for every block."""
+    _check_built(_nvfp4_special(fmt, strength=strength, neg_scales=True), cuda_device)
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "nvfp4_1l"])
+def test_nvfp4_nan_and_inf_updates(fmt, cuda_device):
+    """A NaN row and an infinite row of B: those rows match the oracle byte for byte."""
+    cs = _nvfp4_special(fmt, nan_row=5, inf_row=9, neg_scales=True)
+    _check_built(cs, cuda_device, exact_rows=[5, 9])
+
+
 def test_in_place_identity(cuda_device):
     """Storage tensors keep their data pointers (reference asserts this identity)."""
     c = Case("fp8_row", 64, 256, 16).build()
