@@ -581,17 +581,17 @@ __device__ __forceinline__ void int8_encode32(const float (&m)[32], const Int8Q&
                                               uint32_t (&out)[8]) {
   float inv = div_full(1.0f, q.scale);
   inv = round_dt_rt(inv, scale_dt);
-  float x[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) x[i] = __fmul_rn(m[i], inv);
-  if (scale_dt == kBF16) {  // one dispatch per chunk
-#pragma unroll
-    for (int i = 0; i < 32; i += 2) bf16r2(x[i], x[i + 1]);
-  } else if (scale_dt == kF16) {
-#pragma unroll
-    for (int i = 0; i < 32; i += 2) f16r2(x[i], x[i + 1]);
-  }
   if (!sr) {
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = __fmul_rn(m[i], inv);
+    if (scale_dt == kBF16) {  // one dispatch per chunk
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) bf16r2(x[i], x[i + 1]);
+    } else if (scale_dt == kF16) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) f16r2(x[i], x[i + 1]);
+    }
     // Round to nearest in the integer domain: for |x| < 2^22 the bits of
     // x + 1.5 * 2^23 minus those of 1.5 * 2^23 are rint(x); a chunk holding a
     // NaN or a larger value takes the general path below.
@@ -613,24 +613,34 @@ __device__ __forceinline__ void int8_encode32(const float (&m)[32], const Int8Q&
     }
   }
   const float zpf = static_cast<float>(q.zp);
+  const float qlo = static_cast<float>(qmin), qhi = static_cast<float>(qmax);
 #pragma unroll
-  for (int w = 0; w < 8; ++w) out[w] = 0u;
+  for (int w = 0; w < 8; ++w) {
+    float xs[4], qq[4];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    // rint (half to even) of |x| < 2^22 via the 1.5 * 2^23 magic addend.
-    float qf;
-    if (fabsf(x[i]) < 4194304.0f) {
-      const float y = __fadd_rn(x[i], 12582912.0f);
-      qf = static_cast<float>(static_cast<int>(__float_as_uint(y) - 0x4B400000u) + q.zp);
-    } else {
-      qf = static_cast<float>(__float2ll_rn(x[i]) + q.zp);
+    for (int j = 0; j < 4; ++j) xs[j] = __fmul_rn(m[4 * w + j], inv);
+    round_rt2(xs[0], xs[1], scale_dt);
+    round_rt2(xs[2], xs[3], scale_dt);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // rint (half to even) of |x| < 2^22 via the 1.5 * 2^23 magic addend;
+      // the sum with zp is exact in fp32 there.
+      const float xi = xs[j];
+      if (fabsf(xi) < 4194304.0f) qq[j] = __fadd_rn(__fsub_rn(__fadd_rn(xi, 12582912.0f), 12582912.0f), zpf);
+      else qq[j] = static_cast<float>(__float2ll_rn(xi) + q.zp);
     }
     if (sr) {
-      const float ss = __fadd_rn(div_full(m[i], q.scale), zpf);
-      qf = sr_int(ss, qf, static_cast<float>(qmin), static_cast<float>(qmax), key, off0 + i);
+      float ss[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss[j] = __fadd_rn(div_full(m[4 * w + j], q.scale), zpf);
+      sr_int_x4(ss, qq, qlo, qhi, key, off0 + 4 * w);
     }
-    qf = fminf(fmaxf(qf, static_cast<float>(qmin)), static_cast<float>(qmax));
-    out[i >> 2] |= (static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu) << ((i & 3) * 8);
+    // Clamped codes are integers in [-128, 255]: the low byte of the bits of
+    // q + 1.5 * 2^23 is q mod 256.
+    uint32_t qb[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) qb[j] = __float_as_uint(__fadd_rn(fminf(fmaxf(qq[j], qlo), qhi), 12582912.0f));
+    out[w] = __byte_perm(__byte_perm(qb[0], qb[1], 0x0040), __byte_perm(qb[2], qb[3], 0x0040), 0x5410);
   }
 }
 
@@ -723,21 +733,26 @@ __device__ __forceinline__ void flavor_int8_encode32(int flavor, const float (&m
     }
   }
 #pragma unroll
-  for (int w = 0; w < 8; ++w) out[w] = 0u;
+  for (int w = 0; w < 8; ++w) {
+    float ss[4], qq[4];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    float ss, x;
-    if (flavor == kBnb) {
-      ss = s == 0.0f ? 0.0f : __fmul_rn(div_full(m[i], s), 127.0f);
-      x = ss;
-    } else {
-      ss = div_full(m[i], s);
-      x = round_dt<CDT>(ss);
+    for (int j = 0; j < 4; ++j) {
+      const float mi = m[4 * w + j];
+      float x;
+      if (flavor == kBnb) {
+        ss[j] = s == 0.0f ? 0.0f : __fmul_rn(div_full(mi, s), 127.0f);
+        x = ss[j];
+      } else {
+        ss[j] = div_full(mi, s);
+        x = round_dt<CDT>(ss[j]);
+      }
+      qq[j] = rintf(x);
     }
-    float qf = rintf(x);
-    if (sr) qf = sr_int(ss, qf, lo, 127.0f, key, off0 + i);
-    qf = fminf(fmaxf(qf, lo), 127.0f);
-    out[i >> 2] |= (static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu) << ((i & 3) * 8);
+    if (sr) sr_int_x4(ss, qq, lo, 127.0f, key, off0 + 4 * w);
+    uint32_t qb[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) qb[j] = __float_as_uint(__fadd_rn(fminf(fmaxf(qq[j], lo), 127.0f), 12582912.0f));
+    out[w] = __byte_perm(__byte_perm(qb[0], qb[1], 0x0040), __byte_perm(qb[2], qb[3], 0x0040), 0x5410);
   }
 }
 
@@ -1381,13 +1396,21 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
         qb[i] = static_cast<uint32_t>(min(max(x[i] < 0.0f ? -b : b, -128), 127));
       }
     } else {
+      float q[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float q = roundf_away(x[i]);
-        if (sr) q = sr_int(x[i], q, -127.0f, 127.0f, key, off0 + i);
-        q = fminf(fmaxf(q, -128.0f), 127.0f);
-        qb[i] = float_int_bits(q);
+      for (int i = 0; i < 32; ++i) q[i] = roundf_away(x[i]);
+      if (sr) {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const float v[4] = {x[4 * w], x[4 * w + 1], x[4 * w + 2], x[4 * w + 3]};
+          float qq[4] = {q[4 * w], q[4 * w + 1], q[4 * w + 2], q[4 * w + 3]};
+          sr_int_x4(v, qq, -127.0f, 127.0f, key, off0 + 4 * w);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) q[4 * w + j] = qq[j];
+        }
       }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) qb[i] = float_int_bits(fminf(fmaxf(q[i], -128.0f), 127.0f));
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) ow[j] = pack_low_bytes(qb[4 * j], qb[4 * j + 1], qb[4 * j + 2], qb[4 * j + 3]);
@@ -1447,14 +1470,25 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
       for (int i = 0; i < 32; ++i)
         qb[i] = min(__float_as_uint(__fadd_rz(y[i], 8388608.0f)) - 0x4B000000u, 15u);
     } else {
+      float qf[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float x = __fmul_rn(merged[i], id);
-        float qf = truncf(y[i]);
-        if (sr) qf = sr_int(__fadd_rn(x, 8.0f), qf, 0.0f, 15.0f, key, off0 + i);
-        qf = fminf(fmaxf(qf, 0.0f), 15.0f);
-        qb[i] = float_int_bits(qf);
+      for (int i = 0; i < 32; ++i) qf[i] = truncf(y[i]);
+      if (sr) {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          float v[4], qq[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            v[j] = __fadd_rn(__fmul_rn(merged[4 * w + j], id), 8.0f);
+            qq[j] = qf[4 * w + j];
+          }
+          sr_int_x4(v, qq, 0.0f, 15.0f, key, off0 + 4 * w);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) qf[4 * w + j] = qq[j];
+        }
       }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) qb[i] = float_int_bits(fminf(fmaxf(qf[i], 0.0f), 15.0f));
     }
     // byte j = element j (low nibble) | element j+16 (high nibble)
 #pragma unroll

@@ -317,6 +317,25 @@ __device__ __forceinline__ float sr_int(float v, float det, float qmin, float qm
   return interior ? __fadd_rn(lower, u < p ? 1.0f : 0.0f) : det;
 }
 
+// sr_int for four consecutive elements (offsets off .. off+3): q[j] holds the
+// round-to-nearest value on entry and the result on exit. qmin and qmax lie
+// within +-2^22, so an interior v does too, and there floor(v) is the fp32
+// sum v + 1.5 * 2^23 rounded down, less 1.5 * 2^23 (both steps exact).
+__device__ __forceinline__ void sr_int_x4(const float (&v)[4], float (&q)[4], float qmin, float qmax,
+                                          const PhiloxKey& key, uint64_t off) {
+  uint32_t r[4];
+  philox_word0_x4(key, off, r);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float lower = __fsub_rn(__fadd_rd(v[j], 12582912.0f), 12582912.0f);
+    const float p = __fsub_rn(v[j], lower);
+    const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
+    const float u = __fmul_rn(__int2float_rn(x), __uint_as_float(0x2FFFFFFFu));
+    const bool interior = v[j] > qmin && v[j] < qmax && p > 0.0f;
+    q[j] = interior ? __fadd_rn(lower, u < p ? 1.0f : 0.0f) : q[j];
+  }
+}
+
 }  // namespace pm
 
 namespace pm {
