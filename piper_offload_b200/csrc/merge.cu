@@ -398,11 +398,14 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
     uint32_t out[8];
     if (sr) {
 #pragma unroll
-      for (int w = 0; w < 8; ++w) out[w] = 0u;
+      for (int w8 = 0; w8 < 4; ++w8) {
+        float x[8];
 #pragma unroll
-      for (int w4 = 0; w4 < 8; ++w4) {
-        const float x[4] = {merged[4 * w4], merged[4 * w4 + 1], merged[4 * w4 + 2], merged[4 * w4 + 3]};
-        out[w4] = sr_fp8x4<kE4>(x, P::kMax, key, off0 + 4 * w4);
+        for (int j = 0; j < 8; ++j) x[j] = merged[8 * w8 + j];
+        uint32_t wd[2];
+        sr_fp8xn<kE4, 8>(x, P::kMax, key, off0 + 8 * w8, wd);
+        out[2 * w8] = wd[0];
+        out[2 * w8 + 1] = wd[1];
       }
     } else {
 #pragma unroll
@@ -762,14 +765,22 @@ template <bool E4M3, int CDT>
 __device__ __forceinline__ void quanto_fp8_encode32(const float (&m)[32], float s, float limit, bool sr,
                                                     const PhiloxKey& key, uint64_t off0, uint32_t (&out)[8]) {
 #pragma unroll
-  for (int w4 = 0; w4 < 8; ++w4) {
-    float x[4];
+  for (int w8 = 0; w8 < 4; ++w8) {
+    float x[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float q = div_full(m[4 * w4 + j], s);
+    for (int j = 0; j < 8; ++j) {
+      const float q = div_full(m[8 * w8 + j], s);
       x[j] = fminf(fmaxf(sr ? q : round_dt<CDT>(q), -limit), limit);
     }
-    out[w4] = sr ? sr_fp8x4<E4M3>(x, limit, key, off0 + 4 * w4) : enc_fp8x4<E4M3>(x[0], x[1], x[2], x[3]);
+    if (sr) {
+      uint32_t wd[2];
+      sr_fp8xn<E4M3, 8>(x, limit, key, off0 + 8 * w8, wd);
+      out[2 * w8] = wd[0];
+      out[2 * w8 + 1] = wd[1];
+    } else {
+      out[2 * w8] = enc_fp8x4<E4M3>(x[0], x[1], x[2], x[3]);
+      out[2 * w8 + 1] = enc_fp8x4<E4M3>(x[4], x[5], x[6], x[7]);
+    }
   }
 }
 
@@ -890,6 +901,23 @@ __device__ __forceinline__ void affine_merged_u(const DevWeight& W, const RowCtx
   for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], st, merged[i]);
 #pragma unroll
   for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+}
+
+// Stochastic FP8 codes of 32 values: clamp(m / s) (div.full) rounded with
+// eight Philox counters per batch, so eight multiply chains are in flight.
+template <bool E4M3>
+__device__ __forceinline__ void fp8_encode_sr(const float (&m)[32], float s, float limit, const PhiloxKey& key,
+                                              uint64_t off0, uint32_t (&out)[8]) {
+#pragma unroll
+  for (int w8 = 0; w8 < 4; ++w8) {
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = fminf(fmaxf(div_full(m[8 * w8 + j], s), -limit), limit);
+    uint32_t wd[2];
+    sr_fp8xn<E4M3, 8>(x, limit, key, off0 + 8 * w8, wd);
+    out[2 * w8] = wd[0];
+    out[2 * w8 + 1] = wd[1];
+  }
 }
 
 // FP8 codes of 32 merged values for one scale `s` (round to nearest).
@@ -2277,14 +2305,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
                 } else if constexpr (kFlv == kQuanto) {
                   quanto_fp8_encode32<kE4, CDT>(merged, f_s, kLimit, sr_on, key, off0, out);
                 } else if (sr_on) {
-#pragma unroll
-                  for (int w4 = 0; w4 < 8; ++w4) {
-                    float x[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                      x[j] = fminf(fmaxf(div_full(merged[4 * w4 + j], f_s), -kLimit), kLimit);
-                    out[w4] = sr_fp8x4<kE4>(x, kLimit, key, off0 + 4 * w4);
-                  }
+                  fp8_encode_sr<kE4>(merged, f_s, kLimit, key, off0, out);
                 } else {
                   fp8_encode_rtn<kE4>(merged, f_s, kLimit, out);
                 }
@@ -2346,14 +2367,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
                                       static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) +
                                       c0 + 32 * k;
                 if (W.flags & PIPER_FLAG_STOCHASTIC) {
-#pragma unroll
-                  for (int w4 = 0; w4 < 8; ++w4) {
-                    float x[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                      x[j] = fminf(fmaxf(div_full(merged[4 * w4 + j], s), -kLimit), kLimit);
-                    out[w4] = sr_fp8x4<kE4>(x, kLimit, key, off0 + 4 * w4);
-                  }
+                  fp8_encode_sr<kE4>(merged, s, kLimit, key, off0, out);
                 } else {
                   fp8_encode_rtn<kE4>(merged, s, kLimit, out);
                 }
@@ -2471,14 +2485,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
                   if constexpr (kFlv == kQuanto) {
                     quanto_fp8_encode32<kE4, CDT>(merged, s, kLimit, sr_on, key, off0, out);
                   } else if (sr_on) {
-#pragma unroll
-                    for (int w4 = 0; w4 < 8; ++w4) {
-                      float x[4];
-#pragma unroll
-                      for (int j = 0; j < 4; ++j)
-                        x[j] = fminf(fmaxf(div_full(merged[4 * w4 + j], s), -kLimit), kLimit);
-                      out[w4] = sr_fp8x4<kE4>(x, kLimit, key, off0 + 4 * w4);
-                    }
+                    fp8_encode_sr<kE4>(merged, s, kLimit, key, off0, out);
                   } else {
                     fp8_encode_rtn<kE4>(merged, s, kLimit, out);
                   }

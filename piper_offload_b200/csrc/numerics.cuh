@@ -165,14 +165,15 @@ __device__ __forceinline__ uint32_t sr_fp8(float v, float limit, const PhiloxKey
   return (lo + (up ? 1u : 0u)) | ((bits >> 24) & 0x80u);
 }
 
-// Four consecutive counters advanced round by round, so the four independent
+// N consecutive counters advanced round by round, so the N independent
 // multiply chains issue back to back.
-__device__ __forceinline__ void philox_word0_x4(const PhiloxKey& key, uint64_t offset, uint32_t (&w)[4]) {
+template <int N>
+__device__ __forceinline__ void philox_word0_xn(const PhiloxKey& key, uint64_t offset, uint32_t (&w)[N]) {
   // Round 0 with counter words 2 and 3 zero: the second multiply is zero.
-  uint32_t c0[4], c1[4], c2[4], c3[4];
+  uint32_t c0[N], c1[N], c2[N], c3[N];
   const uint32_t hi0 = static_cast<uint32_t>(offset >> 32);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < N; ++j) {
     const uint64_t o = offset + static_cast<uint64_t>(j);
     const uint32_t lo = static_cast<uint32_t>(o);
     c0[j] = static_cast<uint32_t>(o >> 32) ^ key.k0[0];
@@ -180,26 +181,26 @@ __device__ __forceinline__ void philox_word0_x4(const PhiloxKey& key, uint64_t o
     c1[j] = 0u;
     c3[j] = 0xD2511F53u * lo;
   }
-  // Round 1: word 0 is (offset >> 32) ^ key, the same for the four counters
+  // Round 1: word 0 is (offset >> 32) ^ key, the same for the N counters
   // unless they straddle a multiple of 2^32, so its product is formed once.
-  uint32_t ha[4], la[4];
-  if (static_cast<uint32_t>((offset + 3u) >> 32) == hi0) {
+  uint32_t ha[N], la[N];
+  if (static_cast<uint32_t>((offset + static_cast<uint64_t>(N - 1)) >> 32) == hi0) {
     const uint32_t h = __umulhi(0xD2511F53u, c0[0]);
     const uint32_t l = 0xD2511F53u * c0[0];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < N; ++j) {
       ha[j] = h;
       la[j] = l;
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < N; ++j) {
       ha[j] = __umulhi(0xD2511F53u, c0[j]);
       la[j] = 0xD2511F53u * c0[j];
     }
   }
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < N; ++j) {
     const uint32_t hb = __umulhi(0xCD9E8D57u, c2[j]);
     const uint32_t lb = 0xCD9E8D57u * c2[j];
     c0[j] = hb ^ c1[j] ^ key.k0[1];
@@ -210,7 +211,7 @@ __device__ __forceinline__ void philox_word0_x4(const PhiloxKey& key, uint64_t o
 #pragma unroll
   for (int round = 2; round < 10; ++round) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < N; ++j) {
       const uint32_t hb = __umulhi(0xCD9E8D57u, c2[j]);
       const uint32_t lb = 0xCD9E8D57u * c2[j];
       const uint32_t hm = __umulhi(0xD2511F53u, c0[j]);
@@ -222,25 +223,30 @@ __device__ __forceinline__ void philox_word0_x4(const PhiloxKey& key, uint64_t o
     }
   }
 #pragma unroll
-  for (int j = 0; j < 4; ++j) w[j] = c0[j];
+  for (int j = 0; j < N; ++j) w[j] = c0[j];
 }
 
-// sr_fp8 for four consecutive elements (offsets off .. off+3), packed as the
-// little-endian bytes of one word; same arithmetic as sr_fp8.
-template <bool E4M3>
-__device__ __forceinline__ uint32_t sr_fp8x4(const float (&v)[4], float limit, const PhiloxKey& key, uint64_t off) {
+__device__ __forceinline__ void philox_word0_x4(const PhiloxKey& key, uint64_t offset, uint32_t (&w)[4]) {
+  philox_word0_xn<4>(key, offset, w);
+}
+
+// sr_fp8 for N consecutive elements (offsets off .. off+N-1), packed four to
+// a word as little-endian bytes; same arithmetic as sr_fp8.
+template <bool E4M3, int N>
+__device__ __forceinline__ void sr_fp8xn(const float (&v)[N], float limit, const PhiloxKey& key, uint64_t off,
+                                         uint32_t (&words)[N / 4]) {
   constexpr int kMant = E4M3 ? 3 : 2;
   constexpr int kDrop = 23 - kMant;
   constexpr uint32_t kMinNormal = E4M3 ? 0x3C800000u : 0x38800000u;
   constexpr uint32_t kBiasFix = (127u - (E4M3 ? 7u : 15u)) << kMant;
   constexpr float kSubScale = E4M3 ? 512.0f : 65536.0f;
-  uint32_t r[4];
-  philox_word0_x4(key, off, r);
-  uint32_t lo[4];
-  float p[4];
+  uint32_t r[N];
+  philox_word0_xn<N>(key, off, r);
+  uint32_t lo[N];
+  float p[N];
   bool sub = false;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < N; ++j) {
     const uint32_t abits = __float_as_uint(v[j]) & 0x7FFFFFFFu;
     lo[j] = (abits >> kDrop) - kBiasFix;
     p[j] = __uint_as_float(0x3F800000u | ((abits << kMant) & 0x7FFFFFu)) - 1.0f;
@@ -250,7 +256,7 @@ __device__ __forceinline__ uint32_t sr_fp8x4(const float (&v)[4], float limit, c
   // that path runs only when a lane of the active part of the warp needs it.
   if (__any_sync(__activemask(), sub)) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < N; ++j) {
       const uint32_t abits = __float_as_uint(v[j]) & 0x7FFFFFFFu;
       const float t = __uint_as_float(abits) * kSubScale;
       const float fl = truncf(t);
@@ -260,17 +266,17 @@ __device__ __forceinline__ uint32_t sr_fp8x4(const float (&v)[4], float limit, c
       }
     }
   }
-  uint32_t word = 0u;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int w = 0; w < N / 4; ++w) words[w] = 0u;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
     const uint32_t bits = __float_as_uint(v[j]);
     const float mag = __uint_as_float(bits & 0x7FFFFFFFu);
     const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
     const float u = __fmul_rn(__int2float_rn(x), __uint_as_float(0x2FFFFFFFu));
     const bool up = mag < limit && p[j] > 0.0f && u < p[j];
-    word |= ((lo[j] + (up ? 1u : 0u)) | ((bits >> 24) & 0x80u)) << (8 * j);
+    words[j >> 2] |= ((lo[j] + (up ? 1u : 0u)) | ((bits >> 24) & 0x80u)) << (8 * (j & 3));
   }
-  return word;
 }
 
 // _stochastic_e2m1_code (_triton_stochastic_quantization.py:109-129) for four
