@@ -384,9 +384,13 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
     uint32_t out[4] = {0u, 0u, 0u, 0u};
     if (sr) {
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        const float v[4] = {merged[4 * w], merged[4 * w + 1], merged[4 * w + 2], merged[4 * w + 3]};
-        out[w >> 1] |= sr_e2m1x4(v, key, off0 + 4 * w) << ((w & 1) * 16);
+      for (int w = 0; w < 4; ++w) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = merged[8 * w + j];
+        uint32_t nib[1];
+        sr_e2m1xn<8>(v, key, off0 + 8 * w, nib);
+        out[w] = nib[0];
       }
     } else {
 #pragma unroll
@@ -495,9 +499,13 @@ __device__ __forceinline__ void nvfp4_block(const DevWeight& W, const RowCtx& c,
       const uint64_t off0 =
           W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const float v[4] = {m[4 * w], m[4 * w + 1], m[4 * w + 2], m[4 * w + 3]};
-        out[w >> 1] |= sr_e2m1x4(v, key, off0 + 4 * w) << ((w & 1) * 16);
+      for (int w = 0; w < 2; ++w) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = m[8 * w + j];
+        uint32_t nib[1];
+        sr_e2m1xn<8>(v, key, off0 + 8 * w, nib);
+        out[w] = nib[0];
       }
     } else {
 #pragma unroll
@@ -636,7 +644,7 @@ __device__ __forceinline__ void int8_encode32(const float (&m)[32], const Int8Q&
       float ss[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) ss[j] = __fadd_rn(div_full(m[4 * w + j], q.scale), zpf);
-      sr_int_x4(ss, qq, qlo, qhi, key, off0 + 4 * w);
+      sr_int_xn<4>(ss, qq, qlo, qhi, key, off0 + 4 * w);
     }
     // Clamped codes are integers in [-128, 255]: the low byte of the bits of
     // q + 1.5 * 2^23 is q mod 256.
@@ -751,7 +759,7 @@ __device__ __forceinline__ void flavor_int8_encode32(int flavor, const float (&m
       }
       qq[j] = rintf(x);
     }
-    if (sr) sr_int_x4(ss, qq, lo, 127.0f, key, off0 + 4 * w);
+    if (sr) sr_int_xn<4>(ss, qq, lo, 127.0f, key, off0 + 4 * w);
     uint32_t qb[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) qb[j] = __float_as_uint(__fadd_rn(fminf(fmaxf(qq[j], lo), 127.0f), 12582912.0f));
@@ -1429,12 +1437,16 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
       for (int i = 0; i < 32; ++i) q[i] = roundf_away(x[i]);
       if (sr) {
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const float v[4] = {x[4 * w], x[4 * w + 1], x[4 * w + 2], x[4 * w + 3]};
-          float qq[4] = {q[4 * w], q[4 * w + 1], q[4 * w + 2], q[4 * w + 3]};
-          sr_int_x4(v, qq, -127.0f, 127.0f, key, off0 + 4 * w);
+        for (int w = 0; w < 4; ++w) {
+          float v[8], qq[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) q[4 * w + j] = qq[j];
+          for (int j = 0; j < 8; ++j) {
+            v[j] = x[8 * w + j];
+            qq[j] = q[8 * w + j];
+          }
+          sr_int_xn<8>(v, qq, -127.0f, 127.0f, key, off0 + 8 * w);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) q[8 * w + j] = qq[j];
         }
       }
 #pragma unroll
@@ -1503,16 +1515,16 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
       for (int i = 0; i < 32; ++i) qf[i] = truncf(y[i]);
       if (sr) {
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          float v[4], qq[4];
+        for (int w = 0; w < 4; ++w) {
+          float v[8], qq[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            v[j] = __fadd_rn(__fmul_rn(merged[4 * w + j], id), 8.0f);
-            qq[j] = qf[4 * w + j];
+          for (int j = 0; j < 8; ++j) {
+            v[j] = __fadd_rn(__fmul_rn(merged[8 * w + j], id), 8.0f);
+            qq[j] = qf[8 * w + j];
           }
-          sr_int_x4(v, qq, 0.0f, 15.0f, key, off0 + 4 * w);
+          sr_int_xn<8>(v, qq, 0.0f, 15.0f, key, off0 + 8 * w);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) qf[4 * w + j] = qq[j];
+          for (int j = 0; j < 8; ++j) qf[8 * w + j] = qq[j];
         }
       }
 #pragma unroll

@@ -279,21 +279,24 @@ __device__ __forceinline__ void sr_fp8xn(const float (&v)[N], float limit, const
   }
 }
 
-// _stochastic_e2m1_code (_triton_stochastic_quantization.py:109-129) for four
-// consecutive elements (offsets off .. off+3) of values already clamped to
-// [-6, 6], as four nibbles (element j in bits 4j .. 4j+3).
+// _stochastic_e2m1_code (_triton_stochastic_quantization.py:109-129) for N
+// consecutive elements (offsets off .. off+N-1) of values already clamped to
+// [-6, 6], as nibbles (element j in bits 4j .. 4j+3 of word j / 8).
 // The lower code lc (largest magnitude <= |v|) and p = (|v| - lv) / gap follow
 // from the fp32 bits: below 0.5 lc = 0 and p = 2|v|; in [0.5, 1) lc = 1 and
 // p = 2|v| - 1; from 1 up, (bits >> 22) - 252 is 2e + 2 + the top mantissa bit
 // = lc and p is the mantissa below its top bit (all exact, as the reference's
 // p is). Where the rounding is not stochastic |v| lies on a code (p == 0) or
 // is 6, and the reference's round-to-nearest code is lc there (7 for 6).
-__device__ __forceinline__ uint32_t sr_e2m1x4(const float (&v)[4], const PhiloxKey& key, uint64_t off) {
-  uint32_t r[4];
-  philox_word0_x4(key, off, r);
-  uint32_t out = 0u;
+template <int N>
+__device__ __forceinline__ void sr_e2m1xn(const float (&v)[N], const PhiloxKey& key, uint64_t off,
+                                          uint32_t (&out)[(N + 7) / 8]) {
+  uint32_t r[N];
+  philox_word0_xn<N>(key, off, r);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int w = 0; w < (N + 7) / 8; ++w) out[w] = 0u;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
     const uint32_t bits = __float_as_uint(v[j]);
     const uint32_t abits = bits & 0x7FFFFFFFu;
     const float mag = __uint_as_float(abits);
@@ -307,9 +310,8 @@ __device__ __forceinline__ uint32_t sr_e2m1x4(const float (&v)[4], const PhiloxK
     const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
     const float u = __fmul_rn(__int2float_rn(x), __uint_as_float(0x2FFFFFFFu));
     const bool up = mag < 6.0f && p > 0.0f && u < p;
-    out |= ((lc + (up ? 1u : 0u)) | ((bits >> 28) & 8u)) << (4 * j);
+    out[j >> 3] |= ((lc + (up ? 1u : 0u)) | ((bits >> 28) & 8u)) << (4 * (j & 7));
   }
-  return out;
 }
 
 // _stochastic_round_to_int (_triton_stochastic_quantization.py:24-39);
@@ -323,16 +325,17 @@ __device__ __forceinline__ float sr_int(float v, float det, float qmin, float qm
   return interior ? __fadd_rn(lower, u < p ? 1.0f : 0.0f) : det;
 }
 
-// sr_int for four consecutive elements (offsets off .. off+3): q[j] holds the
+// sr_int for N consecutive elements (offsets off .. off+N-1): q[j] holds the
 // round-to-nearest value on entry and the result on exit. qmin and qmax lie
 // within +-2^22, so an interior v does too, and there floor(v) is the fp32
 // sum v + 1.5 * 2^23 rounded down, less 1.5 * 2^23 (both steps exact).
-__device__ __forceinline__ void sr_int_x4(const float (&v)[4], float (&q)[4], float qmin, float qmax,
+template <int N>
+__device__ __forceinline__ void sr_int_xn(const float (&v)[N], float (&q)[N], float qmin, float qmax,
                                           const PhiloxKey& key, uint64_t off) {
-  uint32_t r[4];
-  philox_word0_x4(key, off, r);
+  uint32_t r[N];
+  philox_word0_xn<N>(key, off, r);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < N; ++j) {
     const float lower = __fsub_rn(__fadd_rd(v[j], 12582912.0f), 12582912.0f);
     const float p = __fsub_rn(v[j], lower);
     const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
