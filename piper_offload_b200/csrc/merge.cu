@@ -1565,25 +1565,23 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
 // full / empty mbarrier pairs. Every wait is bounded (ptx.cuh); a role whose
 // wait gives up stops issuing work and the others then give up in turn, so
 // the CTA always reaches its exit.
-// Epilogue warpgroups per format (tile t -> warpgroup t % EW). Three give the
-// epilogue more warps in flight; GGUF keeps two so that its 256-column tiles
-// (the narrowest whose rows are 16-byte multiples) fit two accumulators, and
-// NVFP4 keeps two for its register-heavy two-level blocks.
-template <int FMT>
-__host__ __device__ constexpr int epi_wgs() {
-  return (FMT == PIPER_FMT_GGUF_Q8_0 || FMT == PIPER_FMT_GGUF_Q4_0 || FMT == PIPER_FMT_NVFP4 ||
-          FMT == PIPER_FMT_BNB4_NF4 || FMT == PIPER_FMT_BNB4_FP4)
+// Epilogue warpgroups per format and tile width (tile t -> warpgroup t % EW).
+// Three give the epilogue more warps in flight; GGUF keeps two so that its
+// 256-column tiles (the narrowest whose rows are 16-byte multiples) fit two
+// accumulators, and bitsandbytes 4-bit keeps two for its per-lane tables.
+// NVFP4 runs two on 256-column tiles (round to nearest: fewer, wider tiles
+// measured faster) and three on narrower ones (stochastic rounding, where the
+// Philox draws want the extra warps).
+__host__ __device__ constexpr int epi_wgs_rt(int fmt, int bn) {
+  return (fmt == PIPER_FMT_GGUF_Q8_0 || fmt == PIPER_FMT_GGUF_Q4_0 || fmt == PIPER_FMT_BNB4_NF4 ||
+          fmt == PIPER_FMT_BNB4_FP4 || (fmt == PIPER_FMT_NVFP4 && bn >= 256))
              ? 2
              : 3;
 }
-__host__ __device__ constexpr int epi_wgs_rt(int fmt) {
-  return (fmt == PIPER_FMT_GGUF_Q8_0 || fmt == PIPER_FMT_GGUF_Q4_0 || fmt == PIPER_FMT_NVFP4 ||
-          fmt == PIPER_FMT_BNB4_NF4 || fmt == PIPER_FMT_BNB4_FP4)
-             ? 2
-             : 3;
-}
-template <int FMT>
-__host__ __device__ constexpr int ws_threads() { return 128 * (1 + epi_wgs<FMT>()); }
+template <int FMT, int BN>
+__host__ __device__ constexpr int epi_wgs() { return epi_wgs_rt(FMT, BN); }
+template <int FMT, int BN>
+__host__ __device__ constexpr int ws_threads() { return 128 * (1 + epi_wgs<FMT, BN>()); }
 constexpr int kLoadThreads = 64;  // warps 2-3
 constexpr int kMaxStages = 8;    // code stages
 constexpr int kMaxAStages = 4;
@@ -1591,11 +1589,11 @@ constexpr int kMaxAcc = 8;        // accumulator buffers: 512 tensor-memory colu
 constexpr uint32_t kCtrlRegs = 56;
 // Registers per epilogue thread after the control warpgroup gives up its share
 // (launch allocation: threads x (65536 / threads rounded down to 8)).
-template <int FMT>
+template <int FMT, int BN>
 __host__ __device__ constexpr uint32_t epi_regs() {
-  constexpr uint32_t threads = ws_threads<FMT>();
+  constexpr uint32_t threads = ws_threads<FMT, BN>();
   constexpr uint32_t launch = (65536u / threads) / 8u * 8u;
-  return ((threads * launch - 128u * kCtrlRegs) / (128u * epi_wgs<FMT>())) / 8u * 8u;
+  return ((threads * launch - 128u * kCtrlRegs) / (128u * epi_wgs<FMT, BN>())) / 8u * 8u;
 }
 constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 
@@ -1678,8 +1676,8 @@ __device__ __forceinline__ uint32_t swizzle_xor(int r, int row_bytes) {
 }
 
 template <int FMT, int PASS, int BN, int CDT>
-__global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __grid_constant__ LaunchParams P) {
-  constexpr int kEpiWGs = epi_wgs<FMT>();
+__global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const __grid_constant__ LaunchParams P) {
+  constexpr int kEpiWGs = epi_wgs<FMT, BN>();
   using G = TileGeom<FMT, BN>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
@@ -2002,7 +2000,7 @@ __global__ void __launch_bounds__(ws_threads<FMT>(), 1) merge_kernel(const __gri
   }
   } else {
     // ---------------------------------------------------------------- epilogue
-    regs_inc<epi_regs<FMT>()>();
+    regs_inc<epi_regs<FMT, BN>()>();
     const int e = tid - 128;
     const int rt = e & 127;         // tile row / tensor-memory lane of this thread
     const int wg = e >> 7;          // processes tiles t with t % kEpiWGs == wg
@@ -2892,9 +2890,12 @@ int validate(const piper_merge_desc& d, Plan& p) {
   // (large ranks) may run with two.
   const int kp = pm::align_up(static_cast<int>(d.rank), 16);
   auto fits = [&](int bn, int min_sc) {
-    return 512 / bn >= pm::epi_wgs_rt(d.format) && plan_pipe(d.format, bn, kp).sc >= min_sc;
+    return 512 / bn >= pm::epi_wgs_rt(d.format, bn) && plan_pipe(d.format, bn, kp).sc >= min_sc;
   };
-  if (fits(256, 4)) p.bn = 256;
+  // Stochastic NVFP4 takes 128-column tiles and their third epilogue warpgroup.
+  const bool nvfp4_sr = d.format == PIPER_FMT_NVFP4 && (d.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+  if (nvfp4_sr && fits(128, 4)) p.bn = 128;
+  else if (fits(256, 4)) p.bn = 256;
   else if (fits(128, 4)) p.bn = 128;
   else if (fits(64, 2)) p.bn = 64;
   else return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(d.rank) + " is too large for the merge pipeline.");
@@ -2949,7 +2950,7 @@ int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
   if (std::getenv("PIPER_MERGE_DEBUG") != nullptr)
     std::fprintf(stderr, "[piper-merge] fmt=%d pass=%d bn=%d kp=%d stages=%d/%d/%d smem=%d items=%d grid=%d\n", FMT,
                  PASS, BN, kp_max, pc.sc, pc.sa, pc.nbb, smem, items, grid);
-  kern<<<grid, pm::ws_threads<FMT>(), smem, stream>>>(lp);
+  kern<<<grid, pm::ws_threads<FMT, BN>(), smem, stream>>>(lp);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
@@ -2960,7 +2961,7 @@ template <int FMT, int PASS, int CDT>
 int launch_bn(int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
   if (bn == 256) {
     // 256-column tiles leave two accumulator buffers: one per epilogue warpgroup at most.
-    if constexpr (512 / 256 >= pm::epi_wgs<FMT>()) return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
+    if constexpr (512 / 256 >= pm::epi_wgs<FMT, 256>()) return launch_t<FMT, PASS, 256, CDT>(lp, items, kp, s);
     else return fail(PIPER_MERGE_EINVAL, "256-column tiles need at most two epilogue warpgroups.");
   }
   if (bn == 128) return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
