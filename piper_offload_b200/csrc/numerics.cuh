@@ -226,9 +226,6 @@ __device__ __forceinline__ void philox_word0_xn(const PhiloxKey& key, uint64_t o
   for (int j = 0; j < N; ++j) w[j] = c0[j];
 }
 
-__device__ __forceinline__ void philox_word0_x4(const PhiloxKey& key, uint64_t offset, uint32_t (&w)[4]) {
-  philox_word0_xn<4>(key, offset, w);
-}
 
 // sr_fp8 for N consecutive elements (offsets off .. off+N-1), packed four to
 // a word as little-endian bytes; same arithmetic as sr_fp8.
