@@ -166,12 +166,15 @@ int piper_merge_float8(void* qdata, void* scale, const void* b, const void* a, i
 
 /* piper_merge_float8 without a workspace argument. No counterpart in the
  * reference: an addition for callers that cannot allocate device memory at
- * merge time. The two-pass scratch comes from a fixed 1 MiB array in device
- * memory (one per device): layouts that need more (more than 65,536
- * quantization blocks, e.g. per-row weights above 65,536 rows) are rejected
- * with PIPER_MERGE_EWORKSPACE. The first call on a device performs the setup
- * (cudaGetSymbolAddress) and should come before any stream capture.
- * Overlapping calls on one device race on the shared scratch. */
+ * merge time. Per-row layouts need no scratch at all; per-tensor scales and
+ * groups wider than one tile (more than 256 columns) keep 16 bytes per
+ * quantization block in a fixed 1 MiB array in device memory (one per device
+ * and CUDA context). Layouts needing more than 65,536 blocks (e.g. 512-column
+ * groups over rows x cols/512 > 65,536) are rejected with
+ * PIPER_MERGE_EWORKSPACE before anything is enqueued. The first call in each
+ * context looks the array up (cudaGetSymbolAddress) and should come before
+ * any stream capture. All calls on a device share the array, so overlapping
+ * calls race on it. */
 int piper_merge_float8_noalloc(void* qdata, void* scale, const void* b, const void* a, int64_t rows,
                                int64_t cols, int64_t rank, int64_t block_rows, int64_t block_cols,
                                int32_t e5m2, int32_t compute_dtype, float strength, int32_t has_seed,

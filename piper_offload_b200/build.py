@@ -26,6 +26,7 @@ NVCC_FLAGS = [
     "--fmad=false",  # only the explicit fmaf() calls fuse, matching the reference's rounding points
     "-Xcompiler", "-fPIC",
     "-shared",
+    "--split-compile", "0",  # optimise the kernel instantiations on every host core in parallel
 ]
 
 

@@ -1,26 +1,33 @@
 // merge.cu - fused quantized LoRA merge for B200 (sm_100a).
 //
-// One CTA (128 threads) owns a 128-row strip of one weight and a range of its
-// columns, walked in tiles of BN columns. Per tile:
-//   1. codes (and GGUF inline scales) stream global -> shared with 1-D bulk
-//      (TMA-engine) copies, one per row, double-buffered and prefetched one
-//      tile ahead; rows are padded by 16 bytes so the thread-per-row epilogue
-//      reads shared memory without bank conflicts;
-//   2. the rank-r update D = B[rows, :] @ A[:, cols] runs on the 5th-gen tensor
-//      core: B (128 x r, K-major) stays resident in shared memory for the
-//      whole strip, the A tile (r x BN, MN-major) is staged per tile, one
-//      thread issues r/16 tcgen05.mma (M=128, N=BN, K=16) into a BN-column fp32
-//      accumulator in tensor memory and commits to an mbarrier;
-//   3. the epilogue: thread t owns row t (tensor-memory lane t), pulls 32
-//      accumulator columns at a time with tcgen05.ld, decodes codes+scales,
-//      adds the update with the reference's rounding points, computes block /
-//      group amax in registers, encodes scales and codes (round-to-nearest or
-//      Philox stochastic rounding by logical element offset) and writes the
-//      codes back in place through the same shared-memory row with a bulk store.
-// Formats whose scale spans more than one tile (per-row / per-tensor FP8 and
-// INT8, NVFP4 two-level global scale) run a REDUCE launch (amax / min into a
-// workspace with atomics) and then an ENCODE launch; the host planner groups
-// row ranges so that the ENCODE pass re-reads codes from L2.
+// merge_kernel is persistent and warp-specialised: one CTA per SM strides over
+// work items (a 128-row strip of one weight and a range of its BN-column
+// tiles, BN = 256, 128 or 64). Its roles:
+//   warp 0      one lane issues 2-D bulk tensor copies (TMA, no multicast):
+//               the B strip (128 x r) per item, the A tile (r x BN) and the
+//               code tile (128 rows x BN columns, swizzled) per tile, into
+//               rings of shared-memory stages with full / empty mbarriers;
+//   warp 1      one lane owns the 512 tensor-memory columns and issues the
+//               rank-r update D = B @ A as tcgen05.mma (M=128, N=BN, K=16)
+//               into one of 512 / BN fp32 accumulators per tile;
+//   warps 2-3   cp.async for per-row scale bytes (MX / NVFP4) and for the
+//               tiles and factors whose alignment rules out TMA;
+//   warps 4..   two or three epilogue warpgroups; tile t goes to warpgroup
+//               t mod W, whose thread i owns tile row i (tensor-memory lane i):
+//               tcgen05.ld of the accumulator 32 columns at a time, decode,
+//               merge with the reference's rounding points, block maxima,
+//               new scales, round-to-nearest or Philox stochastic codes keyed
+//               by logical element offset, written in place in shared memory
+//               and stored back with one bulk tensor copy.
+// Pass kinds (enum Pass): kLocal, one sweep where every scale is local to a
+// tile (MX, NVFP4 single-level, GGUF, bitsandbytes 4-bit, FP8 / INT8 groups of
+// at most 256 columns); kFused, per-row FP8 / INT8 in one launch, each CTA
+// sweeping a strip's tiles twice (row maxima, then codes) with the maxima on
+// chip; kReduce then kEncode (or kLocal), two launches for per-tensor scales,
+// groups wider than a tile and the NVFP4 global scale, with block maxima in a
+// workspace and launch groups sized so the second launch re-reads from L2.
+// Every wait is bounded; a wait that gives up records a status bit and the
+// CTA winds down (ptx.cuh).
 //
 // Reference kernels restated here (Piper Offload 0.2.5):
 //   src/piper_offload/_triton_mx_lora.py:162-295      (MX, in place)
@@ -2917,11 +2924,57 @@ size_t scratch_bytes(int nq, int words) {
   return nq == 0 ? 0 : (static_cast<size_t>(nq) * 4 * words + 255) / 256 * 256;  // 256-byte aligned
 }
 
+// Environment switches, read once per process.
+struct EnvFlags {
+  bool debug;   // PIPER_MERGE_DEBUG: print each launch's plan to stderr
+  bool no_tma;  // PIPER_MERGE_NO_TMA: move every tile by cp.async
+};
+const EnvFlags& env_flags() {
+  static const EnvFlags f{std::getenv("PIPER_MERGE_DEBUG") != nullptr, std::getenv("PIPER_MERGE_NO_TMA") != nullptr};
+  return f;
+}
+
+constexpr int kMaxDevices = 64;
+
 int sm_count() {
+  static std::atomic<int> cached[kMaxDevices] = {};
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
+  if (dev >= 0 && dev < kMaxDevices && (n = cached[dev].load(std::memory_order_relaxed)) > 0) return n;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
+  n = n > 0 ? n : 148;
+  if (dev >= 0 && dev < kMaxDevices) cached[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+// Identity of the calling thread's current CUDA context: cuCtxGetId, which
+// is unique for the life of the process and never reused, plus one; 0 when no
+// context is current or the driver lacks the call. Function attributes and
+// the addresses of module variables belong to one context (a non-primary
+// context, or the primary context re-created after cudaDeviceReset, loads the
+// module anew), so host-side caches of either key on this value.
+uint64_t current_context_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+    cudaGetLastError();
+  });
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return static_cast<uint64_t>(id) + 1u;
 }
 
 // ------------------------------------------------------------- dispatch
@@ -2938,16 +2991,24 @@ int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
     return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(kp_max) + " does not fit the shared-memory pipeline.");
   const int smem =
       std::max(pm::ws_smem_bytes(pm::TileGeom<FMT, BN>::kCodeSlot, kp_max, BN, pc.sc, pc.sa, pc.nbb), kMinSmem);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess)
-    return fail(PIPER_MERGE_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  // The dynamic shared-memory ceiling is raised to the per-CTA limit once per
+  // context and instantiation (every plan's request is below it), not per call.
+  static std::atomic<uint64_t> attr_ctx{0};
+  const uint64_t ctx = current_context_id();
+  cudaError_t e;
+  if (ctx == 0 || attr_ctx.load(std::memory_order_acquire) != ctx) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pm::kSmemLimit);
+    if (e != cudaSuccess)
+      return fail(PIPER_MERGE_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    attr_ctx.store(ctx, std::memory_order_release);
+  }
   lp.n_items = items;
   lp.kp_max = kp_max;
   lp.c_stages = pc.sc;
   lp.a_stages = pc.sa;
   lp.b_bufs = pc.nbb;
   const int grid = std::min(items, sm_count());
-  if (std::getenv("PIPER_MERGE_DEBUG") != nullptr)
+  if (env_flags().debug)
     std::fprintf(stderr, "[piper-merge] fmt=%d pass=%d bn=%d kp=%d stages=%d/%d/%d smem=%d items=%d grid=%d\n", FMT,
                  PASS, BN, kp_max, pc.sc, pc.sa, pc.nbb, smem, items, grid);
   kern<<<grid, pm::ws_threads<FMT, BN>(), smem, stream>>>(lp);
@@ -3169,7 +3230,7 @@ DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws,
   w.nabs = static_cast<const float*>(d.nested_absmax);
   w.noff = static_cast<const float*>(d.nested_offset);
   w.col_axis = p.col_axis ? 1 : 0;
-  if (std::getenv("PIPER_MERGE_NO_TMA") == nullptr) {
+  if (!env_flags().no_tma) {
     setup_tma(w, d, p.bn);
     setup_tma_factors(w, d, w.KP);
   }
@@ -3426,16 +3487,23 @@ int piper_merge_float8(void* qdata, void* scale, const void* b, const void* a, i
 // implicit device synchronization. It calls no allocating routine. The array
 // exists once per device (every device's copy of the module has its own), so
 // overlapping calls on one device, from several host threads or streams, race
-// on it. The first call on a device looks up the array's address
-// (cudaGetSymbolAddress, with that device current); make that first call
-// before any stream capture. Each call zeroes the blocks it uses on the stream
-// before the kernels read them, as the buffer-taking entry point does.
+// on it. The array's address is looked up (cudaGetSymbolAddress, with the
+// device current) by the first call in each CUDA context of a device, and
+// again whenever the calling thread's current context changes identity (a
+// non-primary context, or the primary context re-created after
+// cudaDeviceReset, holds its own copy of the array); make the first call in a
+// context before any stream capture. Each call zeroes the blocks it uses on
+// the stream before the kernels read them, as the buffer-taking entry point
+// does.
 namespace {
 constexpr size_t kNoAllocScratchBytes = size_t{1} << 20;  // 65,536 quantization blocks
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
-constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+struct NoAllocSlot {
+  uint64_t ctx;  // current_context_id() the address belongs to (0: none)
+  void* ptr;
+};
+NoAllocSlot g_noalloc_slot[kMaxDevices] = {};
 }  // namespace
 
 int piper_merge_float8_noalloc(void* qdata, void* scale, const void* b, const void* a, int64_t rows, int64_t cols,
@@ -3445,19 +3513,25 @@ int piper_merge_float8_noalloc(void* qdata, void* scale, const void* b, const vo
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
-  if (dev < 0 || dev >= kNoAllocMaxDevices)
+  if (dev < 0 || dev >= kMaxDevices)
     return fail(PIPER_MERGE_EINVAL, "device " + std::to_string(dev) + " is beyond the static scratch table.");
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
+    uint64_t ctx = current_context_id();
+    NoAllocSlot& slot = g_noalloc_slot[dev];
+    if (ctx == 0 || slot.ctx != ctx || slot.ptr == nullptr) {
+      // Looking the symbol up also makes the runtime's context current on a
+      // thread that had none, so the context is identified afterwards.
       void* ptr = nullptr;
       e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
       if (e != cudaSuccess || ptr == nullptr)
         return fail(PIPER_MERGE_ECUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-      g_noalloc_ptr[dev] = ptr;
+      ctx = current_context_id();
+      slot.ctx = ctx;
+      slot.ptr = ptr;
     }
-    scratch = g_noalloc_ptr[dev];
+    scratch = slot.ptr;
   }
   piper_merge_desc d;
   std::memset(&d, 0, sizeof(d));
