@@ -58,6 +58,8 @@ CONFIGS = {
     "mxfp4": (DIT_12B, 57, 128, 0.005, 0.02, False, "MXFP4 FLOOR, DiT-12B 57 blocks, r128, RTN"),
     "q8_0": (LLAMA_70B, 80, 16, 0.01, 0.015, False, "GGUF Q8_0, 70B-shaped x80, r16, RTN"),
     "q4_0": (LLAMA_70B, 80, 16, 0.01, 0.015, False, "GGUF Q4_0, 70B-shaped x80, r16, RTN"),
+    # one 4096 x 4096 INT8 per-row weight (launch-bound: ~5 us of HBM time per merge).
+    "int8_4096": ([("proj", 4096, 4096)], 1, 16, 0.01, 0.02, False, "INT8 per-row symmetric, one 4096x4096, r16, RTN"),
     # Formats beyond BASELINE's configs (the reference's other Triton merges), on the config-2 stack.
     "static_fp8": (LLAMA3_8B, 32, 32, 0.01, 0.02, True, "static per-tensor FP8 e4m3, Llama-3-8B x32, r32, SR"),
     "bnb8": (LLAMA3_8B, 32, 16, 0.01, 0.02, False, "bitsandbytes LLM.int8, Llama-3-8B x32, r16, fp16, RTN"),
@@ -68,11 +70,11 @@ CONFIGS = {
                    "bitsandbytes NF4, nested absmax, Llama-3-8B x32, r64, RTN"),
 }
 # Algorithmic bytes per element (read + write) and per-row scale bytes.
-BYTES_PER_ELEM = {"fp8": 2.0, "int8": 2.0, "nvfp4": 1.125, "mxfp8": 2.0625, "mxfp4": 1.0625,
+BYTES_PER_ELEM = {"fp8": 2.0, "int8": 2.0, "int8_4096": 2.0, "nvfp4": 1.125, "mxfp8": 2.0625, "mxfp4": 1.0625,
                   "q8_0": 2.125, "q4_0": 1.125, "static_fp8": 2.0, "bnb8": 2.0, "quanto_int8": 2.0,
                   "quanto_fp8": 2.0, "nf4": 1.125, "nf4_nested": 1.03125}
 # fp32 / bf16 row scale read + written
-ROW_SCALE_BYTES = {"fp8": 8, "int8": 4, "bnb8": 8, "quanto_int8": 4, "quanto_fp8": 4}
+ROW_SCALE_BYTES = {"fp8": 8, "int8": 4, "int8_4096": 4, "bnb8": 8, "quanto_int8": 4, "quanto_fp8": 4}
 
 FALLBACK_HBM_GBS = 6650.0
 
@@ -160,55 +162,80 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- workload
-def build_weights(cfg: str, device, seed_base: int, n_layers: int | None = None):
-    """Quantized weights + factors on `device` (torch ops, seeded per weight)."""
+def build_weights(cfg: str, device, seed_base: int, n_layers: int | None = None, shards: dict | None = None):
+    """Quantized weights + factors on `device` (torch ops, seeded per weight).
+
+    ``shards`` maps a weight key to the (row_begin, row_end) ranges this rank
+    merges (multi-GPU partition): the full weight is generated with the same
+    seed on every rank and only those rows are kept, so the shards of all
+    ranks are exactly the single-GPU weight's rows. Weights absent from
+    ``shards`` are skipped. Items are (key, rows, cols, weight, b, a,
+    row_begin)."""
+    import torch
+
+    from piper_offload_b200 import synthetic as S
+
+    _, _, rank, lora_std, base_std, _, _ = CONFIGS[cfg]
+    items = []
+    for k, (key, rows, cols) in enumerate(weight_list(cfg, n_layers=n_layers)):
+        if shards is not None and key not in shards:
+            continue
+        s = seed_base + 7919 * k
+        w_full = S.normal((rows, cols), base_std, seed=s, device=device,
+                          outlier_frac=0.001 if cfg.startswith("mx") else 0.0)
+        for r0, r1 in ([(0, rows)] if shards is None else shards[key]):
+            items.append(_quantized_item(cfg, key, rows, cols, w_full, r0, r1, s, rank, lora_std, device))
+        del w_full
+    torch.cuda.synchronize(device)
+    return items
+
+
+def _quantized_item(cfg: str, key: str, rows: int, cols: int, w_full, r0: int, r1: int, s: int, rank: int,
+                    lora_std: float, device):
+    """One weight (or rows r0..r1 of it) quantized in the config's format, with its LoRA factors."""
     import torch
 
     from piper_offload_b200 import synthetic as S
     from piper_offload_b200 import weights as WT
 
-    _, _, rank, lora_std, base_std, _, _ = CONFIGS[cfg]
-    items = []
-    for k, (key, rows, cols) in enumerate(weight_list(cfg, n_layers=n_layers)):
-        s = seed_base + 7919 * k
-        w = S.normal((rows, cols), base_std, seed=s, device=device,
-                     outlier_frac=0.001 if cfg.startswith("mx") else 0.0)
-        if cfg == "fp8":
-            q = S.quantize_fp8(w)
-            t = WT.Float8Weight(q.qdata, q.scale, (1, cols))
-        elif cfg == "int8":
-            q = S.quantize_int8_per_row(w)
-            t = WT.Int8Weight(q.qdata, q.scale, (1, cols))
-        elif cfg == "nvfp4":
-            q = S.quantize_nvfp4(w, two_level=True)
-            t = WT.NVFP4Weight(q.qdata, q.scale, q.per_tensor_scale)
-        elif cfg in ("mxfp8", "mxfp4"):
-            elem = "e4m3" if cfg == "mxfp8" else "e2m1"
-            q = S.quantize_mx(w, elem)
-            edt = torch.float8_e4m3fn if cfg == "mxfp8" else torch.float4_e2m1fn_x2
-            t = WT.MXWeight(q.qdata, q.scale.view(torch.float8_e8m0fnu), edt)
-        elif cfg == "static_fp8":
-            q = S.quantize_fp8(w, per_tensor=True)
-            t = WT.StaticFloat8Weight(q.qdata, q.scale.reshape(()), torch.ones((), device=device))
-        elif cfg == "bnb8":
-            t = WT.Bnb8Weight(*S.quantize_bnb8(w))
-        elif cfg in ("quanto_int8", "quanto_fp8"):
-            storage = "int8" if cfg == "quanto_int8" else "e4m3"
-            data, qscale = S.quantize_quanto(w, storage, axis=0)
-            t = WT.QuantoWeight(data, qscale, 0, WT.QINT8 if storage == "int8" else WT.QFLOAT8_E4M3)
-        elif cfg in ("nf4", "nf4_nested"):
-            packed, absmax, code, nabs, ncode, off = S.quantize_bnb4(w, nested=cfg == "nf4_nested")
-            st2 = None if nabs is None else WT.Bnb4State(nabs, ncode, (1, 1), blocksize=256, dtype=torch.float32)
-            t = WT.Bnb4Weight(packed, WT.Bnb4State(absmax, code, (rows, cols), "nf4", 64, torch.bfloat16, st2, off))
-        else:
-            q = S.quantize_gguf(w, 8 if cfg == "q8_0" else 2)
-            t = WT.GGUFWeight(q.qdata, 8 if cfg == "q8_0" else 2)
-        del w
-        fdt = torch.float16 if cfg == "bnb8" else torch.bfloat16
-        b, a = S.lora_factors(rows, cols, rank, lora_std, seed=s + 1, device=device, dtype=fdt)
-        items.append((key, rows, cols, t, b, a))
-    torch.cuda.synchronize(device)
-    return items
+    w = w_full if (r0, r1) == (0, rows) else w_full[r0:r1].contiguous()
+    rows_here = r1 - r0
+    if cfg == "fp8":
+        q = S.quantize_fp8(w)
+        t = WT.Float8Weight(q.qdata, q.scale, (1, cols))
+    elif cfg in ("int8", "int8_4096"):
+        q = S.quantize_int8_per_row(w)
+        t = WT.Int8Weight(q.qdata, q.scale, (1, cols))
+    elif cfg == "nvfp4":
+        q = S.quantize_nvfp4(w, two_level=True)
+        t = WT.NVFP4Weight(q.qdata, q.scale, q.per_tensor_scale)
+    elif cfg in ("mxfp8", "mxfp4"):
+        elem = "e4m3" if cfg == "mxfp8" else "e2m1"
+        q = S.quantize_mx(w, elem)
+        edt = torch.float8_e4m3fn if cfg == "mxfp8" else torch.float4_e2m1fn_x2
+        t = WT.MXWeight(q.qdata, q.scale.view(torch.float8_e8m0fnu), edt)
+    elif cfg == "static_fp8":
+        q = S.quantize_fp8(w, per_tensor=True)
+        t = WT.StaticFloat8Weight(q.qdata, q.scale.reshape(()), torch.ones((), device=device))
+    elif cfg == "bnb8":
+        t = WT.Bnb8Weight(*S.quantize_bnb8(w))
+    elif cfg in ("quanto_int8", "quanto_fp8"):
+        storage = "int8" if cfg == "quanto_int8" else "e4m3"
+        data, qscale = S.quantize_quanto(w, storage, axis=0)
+        t = WT.QuantoWeight(data, qscale, 0, WT.QINT8 if storage == "int8" else WT.QFLOAT8_E4M3)
+    elif cfg in ("nf4", "nf4_nested"):
+        packed, absmax, code, nabs, ncode, off = S.quantize_bnb4(w, nested=cfg == "nf4_nested")
+        st2 = None if nabs is None else WT.Bnb4State(nabs, ncode, (1, 1), blocksize=256, dtype=torch.float32)
+        t = WT.Bnb4Weight(packed, WT.Bnb4State(absmax, code, (rows_here, cols), "nf4", 64, torch.bfloat16, st2, off))
+    else:
+        q = S.quantize_gguf(w, 8 if cfg == "q8_0" else 2)
+        t = WT.GGUFWeight(q.qdata, 8 if cfg == "q8_0" else 2)
+    del w
+    fdt = torch.float16 if cfg == "bnb8" else torch.bfloat16
+    b, a = S.lora_factors(rows, cols, rank, lora_std, seed=s + 1, device=device, dtype=fdt)
+    if (r0, r1) != (0, rows):
+        b = b[r0:r1].contiguous()
+    return (key, rows_here, cols, t, b, a, r0)
 
 
 def storage_tensors(t):
@@ -221,10 +248,29 @@ def storage_tensors(t):
 
 
 # ------------------------------------------------------------ CPU baseline
-def _oracle_chunk(args):
-    """Oracle merge of one row chunk (runs in a spawned worker)."""
-    import numpy as np
+def _gguf_reference_chunk(raw, quant_type: int, b, a, strength: float) -> None:
+    """The reference's own GGUF path on CPU tensors: ``gguf_dequant.dequantize``
+    (``gguf_dequant.py:303-331``) to bf16, the update added in fp32 by
+    ``torch.addmm`` and rounded to bf16, and re-encoding by the pinned ``gguf``
+    package (``gguf.quants.quantize``, 0.19.0)."""
+    import gguf
+    import torch
 
+    from baseline import reference
+
+    gd = reference.load("piper_offload.gguf_dequant")
+    base = gd.dequantize(torch.from_numpy(raw), quant_type, dtype=torch.bfloat16)
+    merged = torch.addmm(base.float(), torch.from_numpy(b), torch.from_numpy(a), alpha=strength).to(torch.bfloat16)
+    qtype = gguf.GGMLQuantizationType.Q8_0 if quant_type == 8 else gguf.GGMLQuantizationType.Q4_0
+    gguf.quants.quantize(merged.float().numpy(), qtype)
+
+
+def _oracle_chunk(args):
+    """One row chunk of the CPU baseline (runs in a spawned worker)."""
+    import numpy as np
+    import torch
+
+    torch.set_num_threads(1)
     from oracle import merge as om
 
     cfg, q, scale, b, a, seed, offset_base, extra = args
@@ -233,7 +279,7 @@ def _oracle_chunk(args):
         om.merge_float8(q, scale, (1, a.shape[1]), b, a, 1.0, seed=seed, offset_base=offset_base)
     elif cfg == "static_fp8":
         om.merge_static_float8(q, scale, b, a, 1.0, seed=seed, offset_base=offset_base)
-    elif cfg == "int8":
+    elif cfg in ("int8", "int8_4096"):
         om.merge_int8(q, scale, None, (1, a.shape[1]), b, a, 1.0, seed=seed, offset_base=offset_base)
     elif cfg == "bnb8":
         om.merge_bnb8(q, scale.reshape(-1), b, a, 1.0, seed=seed, offset_base=offset_base)
@@ -244,13 +290,38 @@ def _oracle_chunk(args):
         code, nabs, ncode, off = extra
         om.merge_bnb4(q, scale, code, b, a, 1.0, nested_absmax=nabs, nested_code=ncode, offset=off, seed=seed,
                       offset_base=offset_base)
+    elif cfg == "nvfp4":
+        om.merge_nvfp4(q, scale, extra, b, a, 1.0, seed=seed, offset_base=offset_base)
+    elif cfg in ("mxfp8", "mxfp4"):
+        om.merge_mx(q, scale, "e4m3" if cfg == "mxfp8" else "e2m1", b, a, 1.0, seed=seed, offset_base=offset_base)
+    elif cfg in ("q8_0", "q4_0"):
+        qt = 8 if cfg == "q8_0" else 2
+        if extra == "reference":
+            _gguf_reference_chunk(q, qt, b, a, 1.0)
+        else:
+            om.merge_gguf(q, qt, b, a, 1.0, seed=seed, offset_base=offset_base)
     else:
         raise ValueError(cfg)
     return time.perf_counter() - t0, int(np.asarray(q).size)
 
 
-def cpu_baseline(cfg: str, steps: int, warmup: int, rows_per_step: int = 1024, cols: int = 4096):
-    """Time the oracle (port of the reference algorithm) on the host cores."""
+def _gguf_reference_ready() -> bool:
+    try:
+        import gguf  # noqa: F401
+
+        from baseline import reference
+
+        return reference.available()
+    except ImportError:
+        return False
+
+
+def cpu_baseline(cfg: str, steps: int, warmup: int, rows_per_step: int = 1024, cols: int = 4096,
+                 stochastic: bool | None = None):
+    """Time the reference's CPU path for ``cfg`` on the host cores: for GGUF the
+    reference's own code (``kind: reference``), for the other formats the numpy
+    restatement of the reference's kernels (``kind: port``; TorchAO, which holds
+    the reference's portable CPU fallbacks, is not installed)."""
     import multiprocessing as mp
 
     import numpy as np
@@ -258,46 +329,67 @@ def cpu_baseline(cfg: str, steps: int, warmup: int, rows_per_step: int = 1024, c
 
     from piper_offload_b200 import synthetic as S
 
-    ported = ("fp8", "int8", "static_fp8", "bnb8", "quanto_int8", "quanto_fp8", "nf4", "nf4_nested")
-    cfg_eff = cfg if cfg in ported else "fp8"
-    _, _, rank, lora_std, base_std, stochastic, _ = CONFIGS[cfg]
+    _, _, rank, lora_std, base_std, cfg_sr, _ = CONFIGS[cfg]
+    stochastic = cfg_sr if stochastic is None else stochastic
     cores = max(1, min(os.cpu_count() or 1, 32))
     chunk = max(16, rows_per_step // cores)
-    w = S.normal((rows_per_step, cols), base_std, seed=11, device="cpu")
+    w = S.normal((rows_per_step, cols), base_std, seed=11, device="cpu",
+                 outlier_frac=0.001 if cfg.startswith("mx") else 0.0)
     b, a = S.lora_factors(rows_per_step, cols, rank, lora_std, seed=12, device="cpu")
     extra = None
-    if cfg_eff in ("fp8", "static_fp8"):
-        q = S.quantize_fp8(w, per_tensor=cfg_eff == "static_fp8")
+    kind, what = "port", "numpy restatement of the reference kernels, not reference code"
+    per_chunk_extra = None
+    if cfg in ("fp8", "static_fp8"):
+        q = S.quantize_fp8(w, per_tensor=cfg == "static_fp8")
         qn, sn = q.qdata.view(torch.uint8).numpy(), q.scale.float().numpy()
-    elif cfg_eff == "int8":
+    elif cfg in ("int8", "int8_4096"):
         q = S.quantize_int8_per_row(w)
         qn, sn = q.qdata.numpy(), q.scale.float().numpy()
-    elif cfg_eff == "bnb8":
+    elif cfg == "bnb8":
         cb, scb = S.quantize_bnb8(w)
         qn, sn = cb.numpy(), scb.numpy().reshape(-1, 1)
-    elif cfg_eff in ("quanto_int8", "quanto_fp8"):
-        data, qs = S.quantize_quanto(w, "int8" if cfg_eff == "quanto_int8" else "e4m3", axis=0)
-        qn = data.numpy() if cfg_eff == "quanto_int8" else data.view(torch.uint8).numpy()
+    elif cfg in ("quanto_int8", "quanto_fp8"):
+        data, qs = S.quantize_quanto(w, "int8" if cfg == "quanto_int8" else "e4m3", axis=0)
+        qn = data.numpy() if cfg == "quanto_int8" else data.view(torch.uint8).numpy()
         sn = qs.float().numpy()
-    else:
-        # 4-bit: each row chunk is its own weight, so a nested chunk carries its own nested state.
-        nested = cfg_eff == "nf4_nested"
-        qn, sn, extra = [], [], []
+    elif cfg in ("mxfp8", "mxfp4"):
+        q = S.quantize_mx(w, "e4m3" if cfg == "mxfp8" else "e2m1")
+        qn, sn = q.qdata.view(torch.uint8).numpy(), q.scale.numpy()
+    elif cfg in ("q8_0", "q4_0"):
+        q = S.quantize_gguf(w, 8 if cfg == "q8_0" else 2)
+        qn, sn = q.qdata.numpy(), np.zeros((rows_per_step, 1), np.float32)
+        if _gguf_reference_ready() and not stochastic:
+            extra = "reference"
+            kind = "reference"
+            what = ("the reference's gguf_dequant.dequantize + torch.addmm + gguf 0.19.0 quants.quantize "
+                    "(reference code and its pinned dependency)")
+    elif cfg in ("nvfp4", "nf4", "nf4_nested"):
+        # Each row chunk is merged as its own weight, so a chunk carries its own
+        # per-tensor state (NVFP4 global scale, bitsandbytes nested absmax).
+        qn, sn, per_chunk_extra = [], [], []
         for r in range(0, rows_per_step, chunk):
-            packed, absmax, code, nabs, ncode, off = S.quantize_bnb4(w[r:r + chunk], nested=nested)
-            qn.append(packed.numpy().reshape(-1, cols // 2))
-            sn.append(absmax.numpy().reshape(-1))
-            extra.append((code.numpy(), None if nabs is None else nabs.numpy(),
-                          None if ncode is None else ncode.numpy(), None if off is None else float(off)))
+            if cfg == "nvfp4":
+                q = S.quantize_nvfp4(w[r:r + chunk], two_level=True)
+                qn.append(q.qdata.numpy())
+                sn.append(q.scale.view(torch.uint8).numpy())
+                per_chunk_extra.append(float(q.per_tensor_scale))
+            else:
+                packed, absmax, code, nabs, ncode, off = S.quantize_bnb4(w[r:r + chunk], nested=cfg == "nf4_nested")
+                qn.append(packed.numpy().reshape(-1, cols // 2))
+                sn.append(absmax.numpy().reshape(-1))
+                per_chunk_extra.append((code.numpy(), None if nabs is None else nabs.numpy(),
+                                        None if ncode is None else ncode.numpy(), None if off is None else float(off)))
+    else:
+        raise ValueError(cfg)
     bn, an = b.float().numpy(), a.float().numpy()
     seed = 0x9C3EA68DBAC91AAD if stochastic else None
-    if cfg_eff == "static_fp8":
+    if cfg == "static_fp8":
         sn = np.repeat(sn.reshape(1, 1), rows_per_step, axis=0)  # one scale per chunk
-    if cfg_eff.startswith("nf4"):
-        tasks = [(cfg_eff, qn[j], sn[j], bn[r:r + chunk], an, seed, r * cols, extra[j])
+    if per_chunk_extra is not None:
+        tasks = [(cfg, qn[j], sn[j], bn[r:r + chunk], an, seed, r * cols, per_chunk_extra[j])
                  for j, r in enumerate(range(0, rows_per_step, chunk))]
     else:
-        tasks = [(cfg_eff, qn[r:r + chunk], sn[r] if cfg_eff == "static_fp8" else sn[r:r + chunk], bn[r:r + chunk],
+        tasks = [(cfg, qn[r:r + chunk], sn[r] if cfg == "static_fp8" else sn[r:r + chunk], bn[r:r + chunk],
                   an, seed, r * cols, extra) for r in range(0, rows_per_step, chunk)]
     ctx = mp.get_context("spawn")
     times = []
@@ -308,12 +400,87 @@ def cpu_baseline(cfg: str, steps: int, warmup: int, rows_per_step: int = 1024, c
             dt = time.perf_counter() - t0
             if i >= warmup:
                 times.append(dt)
-    nbytes = algorithmic_bytes(cfg_eff, rows_per_step, cols)
+    nbytes = algorithmic_bytes(cfg, rows_per_step, cols)
     t = statistics.median(times)
-    return {"value": nbytes / t / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"{rows_per_step}x{cols} {cfg_eff}{' SR' if stochastic else ' RTN'} rows of one weight, "
-                      f"{len(tasks)} row chunks over {cores} spawned processes (numpy restatement, not reference code)",
+    return {"value": nbytes / t / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"{rows_per_step}x{cols} {cfg}{' SR' if stochastic else ' RTN'} rows of one weight, "
+                      f"{len(tasks)} row chunks over {cores} spawned processes ({what})",
             "ms_per_sample": t * 1e3}
+
+
+# -------------------------------------------------------------- triton bar
+TRITON_BAR_CONFIGS = ("fp8", "int8", "int8_4096", "nvfp4", "mxfp8", "mxfp4")
+
+
+def triton_bar(cfg: str, items, seeds, steps: int, warmup: int, device, stream) -> dict | None:
+    """The reference's own Triton merge launchers (unmodified, from
+    ``baseline/_ref``) over the same weights, as each reference adapter runs
+    them: the launcher, then the copy of its out-of-place buffers back into the
+    weight's storage (``int8_adapter.py:397-400``, ``float8_adapter.py:252-265``,
+    ``nvfp4_adapter.py:265-282``; the MX launcher merges in place,
+    ``mx_adapter.py:284-300``). Timed like the native step: CUDA events over
+    ``steps`` passes after ``warmup``."""
+    import torch
+
+    if cfg not in TRITON_BAR_CONFIGS:
+        return None
+    try:
+        import triton
+
+        from baseline import reference
+
+        if not reference.available():
+            return {"unavailable": "reference not installed under baseline/_ref"}
+        f8 = reference.load("piper_offload._triton_float8_lora")
+        i8 = reference.load("piper_offload._triton_int8_lora")
+        n4 = reference.load("piper_offload._triton_nvfp4_lora")
+        mx = reference.load("piper_offload._triton_mx_lora")
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"reference import failed: {exc!r}"[:200]}
+
+    def one(i: int, key: str, t, b, a, seed) -> None:
+        if cfg == "fp8":
+            nq, ns = f8.merge_float8_lora(t.qdata, t.scale, tuple(t.block_size), b, a, 1.0, rounding_seed=seed)
+            t.qdata.copy_(nq)
+            t.scale.copy_(ns)
+        elif cfg in ("int8", "int8_4096"):
+            nq, ns, _ = i8.merge_int8_lora(t.qdata, t.scale, None, tuple(t.block_size), b, a, 1.0, asymmetric=False,
+                                           reduce_range=False, rounding_seed=seed)
+            t.qdata.copy_(nq)
+            t.scale.copy_(ns)
+        elif cfg == "nvfp4":
+            nq, ns, npts = n4.merge_nvfp4_lora(t.qdata, t.scale, t.per_tensor_scale, 16, False, b, a, 1.0,
+                                               rounding_seed=seed)
+            t.qdata.copy_(nq)
+            t.scale.copy_(ns)
+            t.per_tensor_scale.copy_(npts.reshape(t.per_tensor_scale.shape))
+        else:
+            mx.merge_mx_lora_(t.qdata, t.scale, t.elem_dtype, 32, torch.bfloat16, b, a, 1.0, scaling_mode=0,
+                              swizzled=False, rounding_seed=seed)
+
+    def step(s: int) -> None:
+        for i, (key, rows, cols, t, b, a, _) in enumerate(items):
+            one(i, key, t, b, a, None if seeds is None else seeds[s][i])
+
+    try:
+        for s in range(warmup):
+            step(s)
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for s in range(steps):
+            step(warmup + s)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"reference Triton launch failed: {exc!r}"[:200]}
+    ms = e0.elapsed_time(e1) / steps
+    total = sum(algorithmic_bytes(cfg, r, c) for _, r, c, *_ in items)
+    return {"value": round(total / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "triton": triton.__version__, "steps": steps, "warmup": warmup,
+            "what": "reference Triton launchers from baseline/_ref (unmodified) + the adapters' copy-back, same "
+                    "weights, seeds and step as `value`"}
 
 
 # ------------------------------------------------------------------ main
@@ -334,8 +501,8 @@ def staging_bench(cfg: str, n_layers: int | None, steps: int, warmup: int) -> di
 
     dev = torch.device("cuda", 0)
     items = build_weights(cfg, dev, 0, n_layers)
-    weights = {key: t for key, _, _, t, _, _ in items}
-    lora = {key: (a.cpu(), b.cpu()) for key, _, _, _, b, a in items}
+    weights = {key: t for key, _, _, t, _, _, _ in items}
+    lora = {key: (a.cpu(), b.cpu()) for key, _, _, _, b, a, _ in items}
     stochastic = CONFIGS[cfg][5]
     del items
 
@@ -387,6 +554,10 @@ def main() -> int:
                     help="override the layer count (small profiling case; the headline uses the config's)")
     ap.add_argument("--kernel-reps", type=int, default=5,
                     help="timed repetitions of the dominant-weight roofline leg")
+    ap.add_argument("--no-triton-bar", action="store_true", help="skip timing the reference's Triton launchers")
+    ap.add_argument("--partition", action="store_true",
+                    help="multi-GPU: ONE model split over the ranks by sharding.partition (whole weights and "
+                         "128-row output shards, global-offset seeds; strong scaling) instead of one model per rank")
     ap.add_argument("--staging", action="store_true",
                     help="time merge_lora() with host-resident factors: batched staging vs the per-weight driver")
     args = ap.parse_args()
@@ -408,7 +579,7 @@ def main() -> int:
     if args.impl == "reference":
         if rank != 0:
             return 0
-        res = cpu_baseline(cfg, args.steps, warmup)
+        res = cpu_baseline(cfg, args.steps, warmup, stochastic=stochastic)
         line = {"metric": metric, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
                 "warmup": warmup, "ms_per_step": res["ms_per_sample"], "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -447,17 +618,33 @@ def main() -> int:
     # CPU baseline first (spawned pool, before heavy GPU allocations), rank 0 only.
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(cfg, steps=1, warmup=1)
+        cpu = cpu_baseline(cfg, steps=1, warmup=1, stochastic=stochastic)
 
-    items = build_weights(cfg, device, seed_base=1000 * rank, n_layers=args.layers)
+    shards = None
+    job_bytes_model = sum(algorithmic_bytes(cfg, r, c) for _, r, c in weight_list(cfg, n_layers=args.layers))
+    if args.partition:
+        from piper_offload_b200.sharding import WorkItem, partition
+
+        # Per-tensor scales (two-level NVFP4, static FP8) span all rows: those weights move whole.
+        row_split = cfg not in ("nvfp4", "static_fp8", "nf4_nested")
+        witems = [WorkItem(key, r, c, algorithmic_bytes(cfg, 1, c), row_splittable=row_split)
+                  for key, r, c in weight_list(cfg, n_layers=args.layers)]
+        shards = {}
+        for sh in partition(witems, world)[rank]:
+            shards.setdefault(sh.key, []).append((sh.row_begin, sh.row_end))
+    items = build_weights(cfg, device, seed_base=0 if args.partition else 1000 * rank, n_layers=args.layers,
+                          shards=shards)
     total_bytes = sum(algorithmic_bytes(cfg, r, c) for _, r, c, *_ in items)
+    # Whole-job bytes per step: one model per rank (weak), or one model split over the ranks (strong).
+    job_bytes = job_bytes_model if args.partition else total_bytes * world
 
     # Device-resident path: descriptors built once through the adapters, then
     # one piper_merge_batch call per step with that step's seeds.
     stream = torch.cuda.current_stream(device)
     keep: list = []
-    descs = [AD.select_adapter(t).merge_desc(t, b, a, 1.0, rounding_seed=0 if stochastic else None, keep=keep)
-             for key, rows, cols, t, b, a in items]
+    descs = [AD.select_adapter(t).merge_desc(t, b, a, 1.0, rounding_seed=0 if stochastic else None,
+                                             offset_base=r0 * cols, keep=keep)
+             for key, rows, cols, t, b, a, r0 in items]
     arr = (_native.MergeDesc * len(descs))(*descs)
     need = _native.workspace_bytes(descs)
     ws = torch.empty(max(64 << 20, need), dtype=torch.uint8, device=device)
@@ -496,7 +683,7 @@ def main() -> int:
     launches = _native.launches() - launches0
     ms = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms)
-    value = total_bytes * world / (ms / 1e3) / 1e9
+    value = job_bytes / (ms / 1e3) / 1e9
     clocks = clk.summary()
     status = _native.device_status(device)
 
@@ -546,6 +733,35 @@ def main() -> int:
         except Exception:  # noqa: BLE001
             pass
 
+    # Host cost per call: wall clock over back-to-back calls of the whole step
+    # (one batched C-ABI call) and of the reference driver's per-weight loop
+    # (merge.py:124: one call per weight), each synchronised once at the end.
+    def wall_us(fn, reps: int) -> float:
+        fn()
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize(device)
+        return (time.perf_counter() - t0) / reps * 1e6
+
+    singles = [(_native.MergeDesc * 1)(arr[i]) for i in range(len(descs))]
+
+    def per_weight_loop() -> None:
+        for one_arr in singles:
+            _native.check(lib.piper_merge_batch(one_arr, 1, ws_ptr, ws_len, stream.cuda_stream))
+
+    reps = max(3, min(200, int(2000 / max(ms, 0.01))))
+    host = {"batched_call_us": round(wall_us(lambda: run_step(step), reps), 2),
+            "per_weight_loop_us": round(wall_us(per_weight_loop, max(3, reps // 4)), 2),
+            "device_step_us": round(ms * 1e3, 2), "weights": len(descs),
+            "what": "wall clock per step over back-to-back calls, one sync at the end: one batched call vs one C-ABI "
+                    "call per weight (the reference's per-weight loop)"}
+
+    bar = None
+    if world == 1 and not args.no_triton_bar:
+        bar = triton_bar(cfg, items, seeds, args.steps, warmup, device, stream)
+
     # End to end through the public API: every weight starts and ends in pinned
     # host memory; streaming.merge_streamed moves each layer through a ring of
     # three device slots, overlapping upload, merge and download on three streams.
@@ -557,7 +773,7 @@ def main() -> int:
 
         host_ops = []
         h2d = d2h = 0
-        for key, rows, cols, t, b, a in items:
+        for key, rows, cols, t, b, a, r0 in items:
             ht = copy.copy(t)
             for name, dt in storages(t):
                 setattr(ht, name, dt.detach().cpu().pin_memory())
@@ -587,7 +803,7 @@ def main() -> int:
         torch.cuda.synchronize(device)
         barrier()
         e_ms = max_over_ranks(e_start.elapsed_time(e_end) / args.e2e_steps)
-        e2e = {"value": total_bytes * world / (e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+        e2e = {"value": job_bytes / (e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": args.e2e_steps,
                "path": "pinned host -> streaming.merge_streamed (per layer: upload / merge via C ABI / download "
                        "on three streams, 3 device slots) -> pinned host"}
@@ -595,15 +811,19 @@ def main() -> int:
     if rank == 0:
         line = {
             "metric": metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong" if args.partition else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": desc, "weights_per_gpu": len(items), "rank": lrank, "stochastic": stochastic,
                        "weight_bytes_per_gpu": total_bytes, "l2": "inputs (~GBs) exceed the 126 MB L2; no flush",
                        "layers": args.layers or CONFIGS[cfg][1],
-                       "parallelism": f"weak x{world}: one model per GPU, no collective"},
+                       "parallelism": (f"partition x{world}: one model split by whole weights and 128-row shards "
+                                       f"(sharding.partition), global-offset seeds, no collective")
+                       if args.partition else f"weak x{world}: one model per GPU, no collective"},
             "roofline": roofline,
             "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": e2e, "gpu_launches": launches, "clocks": clocks, "device_status": status,
+            "host": host, "triton_bar": bar,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -298,13 +298,16 @@ def _nvfp4_merged(qdata, scale, global_scale, swizzled, b, a, strength, compute)
 
 
 def merge_nvfp4(qdata, scale, per_tensor_scale, b, a, strength, *, swizzled=False, seed=None,
-                compute="bf16", offset_base=0):
+                compute="bf16", offset_base=0, global_amax=None):
     """NVFP4 merge (``merge_nvfp4_lora``, ``_triton_nvfp4_lora.py:515-595``).
 
     ``qdata`` uint8 (M x N/2), ``scale`` uint8 E4M3 codes (plain or swizzled),
     ``per_tensor_scale`` fp32 scalar or None. Returns ``(qdata, scale, global)``;
     the returned scale has zeros in swizzle padding like the reference's
-    ``torch.zeros_like`` output buffer.
+    ``torch.zeros_like`` output buffer. ``global_amax`` (two-level only)
+    replaces the maximum |merged| of these rows with the whole tensor's, so a
+    row strip of a larger weight is encoded as the whole-tensor merge encodes
+    it (``_recompute_global_scale``, ``_triton_nvfp4_lora.py:437-512``).
     """
     from .numerics import encode_e4m3, decode_e4m3
 
@@ -315,7 +318,7 @@ def merge_nvfp4(qdata, scale, per_tensor_scale, b, a, strength, *, swizzled=Fals
     merged, sidx = _nvfp4_merged(qdata, scale, g_in, swizzled, b, a, strength, compute)
     g_out = None
     if g_in is not None:
-        amax = nanmax_reduce(np.abs(merged).reshape(-1), axis=0)
+        amax = nanmax_reduce(np.abs(merged).reshape(-1), axis=0) if global_amax is None else np.float32(global_amax)
         g_out = maxnum(fdiv(amax, np.float32(2688.0)), EPS_2_23)
     blocks = merged.reshape(M, sc, 16)
     max_abs = nanmax_reduce(np.abs(blocks), axis=2)
