@@ -129,7 +129,11 @@ typedef struct piper_merge_desc {
 } piper_merge_desc;
 
 /* Bytes of device workspace `piper_merge_batch` needs for these descriptors.
- * 0 means no workspace (NULL may be passed). Returns 0 on success. */
+ * 0 means no workspace (NULL may be passed). Per-row FP8 / INT8 weights of a
+ * call too small to fill the GPU with whole 128-row strips ask for 16 bytes
+ * per row, which lets them split their columns over every SM; given less (or
+ * NULL), the call still runs them, with the fused one-launch pass. Returns 0
+ * on success. */
 int piper_merge_workspace_size(const piper_merge_desc* descs, int32_t count, size_t* bytes);
 
 /* Merge `count` weights, enqueued on `stream`. `workspace` is a device buffer of
@@ -166,10 +170,11 @@ int piper_merge_float8(void* qdata, void* scale, const void* b, const void* a, i
 
 /* piper_merge_float8 without a workspace argument. No counterpart in the
  * reference: an addition for callers that cannot allocate device memory at
- * merge time. Per-row layouts need no scratch at all; per-tensor scales and
- * groups wider than one tile (more than 256 columns) keep 16 bytes per
- * quantization block in a fixed 1 MiB array in device memory (one per device
- * and CUDA context). Layouts needing more than 65,536 blocks (e.g. 512-column
+ * merge time. Per-tensor scales, groups wider than one tile (more than 256
+ * columns) and per-row weights too small to fill the GPU with whole 128-row
+ * strips (fewer than two strips per SM) keep 16 bytes per quantization block
+ * in a fixed 1 MiB array in device memory (one per device and CUDA context);
+ * larger per-row weights need none. Layouts needing more than 65,536 blocks (e.g. 512-column
  * groups over rows x cols/512 > 65,536) are rejected with
  * PIPER_MERGE_EWORKSPACE before anything is enqueued. The first call in each
  * context looks the array up (cudaGetSymbolAddress) and should come before

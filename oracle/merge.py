@@ -560,7 +560,8 @@ def bnb4_nested_quantize(raw_absmax, nested_code):
     """
     raw = np.asarray(raw_absmax, np.float32).reshape(-1)
     n = raw.size
-    offset = np.float32(np.float32(np.sum(raw.astype(np.float64))) / np.float32(n))
+    # ``tl.sum(values) / TOTAL_VALUES`` with a runtime divisor: Triton's fp32 division (``fdiv_t``).
+    offset = np.float32(fdiv_t(np.float32(np.sum(raw.astype(np.float64))), np.float32(n)))
     centered = (raw - offset).astype(np.float32)
     nblk = (n + BNB4_NESTED_BLOCK - 1) // BNB4_NESTED_BLOCK
     pad = np.zeros(nblk * BNB4_NESTED_BLOCK, np.float32)

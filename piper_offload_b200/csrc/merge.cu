@@ -55,7 +55,7 @@
 
 namespace pm {
 
-constexpr int kMaxWeights = 24;
+constexpr int kMaxWeights = 48;  // 48 x 640-byte descriptors stay within the 32 KB of kernel parameters
 constexpr int kMaxRank = 256;
 
 // kLocal: scales local to a tile, one pass. kReduce / kEncode: the two
@@ -108,12 +108,18 @@ struct alignas(64) DevWeight {
 struct LaunchParams {
   DevWeight w[kMaxWeights];
   int n_weights;
-  int n_items;  // work items over all weights; CTAs stride over them
+  int n_items;  // work items over all weights, in order of decreasing cost
+  uint32_t sched_slot;  // this launch's item counter in g_sched_next
   int kp_max;    // shared-memory layout is sized for the largest padded rank
   int c_stages;  // ring of (code tile, scale bytes) stages, freed after the write-back
   int a_stages;  // ring of A tiles, freed when the tensor core has read them
   int b_bufs;    // B strips (1 or 2)
 };
+
+// Item counters of concurrent launches: each launch takes the next slot of
+// this ring, which the host zeroes on the launch's stream just before it.
+constexpr int kSchedSlots = 4096;
+__device__ unsigned int g_sched_next[kSchedSlots];
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
@@ -215,6 +221,61 @@ __device__ __forceinline__ float tree_min(const float (&m)[N]) {
   return t[0];
 }
 
+// Three-source maxima (sm_100 `max` / `min` with three operands, one
+// instruction each). The plain forms ignore a NaN operand like fmaxf; the
+// .NaN forms return NaN when any operand is NaN. `.abs` compares magnitudes.
+__device__ __forceinline__ float max3_abs(float a, float b, float c) {
+  float d;
+  asm("max.abs.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float max3_abs_nan(float a, float b, float c) {
+  float d;
+  asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Reduction of N values by a three-operand associative, commutative op
+// (exact for maxima in any order): ceil(N / 3) operations per level.
+template <int N, class Op3>
+__device__ __forceinline__ float tree3(const float (&m)[N], Op3 op) {
+  if constexpr (N == 1) {
+    return m[0];
+  } else if constexpr (N == 2) {
+    return op(m[0], m[1], m[1]);
+  } else {
+    constexpr int M = (N + 2) / 3;
+    float t[M];
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+      const int a = 3 * i;
+      t[i] = a + 2 < N ? op(m[a], m[a + 1], m[a + 2]) : (a + 1 < N ? op(m[a], m[a + 1], m[a + 1]) : m[a]);
+    }
+    return tree3<M>(t, op);
+  }
+}
+
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float min3_nan(float a, float b, float c) {
+  float d;
+  asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // ------------------------------------------------------------ MX scales
 struct MxScale {
   uint32_t code;
@@ -245,7 +306,7 @@ __device__ __forceinline__ MxScale mx_scale(float amax, int mode, int target, fl
                                             int mbits) {
   MxScale s;
   if (mode == PIPER_MX_RCEIL) {
-    const float d = __fdiv_rn(amax, maxpos);  // `/ MAX_POS` (constexpr): IEEE
+    const float d = __fmul_rn(amax, __frcp_rn(maxpos));  // `/ MAX_POS` (constexpr): x * fp32(1 / MAX_POS) on sm_100
     float u;
     if (d != d) u = __int_as_float(0x7FC00000);
     else if (d == 0.0f) u = __int_as_float(0xFF800000);
@@ -428,6 +489,115 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
   if (c.valid) scale8[scale_index(W, c.row, blk)] = static_cast<uint8_t>(s.code);
 }
 
+// Fast path of mx_chunk, same codes and scale, for the common block: scale
+// code in [20, 230] (every decoded product exact in bf16), merged values all
+// finite with a maximum of 0 or at least 2^-100, and a new inverse scale that
+// is an exact power of two. Then
+//  * merged = fma(acc, strength, elem * scale) runs two elements per packed
+//    instruction and stays unrounded for the block maximum (rounding is
+//    monotone: max |bf16(x)| = bf16(max |x|));
+//  * bf16(merged) * inv = bf16(merged * inv), so the normalized values take one
+//    packed multiply and one packed rounding (a bf16-subnormal merged value
+//    scales to below 2^-18 there, which encodes as zero either way);
+//  * the satfinite conversions clamp to the largest finite code as the
+//    reference's clamp does for finite values.
+// Any other block returns false before writing anything and takes mx_chunk.
+template <int FMT, int CDT>
+__device__ __forceinline__ bool mx_chunk_fast(const DevWeight& W, const RowCtx& c, int k, const float (&acc)[32]) {
+  using P = MxParams<FMT>;
+  const int col = c.tile_col0 + 32 * k;
+  const int blk = col >> 5;
+  const uint32_t sc = c.valid ? c.sscale[blk - c.blk0] : 127u;
+  if (sc < 20u || sc > 230u) {
+    return false;
+  }
+  const float bscale = dec_e8m0(sc);
+  float m[32];
+  if constexpr (FMT == PIPER_FMT_MXFP4) {
+    const uint4 pk = *reinterpret_cast<const uint4*>(chunk_ptr(c, k));
+    const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) dec_e2m1x2(wv[j >> 2] >> ((j & 3) * 8), m[2 * j], m[2 * j + 1]);
+  } else {
+    uint32_t wv[8];
+    load_chunks32(c, k, wv);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      float f[4];
+      dec_fp8x4<FMT == PIPER_FMT_MXFP8_E4M3>(wv[w], f);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) m[4 * w + j] = f[j];
+    }
+  }
+  const float2 b2 = make_float2(bscale, bscale);
+  const float2 st2 = make_float2(W.strength, W.strength);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    const float2 t = __ffma2_rn(make_float2(acc[i], acc[i + 1]), st2, __fmul2_rn(make_float2(m[i], m[i + 1]), b2));
+    m[i] = t.x;
+    m[i + 1] = t.y;
+  }
+  float amax = tree3(m, max3_abs_nan);
+  if (!(amax <= 3.40282347e38f) || (amax != 0.0f && amax < 7.888609052210118e-31f /* 2^-100 */)) {
+    return false;
+  }
+  amax = bf16r(amax);
+  const MxScale s = mx_scale(amax, W.scale_mode, P::kTarget, P::kMax, P::kMbits);
+  if ((__float_as_uint(s.inv) & 0x807FFFFFu) != 0u || s.inv == 0.0f) {
+    return false;
+  }
+  const float2 inv2 = make_float2(s.inv, s.inv);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    float2 t = __fmul2_rn(make_float2(m[i], m[i + 1]), inv2);
+    bf16r2(t.x, t.y);
+    m[i] = t.x;
+    m[i + 1] = t.y;
+  }
+  const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+  const PhiloxKey key = philox_key(W.k0, W.k1);
+  const uint64_t off0 = W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
+  if constexpr (FMT == PIPER_FMT_MXFP4) {
+    uint32_t out[4] = {0u, 0u, 0u, 0u};
+    if (sr) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = m[8 * w + j];
+        uint32_t nib[1];
+        sr_e2m1xn<8>(v, key, off0 + 8 * w, nib);  // |v| < 8: magnitudes from 6 up keep the top code
+        out[w] = nib[0];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j >> 2] |= enc_e2m1x2(m[2 * j], m[2 * j + 1]) << ((j & 3) * 8);
+    }
+    *reinterpret_cast<uint4*>(chunk_ptr(c, k)) = make_uint4(out[0], out[1], out[2], out[3]);
+  } else {
+    constexpr bool kE4 = FMT == PIPER_FMT_MXFP8_E4M3;
+    uint32_t out[8];
+    if (sr) {
+#pragma unroll
+      for (int w8 = 0; w8 < 4; ++w8) {
+        float x[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = m[8 * w8 + j];
+        uint32_t wd[2];
+        sr_fp8xn_finite<kE4, 8>(x, key, off0 + 8 * w8, wd);
+        out[2 * w8] = wd[0];
+        out[2 * w8 + 1] = wd[1];
+      }
+    } else {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) out[w] = enc_fp8x4<kE4>(m[4 * w], m[4 * w + 1], m[4 * w + 2], m[4 * w + 3]);
+    }
+    store_chunks32(c, k, out);
+  }
+  if (c.valid) reinterpret_cast<uint8_t*>(W.scale)[scale_index(W, c.row, blk)] = static_cast<uint8_t>(s.code);
+  return true;
+}
+
 // ============================================================= NVFP4 epilogue
 // One 16-element block. `codes` holds its 8 packed bytes (in: input codes,
 // out: merged codes). PASS kReduce accumulates |merged| into `amax_acc`.
@@ -465,7 +635,7 @@ __device__ __forceinline__ void nvfp4_block(const DevWeight& W, const RowCtx& c,
   if constexpr (PASS == kReduce) {
     if (c.valid) amax_acc = fmaxf(amax_acc, amax);
   } else {
-    float fs = __fdiv_rn(amax, 6.0f);  // `/ 6.0` (literal): IEEE
+    float fs = __fmul_rn(amax, 1.0f / 6.0f);  // `/ 6.0` (literal): x * fp32(1 / 6) on sm_100
     if (two_level) fs = div_full(fs, g_out);
     fs = fminf(fmaxf(fs, 0.015625f), 448.0f);
     const uint32_t fcode = enc_e4m3(fs);
@@ -546,9 +716,12 @@ __device__ __forceinline__ int qparam_index(const DevWeight& W, int row, int col
 }
 
 // New FP8 scale from the block amax (_reduce_row_scale_kernel, _triton_float8_lora.py:249-271).
+// `max_abs / FP8_LIMIT` divides by a constexpr, which Triton evaluates on sm_100
+// as a product with the fp32 reciprocal of the constant (measured on a B200).
 template <int CDT>
 __device__ __forceinline__ float fp8_new_scale(float amax, float limit) {
-  float s = round_dt<CDT>(__fdiv_rn(amax, limit));  // `/ FP8_LIMIT` (constexpr): IEEE
+  const float rcp = limit == 448.0f ? 1.0f / 448.0f : 1.0f / 57344.0f;
+  float s = round_dt<CDT>(__fmul_rn(amax, rcp));
   return s == 0.0f ? 1.1920928955078125e-07f : s;
 }
 
@@ -565,9 +738,10 @@ __device__ __forceinline__ Int8Q int8_qparams(float min_v, float max_v, bool asy
   float s;
   if (asym) {
     const float rng = round_dt<CDT>(__fsub_rn(max_v, min_v));
-    s = __fdiv_rn(rng, static_cast<float>(qmax - qmin));  // constexpr divisor: IEEE
+    // Constexpr divisors: a product with the fp32 reciprocal, as Triton evaluates them on sm_100.
+    s = __fmul_rn(rng, __frcp_rn(static_cast<float>(qmax - qmin)));
   } else {
-    s = __fdiv_rn(fmaxf(-min_v, max_v), static_cast<float>(qmax - qmin) / 2.0f);
+    s = __fmul_rn(fmaxf(-min_v, max_v), __frcp_rn(static_cast<float>(qmax - qmin) / 2.0f));
   }
   s = round_dt<CDT>(s);
   s = fmaxf(s, 1.1920928955078125e-07f);
@@ -958,6 +1132,131 @@ __device__ __forceinline__ void fp8_encode_rtn(const float (&m)[32], float s, fl
   for (int w = 0; w < 8; ++w) out[w] = enc_fp8x4<E4M3>(q[4 * w], q[4 * w + 1], q[4 * w + 2], q[4 * w + 3]);
 }
 
+// ------------------------------------------- packed per-row FP8 (fused pass)
+// Decode + merge of 32 FP8 codes of one row (TorchAO scaled FP8,
+// _triton_float8_lora.py:70-94): base = compute(fp8 * scale), merged =
+// fma(acc, strength, base) in fp32, two elements per packed instruction.
+// ROUND rounds the merged values to the compute dtype; the row-maxima sweep
+// skips it, since rounding is monotone: max |compute(x)| = compute(max |x|).
+template <bool E4M3, int CDT, bool ROUND>
+__device__ __forceinline__ void fp8_merged_pk(const uint32_t (&wv)[8], const float (&acc)[32], float s_in,
+                                              float strength, float (&m)[32]) {
+  const float2 s2 = make_float2(s_in, s_in);
+  const float2 st2 = make_float2(strength, strength);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    float f[4];
+    dec_fp8x4<E4M3>(wv[w], f);
+    float2 b0 = __fmul2_rn(make_float2(f[0], f[1]), s2);
+    float2 b1 = __fmul2_rn(make_float2(f[2], f[3]), s2);
+    round_dt2<CDT>(b0.x, b0.y);
+    round_dt2<CDT>(b1.x, b1.y);
+    float2 m0 = __ffma2_rn(make_float2(acc[4 * w], acc[4 * w + 1]), st2, b0);
+    float2 m1 = __ffma2_rn(make_float2(acc[4 * w + 2], acc[4 * w + 3]), st2, b1);
+    if constexpr (ROUND) {
+      round_dt2<CDT>(m0.x, m0.y);
+      round_dt2<CDT>(m1.x, m1.y);
+    }
+    m[4 * w] = m0.x;
+    m[4 * w + 1] = m0.y;
+    m[4 * w + 2] = m1.x;
+    m[4 * w + 3] = m1.y;
+  }
+}
+
+// Decode + merge of 32 INT8 codes of one row (TorchAO affine INT8,
+// _triton_int8_lora.py:70-94): base = compute((q - zp) * scale) with the
+// mixed bf16 / fp16 rules of int8_f16_scale / int8_half_product, merged =
+// fma(acc, strength, base), two elements per packed instruction. q - zp is
+// exact: the code byte with its sign bit flipped, placed under the exponent of
+// 2^23, is the float 2^23 + q + 128, and subtracting 2^23 + 128 + zp leaves
+// q - zp. ROUND as in fp8_merged_pk.
+template <int CDT, bool ROUND>
+__device__ __forceinline__ void int8_merged_pk(const uint32_t (&wv)[8], const float (&acc)[32], float s_in, int z_in,
+                                               int scale_dt, float strength, float (&m)[32]) {
+  const float off = -(8388736.0f + static_cast<float>(z_in));
+  const float sc = int8_f16_scale<CDT>(scale_dt) ? f16r(s_in) : s_in;
+  const bool half_product = CDT == kBF16 && scale_dt == kF16;
+  const float2 off2 = make_float2(off, off);
+  const float2 s2 = make_float2(sc, sc);
+  const float2 st2 = make_float2(strength, strength);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const uint32_t x = wv[w] ^ 0x80808080u;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float2 raw = make_float2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u + 2u * h)),
+                                     __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7541u + 2u * h)));
+      float2 b = __fmul2_rn(__fadd2_rn(raw, off2), s2);
+      if (half_product) f16r2(b.x, b.y);
+      round_dt2<CDT>(b.x, b.y);
+      float2 r = __ffma2_rn(make_float2(acc[4 * w + 2 * h], acc[4 * w + 2 * h + 1]), st2, b);
+      if constexpr (ROUND) round_dt2<CDT>(r.x, r.y);
+      m[4 * w + 2 * h] = r.x;
+      m[4 * w + 2 * h + 1] = r.y;
+    }
+  }
+}
+
+// Round-to-nearest INT8 codes of 32 merged values of an all-finite row
+// (_quantize_kernel, _triton_int8_lora.py:189-236): x = scale_dtype(m *
+// scale_dtype(1 / scale)), q = rint(x) + zp clamped to [qmin, qmax]. In an
+// all-finite row |x| <= 128 or so, far below 2^22, so rint(x) is the sum
+// x + 1.5 * 2^23 (exact in fp32), the zero point is added exactly after it,
+// and the low byte of the clamped sum's bits is q.
+__device__ __forceinline__ void int8_encode_rtn_finite(const float (&m)[32], const Int8Q& q, int qmin, int qmax,
+                                                       int scale_dt, uint32_t (&out)[8]) {
+  const float inv = round_dt_rt(div_full(1.0f, q.scale), scale_dt);
+  const float2 inv2 = make_float2(inv, inv);
+  const float2 magic2 = make_float2(12582912.0f, 12582912.0f);
+  const float2 zp2 = make_float2(static_cast<float>(q.zp), static_cast<float>(q.zp));
+  const float lo = 12582912.0f + static_cast<float>(qmin), hi = 12582912.0f + static_cast<float>(qmax);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    uint32_t qb[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float2 x = __fmul2_rn(make_float2(m[4 * w + 2 * h], m[4 * w + 2 * h + 1]), inv2);
+      round_rt2(x.x, x.y, scale_dt);
+      const float2 y = __fadd2_rn(__fadd2_rn(x, magic2), zp2);
+      qb[2 * h] = __float_as_uint(fminf(fmaxf(y.x, lo), hi));
+      qb[2 * h + 1] = __float_as_uint(fminf(fmaxf(y.y, lo), hi));
+    }
+    out[w] = __byte_perm(__byte_perm(qb[0], qb[1], 0x0040u), __byte_perm(qb[2], qb[3], 0x0040u), 0x5410u);
+  }
+}
+
+// Round-to-nearest FP8 codes of 32 merged values of a row whose values are all
+// finite (no NaN or infinity in the row): q = div.full(m, s) as the reference
+// divides, then the satfinite RTNE conversion. |q| <= amax / s <= limit *
+// (1 + 2^-8) there, which rounds to the largest finite code exactly as the
+// reference's clamp to [-limit, limit] followed by RTNE does.
+template <bool E4M3>
+__device__ __forceinline__ void fp8_encode_rtn_finite(const float (&m)[32], float s, uint32_t (&out)[8]) {
+  float q[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) q[i] = div_full(m[i], s);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) out[w] = enc_fp8x4<E4M3>(q[4 * w], q[4 * w + 1], q[4 * w + 2], q[4 * w + 3]);
+}
+
+// Stochastic FP8 codes of 32 merged values of an all-finite row: q =
+// div.full(m, s), eight Philox counters per batch (sr_fp8xn_finite).
+template <bool E4M3>
+__device__ __forceinline__ void fp8_encode_sr_finite(const float (&m)[32], float s, const PhiloxKey& key,
+                                                     uint64_t off0, uint32_t (&out)[8]) {
+#pragma unroll
+  for (int w8 = 0; w8 < 4; ++w8) {
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = div_full(m[8 * w8 + j], s);
+    uint32_t wd[2];
+    sr_fp8xn_finite<E4M3, 8>(x, key, off0 + 8 * w8, wd);
+    out[2 * w8] = wd[0];
+    out[2 * w8 + 1] = wd[1];
+  }
+}
+
 // Stored scale of an FP8 / INT8 weight: TorchAO FP8 scales are fp32; INT8,
 // bitsandbytes and Quanto scales have the weight's scale dtype.
 template <int FMT>
@@ -1218,7 +1517,7 @@ __global__ void __launch_bounds__(256) bnb4_nested_kernel(const uint32_t* __rest
   if (threadIdx.x == 0) {
     double t = 0.0;
     for (int b = 0; b < kBnb4Parts; ++b) t += part[b];
-    s_off = __fdiv_rn(__double2float_rn(t), static_cast<float>(n));  // `/ TOTAL_VALUES`
+    s_off = div_full(__double2float_rn(t), static_cast<float>(n));  // `/ TOTAL_VALUES` (runtime divisor: Triton's fp32 division)
     if (blockIdx.x == 0) *off = s_off;
   }
   __syncthreads();
@@ -1381,32 +1680,55 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
 #pragma unroll
   for (int j = 0; j < kCodeWords; ++j) cw[j] = odd ? w[j + 1] : __funnelshift_r(w[j], w[j + 1], 16);
   const float d_in = round_dt<CDT>(__half2float(__ushort_as_half(static_cast<unsigned short>(dbits))));
+  // Codes as exact floats: a byte (Q8_0: sign bit flipped; Q4_0: nibble)
+  // under the exponent of 2^23 is 2^23 + b, and one packed subtraction of 2^23
+  // plus the offset (128 or 8) leaves the signed code.
   float merged[32];
+  const float2 d2 = make_float2(d_in, d_in);
+  const float2 st2 = make_float2(W.strength, W.strength);
   if constexpr (kQ8) {
+    const float2 off2 = make_float2(-8388736.0f, -8388736.0f);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const uint32_t x = cw[j] ^ 0x80808080u;
 #pragma unroll
-      for (int b = 0; b < 4; ++b) merged[4 * j + b] = __fmul_rn(d_in, sbyte_to_float(x, b));
+      for (int h = 0; h < 2; ++h) {
+        const float2 raw = make_float2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u + 2u * h)),
+                                       __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7541u + 2u * h)));
+        const float2 v = __fmul2_rn(d2, __fadd2_rn(raw, off2));
+        merged[4 * j + 2 * h] = v.x;
+        merged[4 * j + 2 * h + 1] = v.y;
+      }
     }
   } else {
+    const float2 off2 = make_float2(-8388616.0f, -8388616.0f);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t lo = cw[j] & 0x0F0F0F0Fu;         // elements 4j .. 4j+3
       const uint32_t hi = (cw[j] >> 4) & 0x0F0F0F0Fu;  // elements 16+4j .. 16+4j+3
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        merged[4 * j + b] = __fmul_rn(d_in, nibble_to_float_m8(lo, b));
-        merged[16 + 4 * j + b] = __fmul_rn(d_in, nibble_to_float_m8(hi, b));
+      for (int h = 0; h < 2; ++h) {
+        const float2 rl = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540u + 2u * h)),
+                                      __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7541u + 2u * h)));
+        const float2 rh = make_float2(__uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540u + 2u * h)),
+                                      __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7541u + 2u * h)));
+        const float2 vl = __fmul2_rn(d2, __fadd2_rn(rl, off2));
+        const float2 vh = __fmul2_rn(d2, __fadd2_rn(rh, off2));
+        merged[4 * j + 2 * h] = vl.x;
+        merged[4 * j + 2 * h + 1] = vl.y;
+        merged[16 + 4 * j + 2 * h] = vh.x;
+        merged[16 + 4 * j + 2 * h + 1] = vh.y;
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
-#pragma unroll
-  for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], W.strength, merged[i]);
-#pragma unroll
-  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+  for (int i = 0; i < 32; i += 2) {
+    round_dt2<CDT>(merged[i], merged[i + 1]);
+    const float2 m2 = __ffma2_rn(make_float2(acc[i], acc[i + 1]), st2, make_float2(merged[i], merged[i + 1]));
+    merged[i] = m2.x;
+    merged[i + 1] = m2.y;
+    round_dt2<CDT>(merged[i], merged[i + 1]);
+  }
   const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
   const PhiloxKey key = philox_key(W.k0, W.k1);
   const int col = c.tile_col0 + 32 * k;
@@ -1415,7 +1737,7 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
   uint32_t ow[kCodeWords];
   uint32_t dh;
   if constexpr (kQ8) {
-    const float amax = tree_max_abs(merged);
+    const float amax = tree3(merged, max3_abs);
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
     dh = __half_as_ushort(__float2half_rn(d));
@@ -1428,15 +1750,15 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
       big |= !(fabsf(x[i]) < 4194304.0f);
     }
     if (!sr && !big) {
-      // Round half away from zero in the integer domain: t = trunc(|x|) from
-      // the bits of |x| + 2^23 added toward zero, plus 1 when |x| - t >= 0.5.
+      // Round half away from zero (roundf is np_roundf exactly); a finite block
+      // has |x| <= 127 * (1 + 2^-22), so no clamp is needed, and the low byte
+      // of the bits of q + 1.5 * 2^23 is the two's-complement code.
+      const float2 magic2 = make_float2(12582912.0f, 12582912.0f);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float a = fabsf(x[i]);
-        const float y = __fadd_rz(a, 8388608.0f);
-        const float frac = __fsub_rn(a, __fsub_rn(y, 8388608.0f));
-        const int b = static_cast<int>(__float_as_uint(y) - 0x4B000000u) + (frac >= 0.5f ? 1 : 0);
-        qb[i] = static_cast<uint32_t>(min(max(x[i] < 0.0f ? -b : b, -128), 127));
+      for (int i = 0; i < 32; i += 2) {
+        const float2 y = __fadd2_rn(make_float2(roundf(x[i]), roundf(x[i + 1])), magic2);
+        qb[i] = __float_as_uint(y.x);
+        qb[i + 1] = __float_as_uint(y.y);
       }
     } else {
       float q[32];
@@ -1590,6 +1912,10 @@ __host__ __device__ constexpr int epi_wgs() { return epi_wgs_rt(FMT, BN); }
 template <int FMT, int BN>
 __host__ __device__ constexpr int ws_threads() { return 128 * (1 + epi_wgs<FMT, BN>()); }
 constexpr int kLoadThreads = 64;  // warps 2-3
+// Dynamic work distribution: warp 0 takes the next item from the launch's
+// counter (atomicAdd, items ordered by decreasing cost) and publishes it in a
+// ring that every role reads in the same order.
+constexpr int kItemRing = 8;
 constexpr int kMaxStages = 8;    // code stages
 constexpr int kMaxAStages = 4;
 constexpr int kMaxAcc = 8;        // accumulator buffers: 512 tensor-memory columns / BN
@@ -1629,9 +1955,11 @@ __host__ __device__ constexpr int ws_code_stage_bytes(int code_slot) {
 }
 __host__ __device__ constexpr int ws_a_stage_bytes(int kp, int bn) { return align_up(kp * bn * 2, 1024); }
 __host__ __device__ constexpr int ws_b_buf_bytes(int kp) { return 128 * kp * 2; }
-// The tail holds the mbarriers (512 B) and, for fused per-row passes, each
-// epilogue warpgroup's partial row maxima for two items (2 x 3 x 128 float2).
-constexpr int kTailBytes = 512 + 2 * 3 * 128 * 8;
+// The tail holds the mbarriers, the TMEM slot and the item ring (640 B) and,
+// for fused per-row passes, each epilogue warpgroup's partial row maxima for
+// two items (2 x 3 x 128 float2).
+constexpr int kBarBytes = 640;
+constexpr int kTailBytes = kBarBytes + 2 * 3 * 128 * 8;
 __host__ __device__ constexpr int ws_smem_bytes(int code_slot, int kp, int bn, int sc, int sa, int nbb) {
   return 1024 + sc * ws_code_stage_bytes(code_slot) + sa * ws_a_stage_bytes(kp, bn) + nbb * ws_b_buf_bytes(kp) +
          kTailBytes;
@@ -1685,7 +2013,14 @@ __device__ __forceinline__ uint32_t swizzle_xor(int r, int row_bytes) {
 template <int FMT, int PASS, int BN, int CDT>
 __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const __grid_constant__ LaunchParams P) {
   constexpr int kEpiWGs = epi_wgs<FMT, BN>();
+  // Arrivals that free an item-ring slot: the MMA lane, the two loader warps
+  // and every epilogue warp.
+  constexpr uint32_t kItemReaders = 1 + 2 + 4 * kEpiWGs;
   using G = TileGeom<FMT, BN>;
+  // Per-row TorchAO FP8 and INT8 run the packed fused sweeps.
+  constexpr bool kPackedRow = PASS == kFused && flavor_of(FMT) == kTorchao &&
+                              (base_fmt(FMT) == PIPER_FMT_FP8_E4M3 || base_fmt(FMT) == PIPER_FMT_FP8_E5M2 ||
+                               base_fmt(FMT) == PIPER_FMT_INT8);
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -1712,8 +2047,11 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
   uint64_t* aempty = afull + kMaxAcc;     // [kMaxAcc]
   uint64_t* mma_done = aempty + kMaxAcc;
   uint64_t* rmax_bar = mma_done + 1;      // [2] partial row maxima published (fused per-row)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rmax_bar + 2);
-  float2* rpart = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + 512);  // [2][kEpiWGs][128]
+  uint64_t* item_full = rmax_bar + 2;     // [kItemRing] next work item published
+  uint64_t* item_empty = item_full + kItemRing;  // [kItemRing] read by every role
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kItemRing);
+  int* item_ring = reinterpret_cast<int*>(tmem_slot + 4);  // [kItemRing]
+  float2* rpart = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);  // [2][kEpiWGs][128]
   auto stage_codes = [&](int s) { return sCode + s * kCodeStage; };
   auto stage_scales = [&](int s) { return sCode + s * kCodeStage + G::kCodeSlot; };
   auto stage_a = [&](int x) { return sAst + x * kAStage; };
@@ -1739,6 +2077,10 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
     }
     mbar_init(mma_done, 1);
     for (int i = 0; i < 2; ++i) mbar_init(&rmax_bar[i], kEpiWGs);
+    for (int i = 0; i < kItemRing; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], kItemReaders);
+    }
     fence_mbar_init();
   }
   constexpr int NB = 512 / BN;  // accumulator buffers in the 512 tensor-memory columns
@@ -1762,7 +2104,19 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
     if (lane == 0) {
       uint32_t t = 0, it = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x, ++it) {
+      for (;; ++it) {
+        if (!ok) break;
+        // Take the next item (-1 past the last) and publish it to every role.
+        const int rs = static_cast<int>(it % kItemRing);
+        if (it >= static_cast<uint32_t>(kItemRing)) {
+          ok = mbar_wait(&item_empty[rs], ((it / kItemRing) - 1) & 1u, kStatusTimeoutLoad);
+          if (!ok) break;
+        }
+        const unsigned int v = atomicAdd(&g_sched_next[P.sched_slot], 1u);
+        const int item = v < static_cast<unsigned int>(P.n_items) ? static_cast<int>(v) : -1;
+        item_ring[rs] = item;
+        mbar_arrive(&item_full[rs]);
+        if (item < 0) break;
         const ItemGeom g = item_geom<BN>(P, item);
         const DevWeight& W = P.w[g.wi];
         const int KP = W.KP;
@@ -1833,7 +2187,14 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
       uint32_t t = 0, it = 0;
       bool ok = true;
       constexpr uint32_t idesc = idesc_f16(BN, CDT == kBF16 ? 1u : 0u);
-      for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x, ++it) {
+      for (;; ++it) {
+        if (!ok) break;
+        const int rs = static_cast<int>(it % kItemRing);
+        ok = mbar_wait(&item_full[rs], (it / kItemRing) & 1u, kStatusTimeoutLoad);
+        if (!ok) break;
+        const int item = *reinterpret_cast<volatile int*>(&item_ring[rs]);
+        mbar_arrive(&item_empty[rs]);
+        if (item < 0) break;
         const ItemGeom g = item_geom<BN>(P, item);
         const int KP = P.w[g.wi].KP;
         const int jb = it % NBB;
@@ -1876,7 +2237,16 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
     const int lt = tid - 64;
     uint32_t t = 0, it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x, ++it) {
+    for (;; ++it) {
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      const int rs = static_cast<int>(it % kItemRing);
+      ok = mbar_wait(&item_full[rs], (it / kItemRing) & 1u, kStatusTimeoutLoad);
+      ok = __all_sync(0xFFFFFFFFu, ok);  // one decision per warp
+      if (!ok) break;
+      const int item = *reinterpret_cast<volatile int*>(&item_ring[rs]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[rs]);
+      if (item < 0) break;
       const ItemGeom g = item_geom<BN>(P, item);
       const DevWeight& W = P.w[g.wi];
       const int KP = W.KP;
@@ -2019,7 +2389,16 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
     // Stages are released by four arrivals when warps release them one by one.
     constexpr uint32_t kStoreRelease = PASS == kFused ? 4u : 1u;
     bool ok = true;
-    for (int item = blockIdx.x; item < P.n_items && ok; item += gridDim.x, ++it_e) {
+    for (;; ++it_e) {
+      if (!ok) break;  // decided per warpgroup
+      const int rs = static_cast<int>(it_e % kItemRing);
+      ok = mbar_wait(&item_full[rs], (it_e / kItemRing) & 1u, kStatusTimeoutLoad);
+      ok = named_bar_and(bar_id, 128, ok);  // one decision per warpgroup
+      if (!ok) break;
+      const int item = *reinterpret_cast<volatile int*>(&item_ring[rs]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[rs]);
+      if (item < 0) break;
       const ItemGeom g = item_geom<BN>(P, item);
       const DevWeight& W = P.w[g.wi];
       const int local = item - W.item_begin;
@@ -2032,6 +2411,9 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
       QpCache qc;  // quantization block of this thread's row (FP8 / INT8)
       // Per-thread running reductions for REDUCE passes.
       float red_max = 0.0f, red_nmin = 0.0f;
+      // Packed per-row FP8 / INT8: this warpgroup saw a NaN or an infinity in the row
+      // (red_special), and so did some warpgroup (f_special, encode sweep).
+      bool red_special = false, f_special = false;
       int red_qp = -1;
       auto flush_reduce = [&]() {
         if (red_qp >= 0) {
@@ -2052,7 +2434,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
           } else {
             g_in = W.old_scale[0];
             const float amax = __uint_as_float(*W.qmax);
-            g_out = fmaxf(__fdiv_rn(amax, 2688.0f), 1.1920928955078125e-07f);  // `/ 2688.0`: IEEE
+            g_out = fmaxf(__fmul_rn(amax, 1.0f / 2688.0f), 1.1920928955078125e-07f);  // `/ 2688.0`: x * fp32(1 / 2688)
           }
         }
       }
@@ -2084,7 +2466,10 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
           if (st == g.n_tiles) {
             // Publish this warpgroup's partial row maxima (zero when it saw no
             // tile of the strip) for the encode steps of every warpgroup.
-            rpart[((it_e & 1u) * kEpiWGs + wg) * 128 + rt] = make_float2(red_max, red_nmin);
+            // A row holding a NaN or an infinity is flagged by the sign bit of
+            // its (non-negative) maximum.
+            rpart[((it_e & 1u) * kEpiWGs + wg) * 128 + rt] =
+                make_float2(__int_as_float(__float_as_int(red_max) | (red_special ? 0x80000000 : 0)), red_nmin);
             named_bar_sync(bar_id, 128);
             if (rt == 0) mbar_arrive(&rmax_bar[it_e & 1u]);
           }
@@ -2096,8 +2481,13 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
 #pragma unroll
           for (int w = 0; w < kEpiWGs; ++w) {
             const float2 v = rpart[((it_e & 1u) * kEpiWGs + w) * 128 + rt];
-            amax = fmaxf(amax, v.x);
+            amax = fmaxf(amax, fabsf(v.x));
             nmin = fmaxf(nmin, v.y);
+            f_special |= __float_as_int(v.x) < 0;
+          }
+          if constexpr (kPackedRow) {  // maxima of unrounded merged values: round them as the values would be
+            amax = round_dt<CDT>(amax);
+            nmin = round_dt<CDT>(nmin);
           }
           if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
             const bool asym = (W.flags & PIPER_FLAG_ASYMMETRIC) != 0u;
@@ -2182,7 +2572,15 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
         {
       if constexpr (FMT == PIPER_FMT_MXFP8_E4M3 || FMT == PIPER_FMT_MXFP8_E5M2 ||
                     FMT == PIPER_FMT_MXFP4) {
-        chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) { mx_chunk<FMT, CDT>(W, c, k, acc); });
+        chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) {
+          if (!mx_chunk_fast<FMT, CDT>(W, c, k, acc)) {
+            // The accumulator chunk is read again from tensor memory, so the
+            // fast path need not keep it live.
+            float acc2[32];
+            tmem_ld32(taddr + 32 * k, acc2);
+            mx_chunk<FMT, CDT>(W, c, k, acc2);
+          }
+        });
       } else if constexpr (FMT == PIPER_FMT_NVFP4) {
         chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) {
           nvfp4_chunk<PASS, CDT>(W, c, k, acc, g_in, g_out, two_level, red_max);
@@ -2290,7 +2688,71 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
         const int qmax = (W.flags & PIPER_FLAG_REDUCE_RANGE) ? 63 : 127;
         const PhiloxKey key = philox_key(W.k0, W.k1);
         const int nchunks = (tcols + 31) / 32;
-        if constexpr (PASS == kFused) {
+        if constexpr (kPackedRow) {
+          // Per-row TorchAO FP8 / INT8: packed decode and merge; the maxima
+          // sweep keeps the merged values unrounded and flags rows holding a
+          // NaN or an infinity, whose encode takes the general clamped path.
+          chunk_loop(0, nchunks, [&](int k, const float (&acc)[32]) {
+            uint32_t wv[8];
+            load_chunks32(c, k, wv);
+            float merged[32];
+            const int nvalid = min(32, tcols - 32 * k);
+            if (!enc_phase) {
+              if constexpr (kInt8) int8_merged_pk<CDT, false>(wv, acc, f_s_in, f_z_in, W.scale_dt, W.strength, merged);
+              else fp8_merged_pk<kE4, CDT, false>(wv, acc, f_s_in, W.strength, merged);
+              if (nvalid < 32) {  // columns past the row end are zero, which leaves the maxima unchanged
+#pragma unroll
+                for (int i = 0; i < 32; ++i) merged[i] = i < nvalid ? merged[i] : 0.0f;
+              }
+              if (valid) {
+                if constexpr (kInt8) {
+                  float hi = tree3(merged, max3_nan), lo = tree3(merged, min3_nan);
+                  if (!(hi <= 3.40282347e38f && lo >= -3.40282347e38f)) {  // a NaN or an infinity
+                    red_special = true;
+                    hi = tree3(merged, max3f);
+                    lo = tree3(merged, min3f);
+                  }
+                  red_max = fmaxf(red_max, hi);
+                  red_nmin = fmaxf(red_nmin, -lo);
+                } else {
+                  float cm = tree3(merged, max3_abs_nan);
+                  if (!(cm <= 3.40282347e38f)) {  // a NaN or an infinity
+                    red_special = true;
+                    cm = tree3(merged, max3_abs);
+                  }
+                  red_max = fmaxf(red_max, cm);
+                }
+              }
+            } else {
+              if constexpr (kInt8) int8_merged_pk<CDT, true>(wv, acc, f_s_in, f_z_in, W.scale_dt, W.strength, merged);
+              else fp8_merged_pk<kE4, CDT, true>(wv, acc, f_s_in, W.strength, merged);
+              uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+              if (valid) {
+                const uint64_t off0 =
+                    W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + c0 + 32 * k;
+                const bool sr_on = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+                if (!f_special) {
+                  if constexpr (kInt8) {
+                    if (sr_on) int8_encode32(merged, f_q, qmin, qmax, W.scale_dt, true, key, off0, out);
+                    else int8_encode_rtn_finite(merged, f_q, qmin, qmax, W.scale_dt, out);
+                  } else {
+                    if (sr_on) fp8_encode_sr_finite<kE4>(merged, f_s, key, off0, out);
+                    else fp8_encode_rtn_finite<kE4>(merged, f_s, out);
+                  }
+                } else {
+                  if (nvalid < 32) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) merged[i] = i < nvalid ? merged[i] : 0.0f;
+                  }
+                  if constexpr (kInt8) int8_encode32(merged, f_q, qmin, qmax, W.scale_dt, sr_on, key, off0, out);
+                  else if (sr_on) fp8_encode_sr<kE4>(merged, f_s, kLimit, key, off0, out);
+                  else fp8_encode_rtn<kE4>(merged, f_s, kLimit, out);
+                }
+              }
+              store_chunks32(c, k, out);
+            }
+          });
+        } else if constexpr (PASS == kFused) {
           // Per-row layout: one quantization block per row, qparams on chip.
           chunk_loop(0, nchunks, [&](int k, const float (&acc)[32]) {
             float merged[32];
@@ -2403,7 +2865,9 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
                 return;
               }
             }
-            if (W.nq_row == 0 || (W.group >= 32 && (col % W.group) + 32 <= W.group)) {
+            // A chunk whose valid columns all lie in one quantization block
+            // (the tail chunk of a row included) decodes with one scale.
+            if (W.nq_row == 0 || (W.group >= 32 && (col % W.group) + nvalid <= W.group)) {
               float s_in = 1.0f;
               int z_in = 0;
               if (valid) {
@@ -2474,7 +2938,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
                   W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + col;
               const bool sr_on = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
               const bool uniform_chunk =
-                  W.nq_row == 0 || (W.group >= 32 && (col % W.group) + 32 <= W.group);
+                  W.nq_row == 0 || (W.group >= 32 && (col % W.group) + nvalid <= W.group);
               if (valid && uniform_chunk) {
                 // One quantization block covers the whole chunk (per-row / per-tensor).
                 const int qp = qparam_index(W, row, col);
@@ -2977,6 +3441,25 @@ uint64_t current_context_id() {
   return static_cast<uint64_t>(id) + 1u;
 }
 
+// Device address of the launch item counters (pm::g_sched_next) in the
+// current context, looked up once per context.
+unsigned int* sched_counters() {
+  static std::mutex mu;
+  static uint64_t cached_ctx[kMaxDevices] = {};
+  static unsigned int* cached_ptr[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  uint64_t ctx = current_context_id();
+  if (ctx == 0 || cached_ctx[dev] != ctx || cached_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, pm::g_sched_next) != cudaSuccess) return nullptr;
+    cached_ptr[dev] = static_cast<unsigned int*>(ptr);
+    cached_ctx[dev] = current_context_id();
+  }
+  return cached_ptr[dev];
+}
+
 // ------------------------------------------------------------- dispatch
 // One CTA per SM: the kernel allocates 2 * BN of the SM's 512 tensor-memory
 // columns, and the shared-memory request (at least half the SM's) keeps a
@@ -3004,6 +3487,13 @@ int launch_t(LaunchParams& lp, int items, int kp_max, cudaStream_t stream) {
   }
   lp.n_items = items;
   lp.kp_max = kp_max;
+  // This launch's item counter: the next slot of the ring, zeroed on the stream.
+  static std::atomic<uint32_t> launch_seq{0};
+  lp.sched_slot = launch_seq.fetch_add(1, std::memory_order_relaxed) % pm::kSchedSlots;
+  unsigned int* counters = sched_counters();
+  if (counters == nullptr) return fail(PIPER_MERGE_ECUDA, "cudaGetSymbolAddress of the item counters failed.");
+  e = cudaMemsetAsync(counters + lp.sched_slot, 0, sizeof(unsigned int), stream);
+  if (e != cudaSuccess) return fail(PIPER_MERGE_ECUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   lp.c_stages = pc.sc;
   lp.a_stages = pc.sa;
   lp.b_bufs = pc.nbb;
@@ -3029,48 +3519,62 @@ int launch_bn(int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
   return launch_t<FMT, PASS, 64, CDT>(lp, items, kp, s);
 }
 
+// Development builds may compile a subset of the formats: -DPIPER_ONLY_FMTS=<bitmask of PIPER_FMT_* ids>.
+#ifdef PIPER_ONLY_FMTS
+constexpr bool fmt_on(int f) { return ((PIPER_ONLY_FMTS) >> f) & 1; }
+#else
+constexpr bool fmt_on(int) { return true; }
+#endif
+
 template <int PASS, int CDT>
 int launch_fmt(int fmt, int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
+  if (!fmt_on(fmt)) return fail(PIPER_MERGE_EINVAL, "format not compiled into this build.");
   switch (fmt) {
     case PIPER_FMT_MXFP8_E4M3:
-      if constexpr (PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_MXFP8_E4M3) && PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_MXFP8_E5M2:
-      if constexpr (PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_MXFP8_E5M2) && PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_MXFP4:
-      if constexpr (PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP4, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_MXFP4) && PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP4, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_NVFP4:
-      if constexpr ((PASS == pm::kLocal || PASS == pm::kReduce) && CDT == pm::kBF16)
+      if constexpr (fmt_on(PIPER_FMT_NVFP4) && (PASS == pm::kLocal || PASS == pm::kReduce) && CDT == pm::kBF16)
         return launch_bn<PIPER_FMT_NVFP4, PASS, CDT>(bn, lp, items, kp, s);
       break;
-    case PIPER_FMT_FP8_E4M3: return launch_bn<PIPER_FMT_FP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
-    case PIPER_FMT_FP8_E5M2: return launch_bn<PIPER_FMT_FP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
-    case PIPER_FMT_INT8: return launch_bn<PIPER_FMT_INT8, PASS, CDT>(bn, lp, items, kp, s);
+    case PIPER_FMT_FP8_E4M3:
+      if constexpr (fmt_on(PIPER_FMT_FP8_E4M3)) return launch_bn<PIPER_FMT_FP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_FP8_E5M2:
+      if constexpr (fmt_on(PIPER_FMT_FP8_E5M2)) return launch_bn<PIPER_FMT_FP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
+      break;
+    case PIPER_FMT_INT8:
+      if constexpr (fmt_on(PIPER_FMT_INT8)) return launch_bn<PIPER_FMT_INT8, PASS, CDT>(bn, lp, items, kp, s);
+      break;
     case PIPER_FMT_BNB8:  // per-row, fp16 only
-      if constexpr (PASS == pm::kFused && CDT == pm::kF16) return launch_bn<PIPER_FMT_BNB8, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_BNB8) && PASS == pm::kFused && CDT == pm::kF16) return launch_bn<PIPER_FMT_BNB8, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_QUANTO_INT8:  // per-row (fused) or per-tensor (reduce + encode)
-      if constexpr (PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_INT8, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_QUANTO_INT8) && PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_INT8, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_QUANTO_FP8_E4M3:
-      if constexpr (PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_FP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_QUANTO_FP8_E4M3) && PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_FP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_QUANTO_FP8_E5M2:
-      if constexpr (PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_FP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_QUANTO_FP8_E5M2) && PASS != pm::kLocal) return launch_bn<PIPER_FMT_QUANTO_FP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_BNB4_NF4:
-      if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_BNB4_NF4, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_BNB4_NF4) && PASS == pm::kLocal) return launch_bn<PIPER_FMT_BNB4_NF4, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_BNB4_FP4:
-      if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_BNB4_FP4, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_BNB4_FP4) && PASS == pm::kLocal) return launch_bn<PIPER_FMT_BNB4_FP4, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_GGUF_Q8_0:
-      if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_GGUF_Q8_0, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_GGUF_Q8_0) && PASS == pm::kLocal) return launch_bn<PIPER_FMT_GGUF_Q8_0, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_GGUF_Q4_0:
-      if constexpr (PASS == pm::kLocal) return launch_bn<PIPER_FMT_GGUF_Q4_0, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_GGUF_Q4_0) && PASS == pm::kLocal) return launch_bn<PIPER_FMT_GGUF_Q4_0, PASS, CDT>(bn, lp, items, kp, s);
       break;
     default: break;
   }
@@ -3243,11 +3747,16 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
   if (segs.empty()) return PIPER_MERGE_OK;
   const piper_merge_desc& d0 = descs[segs[0].desc];
   const Plan& p0 = plans[segs[0].desc];
+  // Items are taken in order by the CTAs (largest first balances the tail):
+  // the widest weights, whose items cost the most, come first.
+  std::vector<Segment> order(segs);
+  std::stable_sort(order.begin(), order.end(),
+                   [&](const Segment& x, const Segment& y) { return descs[x.desc].cols > descs[y.desc].cols; });
   LaunchParams lp;
   std::memset(&lp, 0, sizeof(lp));
   lp.n_weights = static_cast<int>(segs.size());
-  // Work items: (128-row strip, column range) pairs. Persistent CTAs stride
-  // over them; aim for ~32 items per SM so the last wave is short.
+  // Work items: (128-row strip, column range) pairs, taken by the persistent
+  // CTAs one at a time; aim for ~32 items per SM so the last wave is short.
   int kp_max = 16;
   int64_t total_tiles = 0;
   for (const Segment& sg : segs) {
@@ -3257,10 +3766,10 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
   const int64_t target_items = 32ll * sm_count();
   const int tiles_per_item = static_cast<int>(std::max<int64_t>(1, total_tiles / target_items));
   int items = 0;
-  for (size_t i = 0; i < segs.size(); ++i) {
-    const piper_merge_desc& d = descs[segs[i].desc];
-    const Plan& p = plans[segs[i].desc];
-    DevWeight w = make_dev_weight(d, p, ws, segs[i]);
+  for (size_t i = 0; i < order.size(); ++i) {
+    const piper_merge_desc& d = descs[order[i].desc];
+    const Plan& p = plans[order[i].desc];
+    DevWeight w = make_dev_weight(d, p, ws, order[i]);
     const int col_tiles = static_cast<int>((d.cols + p.bn - 1) / p.bn);
     // Fused per-row passes need whole rows in one item.
     const int ci = p.fused ? 1 : std::max(1, (col_tiles + tiles_per_item - 1) / tiles_per_item);
@@ -3310,13 +3819,24 @@ bool same_kernel(const piper_merge_desc& a, const Plan& pa, const piper_merge_de
          pa.two_pass == pb.two_pass && pa.fused == pb.fused && pa.flavor == pb.flavor;  // col_axis is per weight
 }
 
+// Per-row FP8 / INT8 weights run the one-launch fused pass, which keeps each
+// strip's row maxima on chip but has one work item per 128-row strip. When a
+// whole call holds fewer such strips than kSplitStripsPerSm per SM (one small
+// weight, e.g. 4096 rows = 32 strips), most SMs would idle, so those weights
+// run the reduce / encode launches instead, whose items also split the
+// columns, with 16 bytes of workspace per row. A caller that provides no
+// workspace still gets the fused pass (piper_merge_batch plans again without
+// the split).
+constexpr int kSplitStripsPerSm = 2;
+
 int plan_all(const piper_merge_desc* in, int count, std::vector<piper_merge_desc>& descs,
-             std::vector<Plan>& plans, size_t& ws_total) {
+             std::vector<Plan>& plans, size_t& ws_total, bool split_small_rows = true) {
   if (count < 0) return fail(PIPER_MERGE_EINVAL, "negative descriptor count.");
   if (count > 0 && in == nullptr) return fail(PIPER_MERGE_EINVAL, "null descriptor array.");
   descs.assign(in, in + count);
   plans.assign(count, Plan());
   ws_total = 0;
+  int64_t fused_strips = 0;
   for (int i = 0; i < count; ++i) {
     int flavor = pm::kTorchao;
     bool col_axis = false;
@@ -3329,6 +3849,18 @@ int plan_all(const piper_merge_desc* in, int count, std::vector<piper_merge_desc
       plans[i].col_axis = true;
       plans[i].nq = static_cast<int>(descs[i].cols);
     }
+    if (plans[i].fused) fused_strips += (descs[i].rows + 127) / 128;
+  }
+  if (split_small_rows && fused_strips > 0 && fused_strips < static_cast<int64_t>(kSplitStripsPerSm) * sm_count()) {
+    for (int i = 0; i < count; ++i) {
+      Plan& p = plans[i];
+      if (!p.fused || p.flavor == pm::kBnb) continue;  // bitsandbytes 8-bit has the fused pass only
+      p.fused = false;
+      p.two_pass = true;
+      p.nq = static_cast<int>(descs[i].rows) * p.nq_row;
+    }
+  }
+  for (int i = 0; i < count; ++i) {
     plans[i].ws_off = ws_total;
     ws_total += scratch_bytes(plans[i].nq, scratch_words(descs[i].format));
   }
@@ -3357,6 +3889,10 @@ int piper_merge_batch(const piper_merge_desc* in, int32_t count, void* workspace
   size_t total = 0;
   int rc = plan_all(in, count, descs, plans, total);
   if (rc) return rc;
+  if (total > 0 && (workspace == nullptr || workspace_bytes < total)) {
+    rc = plan_all(in, count, descs, plans, total, /*split_small_rows=*/false);
+    if (rc) return rc;
+  }
   if (total > 0 && (workspace == nullptr || workspace_bytes < total))
     return fail(PIPER_MERGE_EWORKSPACE, "workspace of " + std::to_string(workspace_bytes) +
                                              " bytes is smaller than the required " +

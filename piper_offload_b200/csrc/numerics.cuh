@@ -451,4 +451,72 @@ __device__ __forceinline__ bool near_e2m1_edge(float q) {
   const uint32_t low = a & 0x1FFFFFu;
   return e >= -3 && e <= 2 && (low <= 4u || low >= 0x200000u - 4u);
 }
+
+// sr_fp8xn for values that are finite with |v| <= limit * (1 + 2^-8), as the
+// quotients of an all-finite row are: the same codes with fewer instructions.
+//  * Lower neighbour: in the normal range, |v| with the fp32 bits below the
+//    kept mantissa cleared is the largest FP8 value <= |v|; the upper one is
+//    that plus 2^kDrop in the bits. Both keep v's sign, and the satfinite
+//    conversion turns a step past the largest finite value back into it, the
+//    reference's non-stochastic result for |v| >= limit.
+//  * Draw: the reference's u = fp32(fp32(x) * c), c = 2^-31 (1 - 2^-24), is the
+//    float just below z = fp32(x) * 2^-31 for every x >= 1 (the product
+//    z - z * 2^-24 lies within half an ulp above that float), so for p > 0,
+//    u < p holds exactly when z <= p, i.e. fp32(x) <= p * 2^31; x = 0 gives
+//    u = 0 < p as well. p * 2^31 is read off the mantissa bits like p.
+//  * Below the smallest normal the grid is uniform (gap 2^-9 / 2^-16); that
+//    branch runs only when a lane of the active part of the warp needs it.
+template <bool E4M3, int N>
+__device__ __forceinline__ void sr_fp8xn_finite(const float (&v)[N], const PhiloxKey& key, uint64_t off,
+                                                uint32_t (&words)[N / 4]) {
+  constexpr int kMant = E4M3 ? 3 : 2;
+  constexpr int kDrop = 23 - kMant;
+  constexpr uint32_t kMinNormal = E4M3 ? 0x3C800000u : 0x38800000u;
+  constexpr float kSubScale = E4M3 ? 512.0f : 65536.0f;
+  constexpr float kSubGap = E4M3 ? 1.0f / 512.0f : 1.0f / 65536.0f;
+  uint32_t r[N];
+  philox_word0_xn<N>(key, off, r);
+  float P[N];      // p * 2^31
+  uint32_t y[N];   // fp32 bits of the chosen FP8 value
+  bool sub = false;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const uint32_t bits = __float_as_uint(v[j]);
+    const uint32_t abits = bits & 0x7FFFFFFFu;
+    sub |= abits < kMinNormal;
+    P[j] = __uint_as_float(0x4F000000u | ((abits << kMant) & 0x7FFFFFu)) - 2147483648.0f;
+    y[j] = bits & ~((1u << kDrop) - 1u);
+  }
+  const bool any_sub = __any_sync(__activemask(), sub);
+  if (any_sub) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float t = __uint_as_float(__float_as_uint(v[j]) & 0x7FFFFFFFu) * kSubScale;
+      const float fl = truncf(t);
+      if ((__float_as_uint(v[j]) & 0x7FFFFFFFu) < kMinNormal) P[j] = (t - fl) * 2147483648.0f;
+    }
+  }
+  uint32_t upm = 0u;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
+    const bool up = P[j] > 0.0f && __int2float_rn(x) <= P[j];
+    y[j] += up ? (1u << kDrop) : 0u;
+    upm |= up ? (1u << j) : 0u;
+  }
+  if (any_sub) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const uint32_t bits = __float_as_uint(v[j]);
+      const float t = __uint_as_float(bits & 0x7FFFFFFFu) * kSubScale;
+      const float fl = truncf(t) + ((upm >> j) & 1u ? 1.0f : 0.0f);
+      if ((bits & 0x7FFFFFFFu) < kMinNormal) y[j] = __float_as_uint(fl * kSubGap) | (bits & 0x80000000u);
+    }
+  }
+#pragma unroll
+  for (int w = 0; w < N / 4; ++w)
+    words[w] = enc_fp8x4<E4M3>(__uint_as_float(y[4 * w]), __uint_as_float(y[4 * w + 1]), __uint_as_float(y[4 * w + 2]),
+                               __uint_as_float(y[4 * w + 3]));
+}
+
 }  // namespace pm

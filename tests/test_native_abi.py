@@ -76,8 +76,12 @@ def test_invalid_descriptors_are_rejected_on_host(kw, match):
 
 def test_workspace_sizes():
     assert nat.workspace_bytes([_desc(format=nat.FMT_MXFP8_E4M3)]) == 0
-    # per-row layouts keep their row maxima on chip (one fused launch): no workspace
-    assert nat.workspace_bytes([_desc()]) == 0
+    # A per-row weight too small to fill the GPU with whole 128-row strips asks
+    # for 16 bytes per row (column-split reduce / encode launches) ...
+    assert nat.workspace_bytes([_desc()]) == 64 * 16
+    # ... which is optional: with no workspace the fused launch runs (checked
+    # on the GPU); enough strips for two per SM keep their maxima on chip.
+    assert nat.workspace_bytes([_desc(rows=128 * 2 * 148)]) == 0
     # groups wider than a tile: 64 rows x 2 blocks x 16 bytes
     assert nat.workspace_bytes([_desc(cols=1024, block_cols=512)]) == 2048
     per_tensor = nat.workspace_bytes([_desc(block_rows=64, block_cols=256)])
@@ -86,6 +90,8 @@ def test_workspace_sizes():
     assert grouped_local == 0
     two = nat.workspace_bytes([_desc(cols=1024, block_cols=512), _desc(block_rows=64, block_cols=256)])
     assert two == 2048 + 256
+    # several small per-row weights together still fill fewer than two strips per SM
+    assert nat.workspace_bytes([_desc(), _desc(rows=300)]) == 64 * 16 + (300 * 16 + 255) // 256 * 256  # 256-byte aligned
 
 
 def test_workspace_too_small_is_reported():
@@ -136,9 +142,13 @@ def test_new_format_validation_messages():
     assert b"last axis" in nat.load().piper_merge_last_error()
     # last-axis scales: one workspace slot (16 B) per column
     assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_INT8, block_rows=64, block_cols=1)]) == 256 * 16
-    # per-tensor Quanto and static FP8 take the two-pass workspace; per-row needs none
+    # per-tensor Quanto and static FP8 take the two-pass workspace; a per-row
+    # weight needs none once it has two 128-row strips per SM (a small one asks
+    # for the optional 16 bytes per row); bitsandbytes 8-bit has the fused pass only
     assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_FP8_E4M3, block_rows=64, block_cols=256)]) == 256
-    assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_INT8, block_rows=1, block_cols=256)]) == 0
+    assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_INT8, block_rows=1, block_cols=256)]) == 64 * 16
+    assert nat.workspace_bytes([_desc(format=nat.FMT_QUANTO_INT8, rows=128 * 2 * 148, block_rows=1,
+                                      block_cols=256)]) == 0
     assert nat.workspace_bytes([_desc(format=nat.FMT_BNB8, compute_dtype=nat.DT_F16, block_rows=1,
                                       block_cols=256)]) == 0
 

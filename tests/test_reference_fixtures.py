@@ -6,8 +6,10 @@ raw-buffer launchers of the reference (``merge_float8_lora``,
 ``merge_static_float8_lora``, ``merge_bnb8_lora``, ``merge_quanto_qint8_lora``,
 ``merge_quanto_qfloat8_lora``) at the
 reference tests' shapes, across layouts, scale modes, swizzling, rounding
-modes, factor and scale dtypes, negative strengths and zero factors. Their
-divisions are IEEE, which the oracle computes without its GPU-division hook.
+modes, factor and scale dtypes, negative strengths and zero factors. The
+interpreter divides in IEEE fp32, by a tensor and by a constant alike, so the
+oracle runs here without its GPU-division hook and with IEEE constant
+division (on the GPU, Triton multiplies by the constant's fp32 reciprocal).
 """
 
 from __future__ import annotations
@@ -15,8 +17,16 @@ from __future__ import annotations
 import pytest
 
 import reference_fixtures as rf
+from oracle import numerics as onum
 
 CASES = rf.cases()
+
+
+@pytest.fixture(scope="module", autouse=True)
+def interpreter_division():
+    onum.set_constant_division("ieee")
+    yield
+    onum.set_constant_division("reciprocal")
 
 
 def test_fixture_coverage():

@@ -22,6 +22,18 @@ Two input kinds:
 
 With ``PIPER_PARITY_LOG`` set, each comparison appends its counts as a JSON
 line to that file.
+
+One known exception: the reference's FP8 stochastic rounding
+(``_stochastic_float8``, ``_triton_stochastic_quantization.py:132-175``) is
+miscompiled by the triton 3.6 in this image on sm_100 (the reference pins
+triton >= 3.7). Run on its own over 1M values, every odd-indexed element of a
+1-D block decodes to +-2^-9, and where round-to-nearest rounds up (p > 0.5)
+the result is always the upper code, as if the fp32 -> fp8 -> fp32 round trip
+of ``deterministic_value`` were folded into the identity; 2-D blocks show the
+second effect only. Those comparisons (FP8 e4m3/e5m2 and MXFP8 with a seed)
+are expected failures under triton < 3.7; the kernels follow the reference
+source, which the interpreter-recorded fixtures pin
+(``tests/test_reference_fixtures.py``).
 """
 
 from __future__ import annotations
@@ -120,12 +132,29 @@ def log_counts(name: str, case: Case, d, ref) -> None:
         fh.write(json.dumps(rec) + "\n")
 
 
+FP8_SR_FORMATS = ("fp8_row", "fp8_tensor", "fp8_group", "mxfp8", "mxfp8_e5m2")
+
+
+def triton_fp8_sr_broken(ref) -> bool:
+    major, minor = (int(x) for x in ref["triton_version"].split(".")[:2])
+    return (major, minor) < (3, 7)
+
+
 def versus_reference(ref, case: Case, dev, name: str, *, exact: bool):
     got = case.run_native(dev)
-    want = run_reference(ref, case, dev)
+    try:
+        want = run_reference(ref, case, dev)
+    except RuntimeError as exc:  # a compile failure on the host; nothing ran on the device
+        if "PassManager::run failed" in str(exc):
+            pytest.skip(f"the reference kernel for {case.fmt} does not compile under triton {ref['triton_version']} "
+                        "on sm_100 (MLIR: parent layout must have at least rank >= 2)")
+        raise
     torch.cuda.synchronize(dev)
     d = compare(case, got, want)
     log_counts(name, case, d, ref)
+    if case.seed is not None and case.fmt in FP8_SR_FORMATS and triton_fp8_sr_broken(ref) and d.code_mismatch:
+        pytest.xfail(f"reference FP8 stochastic rounding is miscompiled by triton {ref['triton_version']} "
+                     f"on sm_100 ({d.code_mismatch} of {d.n} codes differ)")
     allowed = 0 if exact else math.floor(TIE_FRACTION * d.n)
     assert d.max_step <= (0 if exact else 1), f"{name}: {d}"
     assert d.code_mismatch <= allowed, f"{name}: {d.code_mismatch} > {allowed} ({d})"

@@ -6,10 +6,12 @@ anything. It is for callers that cannot allocate device memory when they
 merge (a C/C++ host without PyTorch's caching allocator, or a process whose
 device memory is already reserved by a model cache).
 
-Only the "tensor" and "group512" cases go through the static scratch array:
-per-row layouts run the one-launch fused pass, which keeps its row maxima on
-chip and needs no scratch; they are kept to show the entry point is a plain
-drop-in there too. Collected last so it also runs after every other test.
+Every case here goes through the static scratch array: per-tensor scales and
+512-column groups always do, and the per-row weights (300 and 70 rows) are too
+small to fill the GPU with whole 128-row strips, so they split their columns
+over the reduce / encode launches, whose row maxima live in the scratch. (A
+per-row weight with at least two strips per SM runs the one-launch fused pass
+and needs none.) Collected last so it also runs after every other test.
 """
 
 from __future__ import annotations
