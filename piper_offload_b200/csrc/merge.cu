@@ -692,6 +692,92 @@ __device__ __forceinline__ void nvfp4_block(const DevWeight& W, const RowCtx& c,
   }
 }
 
+// Fast path of nvfp4_block, same codes and scales, for a block whose decoded
+// scale is a non-negative finite value (so no base value is -0, and
+// fma(acc, strength, base) equals the reference's `where(update == 0, base,
+// base + update)` for every update, signed zeros included) and whose merged
+// values are all finite: the merge runs two elements per packed instruction,
+// the block maximum takes three-operand maxima, and the satfinite E2M1
+// conversion clamps as the reference's clamp to [-6, 6] does for finite
+// values (stochastic codes keep the top code from 6 up). The quotient of a
+// single-level block is div.full, as the reference divides. Returns false,
+// having written nothing, for any other block.
+template <int PASS, int CDT>
+__device__ __forceinline__ bool nvfp4_block_fast(const DevWeight& W, const RowCtx& c, int col, const float* acc,
+                                                 float g_in, float g_out, bool two_level, float& amax_acc,
+                                                 uint2& codes) {
+  const int blk = col >> 4;
+  float bsc = dec_e4m3(c.valid ? c.sscale[blk - c.blk0] : 0u);
+  if (two_level) {
+    bsc = __fmul_rn(bsc, g_in);
+    if (CDT == kBF16) bsc = bf16r(bsc);
+  }
+  if (__float_as_uint(bsc) >= 0x7F800000u) return false;  // negative (incl. -0), infinite or NaN
+  float m[16];
+  const uint32_t wv[2] = {codes.x, codes.y};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) dec_e2m1x2(wv[j >> 2] >> ((j & 3) * 8), m[2 * j], m[2 * j + 1]);
+  const float2 b2 = make_float2(bsc, bsc);
+  const float2 st2 = make_float2(W.strength, W.strength);
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    float2 t = __fmul2_rn(make_float2(m[i], m[i + 1]), b2);
+    if (CDT == kBF16 && two_level) bf16r2(t.x, t.y);  // single-level products are exact bf16 values
+    t = __ffma2_rn(make_float2(acc[i], acc[i + 1]), st2, t);
+    round_dt2<CDT>(t.x, t.y);
+    m[i] = t.x;
+    m[i + 1] = t.y;
+  }
+  const float amax = tree3(m, max3_abs_nan);
+  if (!(amax <= 3.40282347e38f)) return false;
+  if constexpr (PASS == kReduce) {
+    if (c.valid) amax_acc = fmaxf(amax_acc, amax);
+    return true;
+  } else {
+    uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
+    float fs = __fmul_rn(amax, 1.0f / 6.0f);  // `/ 6.0` (literal): x * fp32(1 / 6) on sm_100
+    if (two_level) fs = div_full(fs, g_out);
+    fs = fminf(fmaxf(fs, 0.015625f), 448.0f);
+    const uint32_t fcode = enc_e4m3(fs);
+    fs = dec_e4m3(fcode);
+    const int64_t sidx = scale_index(W, c.row, blk);
+    if (c.valid) scale8[sidx] = static_cast<uint8_t>(fcode);
+    else if (W.flags & PIPER_FLAG_SWIZZLED) scale8[sidx] = 0u;  // swizzle padding rows
+    if (two_level) {
+      const float recip = div_full(div_full(1.0f, g_out), fs);
+      const float2 r2 = make_float2(recip, recip);
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        const float2 t = __fmul2_rn(make_float2(m[i], m[i + 1]), r2);
+        m[i] = t.x;
+        m[i + 1] = t.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m[i] = div_full(m[i], fs);
+    }
+    uint32_t out[2] = {0u, 0u};
+    if (W.flags & PIPER_FLAG_STOCHASTIC) {
+      const PhiloxKey key = philox_key(W.k0, W.k1);
+      const uint64_t off0 = W.offset_base + static_cast<uint64_t>(c.row) * static_cast<uint64_t>(W.N) + col;
+#pragma unroll
+      for (int w = 0; w < 2; ++w) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = m[8 * w + j];
+        uint32_t nib[1];
+        sr_e2m1xn<8>(v, key, off0 + 8 * w, nib);
+        out[w] = nib[0];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j >> 2] |= enc_e2m1x2(m[2 * j], m[2 * j + 1]) << ((j & 3) * 8);
+    }
+    codes = make_uint2(out[0], out[1]);
+    return true;
+  }
+}
+
 template <int PASS, int CDT>
 __device__ __forceinline__ void nvfp4_chunk(const DevWeight& W, const RowCtx& c, int k,
                                             const float (&acc)[32], float g_in, float g_out,
@@ -699,8 +785,10 @@ __device__ __forceinline__ void nvfp4_chunk(const DevWeight& W, const RowCtx& c,
   const int col = c.tile_col0 + 32 * k;
   uint4 pk = *reinterpret_cast<const uint4*>(chunk_ptr(c, k));
   uint2 lo = make_uint2(pk.x, pk.y), hi = make_uint2(pk.z, pk.w);
-  nvfp4_block<PASS, CDT>(W, c, col, acc, g_in, g_out, two_level, amax_acc, lo);
-  nvfp4_block<PASS, CDT>(W, c, col + 16, acc + 16, g_in, g_out, two_level, amax_acc, hi);
+  if (!nvfp4_block_fast<PASS, CDT>(W, c, col, acc, g_in, g_out, two_level, amax_acc, lo))
+    nvfp4_block<PASS, CDT>(W, c, col, acc, g_in, g_out, two_level, amax_acc, lo);
+  if (!nvfp4_block_fast<PASS, CDT>(W, c, col + 16, acc + 16, g_in, g_out, two_level, amax_acc, hi))
+    nvfp4_block<PASS, CDT>(W, c, col + 16, acc + 16, g_in, g_out, two_level, amax_acc, hi);
   if constexpr (PASS != kReduce)
     *reinterpret_cast<uint4*>(chunk_ptr(c, k)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
 }
@@ -1897,13 +1985,12 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
 // Epilogue warpgroups per format and tile width (tile t -> warpgroup t % EW).
 // Three give the epilogue more warps in flight; GGUF keeps two so that its
 // 256-column tiles (the narrowest whose rows are 16-byte multiples) fit two
-// accumulators, and bitsandbytes 4-bit keeps two for its per-lane tables.
-// NVFP4 runs two on 256-column tiles (round to nearest: fewer, wider tiles
-// measured faster) and three on narrower ones (stochastic rounding, where the
-// Philox draws want the extra warps).
-__host__ __device__ constexpr int epi_wgs_rt(int fmt, int bn) {
+// accumulators, bitsandbytes 4-bit keeps two for its per-lane tables, and
+// NVFP4 keeps two for the registers of its two-block chunks (with three, its
+// 152 registers per thread spill).
+__host__ __device__ constexpr int epi_wgs_rt(int fmt, int /*bn*/) {
   return (fmt == PIPER_FMT_GGUF_Q8_0 || fmt == PIPER_FMT_GGUF_Q4_0 || fmt == PIPER_FMT_BNB4_NF4 ||
-          fmt == PIPER_FMT_BNB4_FP4 || (fmt == PIPER_FMT_NVFP4 && bn >= 256))
+          fmt == PIPER_FMT_BNB4_FP4 || fmt == PIPER_FMT_NVFP4)
              ? 2
              : 3;
 }
@@ -3363,10 +3450,7 @@ int validate(const piper_merge_desc& d, Plan& p) {
   auto fits = [&](int bn, int min_sc) {
     return 512 / bn >= pm::epi_wgs_rt(d.format, bn) && plan_pipe(d.format, bn, kp).sc >= min_sc;
   };
-  // Stochastic NVFP4 takes 128-column tiles and their third epilogue warpgroup.
-  const bool nvfp4_sr = d.format == PIPER_FMT_NVFP4 && (d.flags & PIPER_FLAG_STOCHASTIC) != 0u;
-  if (nvfp4_sr && fits(128, 4)) p.bn = 128;
-  else if (fits(256, 4)) p.bn = 256;
+  if (fits(256, 4)) p.bn = 256;
   else if (fits(128, 4)) p.bn = 128;
   else if (fits(64, 2)) p.bn = 64;
   else return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(d.rank) + " is too large for the merge pipeline.");

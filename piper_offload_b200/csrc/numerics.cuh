@@ -496,20 +496,20 @@ __device__ __forceinline__ void sr_fp8xn_finite(const float (&v)[N], const Philo
       if ((__float_as_uint(v[j]) & 0x7FFFFFFFu) < kMinNormal) P[j] = (t - fl) * 2147483648.0f;
     }
   }
-  uint32_t upm = 0u;
 #pragma unroll
   for (int j = 0; j < N; ++j) {
     const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
     const bool up = P[j] > 0.0f && __int2float_rn(x) <= P[j];
     y[j] += up ? (1u << kDrop) : 0u;
-    upm |= up ? (1u << j) : 0u;
   }
-  if (any_sub) {
+  if (any_sub) {  // the draw is taken again for values below the smallest normal
 #pragma unroll
     for (int j = 0; j < N; ++j) {
       const uint32_t bits = __float_as_uint(v[j]);
+      const int32_t x = static_cast<int32_t>(r[j]) ^ (static_cast<int32_t>(r[j]) >> 31);
+      const bool up = P[j] > 0.0f && __int2float_rn(x) <= P[j];
       const float t = __uint_as_float(bits & 0x7FFFFFFFu) * kSubScale;
-      const float fl = truncf(t) + ((upm >> j) & 1u ? 1.0f : 0.0f);
+      const float fl = truncf(t) + (up ? 1.0f : 0.0f);
       if ((bits & 0x7FFFFFFFu) < kMinNormal) y[j] = __float_as_uint(fl * kSubGap) | (bits & 0x80000000u);
     }
   }

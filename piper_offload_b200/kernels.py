@@ -674,6 +674,28 @@ def gguf_logical_cols(packed_cols: int, quant_type: int) -> int:
     return packed_cols // ts * 32
 
 
+def validate_gguf_merge(raw: torch.Tensor, quant_type: int, b: torch.Tensor,
+                        a: torch.Tensor) -> tuple[int, int, int, int]:
+    """The GGUF merge's checks, raising ``ValueError`` before anything is
+    enqueued; returns (compute dtype id, rows, logical cols, rank)."""
+    if raw.device.type != "cuda":
+        raise ValueError("GGUF merge requires CUDA tensors.")
+    if raw.dtype is not torch.uint8 or raw.ndim != 2:
+        raise ValueError("GGUF merge expects a rank-two uint8 tensor of raw blocks.")
+    if not raw.is_contiguous():
+        raise ValueError("GGUF merge requires contiguous raw blocks.")
+    cdt = _factor_dt(b, a, allowed=(torch.float16, torch.bfloat16, torch.float32))
+    _same_device(raw, b, a)
+    rows = raw.shape[0]
+    cols = gguf_logical_cols(raw.shape[1], int(quant_type))
+    rank = a.shape[0]
+    if rows == 0 or cols == 0 or rank == 0:
+        raise ValueError("GGUF merge requires non-empty weight and factors.")
+    if tuple(b.shape) != (rows, rank) or a.shape[1] != cols:
+        raise ValueError("LoRA factors do not match the GGUF weight shape.")
+    return cdt, rows, cols, rank
+
+
 def merge_gguf_lora_(
     raw: torch.Tensor,
     quant_type: int,
@@ -692,21 +714,7 @@ def merge_gguf_lora_(
     ``quants.Q8_0/Q4_0.quantize_blocks`` bit for bit (round-to-nearest) or
     rounds each code stochastically by logical element offset.
     """
-    if raw.device.type != "cuda":
-        raise ValueError("GGUF merge requires CUDA tensors.")
-    if raw.dtype is not torch.uint8 or raw.ndim != 2:
-        raise ValueError("GGUF merge expects a rank-two uint8 tensor of raw blocks.")
-    if not raw.is_contiguous():
-        raise ValueError("GGUF merge requires contiguous raw blocks.")
-    cdt = _factor_dt(b, a, allowed=(torch.float16, torch.bfloat16, torch.float32))
-    _same_device(raw, b, a)
-    rows = raw.shape[0]
-    cols = gguf_logical_cols(raw.shape[1], int(quant_type))
-    rank = a.shape[0]
-    if rows == 0 or cols == 0 or rank == 0:
-        raise ValueError("GGUF merge requires non-empty weight and factors.")
-    if tuple(b.shape) != (rows, rank) or a.shape[1] != cols:
-        raise ValueError("LoRA factors do not match the GGUF weight shape.")
+    cdt, rows, cols, rank = validate_gguf_merge(raw, quant_type, b, a)
     b = b.contiguous()
     a = a.contiguous()
     seed, sflag = _seed_fields(rounding_seed)
