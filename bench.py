@@ -552,8 +552,8 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (small profiling case; the headline uses the config's)")
-    ap.add_argument("--kernel-reps", type=int, default=5,
-                    help="timed repetitions of the dominant-weight roofline leg")
+    ap.add_argument("--kernel-reps", type=int, default=3,
+                    help="timed repetitions of the roofline leg (the step's launches, each timed)")
     ap.add_argument("--no-triton-bar", action="store_true", help="skip timing the reference's Triton launchers")
     ap.add_argument("--partition", action="store_true",
                     help="multi-GPU: ONE model split over the ranks by sharding.partition (whole weights and "
@@ -687,40 +687,46 @@ def main() -> int:
     clocks = clk.summary()
     status = _native.device_status(device)
 
-    # Roofline leg: the dominant weight shape (largest algorithmic bytes) merged
-    # on its own, CUDA events on the launching stream around `kernel_reps`
-    # calls; per launch = the call's bytes and time divided by its launches.
-    dom = max(range(len(items)), key=lambda i: algorithmic_bytes(cfg, items[i][1], items[i][2]))
-    dom_arr = (_native.MergeDesc * 1)(arr[dom])
-    dom_bytes = algorithmic_bytes(cfg, items[dom][1], items[dom][2])
+    # Roofline leg: the step's own merge_kernel launches. The step's
+    # descriptors are issued in calls of at most MAX_WEIGHTS_PER_LAUNCH (the
+    # library packs at most that many weights into one launch), with CUDA
+    # events on the launching stream around each call, `kernel_reps` times.
+    # Per launch = the calls' algorithmic bytes and event time divided by the
+    # launches they made (every launch of a step is the same kernel).
+    chunks = [list(range(i, min(i + _native.MAX_WEIGHTS_PER_LAUNCH, len(descs))))
+              for i in range(0, len(descs), _native.MAX_WEIGHTS_PER_LAUNCH)]
+    chunk_arrs = [(_native.MergeDesc * len(ch))(*[arr[i] for i in ch]) for ch in chunks]
+    chunk_bytes = [sum(algorithmic_bytes(cfg, items[i][1], items[i][2]) for i in ch) for ch in chunks]
 
-    def run_dom(s: int) -> None:
+    def run_chunk(j: int, s: int) -> None:
         if seeds is not None:
-            dom_arr[0].seed = seeds[s][dom]
-        _native.check(lib.piper_merge_batch(dom_arr, 1, ws_ptr, ws_len, stream.cuda_stream))
+            for pos, i in enumerate(chunks[j]):
+                chunk_arrs[j][pos].seed = seeds[s][i]
+        _native.check(lib.piper_merge_batch(chunk_arrs[j], len(chunks[j]), ws_ptr, ws_len, stream.cuda_stream))
 
-    for i in range(3):
-        run_dom(i)
+    for j in range(len(chunks)):
+        run_chunk(j, 0)
     torch.cuda.synchronize(device)
     l0 = _native.launches()
-    k_start = torch.cuda.Event(enable_timing=True)
-    k_end = torch.cuda.Event(enable_timing=True)
-    k_start.record(stream)
-    for i in range(args.kernel_reps):
-        run_dom(3 + i)
-    k_end.record(stream)
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in chunks]
+           for _ in range(args.kernel_reps)]
+    for rep in range(args.kernel_reps):
+        for j in range(len(chunks)):
+            evs[rep][j][0].record(stream)
+            run_chunk(j, 1 + rep)
+            evs[rep][j][1].record(stream)
     torch.cuda.synchronize(device)
-    dom_launches = (_native.launches() - l0) / args.kernel_reps
-    dom_ms = k_start.elapsed_time(k_end) / args.kernel_reps
-    launch_ms = dom_ms / dom_launches
-    launch_bytes = dom_bytes / dom_launches
+    n_launch = (_native.launches() - l0) / args.kernel_reps
+    call_ms = sum(a.elapsed_time(b) for rep in evs for a, b in rep) / args.kernel_reps
+    launch_ms = call_ms / n_launch
+    launch_bytes = sum(chunk_bytes) / n_launch
 
     peak, peak_kind = measured_peak()
     achieved = launch_bytes / (launch_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (hbm_gbs copy)",
-                "kernel": f"merge_kernel over {items[dom][1]}x{items[dom][2]} ({items[dom][0].split('.')[-2]}), "
-                          f"{dom_launches:g} launches per merge",
+                "kernel": f"merge_kernel, the step's {n_launch:g} launches ({len(descs)} weights, calls of at most "
+                          f"{_native.MAX_WEIGHTS_PER_LAUNCH} weights, each timed by CUDA events)",
                 "algorithmic_bytes_per_launch": int(launch_bytes), "launch_ms": round(launch_ms, 5),
                 "step_achieved": round(value / world, 1), "traffic": None}
     tfile = ROOT / "profiles" / f"traffic_{cfg}.json"

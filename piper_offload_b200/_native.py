@@ -50,6 +50,10 @@ FLAG_ASYMMETRIC = 2
 FLAG_REDUCE_RANGE = 4
 FLAG_STOCHASTIC = 8
 
+# Weights packed into one kernel launch at most (their descriptors fill the
+# kernel's parameter space); larger batches take several launches.
+MAX_WEIGHTS_PER_LAUNCH = 48
+
 EXPORTED_SYMBOLS = (
     "piper_merge_workspace_size",
     "piper_merge_batch",

@@ -230,7 +230,7 @@ def compare(case: Case, got: dict, want: dict) -> Diff:
     return Diff(n, mism, max_step, sm, extra)
 
 
-# Reference test shapes (SURVEY / reference tests): 35x69 r7 INT8, 70x130 r7
+# Reference test shapes (the reference tests): 35x69 r7 INT8, 70x130 r7
 # FP8, 19x80 r13 NVFP4, 19x96 r7 MX, 16x64 SR.
 SMALL_SHAPES = {
     "mxfp8": (19, 96, 7), "mxfp8_e5m2": (19, 96, 7), "mxfp4": (19, 96, 7),
