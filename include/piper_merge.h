@@ -59,7 +59,10 @@ extern "C" {
 #define PIPER_FMT_BNB4_NF4 13        /* bitsandbytes 4-bit, NF4 code selection */
 #define PIPER_FMT_BNB4_FP4 14        /* bitsandbytes 4-bit, FP4 code selection */
 
-/* ---- floating dtypes (factors = compute dtype; INT8 scales) ---- */
+/* ---- floating dtypes (factors = compute dtype; INT8 scales) ----
+ * bf16 / fp16 factors: the rank-r update runs on tcgen05 tensor cores.
+ * fp32 factors: the reference's IEEE fp32 dot (one fused multiply-add per rank
+ * step, in rank order; _triton_float8_lora.py:53-66) on CUDA cores. */
 #define PIPER_DT_BF16 0
 #define PIPER_DT_F16 1
 #define PIPER_DT_F32 2

@@ -24,6 +24,8 @@ from .numerics import (
     fdiv,
     fdiv_t,
     fma_f32,
+    fma_f32_exact,
+    fp32_contraction,
     fp8_codec,
     from_bits_f32,
     maxnum,
@@ -42,12 +44,30 @@ FLT_MIN = np.float32(1.1754943508222875e-38)
 # ---------------------------------------------------------------------------
 
 
-def lora_delta(b: np.ndarray, a: np.ndarray) -> np.ndarray:
-    """fp32 ``B @ A``; correctly rounded (tie class: GPU summation order).
+def lora_delta(b: np.ndarray, a: np.ndarray, compute: str = "bf16") -> np.ndarray:
+    """fp32 ``B @ A`` as the reference's ``tl.dot`` forms it.
 
-    The reference accumulates into ``tl.zeros`` (``accumulator += tl.dot(b, a)``),
-    so an all-zero sum is +0.0 whatever the signs of its products.
+    bf16 / fp16 factors (tensor-core dot): correctly rounded (tie class: GPU
+    summation order). The reference accumulates into ``tl.zeros``
+    (``accumulator += tl.dot(b, a)``), so an all-zero sum is +0.0 whatever the
+    signs of its products.
+
+    fp32 factors (``input_precision="ieee"``, e.g. ``_triton_float8_lora.py:53-66``):
+    one fused multiply-add per rank step in rank order from +0, across the rank
+    blocks (16 for rank <= 16, else 32); the zero-padded steps of the last
+    block add +0, which turns a -0 sum into +0.
     """
+    if compute == "f32":
+        b = np.asarray(b, np.float32)
+        a = np.asarray(a, np.float32)
+        rank = b.shape[1]
+        acc = np.zeros((b.shape[0], a.shape[1]), np.float32)
+        for k in range(rank):
+            acc = fma_f32_exact(b[:, k:k + 1], a[k:k + 1, :], acc)
+        block = 16 if rank <= 16 else 32
+        if rank % block:
+            acc = (acc + np.float32(0.0)).astype(np.float32)
+        return acc
     acc = (np.asarray(b, np.float64) @ np.asarray(a, np.float64)).astype(np.float32)
     return (np.float32(0.0) + acc).astype(np.float32)
 
@@ -55,6 +75,21 @@ def lora_delta(b: np.ndarray, a: np.ndarray) -> np.ndarray:
 def merged_values(base: np.ndarray, acc: np.ndarray, strength: float, compute: str) -> np.ndarray:
     """``(base.to(f32) + acc * strength).to(compute)``; Triton contracts it to an FMA."""
     return round_to_compute(fma_f32(acc, np.float32(strength), base), compute)
+
+
+def merged_values_f32_product(values: np.ndarray, scale: np.ndarray, acc: np.ndarray, strength: float) -> np.ndarray:
+    """fp32 compute of ``base = values * scale; merged = base + acc * strength``.
+
+    With no cast between them (``COMPUTE_DTYPE == 2``, e.g. ``_triton_float8_lora.py:80-92``,
+    ``_triton_int8_lora.py:78-94``), the sum of two products is contracted on the
+    first one (LLVM's ``(fadd (fmul x, y), z) -> (fma x, y, z)``): the update is
+    rounded on its own and the element product enters the fused add exactly.
+    """
+    update = (np.asarray(acc, np.float32) * np.float32(strength)).astype(np.float32)
+    if fp32_contraction() == "separate":
+        prod = (np.asarray(values, np.float32) * np.asarray(scale, np.float32)).astype(np.float32)
+        return (prod + update).astype(np.float32)
+    return fma_f32_exact(np.asarray(values, np.float32), np.asarray(scale, np.float32), update)
 
 
 def nanmax_reduce(x: np.ndarray, axis: int) -> np.ndarray:
@@ -226,7 +261,7 @@ def merge_mx(qdata, scale, elem, b, a, strength, *, scaling_mode=0, swizzled=Fal
     M = b.shape[0]
     N = a.shape[1]
     nb = N // 32
-    acc = lora_delta(b, a)
+    acc = lora_delta(b, a, compute)
     if elem == "e2m1":
         codes = unpack_fp4(qdata)
         base_lp = decode_e2m1(codes)
@@ -288,7 +323,7 @@ def _nvfp4_merged(qdata, scale, global_scale, swizzled, b, a, strength, compute)
     base = (base * np.repeat(bs, 16, axis=1)).astype(np.float32)
     if compute == "bf16":
         base = bf16_round(base)
-    acc = lora_delta(b, a)
+    acc = lora_delta(b, a, compute)
     update = (acc * np.float32(strength)).astype(np.float32)
     summed = fma_f32(acc, np.float32(strength), base)
     merged = np.where(update == 0.0, base, summed).astype(np.float32)
@@ -357,7 +392,7 @@ def merge_float8(qdata, scale, block_size, b, a, strength, *, e4m3=True, seed=No
     encode, decode, limit = fp8_codec(e4m3)
     M = b.shape[0]
     N = a.shape[1]
-    acc = lora_delta(b, a)
+    acc = lora_delta(b, a, compute)
     scale = np.asarray(scale, np.float32)
     per_row = tuple(block_size) == (1, N)
     per_tensor = tuple(block_size) == (M, N)
@@ -369,8 +404,11 @@ def merge_float8(qdata, scale, block_size, b, a, strength, *, e4m3=True, seed=No
     else:
         g = block_size[1]
         s_in = np.repeat(scale.reshape(M, N // g), g, axis=1)
-    base = round_to_compute((lp * s_in).astype(np.float32), compute)
-    merged = merged_values(base, acc, strength, compute)
+    if compute == "f32":
+        merged = merged_values_f32_product(lp, np.broadcast_to(s_in, lp.shape), acc, strength)
+    else:
+        base = round_to_compute((lp * s_in).astype(np.float32), compute)
+        merged = merged_values(base, acc, strength, compute)
     absv = np.abs(merged)
     if per_row or per_tensor:
         amax = nanmax_reduce(absv, axis=1) if per_row else nanmax_reduce(absv.reshape(-1), axis=0)
@@ -425,7 +463,7 @@ def merge_bnb8(cb, scb, b, a, strength, *, seed=None, offset_base=0):
     normalized = f16_round((cbf / np.float32(127.0)).astype(np.float32))
     s16 = f16_round(np.asarray(scb, np.float32).reshape(M, 1))
     base = f16_round((normalized * s16).astype(np.float32))
-    acc = lora_delta(b, a)
+    acc = lora_delta(b, a, "f16")
     merged = f16_round(clamp(fma_f32(acc, np.float32(strength), base), -65504.0, 65504.0))
     new_scb = nanmax_reduce(np.abs(merged), axis=1).astype(np.float32)
     safe = np.where(new_scb == 0.0, np.float32(1.0), new_scb).reshape(M, 1)
@@ -599,9 +637,12 @@ def merge_bnb4(packed, absmax, code, b, a, strength, *, quant_type="nf4", nested
         scales = fma_f32(np.asarray(nested_code, np.float32)[q], ns, np.float32(offset))
     else:
         scales = np.asarray(absmax, np.float32).reshape(M, nb)
-    base = round_to_compute((base * np.repeat(scales, BNB4_BLOCK, axis=1)).astype(np.float32), compute)
-    acc = lora_delta(b, a)
-    merged = merged_values(base, acc, strength, compute)
+    acc = lora_delta(b, a, compute)
+    if compute == "f32":
+        merged = merged_values_f32_product(base, np.repeat(scales, BNB4_BLOCK, axis=1), acc, strength)
+    else:
+        base = round_to_compute((base * np.repeat(scales, BNB4_BLOCK, axis=1)).astype(np.float32), compute)
+        merged = merged_values(base, acc, strength, compute)
     out_scale = nanmax_reduce(np.abs(merged).reshape(M, nb, BNB4_BLOCK), axis=2).astype(np.float32)
     safe = np.where(out_scale == 0.0, np.float32(1.0), out_scale)
     normalized = clamp(fdiv_t(merged, np.repeat(safe, BNB4_BLOCK, axis=1)), -1.0, 1.0)
@@ -655,7 +696,7 @@ def merge_quanto(qdata, scale, axis_kind, b, a, strength, *, storage="int8", see
     with np.errstate(invalid="ignore"):
         prod = (lp * s_b).astype(np.float32)
     base = round_to_compute(np.where(s_b == 0.0, np.float32(0.0), prod).astype(np.float32), compute)
-    acc = lora_delta(b, a)
+    acc = lora_delta(b, a, compute)
     merged = merged_values(base, acc, strength, compute)
     absm = np.abs(merged)
     if axis_kind == "tensor":
@@ -716,9 +757,12 @@ def merge_int8(qdata, scale, zero_point, block_size, b, a, strength, *, asymmetr
         prod = f16_round((f16_round(base) * f16_round(sv_in)).astype(np.float32))
     else:
         prod = (base * sv_in).astype(np.float32)
-    base = round_to_compute(prod, compute)
-    acc = lora_delta(b, a).reshape(-1)
-    dense = merged_values(base, acc, strength, compute)
+    acc = lora_delta(b, a, compute).reshape(-1)
+    if compute == "f32":
+        dense = merged_values_f32_product(base, sv_in, acc, strength)
+    else:
+        base = round_to_compute(prod, compute)
+        dense = merged_values(base, acc, strength, compute)
     blocks = dense.reshape(nq, block_numel)
     min_v = nanmin_reduce(minnum(blocks, np.float32(0.0)), axis=1)
     max_v = nanmax_reduce(maxnum(blocks, np.float32(0.0)), axis=1)
@@ -832,5 +876,5 @@ def merge_gguf(raw, quant_type, b, a, strength, *, seed=None, compute="bf16", of
     M = b.shape[0]
     N = a.shape[1]
     base = gguf_dequant(raw, quant_type, M, N, compute)
-    merged = merged_values(base, lora_delta(b, a), strength, compute)
+    merged = merged_values(base, lora_delta(b, a, compute), strength, compute)
     return gguf_quantize(merged, quant_type, seed=seed, offset_base=offset_base)

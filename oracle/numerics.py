@@ -243,6 +243,26 @@ def constant_division() -> str:
     return _constant_division
 
 
+# The reference's fp32-compute ``base = values * scale; merged = base + acc * strength``
+# is compiled for the GPU with floating-point contraction, which fuses the first
+# product into the add (``"gpu"``, default). The Triton CPU interpreter that
+# recorded the golden fixtures evaluates each operation on its own with one
+# rounding each (``"separate"``), so those fixtures are checked in that mode.
+_fp32_contraction = "gpu"
+
+
+def set_fp32_contraction(mode: str) -> None:
+    """``"gpu"`` (the compiled kernels) or ``"separate"`` (the interpreter)."""
+    global _fp32_contraction
+    if mode not in ("gpu", "separate"):
+        raise ValueError(mode)
+    _fp32_contraction = mode
+
+
+def fp32_contraction() -> str:
+    return _fp32_contraction
+
+
 def fdiv(a, b) -> np.ndarray:
     """fp32 quotient of the reference's ``x / CONST`` (see ``set_constant_division``)."""
     if _constant_division == "ieee":
@@ -276,6 +296,34 @@ def fdiv_t(a, b) -> np.ndarray:
     shape = np.broadcast_shapes(a.shape, b.shape)
     out = _tensor_division(np.broadcast_to(a, shape).reshape(-1), np.broadcast_to(b, shape).reshape(-1))
     return np.asarray(out, dtype=np.float32).reshape(shape)
+
+
+def fma_f32_exact(a, b, c) -> np.ndarray:
+    """Single-rounding ``a * b + c`` in fp32, exact in every case (``fma.rn.f32``).
+
+    The product of two fp32 values is exact in fp64. Their fp64 sum ``s``
+    with the TwoSum error ``e`` (Knuth) is the exact result ``s + e``. fp32
+    rounding points are fp64 values, so rounding ``s`` to fp32 gives the
+    fused result unless ``s`` lies exactly on an fp32 midpoint with ``e``
+    nonzero; then the exact result lies on the side of ``e``.
+    """
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    c = np.asarray(c, dtype=np.float64)
+    with np.errstate(over="ignore", invalid="ignore"):
+        p = a * b
+        s = p + c
+        bb = s - p
+        e = (p - (s - bb)) + (c - bb)
+        r = s.astype(np.float32)
+        r64 = r.astype(np.float64)
+        d = s - r64
+        toward = np.where(d > 0, np.float32(np.inf), np.float32(-np.inf)).astype(np.float32)
+        other = np.nextafter(r, toward).astype(np.float32)
+        mid = (d != 0) & np.isfinite(s) & (np.abs(other.astype(np.float64) - r64) == 2.0 * np.abs(d))
+        # On a midpoint the exact value lies past it (toward `other`) when e has d's sign.
+        past = mid & (e != 0) & (np.sign(e) == np.sign(d))
+        return np.where(past, other, r).astype(np.float32)
 
 
 def fma_f32(a, b, c) -> np.ndarray:

@@ -575,8 +575,8 @@ class Nvfp4Adapter:
         if getattr(t, "block_size", 16) != 16:
             raise ValueError(f"{label} merge requires block_size=16.")
         rank, _ = _factors(b, a, rows, cols, label)
-        if b.dtype is not t.orig_dtype or b.dtype is not torch.bfloat16:
-            raise ValueError(f"{label} merge on sm_100a requires bfloat16 weights and factors.")
+        if b.dtype is not t.orig_dtype or b.dtype not in (torch.bfloat16, torch.float32):  # nvfp4_adapter.py:73
+            raise ValueError(f"{label} merge requires bfloat16 or float32 factors in the weight's original dtype.")
         _cuda_same_device(label, t.qdata, t.scale, b, a, t.per_tensor_scale)
         if tuple(t.scale.shape) != K.nvfp4_expected_scale_shape(rows, cols, swizzled=bool(t.is_swizzled_scales)):
             raise ValueError("NVFP4 scale shape does not match its swizzle metadata.")
@@ -596,7 +596,7 @@ class Nvfp4Adapter:
         return K._desc(
             qdata=target.qdata.data_ptr(), scale=target.scale.data_ptr(),
             global_scale=K._ptr(target.per_tensor_scale), b=b.data_ptr(), a=a.data_ptr(), rows=rows, cols=cols,
-            rank=rank, format=nat.FMT_NVFP4, compute_dtype=nat.DT_BF16,
+            rank=rank, format=nat.FMT_NVFP4, compute_dtype=K._dt_id(b.dtype, "LoRA factors"),
             flags=(nat.FLAG_SWIZZLED if target.is_swizzled_scales else 0) | sflag, strength=float(strength),
             seed=seed, offset_base=int(offset_base))
 
@@ -656,8 +656,8 @@ class MxAdapter:
             raise ValueError("TorchAO MX merge supports FLOOR, RCEIL, CEIL and EVEN scale rounding.")
         if t.block_size != 32:
             raise ValueError("MX merge supports block size 32.")
-        if b.dtype is not t.orig_dtype or t.orig_dtype is not torch.bfloat16:
-            raise ValueError("MX merge on sm_100a requires bfloat16 weights and factors.")
+        if b.dtype is not t.orig_dtype or t.orig_dtype not in (torch.bfloat16, torch.float32):  # mx_adapter.py:61
+            raise ValueError("MX merge requires bfloat16 or float32 factors in the weight's original dtype.")
         fmt = K.mx_format_parameters(t.elem_dtype)
         _cuda_same_device("TorchAO MX", t.qdata, t.scale, b, a)
         if tuple(t.scale.shape) != K.mx_expected_scale_shape(rows, cols, swizzled=bool(t.is_swizzled_scales)):
@@ -677,7 +677,8 @@ class MxAdapter:
         seed, sflag = _seed(rounding_seed)
         return K._desc(
             qdata=target.qdata.data_ptr(), scale=target.scale.data_ptr(), b=b.data_ptr(), a=a.data_ptr(),
-            rows=rows, cols=cols, rank=rank, format=fmt, compute_dtype=nat.DT_BF16, scale_mode=mode,
+            rows=rows, cols=cols, rank=rank, format=fmt, compute_dtype=K._dt_id(b.dtype, "LoRA factors"),
+            scale_mode=mode,
             flags=(nat.FLAG_SWIZZLED if target.is_swizzled_scales else 0) | sflag, strength=float(strength),
             seed=seed, offset_base=int(offset_base))
 

@@ -397,6 +397,51 @@ __device__ __forceinline__ uint32_t byte_of(const uint32_t (&w)[8], int i) {
   return (w[i >> 2] >> ((i & 3) * 8)) & 0xFFu;
 }
 
+// ------------------------------------------------- fp32 factors (CUDA cores)
+// The rank-r update of 32 columns [col, col + 32) of one row for fp32 LoRA
+// factors. The reference runs them through `tl.dot(b, a, input_precision=
+// "ieee")` (_triton_float8_lora.py:53-66 and the other launchers' rank
+// loops), which Triton evaluates on CUDA cores as one fused multiply-add per
+// rank step, in rank order, starting from +0 and continuing across its rank
+// blocks (`accumulator += tl.dot(...)` becomes the dot's accumulator input).
+// This function makes the same chain. The rank is padded to the reference's
+// block (16 for rank <= 16, else a multiple of 32) with zero factors; each
+// padded step adds an exact +0, which only turns a -0 sum into +0. Rows past
+// the weight and columns past its end read no memory and give unused values.
+__device__ __forceinline__ void f32_update(const DevWeight& W, int row, bool valid, int col, float (&acc)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+  const float* __restrict__ brow = reinterpret_cast<const float*>(W.b) + static_cast<int64_t>(row) * W.r;
+  const float* __restrict__ acol = reinterpret_cast<const float*>(W.a) + col;
+  const int ncols = min(32, W.N - col);
+  const bool vec = ncols == 32 && ((reinterpret_cast<uintptr_t>(acol) | (static_cast<uintptr_t>(W.N) * 4u)) & 15u) == 0;
+  for (int k = 0; k < W.r; ++k) {
+    const float bk = valid ? __ldg(brow + k) : 0.0f;
+    const float* __restrict__ ak = acol + static_cast<int64_t>(k) * W.N;
+    float av[32];
+    if (vec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(ak) + j);
+        av[4 * j] = v.x;
+        av[4 * j + 1] = v.y;
+        av[4 * j + 2] = v.z;
+        av[4 * j + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) av[j] = j < ncols ? __ldg(ak + j) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = __fmaf_rn(bk, av[j], acc[j]);
+  }
+  const int rank_block = W.r <= 16 ? 16 : 32;
+  if (W.r % rank_block != 0) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(acc[j], 0.0f);
+  }
+}
+
 // ================================================================ MX epilogue
 template <int FMT, int CDT>
 __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, int k,
@@ -427,8 +472,9 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
     }
   }
   // base = bf16(elem * bf16(scale)): for scale codes 20..230 every product is
-  // an exact bf16 normal, so the rounding is the identity.
-  if (sc >= 20u && sc <= 230u) {
+  // an exact bf16 normal, so the rounding is the identity. fp32 compute
+  // (float32 weights) keeps the fp32 product (_triton_mx_lora.py:239-245).
+  if (CDT == kF32 || (sc >= 20u && sc <= 230u)) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) merged[i] = __fmul_rn(merged[i], bscale);
   } else {
@@ -439,7 +485,7 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
 #pragma unroll
   for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], W.strength, merged[i]);
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) bf16r2(merged[i], merged[i + 1]);
+  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
   const float amax = tree_max_abs(merged);
   const MxScale s = mx_scale(amax, W.scale_mode, P::kTarget, P::kMax, P::kMbits);
   const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
@@ -505,6 +551,7 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
 template <int FMT, int CDT>
 __device__ __forceinline__ bool mx_chunk_fast(const DevWeight& W, const RowCtx& c, int k, const float (&acc)[32]) {
   using P = MxParams<FMT>;
+  if constexpr (CDT == kF32) return false;  // the shortcuts below rely on bf16 rounding
   const int col = c.tile_col0 + 32 * k;
   const int blk = col >> 5;
   const uint32_t sc = c.valid ? c.sscale[blk - c.blk0] : 127u;
@@ -1108,31 +1155,51 @@ __device__ __forceinline__ void affine_merged(const DevWeight& W, const RowCtx& 
                                               const int* zp_in, float (&merged)[32]) {
   uint32_t wv[8];
   load_chunks32(c, k, wv);
-  if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
-    const bool f16_scale = int8_f16_scale<CDT>(W.scale_dt);
+  if constexpr (CDT == kF32 && flavor_of(FMT) == kTorchao) {
+    // fp32 compute: fma(q - zp, scale, acc * strength) (see fp8_merged_pk).
+    if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
-      // q - zp is an integer in [-255, 255]: exact in bf16 / fp16.
-      const float s = f16_scale ? f16r(scale_in[i]) : scale_in[i];
-      merged[i] = __fmul_rn(__fsub_rn(qv, static_cast<float>(zp_in[i])), s);
+      for (int i = 0; i < 32; ++i) {
+        const float qz = __fsub_rn(static_cast<float>(static_cast<int8_t>(byte_of(wv, i))), static_cast<float>(zp_in[i]));
+        merged[i] = fmaf(qz, scale_in[i], __fmul_rn(acc[i], W.strength));
+      }
+    } else {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        float f[4];
+        dec_fp8x4<base_fmt(FMT) == PIPER_FMT_FP8_E4M3>(wv[w], f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          merged[4 * w + j] = fmaf(f[j], scale_in[4 * w + j], __fmul_rn(acc[4 * w + j], W.strength));
+      }
     }
-    int8_half_product<CDT>(W.scale_dt, merged);
   } else {
+    if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
+      const bool f16_scale = int8_f16_scale<CDT>(W.scale_dt);
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      float f[4];
-      dec_fp8x4<base_fmt(FMT) == PIPER_FMT_FP8_E4M3>(wv[w], f);
+      for (int i = 0; i < 32; ++i) {
+        const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
+        // q - zp is an integer in [-255, 255]: exact in bf16 / fp16.
+        const float s = f16_scale ? f16r(scale_in[i]) : scale_in[i];
+        merged[i] = __fmul_rn(__fsub_rn(qv, static_cast<float>(zp_in[i])), s);
+      }
+      int8_half_product<CDT>(W.scale_dt, merged);
+    } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) merged[4 * w + j] = __fmul_rn(f[j], scale_in[4 * w + j]);
+      for (int w = 0; w < 8; ++w) {
+        float f[4];
+        dec_fp8x4<base_fmt(FMT) == PIPER_FMT_FP8_E4M3>(wv[w], f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) merged[4 * w + j] = __fmul_rn(f[j], scale_in[4 * w + j]);
+      }
     }
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], W.strength, merged[i]);
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
   }
-#pragma unroll
-  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
-#pragma unroll
-  for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], W.strength, merged[i]);
-#pragma unroll
-  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
 }
 
 // affine_merged for a chunk inside one quantization block (one scale / zero point).
@@ -1142,42 +1209,62 @@ __device__ __forceinline__ void affine_merged_u(const DevWeight& W, const RowCtx
                                                 float (&merged)[32]) {
   uint32_t wv[8];
   load_chunks32(c, k, wv);
-  if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
-    if constexpr (flavor_of(FMT) == kBnb) {
-      bnb8_merged(wv, acc, s_in, W.strength, merged);
-      return;
-    }
-    const float zf = static_cast<float>(z_in);
-    const float s = int8_f16_scale<CDT>(W.scale_dt) ? f16r(s_in) : s_in;
+  if constexpr (CDT == kF32 && flavor_of(FMT) == kTorchao) {
+    // fp32 compute: fma(q - zp, scale, acc * strength) (see fp8_merged_pk).
+    if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
+      const float zf = static_cast<float>(z_in);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
-      merged[i] = __fmul_rn(__fsub_rn(qv, zf), s);
+      for (int i = 0; i < 32; ++i) {
+        const float qz = __fsub_rn(static_cast<float>(static_cast<int8_t>(byte_of(wv, i))), zf);
+        merged[i] = fmaf(qz, s_in, __fmul_rn(acc[i], W.strength));
+      }
+    } else {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        float f[4];
+        dec_fp8x4<base_fmt(FMT) == PIPER_FMT_FP8_E4M3>(wv[w], f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) merged[4 * w + j] = fmaf(f[j], s_in, __fmul_rn(acc[4 * w + j], W.strength));
+      }
     }
-    int8_half_product<CDT>(W.scale_dt, merged);
   } else {
+    if constexpr (base_fmt(FMT) == PIPER_FMT_INT8) {
+      if constexpr (flavor_of(FMT) == kBnb) {
+        bnb8_merged(wv, acc, s_in, W.strength, merged);
+        return;
+      }
+      const float zf = static_cast<float>(z_in);
+      const float s = int8_f16_scale<CDT>(W.scale_dt) ? f16r(s_in) : s_in;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      float f[4];
-      dec_fp8x4<base_fmt(FMT) == PIPER_FMT_FP8_E4M3>(wv[w], f);
+      for (int i = 0; i < 32; ++i) {
+        const float qv = static_cast<float>(static_cast<int8_t>(byte_of(wv, i)));
+        merged[i] = __fmul_rn(__fsub_rn(qv, zf), s);
+      }
+      int8_half_product<CDT>(W.scale_dt, merged);
+    } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) merged[4 * w + j] = __fmul_rn(f[j], s_in);
+      for (int w = 0; w < 8; ++w) {
+        float f[4];
+        dec_fp8x4<base_fmt(FMT) == PIPER_FMT_FP8_E4M3>(wv[w], f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) merged[4 * w + j] = __fmul_rn(f[j], s_in);
+      }
     }
-  }
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
-  if constexpr (flavor_of(FMT) == kQuanto) {
-    if (s_in == 0.0f) {
-      // where(scale == 0, 0, q * scale): Quanto's FP8 codes are NaN under a zero scale (:90-94).
+    for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
+    if constexpr (flavor_of(FMT) == kQuanto) {
+      if (s_in == 0.0f) {
+        // where(scale == 0, 0, q * scale): Quanto's FP8 codes are NaN under a zero scale (:90-94).
 #pragma unroll
-      for (int i = 0; i < 32; ++i) merged[i] = 0.0f;
+        for (int i = 0; i < 32; ++i) merged[i] = 0.0f;
+      }
     }
+    const float st = W.strength;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], st, merged[i]);
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
   }
-  const float st = W.strength;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) merged[i] = fmaf(acc[i], st, merged[i]);
-#pragma unroll
-  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(merged[i], merged[i + 1]);
 }
 
 // Stochastic FP8 codes of 32 values: clamp(m / s) (div.full) rounded with
@@ -1231,24 +1318,37 @@ __device__ __forceinline__ void fp8_merged_pk(const uint32_t (&wv)[8], const flo
                                               float strength, float (&m)[32]) {
   const float2 s2 = make_float2(s_in, s_in);
   const float2 st2 = make_float2(strength, strength);
+  if constexpr (CDT == kF32) {
+    // fp32 compute: the reference's `base = q * scale; merged = base + acc *
+    // strength` has no cast in between, and its compilation contracts the
+    // first product into the add: fma(q, scale, acc * strength).
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    float f[4];
-    dec_fp8x4<E4M3>(wv[w], f);
-    float2 b0 = __fmul2_rn(make_float2(f[0], f[1]), s2);
-    float2 b1 = __fmul2_rn(make_float2(f[2], f[3]), s2);
-    round_dt2<CDT>(b0.x, b0.y);
-    round_dt2<CDT>(b1.x, b1.y);
-    float2 m0 = __ffma2_rn(make_float2(acc[4 * w], acc[4 * w + 1]), st2, b0);
-    float2 m1 = __ffma2_rn(make_float2(acc[4 * w + 2], acc[4 * w + 3]), st2, b1);
-    if constexpr (ROUND) {
-      round_dt2<CDT>(m0.x, m0.y);
-      round_dt2<CDT>(m1.x, m1.y);
+    for (int w = 0; w < 8; ++w) {
+      float f[4];
+      dec_fp8x4<E4M3>(wv[w], f);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) m[4 * w + j] = fmaf(f[j], s_in, __fmul_rn(acc[4 * w + j], strength));
     }
-    m[4 * w] = m0.x;
-    m[4 * w + 1] = m0.y;
-    m[4 * w + 2] = m1.x;
-    m[4 * w + 3] = m1.y;
+  } else {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      float f[4];
+      dec_fp8x4<E4M3>(wv[w], f);
+      float2 b0 = __fmul2_rn(make_float2(f[0], f[1]), s2);
+      float2 b1 = __fmul2_rn(make_float2(f[2], f[3]), s2);
+      round_dt2<CDT>(b0.x, b0.y);
+      round_dt2<CDT>(b1.x, b1.y);
+      float2 m0 = __ffma2_rn(make_float2(acc[4 * w], acc[4 * w + 1]), st2, b0);
+      float2 m1 = __ffma2_rn(make_float2(acc[4 * w + 2], acc[4 * w + 3]), st2, b1);
+      if constexpr (ROUND) {
+        round_dt2<CDT>(m0.x, m0.y);
+        round_dt2<CDT>(m1.x, m1.y);
+      }
+      m[4 * w] = m0.x;
+      m[4 * w + 1] = m0.y;
+      m[4 * w + 2] = m1.x;
+      m[4 * w + 3] = m1.y;
+    }
   }
 }
 
@@ -1268,20 +1368,29 @@ __device__ __forceinline__ void int8_merged_pk(const uint32_t (&wv)[8], const fl
   const float2 off2 = make_float2(off, off);
   const float2 s2 = make_float2(sc, sc);
   const float2 st2 = make_float2(strength, strength);
+  if constexpr (CDT == kF32) {
+    // fp32 compute: fma(q - zp, scale, acc * strength), as in fp8_merged_pk.
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    const uint32_t x = wv[w] ^ 0x80808080u;
+    for (int i = 0; i < 32; ++i) {
+      const float qz = __fsub_rn(static_cast<float>(static_cast<int8_t>(byte_of(wv, i))), static_cast<float>(z_in));
+      m[i] = fmaf(qz, sc, __fmul_rn(acc[i], strength));
+    }
+  } else {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float2 raw = make_float2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u + 2u * h)),
-                                     __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7541u + 2u * h)));
-      float2 b = __fmul2_rn(__fadd2_rn(raw, off2), s2);
-      if (half_product) f16r2(b.x, b.y);
-      round_dt2<CDT>(b.x, b.y);
-      float2 r = __ffma2_rn(make_float2(acc[4 * w + 2 * h], acc[4 * w + 2 * h + 1]), st2, b);
-      if constexpr (ROUND) round_dt2<CDT>(r.x, r.y);
-      m[4 * w + 2 * h] = r.x;
-      m[4 * w + 2 * h + 1] = r.y;
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t x = wv[w] ^ 0x80808080u;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float2 raw = make_float2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u + 2u * h)),
+                                       __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7541u + 2u * h)));
+        float2 b = __fmul2_rn(__fadd2_rn(raw, off2), s2);
+        if (half_product) f16r2(b.x, b.y);
+        round_dt2<CDT>(b.x, b.y);
+        float2 r = __ffma2_rn(make_float2(acc[4 * w + 2 * h], acc[4 * w + 2 * h + 1]), st2, b);
+        if constexpr (ROUND) round_dt2<CDT>(r.x, r.y);
+        m[4 * w + 2 * h] = r.x;
+        m[4 * w + 2 * h + 1] = r.y;
+      }
     }
   }
 }
@@ -1457,14 +1566,21 @@ __device__ __forceinline__ void bnb4_merged32(const uint32_t (&wv)[4], float sca
     m[2 * j] = lane_lut(lut, static_cast<int>(byte >> 4));
     m[2 * j + 1] = lane_lut(lut, static_cast<int>(byte & 15u));
   }
+  if constexpr (CDT == kF32) {
+    // fp32 compute: fma(code, scale, acc * strength) (see fp8_merged_pk;
+    // _triton_bnb4_lora.py:247-254).
 #pragma unroll
-  for (int i = 0; i < 32; ++i) m[i] = __fmul_rn(m[i], scale);
+    for (int i = 0; i < 32; ++i) m[i] = fmaf(m[i], scale, __fmul_rn(acc[i], strength));
+  } else {
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+    for (int i = 0; i < 32; ++i) m[i] = __fmul_rn(m[i], scale);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) m[i] = fmaf(acc[i], strength, m[i]);
+    for (int i = 0; i < 32; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+    for (int i = 0; i < 32; ++i) m[i] = fmaf(acc[i], strength, m[i]);
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) round_dt2<CDT>(m[i], m[i + 1]);
+  }
 }
 
 // NF4 index of the reference's binary search (_nearest_sorted_code :29-50,
@@ -2298,6 +2414,13 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
           ok = mbar_wait(&full_a[x], (t / SA) & 1u, kStatusTimeoutLoad);
           if (ok && t >= static_cast<uint32_t>(NB)) ok = mbar_wait(&aempty[ab], ((t / NB) - 1) & 1u, kStatusTimeoutMma);
           if (!ok) break;
+          if constexpr (CDT == kF32) {
+            // fp32 factors: the epilogue forms the update on CUDA cores, so this
+            // role only keeps the accumulator and stage rings turning.
+            mbar_arrive(&afull[ab]);
+            mbar_arrive(&empty_a[x]);
+            continue;
+          }
           fence_proxy_async_smem();  // cp.async-written operands -> tensor core
           tc_fence_after();
           const uint32_t b_base = smem_u32(stage_a(x));
@@ -2313,10 +2436,13 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
           umma_commit(&afull[ab]);
           umma_commit(&empty_a[x]);  // the A stage is free once these MMAs complete
         }
-        umma_commit(&bempty[jb]);  // the strip is free once these MMAs complete
+        if constexpr (CDT == kF32) mbar_arrive(&bempty[jb]);
+        else umma_commit(&bempty[jb]);  // the strip is free once these MMAs complete
       }
-      umma_commit(mma_done);
-      mbar_wait(mma_done, 0u, kStatusTimeoutMma);
+      if constexpr (CDT != kF32) {
+        umma_commit(mma_done);
+        mbar_wait(mma_done, 0u, kStatusTimeoutMma);
+      }
     }
     __syncwarp();
   } else if (warp < 4) {
@@ -2344,7 +2470,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
         ok = mbar_wait(&bempty[jb], ((it / NBB) - 1) & 1u, kStatusTimeoutMma);
         if (!ok) break;
       }
-      if (!W.use_tma_b) {
+      if (CDT != kF32 && !W.use_tma_b) {  // fp32 factors are read by the epilogue itself
         // Same swizzled K-major layout the bulk tensor copy would produce.
         uint8_t* sBj = sB + jb * ws_b_buf_bytes(KPL);
         const int kb = kb_row(KP);
@@ -2387,7 +2513,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
         }
         // A tile when it cannot move by bulk tensor copies: the same MN-major
         // layout, 64-column blocks of KP rows x 128 bytes, 128-byte swizzle.
-        if (!W.use_tma_a) {
+        if (CDT != kF32 && !W.use_tma_a) {
           uint8_t* sA = stage_a(x);
           const int chunks = KP * BN / 8;
           for (int idx = lt; idx < chunks; idx += kLoadThreads) {
@@ -2621,18 +2747,32 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
         }
         tc_fence_after();
         const uint32_t taddr = tmem + lane_off + ab * BN;
+        // The update of chunk k (32 columns) of this thread's tile row: the
+        // tensor-core accumulator, or for fp32 factors the CUDA-core chain.
+        auto acc_at = [&](int k, float (&acc)[32]) {
+          if constexpr (CDT == kF32) f32_update(W, row, valid, c0 + 32 * k, acc);
+          else tmem_ld32(taddr + 32 * k, acc);
+        };
         // Chunks kbeg .. kend-1 of the accumulator, each loaded from tensor
         // memory while the previous one is being processed.
         auto chunk_loop = [&](int kbeg, int kend, auto&& body) {
-          uint32_t cur[32];
-          if (kbeg < kend) tmem_ld32_async(taddr + 32 * kbeg, cur);
-          for (int k = kbeg; k < kend; ++k) {
-            tmem_ld_wait(cur);
-            float acc[32];
+          if constexpr (CDT == kF32) {
+            for (int k = kbeg; k < kend; ++k) {
+              float acc[32];
+              acc_at(k, acc);
+              body(k, acc);
+            }
+          } else {
+            uint32_t cur[32];
+            if (kbeg < kend) tmem_ld32_async(taddr + 32 * kbeg, cur);
+            for (int k = kbeg; k < kend; ++k) {
+              tmem_ld_wait(cur);
+              float acc[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(cur[i]);
-            if (k + 1 < kend) tmem_ld32_async(taddr + 32 * (k + 1), cur);
-            body(k, acc);
+              for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(cur[i]);
+              if (k + 1 < kend) tmem_ld32_async(taddr + 32 * (k + 1), cur);
+              body(k, acc);
+            }
           }
         };
 
@@ -2664,7 +2804,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
             // The accumulator chunk is read again from tensor memory, so the
             // fast path need not keep it live.
             float acc2[32];
-            tmem_ld32(taddr + 32 * k, acc2);
+            acc_at(k, acc2);
             mx_chunk<FMT, CDT>(W, c, k, acc2);
           }
         });
@@ -2675,7 +2815,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
         if (tcols & 31) {  // trailing 16-column block
           float acc[32];
           const int k = tcols / 32;
-          tmem_ld32(taddr + 32 * k, acc);
+          acc_at(k, acc);
           uint2 codes = *reinterpret_cast<const uint2*>(chunk_ptr(c, k));
           nvfp4_block<PASS, CDT>(W, c, c0 + 32 * k, acc, g_in, g_out, two_level, red_max, codes);
           if (PASS != kReduce) *reinterpret_cast<uint2*>(chunk_ptr(c, k)) = codes;
@@ -2725,7 +2865,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
             const uint4 v4 = *reinterpret_cast<const uint4*>(chunk_ptr(c, k + h));
             const uint32_t wq[4] = {v4.x, v4.y, v4.z, v4.w};
             float acc[32], m[32];
-            tmem_ld32(taddr + 32 * (k + h), acc);
+            acc_at((k + h), acc);
             bnb4_merged32<CDT>(wq, scale, dec, W.strength, acc, m);
 #pragma unroll
             for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(m[i]));
@@ -2739,7 +2879,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
             const uint4 v4 = *reinterpret_cast<const uint4*>(chunk_ptr(c, k + h));
             const uint32_t wq[4] = {v4.x, v4.y, v4.z, v4.w};
             float acc[32], m[32];
-            tmem_ld32(taddr + 32 * (k + h), acc);
+            acc_at((k + h), acc);
             bnb4_merged32<CDT>(wq, scale, dec, W.strength, acc, m);
             const uint64_t off0 =
                 W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + col + 32 * h;
@@ -2893,7 +3033,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
             }
             for (int k = g0; k < g0 + gch; ++k) {
               float acc[32], merged[32];
-              tmem_ld32(taddr + 32 * k, acc);
+              acc_at(k, acc);
               affine_merged_u<FMT, CDT>(W, c, k, acc, s_in, z_in, merged);
               if constexpr (kInt8) {
                 gmax = fmaxf(gmax, tree_max(merged));
@@ -2911,7 +3051,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
               }
               for (int k = g0; k < g0 + gch; ++k) {
                 float acc[32], merged[32];
-                tmem_ld32(taddr + 32 * k, acc);
+                acc_at(k, acc);
                 affine_merged_u<FMT, CDT>(W, c, k, acc, s_in, z_in, merged);
                 uint32_t out[8];
                 const uint64_t off0 = W.offset_base +
@@ -2926,7 +3066,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
               if (valid) reinterpret_cast<float*>(W.scale)[qp] = s;
               for (int k = g0; k < g0 + gch; ++k) {
                 float acc[32], merged[32];
-                tmem_ld32(taddr + 32 * k, acc);
+                acc_at(k, acc);
                 affine_merged_u<FMT, CDT>(W, c, k, acc, s_in, z_in, merged);
                 uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
                 const uint64_t off0 = W.offset_base +
@@ -3363,24 +3503,24 @@ int validate(const piper_merge_desc& d, Plan& p) {
                                         std::to_string(d.rank) + ").");
   if (d.qdata == nullptr || d.b == nullptr || d.a == nullptr)
     return fail(PIPER_MERGE_EINVAL, "null qdata or factor pointer.");
-  if (d.compute_dtype != PIPER_DT_BF16 && d.compute_dtype != PIPER_DT_F16)
-    return fail(PIPER_MERGE_EINVAL, "the sm_100a merge supports bfloat16 and float16 LoRA factors.");
+  if (!is_fp_dt(d.compute_dtype))
+    return fail(PIPER_MERGE_EINVAL, "merge supports float16, bfloat16, and float32 LoRA factors.");
   p = Plan();
   switch (d.format) {
     case PIPER_FMT_MXFP8_E4M3:
     case PIPER_FMT_MXFP8_E5M2:
     case PIPER_FMT_MXFP4:
       if (d.cols % 32 != 0) return fail(PIPER_MERGE_EINVAL, "MX merge requires columns divisible by 32.");
-      if (d.compute_dtype != PIPER_DT_BF16)
-        return fail(PIPER_MERGE_EINVAL, "MX merge supports bfloat16 weights and factors.");
+      if (d.compute_dtype != PIPER_DT_BF16 && d.compute_dtype != PIPER_DT_F32)
+        return fail(PIPER_MERGE_EINVAL, "MX merge supports bfloat16 and float32 weights and factors.");
       if (d.scale_mode < 0 || d.scale_mode > 3)
         return fail(PIPER_MERGE_EINVAL, "Unsupported MX scaling mode id " + std::to_string(d.scale_mode) + ".");
       if (d.scale == nullptr) return fail(PIPER_MERGE_EINVAL, "MX merge requires E8M0 scales.");
       break;
     case PIPER_FMT_NVFP4:
       if (d.cols % 16 != 0) return fail(PIPER_MERGE_EINVAL, "NVFP4 merge requires columns divisible by 16.");
-      if (d.compute_dtype != PIPER_DT_BF16)
-        return fail(PIPER_MERGE_EINVAL, "NVFP4 merge supports bfloat16 factors.");
+      if (d.compute_dtype != PIPER_DT_BF16 && d.compute_dtype != PIPER_DT_F32)
+        return fail(PIPER_MERGE_EINVAL, "NVFP4 merge supports bfloat16 and float32 LoRA factors.");
       if (d.scale == nullptr) return fail(PIPER_MERGE_EINVAL, "NVFP4 merge requires E4M3 block scales.");
       if (d.global_scale != nullptr) {
         p.two_pass = true;
@@ -3446,7 +3586,8 @@ int validate(const piper_merge_desc& d, Plan& p) {
   // The widest tile (256, 128 or 64 columns) whose pipeline keeps three
   // stages of (codes, A tile, scales) next to two B strips; 64-column tiles
   // (large ranks) may run with two.
-  const int kp = pm::align_up(static_cast<int>(d.rank), 16);
+  // fp32 factors are read by the epilogue from global memory: no factor stages.
+  const int kp = d.compute_dtype == PIPER_DT_F32 ? 16 : pm::align_up(static_cast<int>(d.rank), 16);
   auto fits = [&](int bn, int min_sc) {
     return 512 / bn >= pm::epi_wgs_rt(d.format, bn) && plan_pipe(d.format, bn, kp).sc >= min_sc;
   };
@@ -3600,7 +3741,10 @@ int launch_bn(int bn, LaunchParams& lp, int items, int kp, cudaStream_t s) {
     else return fail(PIPER_MERGE_EINVAL, "256-column tiles need at most two epilogue warpgroups.");
   }
   if (bn == 128) return launch_t<FMT, PASS, 128, CDT>(lp, items, kp, s);
-  return launch_t<FMT, PASS, 64, CDT>(lp, items, kp, s);
+  // fp32 factors take no shared-memory factor stages, so the planner never
+  // narrows their tiles to 64 columns.
+  if constexpr (CDT == pm::kF32) return fail(PIPER_MERGE_EINVAL, "fp32 factors run on 128- or 256-column tiles.");
+  else return launch_t<FMT, PASS, 64, CDT>(lp, items, kp, s);
 }
 
 // Development builds may compile a subset of the formats: -DPIPER_ONLY_FMTS=<bitmask of PIPER_FMT_* ids>.
@@ -3615,16 +3759,17 @@ int launch_fmt(int fmt, int bn, LaunchParams& lp, int items, int kp, cudaStream_
   if (!fmt_on(fmt)) return fail(PIPER_MERGE_EINVAL, "format not compiled into this build.");
   switch (fmt) {
     case PIPER_FMT_MXFP8_E4M3:
-      if constexpr (fmt_on(PIPER_FMT_MXFP8_E4M3) && PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_MXFP8_E4M3) && PASS == pm::kLocal && (CDT == pm::kBF16 || CDT == pm::kF32)) return launch_bn<PIPER_FMT_MXFP8_E4M3, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_MXFP8_E5M2:
-      if constexpr (fmt_on(PIPER_FMT_MXFP8_E5M2) && PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_MXFP8_E5M2) && PASS == pm::kLocal && (CDT == pm::kBF16 || CDT == pm::kF32)) return launch_bn<PIPER_FMT_MXFP8_E5M2, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_MXFP4:
-      if constexpr (fmt_on(PIPER_FMT_MXFP4) && PASS == pm::kLocal && CDT == pm::kBF16) return launch_bn<PIPER_FMT_MXFP4, PASS, CDT>(bn, lp, items, kp, s);
+      if constexpr (fmt_on(PIPER_FMT_MXFP4) && PASS == pm::kLocal && (CDT == pm::kBF16 || CDT == pm::kF32)) return launch_bn<PIPER_FMT_MXFP4, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_NVFP4:
-      if constexpr (fmt_on(PIPER_FMT_NVFP4) && (PASS == pm::kLocal || PASS == pm::kReduce) && CDT == pm::kBF16)
+      if constexpr (fmt_on(PIPER_FMT_NVFP4) && (PASS == pm::kLocal || PASS == pm::kReduce) &&
+                    (CDT == pm::kBF16 || CDT == pm::kF32))
         return launch_bn<PIPER_FMT_NVFP4, PASS, CDT>(bn, lp, items, kp, s);
       break;
     case PIPER_FMT_FP8_E4M3:
@@ -3672,6 +3817,12 @@ int launch(int pass, int cdt, int fmt, int bn, LaunchParams& lp, int items, int 
     if (pass == pm::kReduce) return launch_fmt<pm::kReduce, pm::kBF16>(fmt, bn, lp, items, kp, s);
     if (pass == pm::kFused) return launch_fmt<pm::kFused, pm::kBF16>(fmt, bn, lp, items, kp, s);
     return launch_fmt<pm::kEncode, pm::kBF16>(fmt, bn, lp, items, kp, s);
+  }
+  if (cdt == PIPER_DT_F32) {
+    if (pass == pm::kLocal) return launch_fmt<pm::kLocal, pm::kF32>(fmt, bn, lp, items, kp, s);
+    if (pass == pm::kReduce) return launch_fmt<pm::kReduce, pm::kF32>(fmt, bn, lp, items, kp, s);
+    if (pass == pm::kFused) return launch_fmt<pm::kFused, pm::kF32>(fmt, bn, lp, items, kp, s);
+    return launch_fmt<pm::kEncode, pm::kF32>(fmt, bn, lp, items, kp, s);
   }
   if (pass == pm::kLocal) return launch_fmt<pm::kLocal, pm::kF16>(fmt, bn, lp, items, kp, s);
   if (pass == pm::kReduce) return launch_fmt<pm::kReduce, pm::kF16>(fmt, bn, lp, items, kp, s);
@@ -3805,7 +3956,10 @@ DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws,
   w.M = static_cast<int>(d.rows);
   w.N = static_cast<int>(d.cols);
   w.r = static_cast<int>(d.rank);
-  w.KP = pm::align_up(static_cast<int>(d.rank), 16);
+  // fp32 factors stay in global memory (the epilogue's CUDA-core update reads
+  // them); the smallest factor stages are laid out and left unused.
+  const bool f32_factors = d.compute_dtype == PIPER_DT_F32;
+  w.KP = f32_factors ? 16 : pm::align_up(static_cast<int>(d.rank), 16);
   w.row_begin = seg.row_begin;
   w.row_blocks = (seg.rows + 127) / 128;
   w.group = p.group;
@@ -3820,7 +3974,7 @@ DevWeight make_dev_weight(const piper_merge_desc& d, const Plan& p, uint8_t* ws,
   w.col_axis = p.col_axis ? 1 : 0;
   if (!env_flags().no_tma) {
     setup_tma(w, d, p.bn);
-    setup_tma_factors(w, d, w.KP);
+    if (!f32_factors) setup_tma_factors(w, d, w.KP);
   }
   return w;
 }

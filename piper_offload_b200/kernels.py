@@ -50,11 +50,6 @@ def _factor_dt(b: torch.Tensor, a: torch.Tensor, *, allowed: tuple[torch.dtype, 
     if b.dtype not in allowed:
         names = ", ".join(str(d).replace("torch.", "") for d in allowed)
         raise ValueError(f"merge supports {names} LoRA factors, got {b.dtype}.")
-    if b.dtype is torch.float32:
-        raise ValueError(
-            "the sm_100a merge computes the rank-r update on tcgen05 tensor cores and needs "
-            "bfloat16 or float16 factors; float32 factors are not supported."
-        )
     return _dt_id(b.dtype, "LoRA factors")
 
 
@@ -128,10 +123,8 @@ def merge_mx_lora_(
         raise ValueError("MX merge supports block size 32.")
     if b.dtype is not a.dtype or b.dtype is not orig_dtype:
         raise ValueError("MX merge requires factors in the weight's original dtype.")
-    if orig_dtype is not torch.bfloat16:
-        raise ValueError(
-            f"MX merge on sm_100a supports bfloat16 weights and factors, got {orig_dtype}."
-        )
+    if orig_dtype not in (torch.bfloat16, torch.float32):  # _triton_mx_lora.py:311-316
+        raise ValueError(f"MX merge supports bfloat16 and float32 weights and factors, got {orig_dtype}.")
     _same_device(qdata, scale, b, a)
     if not qdata.is_contiguous() or not scale.is_contiguous():
         raise ValueError("MX merge requires contiguous MX storage.")
@@ -163,7 +156,7 @@ def merge_mx_lora_(
     seed, sflag = _seed_fields(rounding_seed)
     d = _desc(
         qdata=qdata.data_ptr(), scale=scale.data_ptr(), b=b.data_ptr(), a=a.data_ptr(),
-        rows=rows, cols=cols, rank=rank, format=fmt, compute_dtype=nat.DT_BF16,
+        rows=rows, cols=cols, rank=rank, format=fmt, compute_dtype=_dt_id(orig_dtype, "MX weights"),
         scale_mode=int(scaling_mode), flags=(nat.FLAG_SWIZZLED if swizzled else 0) | sflag,
         strength=float(strength), seed=seed, offset_base=int(offset_base),
     )
@@ -201,7 +194,7 @@ def merge_nvfp4_lora(
         raise ValueError("NVFP4 merge expects rank-two tensors.")
     if not qdata.is_contiguous() or not scale.is_contiguous():
         raise ValueError("NVFP4 merge requires contiguous packed data and scales.")
-    _factor_dt(b, a, allowed=(torch.bfloat16, torch.float32))
+    cdt = _factor_dt(b, a, allowed=(torch.bfloat16, torch.float32))
     _same_device(qdata, scale, b, a, per_tensor_scale)
     if block_size != _NVFP4_BLOCK_SIZE:
         raise ValueError("NVFP4 merge requires block_size=16.")
@@ -226,7 +219,7 @@ def merge_nvfp4_lora(
     d = _desc(
         qdata=qdata.data_ptr(), scale=scale.data_ptr(), global_scale=_ptr(per_tensor_scale),
         b=b.data_ptr(), a=a.data_ptr(), rows=rows, cols=cols, rank=rank, format=nat.FMT_NVFP4,
-        compute_dtype=nat.DT_BF16, flags=(nat.FLAG_SWIZZLED if is_swizzled_scales else 0) | sflag,
+        compute_dtype=cdt, flags=(nat.FLAG_SWIZZLED if is_swizzled_scales else 0) | sflag,
         strength=float(strength), seed=seed, offset_base=int(offset_base),
     )
     nat.merge_batch([d], qdata.device)

@@ -518,6 +518,74 @@ def gen_bnb4(bnb4, w: Writer, g) -> None:
         one(19, 128, 13, quant_type, SEED, "bf16", zero_b=True)
 
 
+def gen_f32(mods, w: Writer, g) -> None:
+    """fp32 LoRA factors (the launchers' IEEE fp32 ``tl.dot`` path, and fp32
+    compute for the adapters' float32 weights): scaled FP8, INT8, NVFP4 and MX."""
+    f8, i8, n4, mx = mods["float8"], mods["int8"], mods["nvfp4"], mods["mx"]
+    for layout, seed, rank in (("row", SEED, 7), ("row", None, 40), ("tensor", SEED, 19), ("group", None, 7)):
+        rows, cols = 70, 130 if layout != "group" else 120
+        base = torch.randn(rows, cols, generator=g) * 0.02
+        if layout == "row":
+            block, s = (1, cols), base.abs().amax(1, keepdim=True) / 448.0
+            sx = s
+        elif layout == "tensor":
+            block, s = (rows, cols), (base.abs().amax() / 448.0).reshape(1, 1)
+            sx = s
+        else:
+            block = (1, 10)
+            s = base.reshape(rows, cols // 10, 10).abs().amax(2) / 448.0
+            sx = s.repeat_interleave(10, 1)
+        s = s.float()
+        q = (base / sx).clamp(-448, 448).to(torch.float8_e4m3fn)
+        b, a = exact_factors(g, rows, cols, rank, torch.float32)
+        oq, os_ = f8.merge_float8_lora(q.clone(), s.clone(), block, b, a, 1.0, rounding_seed=seed)
+        w.add({"launcher": "float8", "rows": rows, "cols": cols, "rank": rank, "e4m3": True, "block": list(block),
+               "seed": seed, "dtype": "f32", "strength": 1.0},
+              qdata=q, scale=s, b=b, a=a, out_qdata=oq, out_scale=os_)
+    for asym, seed, sdt in ((False, SEED, "bf16"), (True, None, "f32"), (False, None, "f16")):
+        rows, cols, rank = 35, 69, 19
+        q = torch.randint(-128, 128, (rows, cols), generator=g, dtype=torch.int8)
+        scale = (torch.rand((rows, 1), generator=g) * 2e-4 + 1e-4).to(DTYPES[sdt])
+        zp = torch.randint(-10, 10, (rows, 1), generator=g, dtype=torch.int8) if asym else None
+        b, a = exact_factors(g, rows, cols, rank, torch.float32, exp=9)
+        oq, os_, oz = i8.merge_int8_lora(q.clone(), scale.clone(), None if zp is None else zp.clone(), (1, cols),
+                                         b, a, 1.0, asymmetric=asym, reduce_range=False, rounding_seed=seed)
+        w.add({"launcher": "int8", "rows": rows, "cols": cols, "rank": rank, "block": [1, cols], "asymmetric": asym,
+               "reduce_range": False, "seed": seed, "dtype": "f32", "scale_dtype": sdt, "strength": 1.0},
+              qdata=q, scale=scale, zero_point=zp, b=b, a=a, out_qdata=oq, out_scale=os_, out_zero_point=oz)
+    for two_level, seed in ((True, SEED), (False, None), (True, None)):
+        rows, cols, rank = 19, 80, 13
+        q = torch.randint(0, 256, (rows, cols // 2), generator=g, dtype=torch.uint8)
+        if two_level:
+            scale = (torch.rand((rows, cols // 16), generator=g) * 3 + 0.5).to(torch.float8_e4m3fn)
+            pts = torch.tensor(0.003, dtype=torch.float32)
+        else:
+            scale = (torch.rand((rows, cols // 16), generator=g) * 0.01 + 0.002).to(torch.float8_e4m3fn)
+            pts = None
+        b, a = exact_factors(g, rows, cols, rank, torch.float32)
+        oq, os_, og = n4.merge_nvfp4_lora(q.clone(), scale.clone(), None if pts is None else pts.clone(), 16, False,
+                                          b, a, 1.0, rounding_seed=seed)
+        w.add({"launcher": "nvfp4", "rows": rows, "cols": cols, "rank": rank, "swizzled": False,
+               "two_level": two_level, "seed": seed, "dtype": "f32", "strength": 1.0},
+              qdata=q, scale=scale, per_tensor_scale=pts, b=b, a=a, out_qdata=oq, out_scale=os_,
+              out_per_tensor_scale=og)
+    elem_dtypes = {"e4m3": torch.float8_e4m3fn, "e2m1": torch.float4_e2m1fn_x2}
+    for elem, mode, seed in (("e4m3", 0, SEED), ("e4m3", 1, None), ("e2m1", 0, None), ("e2m1", 3, SEED)):
+        rows, cols, rank = 19, 96, 7
+        if elem == "e2m1":
+            q = torch.randint(0, 256, (rows, cols // 2), generator=g, dtype=torch.uint8)
+        else:
+            q = (torch.randn(rows, cols, generator=g) * 100).clamp(-400, 400).to(elem_dtypes[elem])
+        scale = torch.randint(110, 122, (rows, cols // 32), generator=g, dtype=torch.uint8).view(torch.float8_e8m0fnu)
+        b, a = exact_factors(g, rows, cols, rank, torch.float32, exp=9)
+        oq, os_ = q.clone(), scale.clone()
+        mx.merge_mx_lora_(oq, os_, elem_dtypes[elem], 32, torch.float32, b, a, 1.0, scaling_mode=mode,
+                          swizzled=False, rounding_seed=seed)
+        w.add({"launcher": "mx", "rows": rows, "cols": cols, "rank": rank, "elem": elem, "scaling_mode": mode,
+               "swizzled": False, "seed": seed, "dtype": "f32", "strength": 1.0},
+              qdata=q, scale=scale, b=b, a=a, out_qdata=oq, out_scale=os_)
+
+
 def main() -> None:
     ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PIPER_OFFLOAD_SRC", ""))
     mods = load_reference(ref / "src")
@@ -530,6 +598,7 @@ def main() -> None:
     gen_bnb8(mods["bnb8"], w, torch.Generator().manual_seed(85))
     gen_quanto(mods["quanto"], w, torch.Generator().manual_seed(86))
     gen_bnb4(mods["bnb4"], w, torch.Generator().manual_seed(87))
+    gen_f32(mods, w, torch.Generator().manual_seed(88))
     w.save()
     print(f"{len(w.cases)} reference merge cases written to", HERE)
 

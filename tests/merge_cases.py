@@ -100,7 +100,7 @@ class Case:
             if f == "mxfp4" and elem is None:
                 raise RuntimeError("torch lacks float4_e2m1fn_x2")
             scale_e8 = sc.view(torch.float8_e8m0fnu)
-            K.merge_mx_lora_(qd, scale_e8, elem, 32, torch.bfloat16, b, a, self.strength,
+            K.merge_mx_lora_(qd, scale_e8, elem, 32, self.factor_dtype, b, a, self.strength,
                              scaling_mode=self.scale_mode, swizzled=self.swizzled, **kw)
             out["q"] = u8np(qd)
             out["scale"] = u8np(scale_e8)

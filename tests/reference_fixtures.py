@@ -218,7 +218,7 @@ def native(case: dict, device) -> dict:
     elem = {"e4m3": torch.float8_e4m3fn, "e5m2": torch.float8_e5m2, "e2m1": torch.float4_e2m1fn_x2}[case["elem"]]
     q = dev(arr(case, "qdata"), None if case["elem"] == "e2m1" else elem)
     sc = dev(arr(case, "scale"), torch.float8_e8m0fnu)
-    K.merge_mx_lora_(q, sc, elem, 32, torch.bfloat16, b, a, s, scaling_mode=case["scaling_mode"],
+    K.merge_mx_lora_(q, sc, elem, 32, fdt, b, a, s, scaling_mode=case["scaling_mode"],
                      swizzled=case["swizzled"], **kw)
     return {"q": q.view(torch.uint8).cpu().numpy().reshape(-1), "scale": sc.view(torch.uint8).cpu().numpy().reshape(-1)}
 

@@ -101,6 +101,26 @@ def test_fp16_factors(fmt, cuda_device):
     check(Case(fmt, 96, 256, 16, factor_dtype=torch.float16, group=_group(fmt)), cuda_device)
 
 
+# fp32 factors: the reference's IEEE fp32 dot (one fused multiply-add per rank
+# step in rank order) has no summation-order tie class, so the CUDA-core update
+# matches the oracle's exact chain bit for bit. Ranks below, at and above the
+# reference's rank blocks (16, then multiples of 32), ragged shapes included.
+F32_CASES = [
+    ("fp8_row", 70, 130, 7), ("fp8_row", 256, 1024, 48), ("fp8_tensor", 96, 256, 16), ("fp8_group", 64, 256, 32),
+    ("int8_row", 35, 69, 19), ("int8_tensor", 96, 256, 40), ("int8_group", 64, 512, 16), ("int8_asym", 35, 69, 7),
+    ("mxfp8", 19, 96, 7), ("mxfp8", 256, 1024, 64), ("mxfp8_e5m2", 64, 256, 33), ("mxfp4", 128, 512, 32),
+    ("nvfp4", 19, 80, 13), ("nvfp4", 256, 1024, 64), ("nvfp4_1l", 130, 1040, 20),
+    ("q8_0", 96, 256, 16), ("q4_0", 64, 512, 24),
+]
+
+
+@pytest.mark.parametrize("stochastic", [False, True], ids=["rtn", "sr"])
+@pytest.mark.parametrize("fmt,rows,cols,rank", F32_CASES, ids=[f"{c[0]}-{c[1]}x{c[2]}-r{c[3]}" for c in F32_CASES])
+def test_fp32_factors_exact(fmt, rows, cols, rank, stochastic, cuda_device):
+    check(Case(fmt, rows, cols, rank, seed=SEED if stochastic else None, factor_dtype=torch.float32,
+               group=_group(fmt), outliers=0.001), cuda_device, exact=True)
+
+
 @pytest.mark.parametrize("strength", [0.0, -0.75, 3.5])
 def test_strengths(strength, cuda_device):
     for fmt in ("mxfp8", "nvfp4", "fp8_row", "int8_row", "q8_0"):

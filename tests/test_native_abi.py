@@ -55,7 +55,7 @@ def _desc(**kw) -> nat.MergeDesc:
         ({"rows": 0}, "non-empty"),
         ({"rank": 300}, "rank above 256"),
         ({"format": 99}, "unknown format"),
-        ({"compute_dtype": nat.DT_F32}, "bfloat16 and float16"),
+        ({"compute_dtype": 7}, "float16, bfloat16, and float32"),
         ({"block_rows": 3, "block_cols": 7}, "per-group"),
         ({"format": nat.FMT_MXFP8_E4M3, "cols": 100}, "divisible by 32"),
         ({"format": nat.FMT_MXFP8_E4M3, "scale_mode": 9}, "scaling mode"),
@@ -72,6 +72,17 @@ def test_invalid_descriptors_are_rejected_on_host(kw, match):
     arr = (nat.MergeDesc * 1)(d)
     rc = nat.load().piper_merge_batch(arr, 1, None, 0, None)
     assert rc == nat.EINVAL
+
+
+@pytest.mark.parametrize("fmt,extra", [
+    (nat.FMT_FP8_E4M3, {}), (nat.FMT_INT8, {"scale_dtype": nat.DT_BF16}), (nat.FMT_MXFP8_E4M3, {}),
+    (nat.FMT_MXFP4, {}), (nat.FMT_NVFP4, {}), (nat.FMT_GGUF_Q8_0, {}),
+])
+def test_fp32_factors_are_accepted_on_host(fmt, extra):
+    """fp32 LoRA factors pass the host checks as the reference launchers accept
+    them (_triton_float8_lora.py:311-318, _triton_mx_lora.py:311-316,
+    _triton_nvfp4_lora.py:370-375)."""
+    assert nat.workspace_bytes([_desc(format=fmt, compute_dtype=nat.DT_F32, **extra)]) >= 0
 
 
 def test_workspace_sizes():

@@ -24,9 +24,13 @@ CASES = rf.cases()
 
 @pytest.fixture(scope="module", autouse=True)
 def interpreter_division():
+    # The interpreter divides by constants in IEEE fp32 and rounds every
+    # operation on its own (no fp32 contraction).
     onum.set_constant_division("ieee")
+    onum.set_fp32_contraction("separate")
     yield
     onum.set_constant_division("reciprocal")
+    onum.set_fp32_contraction("gpu")
 
 
 def test_fixture_coverage():

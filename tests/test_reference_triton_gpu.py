@@ -94,7 +94,7 @@ def run_reference(ref, case: Case, dev) -> dict:
         elem = {"mxfp8": torch.float8_e4m3fn, "mxfp8_e5m2": torch.float8_e5m2,
                 "mxfp4": torch.float4_e2m1fn_x2}[f]
         scale_e8 = sc.view(torch.float8_e8m0fnu)
-        ref["mx"].merge_mx_lora_(qd, scale_e8, elem, 32, torch.bfloat16, b, a, case.strength,
+        ref["mx"].merge_mx_lora_(qd, scale_e8, elem, 32, case.factor_dtype, b, a, case.strength,
                                  scaling_mode=case.scale_mode, swizzled=case.swizzled, rounding_seed=case.seed)
         out["q"], out["scale"] = u8np(qd), u8np(scale_e8)
     elif f.startswith("nvfp4"):
@@ -218,3 +218,34 @@ def test_reference_exact_at_config_size_with_exact_factors(ref, cuda_device):
     case = Case("fp8_row", 4096, 14336, 32, seed=SEED).build(data_seed=3)
     exact_factors(case, 99)
     versus_reference(ref, case, cuda_device, "exact-fp8-4096x14336-sr", exact=True)
+
+
+# fp32 factors with the configs' own factor distributions (not exact in any
+# summation order): the reference's IEEE fp32 dot is one fused multiply-add per
+# rank step in rank order, which the CUDA-core update reproduces, so no tie
+# class remains and the codes and scales must be identical. Ranks below and
+# above the reference's rank blocks (16, then multiples of 32).
+F32_REFERENCE = [
+    ("fp8_row", 256, 1024, 48, {}), ("fp8_tensor", 70, 130, 7, {}), ("int8_row", 128, 512, 19, {}),
+    ("int8_asym", 35, 69, 7, {}), ("mxfp8", 128, 1024, 64, {}), ("mxfp4", 64, 512, 16, {}),
+    ("nvfp4", 128, 1024, 33, {}), ("nvfp4_1l", 19, 80, 13, {}),
+]
+
+
+@pytest.mark.parametrize("stochastic", [False, True], ids=["rtn", "sr"])
+@pytest.mark.parametrize("fmt,rows,cols,rank,kw", F32_REFERENCE,
+                         ids=[f"{e[0]}-{e[1]}x{e[2]}-r{e[3]}" for e in F32_REFERENCE])
+def test_fp32_factors_against_reference(ref, fmt, rows, cols, rank, kw, stochastic, cuda_device):
+    case = Case(fmt, rows, cols, rank, seed=SEED if stochastic else None, factor_dtype=torch.float32,
+                outliers=0.001, **kw).build(data_seed=rows + rank)
+    versus_reference(ref, case, cuda_device, f"f32-{fmt}-{rows}x{cols}-r{rank}", exact=True)
+
+
+@pytest.mark.parametrize("stochastic", [False, True], ids=["rtn", "sr"])
+def test_fp32_factors_int8_fp32_scales_against_reference(ref, stochastic, cuda_device):
+    """fp32 scales make ``(q - zp) * scale`` inexact, so the contraction of the
+    fp32-compute ``base + acc * strength`` onto that product is visible."""
+    case = Case("int8_row", 128, 512, 24, seed=SEED if stochastic else None, factor_dtype=torch.float32,
+                outliers=0.001).build(data_seed=5)
+    case.tensors["q"].scale = case.tensors["q"].scale.float()
+    versus_reference(ref, case, cuda_device, "f32-int8-f32scales", exact=True)
