@@ -2307,6 +2307,9 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
     if (lane == 0) {
       uint32_t t = 0, it = 0;
       bool ok = true;
+      // The next item's counter value is fetched one item ahead, so the
+      // atomic's round trip overlaps the current item's loads.
+      unsigned int next_v = atomicAdd(&g_sched_next[P.sched_slot], 1u);
       for (;; ++it) {
         if (!ok) break;
         // Take the next item (-1 past the last) and publish it to every role.
@@ -2315,8 +2318,9 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
           ok = mbar_wait(&item_empty[rs], ((it / kItemRing) - 1) & 1u, kStatusTimeoutLoad);
           if (!ok) break;
         }
-        const unsigned int v = atomicAdd(&g_sched_next[P.sched_slot], 1u);
+        const unsigned int v = next_v;
         const int item = v < static_cast<unsigned int>(P.n_items) ? static_cast<int>(v) : -1;
+        if (item >= 0) next_v = atomicAdd(&g_sched_next[P.sched_slot], 1u);
         item_ring[rs] = item;
         mbar_arrive(&item_full[rs]);
         if (item < 0) break;
@@ -4001,8 +4005,11 @@ int run_group(const piper_merge_desc* descs, const std::vector<Plan>& plans, uin
     const Plan& p = plans[sg.desc];
     total_tiles += static_cast<int64_t>((sg.rows + 127) / 128) * ((descs[sg.desc].cols + p.bn - 1) / p.bn);
   }
+  // Items take at least two column tiles where a strip has them: each item
+  // reloads its B strip and takes one atomic from the item counter, and with
+  // dynamic distribution a small tail costs little.
   const int64_t target_items = 32ll * sm_count();
-  const int tiles_per_item = static_cast<int>(std::max<int64_t>(1, total_tiles / target_items));
+  const int tiles_per_item = static_cast<int>(std::max<int64_t>(2, total_tiles / target_items));
   int items = 0;
   for (size_t i = 0; i < order.size(); ++i) {
     const piper_merge_desc& d = descs[order[i].desc];
