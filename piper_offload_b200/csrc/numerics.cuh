@@ -172,14 +172,29 @@ __device__ __forceinline__ void philox_word0_xn(const PhiloxKey& key, uint64_t o
   // Round 0 with counter words 2 and 3 zero: the second multiply is zero.
   uint32_t c0[N], c1[N], c2[N], c3[N];
   const uint32_t hi0 = static_cast<uint32_t>(offset >> 32);
+  if (static_cast<uint32_t>((offset + static_cast<uint64_t>(N - 1)) >> 32) == hi0) {
+    // The N low counter words are lo0 + j with no carry out of 32 bits, so the
+    // round-0 products A * (lo0 + j) are A * lo0 + A * j: one wide multiply
+    // and N 64-bit additions of constants.
+    const uint64_t p0 = static_cast<uint64_t>(0xD2511F53u) * static_cast<uint32_t>(offset);
 #pragma unroll
-  for (int j = 0; j < N; ++j) {
-    const uint64_t o = offset + static_cast<uint64_t>(j);
-    const uint32_t lo = static_cast<uint32_t>(o);
-    c0[j] = static_cast<uint32_t>(o >> 32) ^ key.k0[0];
-    c2[j] = __umulhi(0xD2511F53u, lo) ^ key.k1[0];
-    c1[j] = 0u;
-    c3[j] = 0xD2511F53u * lo;
+    for (int j = 0; j < N; ++j) {
+      const uint64_t p = p0 + static_cast<uint64_t>(0xD2511F53u) * static_cast<uint64_t>(j);
+      c0[j] = hi0 ^ key.k0[0];
+      c2[j] = static_cast<uint32_t>(p >> 32) ^ key.k1[0];
+      c1[j] = 0u;
+      c3[j] = static_cast<uint32_t>(p);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const uint64_t o = offset + static_cast<uint64_t>(j);
+      const uint32_t lo = static_cast<uint32_t>(o);
+      c0[j] = static_cast<uint32_t>(o >> 32) ^ key.k0[0];
+      c2[j] = __umulhi(0xD2511F53u, lo) ^ key.k1[0];
+      c1[j] = 0u;
+      c3[j] = 0xD2511F53u * lo;
+    }
   }
   // Round 1: word 0 is (offset >> 32) ^ key, the same for the N counters
   // unless they straddle a multiple of 2^32, so its product is formed once.
@@ -350,8 +365,10 @@ namespace pm {
 __device__ __forceinline__ void bf16r2(float& a, float& b) {
   uint32_t d;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
-  a = __uint_as_float(d << 16);
-  b = __uint_as_float(d & 0xFFFF0000u);
+  // Widen with byte permutes (the ALU pipe), leaving the integer multiply pipe
+  // to the Philox multiplies.
+  a = __uint_as_float(__byte_perm(d, 0u, 0x1044u));
+  b = __uint_as_float(__byte_perm(d, 0u, 0x3244u));
 }
 __device__ __forceinline__ void f16r2(float& a, float& b) {
   const __half2 h = __floats2half2_rn(a, b);
@@ -395,7 +412,7 @@ __device__ __forceinline__ uint32_t enc_fp8x4(float a, float b, float c, float d
     asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
     asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
   }
-  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  return __byte_perm(static_cast<uint32_t>(lo), static_cast<uint32_t>(hi), 0x5410u);
 }
 
 // Two E2M1 codes (low nibble first) of one byte to fp32. The reference applies
