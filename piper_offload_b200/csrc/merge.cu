@@ -442,6 +442,41 @@ __device__ __forceinline__ void f32_update(const DevWeight& W, int row, bool val
   }
 }
 
+// Stores the new scale bytes of this thread's row for one tile (MX: one per
+// 32 columns, NVFP4: one per 16), which the encoders leave in the tile's
+// shared-memory scale slot in place of the input bytes: one wide store per row
+// and tile instead of a one-byte store per block, whose 32 lanes (32 rows)
+// would each touch another sector.
+template <int FMT>
+__device__ __forceinline__ void flush_tile_scales(const DevWeight& W, const RowCtx& c) {
+  if (!c.valid) return;
+  constexpr int kBlk = FMT == PIPER_FMT_NVFP4 ? 16 : 32;
+  const int nb = (c.tile_cols + kBlk - 1) / kBlk;
+  uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
+  const uint8_t* src = c.sscale;
+  if (W.flags & PIPER_FLAG_SWIZZLED) {
+    // 128x4 blocked layout: blocks 4j .. 4j+3 of a row are 4 contiguous bytes
+    // (tiles start on a multiple of 4 blocks).
+    int j = 0;
+    for (; j + 4 <= nb; j += 4)
+      *reinterpret_cast<uint32_t*>(scale8 + swizzled_index(c.row, c.blk0 + j, W.scale_cols)) =
+          *reinterpret_cast<const uint32_t*>(src + j);
+    for (; j < nb; ++j) scale8[swizzled_index(c.row, c.blk0 + j, W.scale_cols)] = src[j];
+    return;
+  }
+  uint8_t* dst = scale8 + static_cast<int64_t>(c.row) * W.scale_cols + c.blk0;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(dst);
+  if (nb == 16 && (a & 15u) == 0) {
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  } else if (nb == 8 && (a & 7u) == 0) {
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
+  } else if (nb == 4 && (a & 3u) == 0) {
+    *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(src);
+  } else {
+    for (int j = 0; j < nb; ++j) dst[j] = src[j];
+  }
+}
+
 // ================================================================ MX epilogue
 template <int FMT, int CDT>
 __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, int k,
@@ -449,7 +484,6 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
   using P = MxParams<FMT>;
   const int col = c.tile_col0 + 32 * k;
   const int blk = col >> 5;
-  uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
   const uint32_t sc = c.valid ? c.sscale[blk - c.blk0] : 127u;
   const float bscale = dec_e8m0(sc);
   // Decode: FP8 / FP4 values are exactly representable in bf16, so the
@@ -532,7 +566,9 @@ __device__ __forceinline__ void mx_chunk(const DevWeight& W, const RowCtx& c, in
     }
     store_chunks32(c, k, out);
   }
-  if (c.valid) scale8[scale_index(W, c.row, blk)] = static_cast<uint8_t>(s.code);
+  // The new scale byte replaces the input one in the tile's shared-memory slot;
+  // flush_tile_scales stores the row's bytes of the tile at once.
+  const_cast<uint8_t*>(c.sscale)[blk - c.blk0] = static_cast<uint8_t>(s.code);
 }
 
 // Fast path of mx_chunk, same codes and scale, for the common block: scale
@@ -641,7 +677,7 @@ __device__ __forceinline__ bool mx_chunk_fast(const DevWeight& W, const RowCtx& 
     }
     store_chunks32(c, k, out);
   }
-  if (c.valid) reinterpret_cast<uint8_t*>(W.scale)[scale_index(W, c.row, blk)] = static_cast<uint8_t>(s.code);
+  const_cast<uint8_t*>(c.sscale)[blk - c.blk0] = static_cast<uint8_t>(s.code);  // flushed per tile
   return true;
 }
 
@@ -688,7 +724,7 @@ __device__ __forceinline__ void nvfp4_block(const DevWeight& W, const RowCtx& c,
     const uint32_t fcode = enc_e4m3(fs);
     fs = dec_e4m3(fcode);
     const int64_t sidx = scale_index(W, c.row, blk);
-    if (c.valid) scale8[sidx] = static_cast<uint8_t>(fcode);
+    if (c.valid) const_cast<uint8_t*>(c.sscale)[blk - c.blk0] = static_cast<uint8_t>(fcode);  // flushed per tile
     else if (W.flags & PIPER_FLAG_SWIZZLED) scale8[sidx] = 0u;  // swizzle padding rows
     const bool sr = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
     if (two_level) {
@@ -788,7 +824,7 @@ __device__ __forceinline__ bool nvfp4_block_fast(const DevWeight& W, const RowCt
     const uint32_t fcode = enc_e4m3(fs);
     fs = dec_e4m3(fcode);
     const int64_t sidx = scale_index(W, c.row, blk);
-    if (c.valid) scale8[sidx] = static_cast<uint8_t>(fcode);
+    if (c.valid) const_cast<uint8_t*>(c.sscale)[blk - c.blk0] = static_cast<uint8_t>(fcode);  // flushed per tile
     else if (W.flags & PIPER_FLAG_SWIZZLED) scale8[sidx] = 0u;  // swizzle padding rows
     if (two_level) {
       const float recip = div_full(div_full(1.0f, g_out), fs);
@@ -2809,6 +2845,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
             mx_chunk<FMT, CDT>(W, c, k, acc2);
           }
         });
+        flush_tile_scales<FMT>(W, c);
       } else if constexpr (FMT == PIPER_FMT_NVFP4) {
         chunk_loop(0, tcols / 32, [&](int k, const float (&acc)[32]) {
           nvfp4_chunk<PASS, CDT>(W, c, k, acc, g_in, g_out, two_level, red_max);
@@ -2821,6 +2858,7 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
           nvfp4_block<PASS, CDT>(W, c, c0 + 32 * k, acc, g_in, g_out, two_level, red_max, codes);
           if (PASS != kReduce) *reinterpret_cast<uint2*>(chunk_ptr(c, k)) = codes;
         }
+        if constexpr (PASS != kReduce) flush_tile_scales<FMT>(W, c);
       } else if constexpr (FMT == PIPER_FMT_BNB4_NF4 || FMT == PIPER_FMT_BNB4_FP4) {
         // One 64-value block of _merge_quantize_kernel (_triton_bnb4_lora.py:163-313)
         // per pair of 32-column chunks: the block maximum from a first decode,
@@ -3373,7 +3411,7 @@ using pm::LaunchParams;
 
 // Bytes of codes a two-pass launch group covers, so that its ENCODE launch
 // re-reads them from L2 (126 MB on B200).
-constexpr int64_t kL2GroupBytes = 48ll << 20;
+constexpr int64_t kL2GroupBytes = 96ll << 20;
 
 // Code bytes of `cols` columns (host mirror of code_bytes<FMT>).
 int host_code_bytes(int fmt, int cols) {
