@@ -807,14 +807,16 @@ __device__ __forceinline__ bool nvfp4_block_fast(const DevWeight& W, const RowCt
     float2 t = __fmul2_rn(make_float2(m[i], m[i + 1]), b2);
     if (CDT == kBF16 && two_level) bf16r2(t.x, t.y);  // single-level products are exact bf16 values
     t = __ffma2_rn(make_float2(acc[i], acc[i + 1]), st2, t);
-    round_dt2<CDT>(t.x, t.y);
+    // The maxima pass rounds only the block maximum below (rounding is
+    // monotone: max |compute(x)| = compute(max |x|)).
+    if constexpr (PASS != kReduce) round_dt2<CDT>(t.x, t.y);
     m[i] = t.x;
     m[i + 1] = t.y;
   }
   const float amax = tree3(m, max3_abs_nan);
   if (!(amax <= 3.40282347e38f)) return false;
   if constexpr (PASS == kReduce) {
-    if (c.valid) amax_acc = fmaxf(amax_acc, amax);
+    if (c.valid) amax_acc = fmaxf(amax_acc, round_dt<CDT>(amax));
     return true;
   } else {
     uint8_t* scale8 = reinterpret_cast<uint8_t*>(W.scale);
@@ -2137,12 +2139,14 @@ __device__ __forceinline__ void gguf_chunk(const DevWeight& W, const RowCtx& c, 
 // Epilogue warpgroups per format and tile width (tile t -> warpgroup t % EW).
 // Three give the epilogue more warps in flight; GGUF keeps two so that its
 // 256-column tiles (the narrowest whose rows are 16-byte multiples) fit two
-// accumulators, bitsandbytes 4-bit keeps two for its per-lane tables, and
-// NVFP4 keeps two for the registers of its two-block chunks (with three, its
-// 152 registers per thread spill).
-__host__ __device__ constexpr int epi_wgs_rt(int fmt, int /*bn*/) {
+// accumulators, and bitsandbytes 4-bit keeps two for its per-lane tables.
+// NVFP4 runs both: 256-column tiles with two warpgroups for round-to-nearest,
+// 128-column tiles with three for stochastic rounding (the host plan picks
+// the width by rounding mode; measured 543 vs 476 GB/s RTN, 146 vs 191 SR).
+__host__ __device__ constexpr int epi_wgs_rt(int fmt, int bn) {
+  if (fmt == PIPER_FMT_NVFP4) return bn >= 256 ? 2 : 3;
   return (fmt == PIPER_FMT_GGUF_Q8_0 || fmt == PIPER_FMT_GGUF_Q4_0 || fmt == PIPER_FMT_BNB4_NF4 ||
-          fmt == PIPER_FMT_BNB4_FP4 || fmt == PIPER_FMT_NVFP4)
+          fmt == PIPER_FMT_BNB4_FP4)
              ? 2
              : 3;
 }
@@ -3630,7 +3634,9 @@ int validate(const piper_merge_desc& d, Plan& p) {
   auto fits = [&](int bn, int min_sc) {
     return 512 / bn >= pm::epi_wgs_rt(d.format, bn) && plan_pipe(d.format, bn, kp).sc >= min_sc;
   };
-  if (fits(256, 4)) p.bn = 256;
+  // Stochastic NVFP4 prefers three epilogue warpgroups, i.e. 128-column tiles.
+  const bool narrow = d.format == PIPER_FMT_NVFP4 && (d.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+  if (!narrow && fits(256, 4)) p.bn = 256;
   else if (fits(128, 4)) p.bn = 128;
   else if (fits(64, 2)) p.bn = 64;
   else return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(d.rank) + " is too large for the merge pipeline.");
