@@ -26,7 +26,9 @@ NVCC_FLAGS = [
     "--fmad=false",  # only the explicit fmaf() calls fuse, matching the reference's rounding points
     "-Xcompiler", "-fPIC",
     "-shared",
-    "--split-compile", "0",  # optimise the kernel instantiations on every host core in parallel
+    # No --split-compile: its parallel device optimisation gave a different
+    # binary on every build of the same source (instantiations measured up to
+    # 20 % apart on a B200); one thread gives the same code each time.
 ]
 
 

@@ -1437,25 +1437,31 @@ __device__ __forceinline__ void int8_merged_pk(const uint32_t (&wv)[8], const fl
 // (_quantize_kernel, _triton_int8_lora.py:189-236): x = scale_dtype(m *
 // scale_dtype(1 / scale)), q = rint(x) + zp clamped to [qmin, qmax]. In an
 // all-finite row |x| <= 128 or so, far below 2^22, so rint(x) is the sum
-// x + 1.5 * 2^23 (exact in fp32), the zero point is added exactly after it,
-// and the low byte of the clamped sum's bits is q.
+// x + 1.5 * 2^23 (exact in fp32), whose bits are 0x4B400000 + rint(x); after
+// the clamp the zero point is added to those bits, and their low byte is q.
 __device__ __forceinline__ void int8_encode_rtn_finite(const float (&m)[32], const Int8Q& q, int qmin, int qmax,
                                                        int scale_dt, uint32_t (&out)[8]) {
   const float inv = round_dt_rt(div_full(1.0f, q.scale), scale_dt);
-  const float2 inv2 = make_float2(inv, inv);
   const float2 magic2 = make_float2(12582912.0f, 12582912.0f);
-  const float2 zp2 = make_float2(static_cast<float>(q.zp), static_cast<float>(q.zp));
-  const float lo = 12582912.0f + static_cast<float>(qmin), hi = 12582912.0f + static_cast<float>(qmax);
+  // rint(x) is clamped to [qmin - zp, qmax - zp] in the float domain and the
+  // zero point is added to the bits.
+  const float lo = 12582912.0f + static_cast<float>(qmin - q.zp);
+  const float hi = 12582912.0f + static_cast<float>(qmax - q.zp);
+  const uint32_t zpu = static_cast<uint32_t>(q.zp);
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
     uint32_t qb[4];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      float2 x = __fmul2_rn(make_float2(m[4 * w + 2 * h], m[4 * w + 2 * h + 1]), inv2);
+      // Scalar products: with fp32 scales nothing separates the product from
+      // the magic add, and a packed product followed by the packed add was
+      // measured to round as one fused multiply-add (codes off by one at
+      // x = n + 1/2); __fmul_rn is never fused.
+      float2 x = make_float2(__fmul_rn(m[4 * w + 2 * h], inv), __fmul_rn(m[4 * w + 2 * h + 1], inv));
       round_rt2(x.x, x.y, scale_dt);
-      const float2 y = __fadd2_rn(__fadd2_rn(x, magic2), zp2);
-      qb[2 * h] = __float_as_uint(fminf(fmaxf(y.x, lo), hi));
-      qb[2 * h + 1] = __float_as_uint(fminf(fmaxf(y.y, lo), hi));
+      const float2 y = __fadd2_rn(x, magic2);
+      qb[2 * h] = __float_as_uint(fminf(fmaxf(y.x, lo), hi)) + zpu;
+      qb[2 * h + 1] = __float_as_uint(fminf(fmaxf(y.y, lo), hi)) + zpu;
     }
     out[w] = __byte_perm(__byte_perm(qb[0], qb[1], 0x0040u), __byte_perm(qb[2], qb[3], 0x0040u), 0x5410u);
   }
@@ -2672,6 +2678,12 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
       // (red_special), and so did some warpgroup (f_special, encode sweep).
       bool red_special = false, f_special = false;
       int red_qp = -1;
+      // ENCODE passes: qparams of the last quantization block encoded.
+      int enc_qp = -1;
+      Int8Q enc_q;
+      enc_q.scale = 1.0f;
+      enc_q.zp = 0;
+      float enc_s = 1.0f;
       auto flush_reduce = [&]() {
         if (red_qp >= 0) {
           atomic_max_nonneg(&W.qmax[red_qp], red_max);
@@ -3132,6 +3144,79 @@ __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const _
             if constexpr (kFlv == kQuanto) {
               if (W.col_axis) {
                 quanto_column_chunk<FMT, PASS, CDT>(W, c, k, col, nvalid, acc, lane, key);
+                return;
+              }
+            }
+            if constexpr (kFlv == kTorchao) {
+              // TorchAO FP8 / INT8, a full chunk inside one quantization block
+              // (per-row weights too small for the fused pass, per-tensor,
+              // groups wider than a tile): the packed decode and merge of the
+              // fused sweeps, block qparams computed once per block.
+              if (nvalid == 32 && (W.nq_row == 0 || (W.group >= 32 && (col % W.group) + 32 <= W.group))) {
+                uint32_t out[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+                if (valid) {
+                  const int qp = qparam_index(W, row, col);
+                  qp_load<FMT, PASS>(W, qp, qc);
+                  uint32_t wv[8];
+                  load_chunks32(c, k, wv);
+                  const bool owner = W.nq_row == 0 ? (row == 0 && col == 0) : (col % W.group == 0);
+                  if constexpr (PASS == kReduce) {
+                    // Unrounded merged values: rounding is monotone, so the
+                    // rounded block maxima are the maxima of the rounded values.
+                    if constexpr (kInt8) int8_merged_pk<CDT, false>(wv, acc, qc.s_in, qc.z_in, W.scale_dt, W.strength, merged);
+                    else fp8_merged_pk<kE4, CDT, false>(wv, acc, qc.s_in, W.strength, merged);
+                    if (qp != red_qp) {
+                      flush_reduce();
+                      red_qp = qp;
+                    }
+                    if (owner) {  // first touch of the block saves its input qparams
+                      W.old_scale[qp] = qc.s_in;
+                      if constexpr (kInt8) W.old_zp[qp] = qc.z_in;
+                    }
+                    if constexpr (kInt8) {
+                      red_max = fmaxf(red_max, round_dt<CDT>(tree3(merged, max3f)));
+                      red_nmin = fmaxf(red_nmin, -round_dt<CDT>(tree3(merged, min3f)));
+                    } else {
+                      red_max = fmaxf(red_max, round_dt<CDT>(tree3(merged, max3_abs)));
+                    }
+                    return;
+                  } else {
+                    if (qp != enc_qp) {
+                      enc_qp = qp;
+                      if constexpr (kInt8) enc_q = int8_qparams<CDT>(-qc.nmin, qc.qmax, asym, qmin, qmax, W.scale_dt);
+                      else enc_s = fp8_new_scale<CDT>(qc.qmax, kLimit);
+                    }
+                    if (owner) {
+                      if constexpr (kInt8) {
+                        store_scale_dt(W.scale, qp, W.scale_dt, enc_q.scale);
+                        if (W.zp != nullptr) W.zp[qp] = static_cast<int8_t>(enc_q.zp);
+                      } else {
+                        store_scale<FMT>(W, qp, enc_s);
+                      }
+                    }
+                    if constexpr (kInt8) int8_merged_pk<CDT, true>(wv, acc, qc.s_in, qc.z_in, W.scale_dt, W.strength, merged);
+                    else fp8_merged_pk<kE4, CDT, true>(wv, acc, qc.s_in, W.strength, merged);
+                    const uint64_t off0 =
+                        W.offset_base + static_cast<uint64_t>(row) * static_cast<uint64_t>(W.N) + col;
+                    const bool sr_on = (W.flags & PIPER_FLAG_STOCHASTIC) != 0u;
+                    // Finite values under finite block maxima stay within the
+                    // range the shortcut encoders assume (|m| <= the maxima).
+                    const bool finite = tree3(merged, max3_abs_nan) <= 3.40282347e38f &&
+                                        qc.qmax <= 3.40282347e38f && (!kInt8 || qc.nmin <= 3.40282347e38f);
+                    if constexpr (kInt8) {
+                      if (!sr_on && finite) int8_encode_rtn_finite(merged, enc_q, qmin, qmax, W.scale_dt, out);
+                      else int8_encode32(merged, enc_q, qmin, qmax, W.scale_dt, sr_on, key, off0, out);
+                    } else if (finite) {
+                      if (sr_on) fp8_encode_sr_finite<kE4>(merged, enc_s, key, off0, out);
+                      else fp8_encode_rtn_finite<kE4>(merged, enc_s, out);
+                    } else if (sr_on) {
+                      fp8_encode_sr<kE4>(merged, enc_s, kLimit, key, off0, out);
+                    } else {
+                      fp8_encode_rtn<kE4>(merged, enc_s, kLimit, out);
+                    }
+                  }
+                }
+                if constexpr (PASS == kEncode) store_chunks32(c, k, out);
                 return;
               }
             }

@@ -161,7 +161,9 @@ class Case:
                      "int8_group": (1, self.group), "int8_asym": (1, self.cols)}[f]
             zp = None if q.zero_point is None else q.zero_point.numpy()
             nq, ns, nz = om.merge_int8(q.qdata.numpy(), f32np(q.scale), zp, block, b, a, self.strength,
-                                       asymmetric=zp is not None, compute=cdt, qparam="bf16", **kw)
+                                       asymmetric=zp is not None, compute=cdt,
+                                       qparam={torch.float16: "f16", torch.float32: "f32"}.get(q.scale.dtype, "bf16"),
+                                       **kw)
             return {"q": nq, "scale": ns, "zp": None if zp is None else nz}
         qt = om.Q8_0 if f == "q8_0" else om.Q4_0
         return {"q": om.merge_gguf(u8np(q.qdata), qt, b, a, self.strength, compute=cdt, **kw)}

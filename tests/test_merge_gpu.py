@@ -82,6 +82,27 @@ def test_medium_shapes(fmt, stochastic, cuda_device):
                outliers=0.001), cuda_device)
 
 
+@pytest.mark.parametrize("stochastic", [False, True], ids=["rtn", "sr"])
+@pytest.mark.parametrize("fmt", ["int8_row", "int8_asym", "fp8_row"])
+def test_per_row_fused_pass_exact(fmt, stochastic, cuda_device):
+    """Per-row weights with more than two 128-row strips per SM (298 strips,
+    the last one 12 rows) run the one-launch fused pass and its shortcut
+    encoders for all-finite rows; smaller ones run the reduce / encode pair."""
+    check(Case(fmt, 297 * 128 + 12, 160, 8, seed=SEED if stochastic else None), cuda_device, exact=True)
+
+
+@pytest.mark.parametrize("fmt", ["int8_row", "int8_asym"])
+def test_per_row_fused_pass_fp32_scales_exact(fmt, cuda_device):
+    """fp32 INT8 scales leave no rounding between ``m * inv`` and the
+    round-to-integer step, so a fused multiply-add there shows at ties."""
+    cs = Case(fmt, 297 * 128 + 12, 160, 8).build(data_seed=5)
+    cs.tensors["q"].scale = cs.tensors["q"].scale.float()
+    got = cs.run_native(cuda_device)
+    torch.cuda.synchronize(cuda_device)
+    d = compare(cs, got, cs.run_oracle())
+    assert d.code_mismatch == 0 and d.scale_mismatch == 0, d
+
+
 @pytest.mark.parametrize("mode", [0, 1, 2, 3], ids=["floor", "rceil", "ceil", "even"])
 @pytest.mark.parametrize("fmt", ["mxfp8", "mxfp8_e5m2", "mxfp4"])
 def test_mx_scale_modes(fmt, mode, cuda_device):
