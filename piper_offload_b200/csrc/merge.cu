@@ -2262,6 +2262,7 @@ __device__ __forceinline__ uint32_t swizzle_xor(int r, int row_bytes) {
 template <int FMT, int PASS, int BN, int CDT>
 __global__ void __launch_bounds__(ws_threads<FMT, BN>(), 1) merge_kernel(const __grid_constant__ LaunchParams P) {
   constexpr int kEpiWGs = epi_wgs<FMT, BN>();
+  static_assert(kEpiWGs <= 3, "kTailBytes reserves the row-maxima exchange (rpart) for three epilogue warpgroups");
   // Arrivals that free an item-ring slot: the MMA lane, the two loader warps
   // and every epilogue warp.
   constexpr uint32_t kItemReaders = 1 + 2 + 4 * kEpiWGs;
