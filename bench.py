@@ -69,6 +69,20 @@ CONFIGS = {
     "nf4_nested": (LLAMA3_8B, 32, 64, 0.005, 0.02, False,
                    "bitsandbytes NF4, nested absmax, Llama-3-8B x32, r64, RTN"),
 }
+
+
+def apply_rank(rank: int) -> None:
+    """Run every config at LoRA rank ``rank`` (``--rank``); spawned CPU-baseline
+    workers re-import this module and read it from ``PIPER_BENCH_RANK``."""
+    import re
+
+    os.environ["PIPER_BENCH_RANK"] = str(rank)
+    for k, v in list(CONFIGS.items()):
+        CONFIGS[k] = (v[0], v[1], rank, *v[3:6], re.sub(r"\br\d+\b", f"r{rank}", v[6]))
+
+
+if os.environ.get("PIPER_BENCH_RANK"):
+    apply_rank(int(os.environ["PIPER_BENCH_RANK"]))
 # Algorithmic bytes per element (read + write) and per-row scale bytes.
 BYTES_PER_ELEM = {"fp8": 2.0, "int8": 2.0, "int8_4096": 2.0, "nvfp4": 1.125, "mxfp8": 2.0625, "mxfp4": 1.0625,
                   "q8_0": 2.125, "q4_0": 1.125, "static_fp8": 2.0, "bnb8": 2.0, "quanto_int8": 2.0,
@@ -547,6 +561,7 @@ def main() -> int:
     ap.add_argument("--config", default="fp8", choices=sorted(CONFIGS))
     ap.add_argument("--rtn", action="store_true", help="round-to-nearest instead of the config's rounding")
     ap.add_argument("--sr", action="store_true", help="stochastic rounding instead of the config's rounding")
+    ap.add_argument("--rank", type=int, default=None, help="LoRA rank instead of the config's")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -561,6 +576,8 @@ def main() -> int:
     ap.add_argument("--staging", action="store_true",
                     help="time merge_lora() with host-resident factors: batched staging vs the per-weight driver")
     args = ap.parse_args()
+    if args.rank:
+        apply_rank(args.rank)
     warmup = max(3, args.warmup)
     if args.staging:
         print(json.dumps(staging_bench(args.config, args.layers, args.steps, warmup)), flush=True)

@@ -3722,7 +3722,11 @@ int validate(const piper_merge_desc& d, Plan& p) {
   };
   // Stochastic NVFP4 prefers three epilogue warpgroups, i.e. 128-column tiles.
   const bool narrow = d.format == PIPER_FMT_NVFP4 && (d.flags & PIPER_FLAG_STOCHASTIC) != 0u;
-  if (!narrow && fits(256, 4)) p.bn = 256;
+  // GGUF rows reach the tile by TMA only when a tile row is a multiple of 16
+  // bytes, i.e. at 256 columns (Q8_0: 272 bytes, Q4_0: 144); narrower tiles
+  // take the cp.async fallback, so GGUF keeps 256 columns down to two stages.
+  const bool gguf = d.format == PIPER_FMT_GGUF_Q8_0 || d.format == PIPER_FMT_GGUF_Q4_0;
+  if (!narrow && fits(256, gguf ? 2 : 4)) p.bn = 256;
   else if (fits(128, 4)) p.bn = 128;
   else if (fits(64, 2)) p.bn = 64;
   else return fail(PIPER_MERGE_EINVAL, "rank " + std::to_string(d.rank) + " is too large for the merge pipeline.");

@@ -150,7 +150,9 @@ def test_strengths(strength, cuda_device):
 
 @pytest.mark.parametrize("rank", [1, 16, 128, 200, 256])
 def test_ranks(rank, cuda_device):
-    for fmt in ("mxfp4", "fp8_row"):
+    # GGUF: 256-column TMA tiles up to rank 160 (Q8_0) / 224 (Q4_0), the
+    # cp.async fallback on narrower tiles above.
+    for fmt in ("mxfp4", "fp8_row", "q8_0", "q4_0"):
         check(Case(fmt, 160, 512, rank), cuda_device)
 
 
